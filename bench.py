@@ -1,0 +1,345 @@
+#!/usr/bin/env python
+"""Benchmark of the int4-g128 decode GEMV (the quantised-weight matmul hot path).
+
+Workload (one step): y_r[M, N] = x[M, K] . W_r^T for R distinct int4 group-128
+asymmetric weights W_r (K=4096, N=12288, M=1; W ~ N(0, 0.02), quantised with
+the exporter's per-group rule), all resident in HBM.  R copies (> 3x L2 in
+total) rotate, so every step streams its weights from HBM.  With --gpus G the
+weight rows are N-sharded (each GPU holds 12288 rows of a 12288*G-row weight:
+per-GPU work is fixed, "weak" scaling) and the output slices are all-gathered
+over NCCL inside the step.
+
+Prints one JSON line (rank 0): value = algorithmic bytes streamed by all ranks
+per second (GB/s), the roofline of the GEMV kernel, an end-to-end number
+through the C ABI with host buffers, and (N=1) the CPU reference path timed on
+the host.  --impl reference times the reference's CPU path (the C restatement
+of gpubackend.nim cpuDequantMatmulQ4Fallback + cpuMatmul) instead.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "nimformers-framework_b200"))
+
+K, N_PER_GPU, M, GS = 4096, 12288, 1, 128
+METRIC = "int4 GEMV HBM GB/s"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0}
+
+
+def algo_bytes(n, k, m, gs):
+    """Bytes a GEMV must move: packed nibbles + fp32 scale and zero per group
+    + x + y (the per-unit figure the roofline uses)."""
+    return n * k // 2 + n * ((k + gs - 1) // gs) * 8 + 4 * m * k + 4 * m * n
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return d, "measured"
+    except Exception:
+        return PEAKS_FALLBACK, "fallback"
+
+
+def profile_traffic():
+    """DRAM bytes per GEMV launch from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", "q4g_gemv_k4096_n12288_m1.txt")
+    try:
+        for line in open(p):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(float(line.split(":", 1)[1].strip()))
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), "--query-gpu=" + self.FIELDS,
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.15)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [v.strip() for v in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_reference_gemv_rate(p, s, z, x, seconds, rows=None):
+    """Times the reference CPU path (oracle restatement of
+    gpubackend.nim:628-653 + :560-582) on the first `rows` output rows.
+    Returns (GB/s of the metric, description)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import pyoracle as O
+    n = N_PER_GPU if rows is None else rows
+    bpr = K // 2
+    ngr = K // GS
+    pp, ss, zz = p[: n * bpr], s[: n * ngr], z[: n * ngr]
+    it, t0 = 0, time.perf_counter()
+    while True:
+        O.dequant_matmul_q4(x, pp, ss, zz, M, K, n, GS, ngr)
+        it += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    rate = algo_bytes(n, K, M, GS) * it / el / 1e9
+    desc = ("%d x GEMV K=%d N=%d M=%d through cpuDequantMatmulQ4Fallback+cpuMatmul "
+            "(C restatement, 1 thread) in %.1f s" % (it, K, n, M, el))
+    return rate, desc
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    import numpy as np
+    import nimf
+    w = (np.random.default_rng(0).standard_normal((N_PER_GPU, K)) * 0.02).astype(np.float32)
+    p, s, z = nimf.quantize_int4_per_group(w, GS)
+    x = np.random.default_rng(1).standard_normal((M, K)).astype(np.float32)
+    # bounded sample per step: a row slice sized so the whole run takes ~1-2 min
+    t0 = time.perf_counter()
+    cpu_reference_gemv_rate(p, s, z, x, 0.0, rows=512)
+    t512 = time.perf_counter() - t0
+    budget = 90.0 / max(1, args.steps + args.warmup)
+    rows = int(min(N_PER_GPU, max(16, 512 * budget / max(t512, 1e-6))))
+    rows = max(16, rows - rows % 16)
+    for _ in range(args.warmup):
+        cpu_reference_gemv_rate(p, s, z, x, 0.0, rows=rows)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_reference_gemv_rate(p, s, z, x, 0.0, rows=rows)
+    el = time.perf_counter() - t0
+    value = algo_bytes(rows, K, M, GS) * args.steps / el / 1e9
+    sample = "each step: GEMV K=%d N=%d (row slice of 12288) M=%d, 1 thread" % (K, rows, M)
+    line = {"metric": METRIC, "value": value, "unit": "GB/s", "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u4 weights, f32",
+            "data": "synthetic",
+            "config": {"workload": "int4-g128 decode GEMV K=4096 N=12288 M=1", "K": K,
+                       "N": N_PER_GPU, "M": M, "group_size": GS},
+            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": 1, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank, world, local_rank):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import nimf
+
+    torch.cuda.set_device(local_rank)
+    nimf.init(local_rank)
+    R = args.copies
+    n_total = N_PER_GPU * world
+    r0, r1 = rank * N_PER_GPU, (rank + 1) * N_PER_GPU
+
+    # synthetic weights: the same quantised matrix on every rank's shard rows
+    w = (np.random.default_rng(0).standard_normal((N_PER_GPU, K)) * 0.02).astype(np.float32)
+    p, s, z = nimf.quantize_int4_per_group(w, GS)
+    if world > 1:
+        p = np.tile(p, world)
+        s = np.tile(s, world)
+        z = np.tile(z, world)
+    weights = [nimf.Weight.q4g(p, s, z, n_total, K, GS, rows=(r0, r1)) for _ in range(R)]
+    x = torch.randn(M, K, device="cuda", dtype=torch.float32, generator=torch.Generator("cuda").manual_seed(1))
+    ys = torch.empty(R, M, N_PER_GPU, device="cuda", dtype=torch.float32)
+    gathered = torch.empty(world, R, M, N_PER_GPU, device="cuda", dtype=torch.float32) if world > 1 else None
+
+    stream = torch.cuda.Stream()
+
+    def step(st):
+        for r in range(R):
+            weights[r].matmul_dev(x.data_ptr(), M, ys[r].data_ptr(), st.cuda_stream)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered.view(-1), ys.view(-1))
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(1, args.warmup)):
+            step(stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step(stream)
+    torch.cuda.synchronize()
+
+    # correctness spot check of one output against a host computation
+    if rank == 0:
+        y0 = ys[0].cpu().numpy()
+        wd = weights[0].dequant()
+        ref = wd.astype(np.float64) @ x.cpu().numpy().astype(np.float64).T
+        err = float(np.max(np.abs(y0.ravel() - ref.ravel())) / np.max(np.abs(ref)))
+        if not err <= 1e-3:
+            raise RuntimeError("bench: GEMV output check failed (rel err %.3g)" % err)
+
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.2)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        graph.replay()
+    end.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    bytes_step = R * algo_bytes(N_PER_GPU, K, M, GS) * world
+    value = bytes_step / (ms_per_step * 1e-3) / 1e9
+
+    # kernel-level roofline: average duration of one GEMV launch in the region
+    pk, how = peaks()
+    per_launch_bytes = algo_bytes(N_PER_GPU, K, M, GS)
+    launch_s = ms * 1e-3 / (args.steps * R)
+    achieved = per_launch_bytes / launch_s / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / pk["hbm_gbs"], "traffic": profile_traffic(),
+                "peak_source": how, "kernel": "q4g_gemv_kernel<1>",
+                "note": "launch duration = timed region / launches (back-to-back, PDL)"}
+
+    # end to end through the C ABI with host buffers (pinned), per step R calls
+    xh = torch.randn(M, K, dtype=torch.float32).pin_memory()
+    yh = torch.empty(R, M, N_PER_GPU, dtype=torch.float32).pin_memory()
+    L = nimf.lib()
+    import ctypes
+    xp = ctypes.c_void_p(xh.data_ptr())
+    yps = [ctypes.c_void_p(yh[r].data_ptr()) for r in range(R)]
+
+    def e2e_step():
+        for r in range(R):
+            nimf.check(L.nimf_matmul_w(weights[r].handle, xp, M, yps[r]))
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    e2e_steps = max(5, min(args.steps, 200))
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = {"value": bytes_step / e2e_s / 1e9, "unit": "GB/s",
+           "h2d_bytes_per_step": R * M * K * 4, "d2h_bytes_per_step": R * M * N_PER_GPU * 4,
+           "api": "nimf_matmul_w (host buffers, blocking, per weight)",
+           "note": "per-rank shard outputs; no host all-gather" if world > 1 else ""}
+
+    cpu = None
+    if rank == 0 and world == 1 and args.cpu_seconds > 0:
+        xs = np.random.default_rng(1).standard_normal((M, K)).astype(np.float32)
+        rate, desc = cpu_reference_gemv_rate(p[: N_PER_GPU * K // 2], s, z, xs, args.cpu_seconds)
+        cpu = {"value": rate, "unit": "GB/s", "cores": 1, "kind": "port", "sample": desc}
+
+    graph.reset()
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "u4 weights, f32 activations/accumulate", "data": "synthetic",
+                "config": {"workload": "int4-g128 decode GEMV K=4096 N=12288 M=1 per GPU",
+                           "K": K, "N_per_gpu": N_PER_GPU, "N_total": n_total, "M": M,
+                           "group_size": GS, "weight_copies": R,
+                           "l2": "inputs larger than L2: %d rotating weight copies, %.0f MB per GPU"
+                                 % (R, R * algo_bytes(N_PER_GPU, K, M, GS) / 1e6),
+                           "parallelism": "N-shard x%d + NCCL all-gather" % world if world > 1 else "single GPU"},
+                "pct_of_hbm_peak": value / world / pk["hbm_gbs"],
+                "roofline": roofline, "e2e": e2e, "gpu_launches": args.steps * R,
+                "clocks": clocks}
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    for wt in weights:
+        wt.free()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--copies", type=int, default=14)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,207 @@
+/*
+ * nimf_cuda.h -- C ABI of libnimf_cuda.so, the B200 (sm_100a) implementation
+ * of Nimformer's quantised-weight matmul path.
+ *
+ * Drop-in boundary.  Every entry point below replaces one call of the
+ * reference's backend path; the citation beside it names the reference
+ * procedure ("file:line" inside the Nimformer project).  The reference host
+ * code binds these with {.importc: "nimf_...", dynlib: "libnimf_cuda.so".}.
+ *
+ * Conventions
+ *   - Plain C types only; all sizes are int64_t element counts.
+ *   - Every function returns NIMF_OK (0) or a negative NIMF_ERR_* code and
+ *     never falls back to the CPU.  nimf_last_error() returns a thread-local
+ *     message for the last failure on the calling thread (the Nim wrapper
+ *     raises CatchableError(msg), like cuda_runtime.nim:64-66).
+ *   - One process drives one GPU (nimf_init(device)).  Calls are made from
+ *     one host thread; the library is not re-entrant.
+ *   - Functions taking HOST pointers are blocking: inputs are copied to the
+ *     device, the kernel runs, results are copied back before return (the
+ *     same contract as backend.nim's be* procs).  Functions with the _dev
+ *     suffix take DEVICE pointers and a cudaStream_t (passed as void*, NULL =
+ *     the library stream) and are asynchronous.
+ *   - Weight layout on entry is the reference's QuantTensor layout
+ *     (quant.nim:22-35): row = output channel, W[N][K].
+ */
+#ifndef NIMF_CUDA_H
+#define NIMF_CUDA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NIMF_OK 0
+#define NIMF_ERR_ARG (-1)         /* bad pointer / argument                    */
+#define NIMF_ERR_SHAPE (-2)       /* inconsistent sizes                        */
+#define NIMF_ERR_CUDA (-3)        /* CUDA runtime / launch failure             */
+#define NIMF_ERR_NCCL (-4)        /* collective failure                        */
+#define NIMF_ERR_TIMEOUT (-5)     /* bounded device / host wait expired        */
+#define NIMF_ERR_UNSUPPORTED (-6) /* format or shape not implemented           */
+#define NIMF_ERR_STATE (-7)       /* nimf_init not called / bad handle         */
+
+typedef uint64_t nimf_weight_t; /* opaque handle of a device-resident weight */
+
+/* Weight kinds (values equal the reference's on-disk QuantKind ordinal,
+ * quant.nim:12-20, where one exists). */
+#define NIMF_KIND_F32 0
+#define NIMF_KIND_INT8 1
+#define NIMF_KIND_INT4_SYM 2
+#define NIMF_KIND_INT4_ASYM 3
+#define NIMF_KIND_CUSTOM_FLOAT 6
+#define NIMF_KIND_FP4_E2M1 100 /* no reference counterpart (extension) */
+
+/* ------------------------------------------------------------ lifetime */
+
+/* Replaces cuda_driver.nim:173-194 ensureInit (context, stream, PTX module
+ * load) for this path: binds the calling process to `device`, creates the
+ * library stream.  Idempotent for the same device. */
+int nimf_init(int device);
+
+/* Frees every registered weight and the library stream.  cuda_driver.nim has
+ * no counterpart (its singletons live until exit). */
+int nimf_shutdown(void);
+
+/* Thread-local message of the last failure (cuda_driver.nim:88-92 gpuCheck
+ * raises with such a message). */
+const char* nimf_last_error(void);
+
+/* Number of visible CUDA devices (cuda_runtime.nim:116-120 cudaRuntimeAvailable). */
+int nimf_device_count(int* count);
+
+/* Blocks until all work on the library stream is done. */
+int nimf_sync(void);
+
+/* ------------------------------------------------------------ weights */
+
+/* int4 asymmetric per-group weights exactly as QuantTensor holds them
+ * (quant.nim:131-167, export_to_nimq.py:363-395):
+ *   wq      : N rows of ceil(K/2) bytes, element k of a row in byte k/2,
+ *             even k in the low nibble
+ *   scales, zeros : float32 [N * n_groups_per_row], group g = k / group_size
+ *   w[n,k] = (float(nibble) - zero) * scale
+ * group_size <= 0 means one group per row (gpubackend.nim:645, gc = 0).
+ * Rows [row_begin, row_end) are uploaded (an N-shard); pass 0, N for all.
+ * Uploads once; the returned handle replaces the per-call copies of
+ * beMatmulQ4 (backend.nim:93-101).  Weights are repacked on the device into
+ * a tensor-core fragment order (the dequantised values are unchanged). */
+int nimf_weight_register_q4g(const uint8_t* wq, const float* scales, const float* zeros,
+                             int64_t n, int64_t k, int64_t group_size,
+                             int64_t n_groups_per_row, int64_t row_begin, int64_t row_end,
+                             nimf_weight_t* out);
+
+/* int8 symmetric weights, quant.nim:51-67: q int8 [N][K], n_scales == 1
+ * (per-tensor, the reference) or n_scales == N (per output channel, an
+ * extension the reference does not have).  w = float(q) * scale. */
+int nimf_weight_register_i8(const int8_t* q, const float* scales, int64_t n_scales,
+                            int64_t n, int64_t k, int64_t row_begin, int64_t row_end,
+                            nimf_weight_t* out);
+
+/* CustomFloat-encoded weights (customfloat.nim:49-136, quant.nim:198-206,254):
+ * data holds N*K items of ceil((1+e+m)/8) little-endian bytes, decoded with
+ * packedU64ToFp32 semantics.  row_scales (nullable) multiplies output channel
+ * n after decoding (the per-channel fp8 scale extension; the reference stores
+ * no scale, quant.nim:203). */
+int nimf_weight_register_cf(const uint8_t* data, int exponent_bits, int mantissa_bits,
+                            const float* row_scales, int64_t n, int64_t k,
+                            int64_t row_begin, int64_t row_end, nimf_weight_t* out);
+
+/* FP4 E2M1 with one OCP-E4M3 scale per 16 elements of a row and a float32
+ * tensor scale (no reference counterpart: the reference's CustomFloat(2,1)
+ * is a different format).  packed: N rows of ceil(K/2) bytes, even k low
+ * nibble; block_scales: N * ceil(K/16) bytes.
+ * w = e2m1(nibble) * (e4m3(block_scale) * tensor_scale). */
+int nimf_weight_register_fp4(const uint8_t* packed, const uint8_t* block_scales,
+                             float tensor_scale, int64_t n, int64_t k, int64_t row_begin,
+                             int64_t row_end, nimf_weight_t* out);
+
+/* Raw float32 weights given as beMatmul's b operand [K][N] row-major
+ * (backend.nim:87, gpubackend.nim:584). */
+int nimf_weight_register_f32(const float* b_kn, int64_t k, int64_t n, nimf_weight_t* out);
+
+/* Releases the device copy (cuda_driver.nim:262-265 freeResident). */
+int nimf_weight_free(nimf_weight_t w);
+
+/* Logical shape, kind and device bytes of a registered weight. */
+int nimf_weight_info(nimf_weight_t w, int64_t* n_rows, int64_t* k, int* kind,
+                     int64_t* device_bytes);
+
+/* ------------------------------------------------------------ matmul */
+
+/* y[M][N_shard] = x[M][K] . W^T for any registered weight, HOST buffers,
+ * blocking.  Format-generic form of Linear.forward's dispatch
+ * (nimformer.nim:101-133): int4 -> beMatmulQ4, other kinds -> the
+ * dequantizeTensorTransposed + beMatmul branch, without the host dequant. */
+int nimf_matmul_w(nimf_weight_t w, const float* x, int64_t m, float* y);
+
+/* Same on DEVICE buffers (x [M][K], y [M][N_shard] row-major, fp32),
+ * asynchronous on `stream` (NULL = library stream).  This is the resident
+ * form the reference's CUDA session API has for fp32 only
+ * (cuda_runtime.nim:158-180 cudaMatmulF32R). */
+int nimf_matmul_w_dev(nimf_weight_t w, const float* x_dev, int64_t m, float* y_dev,
+                      void* stream);
+
+/* Drop-in for beMatmulQ4 (backend.nim:93-110 -> gpubackend.nim:655-676):
+ * same arguments, HOST arrays, out = float32 [M*N].  The packed weights are
+ * cached on the device keyed by (wq pointer, bytes, K, N, group size), valid
+ * because Nim weights are immutable after setQuantWeight (nimformer.nim:94-100);
+ * nimf_weight_cache_clear() drops the cache. */
+int nimf_matmul_q4(const float* a, const uint8_t* wq, const float* scales,
+                   const float* zeros, int64_t m, int64_t k, int64_t n, int64_t group_size,
+                   int64_t n_groups_per_row, float* out);
+int nimf_weight_cache_clear(void);
+
+/* Drop-in for beMatmul (backend.nim:87-91 -> cuda_runtime.nim:122-152):
+ * C[M][N] = A[M][K] . B[K][N], fp32, HOST arrays.  k2 must equal k. */
+int nimf_matmul_f32(const float* a, int64_t m, int64_t k, const float* b, int64_t k2,
+                    int64_t n, float* out);
+
+/* Drop-in for beMatmul2 (backend.nim:112-119 -> gpubackend.nim:606-626):
+ * two independent fp32 GEMMs issued together. */
+int nimf_matmul2_f32(const float* a1, int64_t m1, int64_t k1, const float* b1, int64_t k1b,
+                     int64_t n1, const float* a2, int64_t m2, int64_t k2, const float* b2,
+                     int64_t k2b, int64_t n2, float* out1, float* out2);
+
+/* Test hook: writes the dequantised weight of a registered int / fp format as
+ * float32 [N_shard][K] in the reference's row-major layout, computed by the
+ * device with the reference's rounding ((float(q) - zero) * scale,
+ * quant.nim:162), so a bit-exact comparison with dequantizeTensor is possible. */
+int nimf_dequant_w(nimf_weight_t w, float* out_host);
+
+/* ------------------------------------------------------------ CustomFloat / APF */
+
+/* beCustomfloatEncode (backend.nim:177-178 -> customfloat.nim:125-129):
+ * out receives n * itemSize bytes.  total bits must be <= 64. */
+int nimf_cf_encode(const float* x, int64_t n, int exponent_bits, int mantissa_bits,
+                   uint8_t* out);
+
+/* beCustomfloatDecode (backend.nim:180-181 -> customfloat.nim:131-136):
+ * nbytes must be a multiple of itemSize; out receives nbytes/itemSize floats. */
+int nimf_cf_decode(const uint8_t* buf, int64_t nbytes, int exponent_bits, int mantissa_bits,
+                   float* out);
+
+/* Device-buffer forms of the two above (asynchronous on `stream`). */
+int nimf_cf_encode_dev(const float* x_dev, int64_t n, int exponent_bits, int mantissa_bits,
+                       uint8_t* out_dev, void* stream);
+int nimf_cf_decode_dev(const uint8_t* buf_dev, int64_t nbytes, int exponent_bits,
+                       int mantissa_bits, float* out_dev, void* stream);
+
+/* buildCustomDtypeForTensor (customfloat.nim:149-206): chooses exponent and
+ * mantissa bits for x (grad nullable, n_grad may be 0). */
+int nimf_cf_autoselect(const float* x, int64_t n, const float* grad, int64_t n_grad,
+                       double rel_error_tol, int exp_margin, int* exponent_bits,
+                       int* mantissa_bits);
+
+/* beApfCastForTraining (backend.nim:183-186 -> customfloat.nim:208-213):
+ * autoselect + encode.  out must hold n * 8 bytes (the largest itemSize);
+ * the chosen format is returned in exponent_bits / mantissa_bits and the
+ * encoded length is n * ceil((1+e+m)/8). */
+int nimf_apf_cast(const float* x, int64_t n, const float* grad, int64_t n_grad,
+                  double rel_error_tol, int exp_margin, int* exponent_bits,
+                  int* mantissa_bits, uint8_t* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

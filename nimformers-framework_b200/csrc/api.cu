@@ -1,0 +1,697 @@
+// api.cu -- the extern "C" entry points of libnimf_cuda.so (declared in
+// include/nimf_cuda.h): error reporting, the per-process device context, the
+// device weight registry and the host-buffer drop-ins for backend.nim's be*
+// procs.  No entry point falls back to the CPU: a missing device or a failed
+// launch is returned as an error status, like gpubackend.nim:46-61 with
+// gForbidCpuFallback = true.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <tuple>
+#include <unordered_map>
+#include <vector>
+
+#include "nimf_internal.h"
+
+namespace nimf {
+
+namespace {
+thread_local char g_err[1024] = "";
+Context g_ctx;
+bool g_ready = false;
+std::mutex g_mu;
+std::unordered_map<nimf_weight_t, std::unique_ptr<Weight>> g_weights;
+nimf_weight_t g_next = 1;
+// beMatmulQ4 host-array cache: (ptr, bytes, k, n, gs, ngr) -> handle
+std::map<std::tuple<uintptr_t, int64_t, int64_t, int64_t, int64_t, int64_t>, nimf_weight_t>
+    g_q4_cache;
+}  // namespace
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+Context* ctx() { return g_ready ? &g_ctx : nullptr; }
+
+int require_ctx(Context** out) {
+  if (!g_ready) return set_error(NIMF_ERR_STATE, "nimf_init() has not been called");
+  NIMF_CUDA_TRY(cudaSetDevice(g_ctx.device));
+  *out = &g_ctx;
+  return NIMF_OK;
+}
+
+int device_alloc(void** p, size_t bytes) {
+  *p = nullptr;
+  if (bytes == 0) bytes = 16;
+  cudaError_t e = cudaMalloc(p, bytes);
+  if (e != cudaSuccess) {
+    *p = nullptr;
+    return set_error(NIMF_ERR_CUDA, "cudaMalloc(%zu) failed: %s", bytes, cudaGetErrorString(e));
+  }
+  return NIMF_OK;
+}
+
+void device_free(void* p) {
+  if (p) cudaFree(p);
+}
+
+static int grow(void** buf, size_t* have, size_t bytes) {
+  if (bytes <= *have && *buf) return NIMF_OK;
+  size_t want = std::max<size_t>(bytes, 1 << 20);
+  want = std::max(want, *have * 2);
+  if (*buf) {
+    cudaStreamSynchronize(g_ctx.stream);
+    device_free(*buf);
+    *buf = nullptr;
+    *have = 0;
+  }
+  NIMF_TRY(device_alloc(buf, want));
+  *have = want;
+  return NIMF_OK;
+}
+
+int stage_in(size_t bytes, void** p) {
+  NIMF_TRY(grow(&g_ctx.stage_in, &g_ctx.stage_in_bytes, bytes));
+  *p = g_ctx.stage_in;
+  return NIMF_OK;
+}
+
+int stage_out(size_t bytes, void** p) {
+  NIMF_TRY(grow(&g_ctx.stage_out, &g_ctx.stage_out_bytes, bytes));
+  *p = g_ctx.stage_out;
+  return NIMF_OK;
+}
+
+int64_t Weight::rows() const {
+  switch (kind) {
+    case NIMF_KIND_INT4_ASYM: return q4.rows;
+    case NIMF_KIND_INT8: return i8.rows;
+    case NIMF_KIND_CUSTOM_FLOAT: return cf.rows;
+    case NIMF_KIND_FP4_E2M1: return fp4.rows;
+    case NIMF_KIND_F32: return f32.rows;
+  }
+  return 0;
+}
+
+int64_t Weight::k() const {
+  switch (kind) {
+    case NIMF_KIND_INT4_ASYM: return q4.k;
+    case NIMF_KIND_INT8: return i8.k;
+    case NIMF_KIND_CUSTOM_FLOAT: return cf.k;
+    case NIMF_KIND_FP4_E2M1: return fp4.k;
+    case NIMF_KIND_F32: return f32.k;
+  }
+  return 0;
+}
+
+void free_weight_storage(Weight* w) {
+  device_free(w->q4.frag);
+  device_free(w->q4.sz);
+  device_free(w->q4.raw);
+  device_free(w->q4.scales);
+  device_free(w->q4.zeros);
+  device_free(w->i8.q);
+  device_free(w->i8.scales);
+  device_free(w->cf.data);
+  device_free(w->cf.row_scales);
+  device_free(w->fp4.packed);
+  device_free(w->fp4.bscale);
+  device_free(w->f32.w);
+  w->q4 = Q4GWeight();
+  w->i8 = I8Weight();
+  w->cf = CFWeight();
+  w->fp4 = FP4Weight();
+  w->f32 = F32Weight();
+}
+
+Weight* lookup(nimf_weight_t h) {
+  auto it = g_weights.find(h);
+  return it == g_weights.end() ? nullptr : it->second.get();
+}
+
+nimf_weight_t insert(std::unique_ptr<Weight> w) {
+  nimf_weight_t h = g_next++;
+  g_weights.emplace(h, std::move(w));
+  return h;
+}
+
+// Temporary device copies of host arrays used while building a weight.
+struct TempBuffers {
+  std::vector<void*> ptrs;
+  ~TempBuffers() {
+    for (void* p : ptrs) device_free(p);
+  }
+  int upload(const void* host, size_t bytes, void** dev, cudaStream_t st) {
+    NIMF_TRY(device_alloc(dev, bytes));
+    ptrs.push_back(*dev);
+    if (bytes) NIMF_CUDA_TRY(cudaMemcpyAsync(*dev, host, bytes, cudaMemcpyHostToDevice, st));
+    return NIMF_OK;
+  }
+};
+
+static int check_rows(int64_t n, int64_t row_begin, int64_t row_end) {
+  if (n < 0 || row_begin < 0 || row_end < row_begin || row_end > n)
+    return set_error(NIMF_ERR_SHAPE, "row range [%lld, %lld) outside [0, %lld)",
+                     (long long)row_begin, (long long)row_end, (long long)n);
+  return NIMF_OK;
+}
+
+static int finish_register(std::unique_ptr<Weight> w, nimf_weight_t* out) {
+  NIMF_CUDA_TRY(cudaStreamSynchronize(g_ctx.stream));
+  NIMF_CUDA_TRY(cudaGetLastError());
+  *out = insert(std::move(w));
+  return NIMF_OK;
+}
+
+// Runs the kernel path of a weight on device buffers.
+static int matmul_dev(Weight* w, const float* x, int64_t m, float* y, cudaStream_t st) {
+  switch (w->kind) {
+    case NIMF_KIND_INT4_ASYM: return q4g_gemv(w->q4, x, m, y, st);
+    case NIMF_KIND_INT8: return i8_gemv(w->i8, x, m, y, st);
+    case NIMF_KIND_CUSTOM_FLOAT: return cf_gemv(w->cf, x, m, y, st);
+    case NIMF_KIND_FP4_E2M1: return fp4_gemv(w->fp4, x, m, y, st);
+    case NIMF_KIND_F32: return f32_gemm(x, m, w->f32.k, (const float*)w->f32.w, w->f32.rows, y, st);
+  }
+  return set_error(NIMF_ERR_UNSUPPORTED, "weight kind %d has no matmul path", w->kind);
+}
+
+}  // namespace nimf
+
+using namespace nimf;
+
+extern "C" {
+
+const char* nimf_last_error(void) { return g_err; }
+
+int nimf_device_count(int* count) {
+  if (!count) return set_error(NIMF_ERR_ARG, "count is NULL");
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) {
+    *count = 0;
+    return set_error(NIMF_ERR_CUDA, "cudaGetDeviceCount failed: %s", cudaGetErrorString(e));
+  }
+  *count = n;
+  return NIMF_OK;
+}
+
+int nimf_init(int device) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_ready) {
+    if (device == g_ctx.device) return NIMF_OK;
+    return set_error(NIMF_ERR_STATE, "already initialised on device %d (asked %d)", g_ctx.device,
+                     device);
+  }
+  int n = 0;
+  NIMF_CUDA_TRY(cudaGetDeviceCount(&n));
+  if (device < 0 || device >= n)
+    return set_error(NIMF_ERR_ARG, "device %d not in [0, %d)", device, n);
+  NIMF_CUDA_TRY(cudaSetDevice(device));
+  cudaDeviceProp prop;
+  NIMF_CUDA_TRY(cudaGetDeviceProperties(&prop, device));
+  if (prop.major < 10)
+    return set_error(NIMF_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a",
+                     device, prop.major, prop.minor);
+  g_ctx = Context();
+  g_ctx.device = device;
+  g_ctx.num_sms = prop.multiProcessorCount;
+  NIMF_CUDA_TRY(cudaStreamCreateWithFlags(&g_ctx.stream, cudaStreamNonBlocking));
+  g_ready = true;
+  return NIMF_OK;
+}
+
+int nimf_shutdown(void) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_ready) return NIMF_OK;
+  cudaSetDevice(g_ctx.device);
+  cudaStreamSynchronize(g_ctx.stream);
+  for (auto& kv : g_weights) free_weight_storage(kv.second.get());
+  g_weights.clear();
+  g_q4_cache.clear();
+  device_free(g_ctx.stage_in);
+  device_free(g_ctx.stage_out);
+  cudaStreamDestroy(g_ctx.stream);
+  g_ctx = Context();
+  g_ready = false;
+  return NIMF_OK;
+}
+
+int nimf_sync(void) {
+  Context* c;
+  NIMF_TRY(require_ctx(&c));
+  NIMF_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  return NIMF_OK;
+}
+
+// ------------------------------------------------------------------ weights
+
+int nimf_weight_register_q4g(const uint8_t* wq, const float* scales, const float* zeros,
+                             int64_t n, int64_t k, int64_t group_size,
+                             int64_t n_groups_per_row, int64_t row_begin, int64_t row_end,
+                             nimf_weight_t* out) {
+  Context* c;
+  NIMF_TRY(require_ctx(&c));
+  if (!out) return set_error(NIMF_ERR_ARG, "out is NULL");
+  if (k < 0) return set_error(NIMF_ERR_SHAPE, "k = %lld < 0", (long long)k);
+  NIMF_TRY(check_rows(n, row_begin, row_end));
+  const int64_t need = group_size > 0 ? (k + group_size - 1) / group_size : 1;
+  if (n_groups_per_row < need)
+    return set_error(NIMF_ERR_SHAPE, "n_groups_per_row = %lld < ceil(K/group_size) = %lld",
+                     (long long)n_groups_per_row, (long long)need);
+  if ((n * k > 0) && (!wq || !scales || !zeros))
+    return set_error(NIMF_ERR_ARG, "NULL weight array");
+  const int64_t bpr = (k + 1) / 2;
+  const int64_t rows = row_end - row_begin;
+  auto w = std::make_unique<Weight>();
+  w->kind = NIMF_KIND_INT4_ASYM;
+  TempBuffers tmp;
+  void *dq = nullptr, *ds = nullptr, *dz = nullptr;
+  // upload only the shard's rows
+  NIMF_TRY(tmp.upload(wq ? wq + row_begin * bpr : nullptr, (size_t)(rows * bpr), &dq, c->stream));
+  NIMF_TRY(tmp.upload(scales ? scales + row_begin * n_groups_per_row : nullptr,
+                      (size_t)(rows * n_groups_per_row) * 4, &ds, c->stream));
+  NIMF_TRY(tmp.upload(zeros ? zeros + row_begin * n_groups_per_row : nullptr,
+                      (size_t)(rows * n_groups_per_row) * 4, &dz, c->stream));
+  int st = q4g_build(w.get(), (const uint8_t*)dq, (const float*)ds, (const float*)dz, 0, rows, n,
+                     k, group_size, n_groups_per_row, c->stream);
+  if (st != NIMF_OK) {
+    free_weight_storage(w.get());
+    return st;
+  }
+  return finish_register(std::move(w), out);
+}
+
+int nimf_weight_register_i8(const int8_t* q, const float* scales, int64_t n_scales, int64_t n,
+                            int64_t k, int64_t row_begin, int64_t row_end, nimf_weight_t* out) {
+  Context* c;
+  NIMF_TRY(require_ctx(&c));
+  if (!out) return set_error(NIMF_ERR_ARG, "out is NULL");
+  if (k < 0) return set_error(NIMF_ERR_SHAPE, "k < 0");
+  NIMF_TRY(check_rows(n, row_begin, row_end));
+  if (n_scales != 1 && n_scales != n)
+    return set_error(NIMF_ERR_SHAPE, "n_scales = %lld must be 1 or N = %lld", (long long)n_scales,
+                     (long long)n);
+  if (!scales || ((n * k > 0) && !q)) return set_error(NIMF_ERR_ARG, "NULL weight array");
+  const int64_t rows = row_end - row_begin;
+  auto w = std::make_unique<Weight>();
+  w->kind = NIMF_KIND_INT8;
+  I8Weight& d = w->i8;
+  d.rows = rows;
+  d.k = k;
+  d.n_scales = n_scales == 1 ? 1 : rows;
+  NIMF_TRY(device_alloc(&d.q, (size_t)(rows * k)));
+  NIMF_TRY(device_alloc(&d.scales, (size_t)d.n_scales * 4));
+  if (rows * k > 0)
+    NIMF_CUDA_TRY(cudaMemcpyAsync(d.q, q + row_begin * k, (size_t)(rows * k),
+                                  cudaMemcpyHostToDevice, c->stream));
+  NIMF_CUDA_TRY(cudaMemcpyAsync(d.scales, n_scales == 1 ? scales : scales + row_begin,
+                                (size_t)d.n_scales * 4, cudaMemcpyHostToDevice, c->stream));
+  w->device_bytes = rows * k + d.n_scales * 4;
+  return finish_register(std::move(w), out);
+}
+
+int nimf_weight_register_cf(const uint8_t* data, int e, int m, const float* row_scales,
+                            int64_t n, int64_t k, int64_t row_begin, int64_t row_end,
+                            nimf_weight_t* out) {
+  Context* c;
+  NIMF_TRY(require_ctx(&c));
+  if (!out) return set_error(NIMF_ERR_ARG, "out is NULL");
+  if (e < 0 || m < 0 || 1 + e + m > 64)
+    return set_error(NIMF_ERR_UNSUPPORTED, "CustomFloat e=%d m=%d: total bits must be <= 64", e, m);
+  if (k < 0) return set_error(NIMF_ERR_SHAPE, "k < 0");
+  NIMF_TRY(check_rows(n, row_begin, row_end));
+  if ((n * k > 0) && !data) return set_error(NIMF_ERR_ARG, "NULL weight array");
+  const int item = (1 + e + m + 7) / 8;
+  const int64_t rows = row_end - row_begin;
+  auto w = std::make_unique<Weight>();
+  w->kind = NIMF_KIND_CUSTOM_FLOAT;
+  CFWeight& d = w->cf;
+  d.rows = rows;
+  d.k = k;
+  d.e = e;
+  d.m = m;
+  d.item = item;
+  const size_t nb = (size_t)(rows * k * item);
+  NIMF_TRY(device_alloc(&d.data, nb));
+  if (nb)
+    NIMF_CUDA_TRY(cudaMemcpyAsync(d.data, data + row_begin * k * item, nb, cudaMemcpyHostToDevice,
+                                  c->stream));
+  w->device_bytes = (int64_t)nb;
+  if (row_scales) {
+    NIMF_TRY(device_alloc(&d.row_scales, (size_t)rows * 4));
+    NIMF_CUDA_TRY(cudaMemcpyAsync(d.row_scales, row_scales + row_begin, (size_t)rows * 4,
+                                  cudaMemcpyHostToDevice, c->stream));
+    w->device_bytes += rows * 4;
+  }
+  return finish_register(std::move(w), out);
+}
+
+int nimf_weight_register_fp4(const uint8_t* packed, const uint8_t* block_scales,
+                             float tensor_scale, int64_t n, int64_t k, int64_t row_begin,
+                             int64_t row_end, nimf_weight_t* out) {
+  Context* c;
+  NIMF_TRY(require_ctx(&c));
+  if (!out) return set_error(NIMF_ERR_ARG, "out is NULL");
+  if (k < 0) return set_error(NIMF_ERR_SHAPE, "k < 0");
+  NIMF_TRY(check_rows(n, row_begin, row_end));
+  if ((n * k > 0) && (!packed || !block_scales)) return set_error(NIMF_ERR_ARG, "NULL array");
+  const int64_t rows = row_end - row_begin;
+  const int64_t bpr = (k + 1) / 2, nb = (k + 15) / 16;
+  auto w = std::make_unique<Weight>();
+  w->kind = NIMF_KIND_FP4_E2M1;
+  FP4Weight& d = w->fp4;
+  d.rows = rows;
+  d.k = k;
+  d.tensor_scale = tensor_scale;
+  NIMF_TRY(device_alloc(&d.packed, (size_t)(rows * bpr)));
+  NIMF_TRY(device_alloc(&d.bscale, (size_t)(rows * nb)));
+  if (rows * bpr > 0)
+    NIMF_CUDA_TRY(cudaMemcpyAsync(d.packed, packed + row_begin * bpr, (size_t)(rows * bpr),
+                                  cudaMemcpyHostToDevice, c->stream));
+  if (rows * nb > 0)
+    NIMF_CUDA_TRY(cudaMemcpyAsync(d.bscale, block_scales + row_begin * nb, (size_t)(rows * nb),
+                                  cudaMemcpyHostToDevice, c->stream));
+  w->device_bytes = rows * bpr + rows * nb;
+  return finish_register(std::move(w), out);
+}
+
+int nimf_weight_register_f32(const float* b_kn, int64_t k, int64_t n, nimf_weight_t* out) {
+  Context* c;
+  NIMF_TRY(require_ctx(&c));
+  if (!out) return set_error(NIMF_ERR_ARG, "out is NULL");
+  if (k < 0 || n < 0) return set_error(NIMF_ERR_SHAPE, "negative shape");
+  if ((n * k > 0) && !b_kn) return set_error(NIMF_ERR_ARG, "NULL weight array");
+  auto w = std::make_unique<Weight>();
+  w->kind = NIMF_KIND_F32;
+  w->f32.rows = n;
+  w->f32.k = k;
+  // stored as given, [K][N] row-major (beMatmul's b)
+  NIMF_TRY(device_alloc(&w->f32.w, (size_t)(k * n) * 4));
+  if (k * n > 0)
+    NIMF_CUDA_TRY(cudaMemcpyAsync(w->f32.w, b_kn, (size_t)(k * n) * 4, cudaMemcpyHostToDevice,
+                                  c->stream));
+  w->device_bytes = k * n * 4;
+  return finish_register(std::move(w), out);
+}
+
+int nimf_weight_free(nimf_weight_t h) {
+  Context* c;
+  NIMF_TRY(require_ctx(&c));
+  Weight* w = lookup(h);
+  if (!w) return set_error(NIMF_ERR_STATE, "unknown weight handle %llu", (unsigned long long)h);
+  NIMF_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  free_weight_storage(w);
+  g_weights.erase(h);
+  for (auto it = g_q4_cache.begin(); it != g_q4_cache.end();) {
+    if (it->second == h) it = g_q4_cache.erase(it);
+    else ++it;
+  }
+  return NIMF_OK;
+}
+
+int nimf_weight_info(nimf_weight_t h, int64_t* n_rows, int64_t* k, int* kind,
+                     int64_t* device_bytes) {
+  Weight* w = lookup(h);
+  if (!w) return set_error(NIMF_ERR_STATE, "unknown weight handle %llu", (unsigned long long)h);
+  if (n_rows) *n_rows = w->rows();
+  if (k) *k = w->k();
+  if (kind) *kind = w->kind;
+  if (device_bytes) *device_bytes = w->device_bytes;
+  return NIMF_OK;
+}
+
+// ------------------------------------------------------------------ matmul
+
+int nimf_matmul_w_dev(nimf_weight_t h, const float* x_dev, int64_t m, float* y_dev,
+                      void* stream) {
+  Context* c;
+  NIMF_TRY(require_ctx(&c));
+  Weight* w = lookup(h);
+  if (!w) return set_error(NIMF_ERR_STATE, "unknown weight handle %llu", (unsigned long long)h);
+  if (m < 0) return set_error(NIMF_ERR_SHAPE, "m < 0");
+  if (m == 0 || w->rows() == 0) return NIMF_OK;
+  if (!y_dev || (!x_dev && w->k() > 0)) return set_error(NIMF_ERR_ARG, "NULL x or y");
+  cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+  return matmul_dev(w, x_dev, m, y_dev, st);
+}
+
+int nimf_matmul_w(nimf_weight_t h, const float* x, int64_t m, float* y) {
+  Context* c;
+  NIMF_TRY(require_ctx(&c));
+  Weight* w = lookup(h);
+  if (!w) return set_error(NIMF_ERR_STATE, "unknown weight handle %llu", (unsigned long long)h);
+  if (m < 0) return set_error(NIMF_ERR_SHAPE, "m < 0");
+  const int64_t rows = w->rows(), k = w->k();
+  if (m == 0 || rows == 0) return NIMF_OK;
+  if (!y || (!x && k > 0)) return set_error(NIMF_ERR_ARG, "NULL x or y");
+  void *dx, *dy;
+  NIMF_TRY(stage_in((size_t)(m * k) * 4, &dx));
+  NIMF_TRY(stage_out((size_t)(m * rows) * 4, &dy));
+  if (m * k > 0)
+    NIMF_CUDA_TRY(cudaMemcpyAsync(dx, x, (size_t)(m * k) * 4, cudaMemcpyHostToDevice, c->stream));
+  NIMF_TRY(matmul_dev(w, (const float*)dx, m, (float*)dy, c->stream));
+  NIMF_CUDA_TRY(cudaMemcpyAsync(y, dy, (size_t)(m * rows) * 4, cudaMemcpyDeviceToHost, c->stream));
+  NIMF_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  return NIMF_OK;
+}
+
+int nimf_dequant_w(nimf_weight_t h, float* out_host) {
+  Context* c;
+  NIMF_TRY(require_ctx(&c));
+  Weight* w = lookup(h);
+  if (!w) return set_error(NIMF_ERR_STATE, "unknown weight handle %llu", (unsigned long long)h);
+  const int64_t n = w->rows() * w->k();
+  if (n == 0) return NIMF_OK;
+  if (!out_host) return set_error(NIMF_ERR_ARG, "out is NULL");
+  void* d;
+  NIMF_TRY(stage_out((size_t)n * 4, &d));
+  float* o = (float*)d;
+  switch (w->kind) {
+    case NIMF_KIND_INT4_ASYM: NIMF_TRY(q4g_dequant(w->q4, o, c->stream)); break;
+    case NIMF_KIND_INT8: NIMF_TRY(i8_dequant(w->i8, o, c->stream)); break;
+    case NIMF_KIND_CUSTOM_FLOAT: NIMF_TRY(cf_dequant(w->cf, o, c->stream)); break;
+    case NIMF_KIND_FP4_E2M1: NIMF_TRY(fp4_dequant(w->fp4, o, c->stream)); break;
+    case NIMF_KIND_F32:
+      NIMF_TRY(f32_transpose((const float*)w->f32.w, w->f32.k, w->f32.rows, o, c->stream));
+      break;
+    default: return set_error(NIMF_ERR_UNSUPPORTED, "kind %d", w->kind);
+  }
+  NIMF_CUDA_TRY(cudaMemcpyAsync(out_host, o, (size_t)n * 4, cudaMemcpyDeviceToHost, c->stream));
+  NIMF_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  return NIMF_OK;
+}
+
+int nimf_matmul_q4(const float* a, const uint8_t* wq, const float* scales, const float* zeros,
+                   int64_t m, int64_t k, int64_t n, int64_t group_size, int64_t n_groups_per_row,
+                   float* out) {
+  Context* c;
+  NIMF_TRY(require_ctx(&c));
+  if (m < 0 || k < 0 || n < 0) return set_error(NIMF_ERR_SHAPE, "negative shape");
+  if (m == 0 || n == 0) return NIMF_OK;
+  const int64_t bytes = n * ((k + 1) / 2);
+  auto key = std::make_tuple((uintptr_t)wq, bytes, k, n, group_size, n_groups_per_row);
+  nimf_weight_t h;
+  auto it = g_q4_cache.find(key);
+  if (it != g_q4_cache.end() && lookup(it->second)) {
+    h = it->second;
+  } else {
+    NIMF_TRY(nimf_weight_register_q4g(wq, scales, zeros, n, k, group_size, n_groups_per_row, 0, n,
+                                      &h));
+    g_q4_cache[key] = h;
+  }
+  return nimf_matmul_w(h, a, m, out);
+}
+
+int nimf_weight_cache_clear(void) {
+  Context* c;
+  NIMF_TRY(require_ctx(&c));
+  std::vector<nimf_weight_t> hs;
+  for (auto& kv : g_q4_cache) hs.push_back(kv.second);
+  g_q4_cache.clear();
+  for (nimf_weight_t h : hs)
+    if (lookup(h)) NIMF_TRY(nimf_weight_free(h));
+  return NIMF_OK;
+}
+
+int nimf_matmul_f32(const float* a, int64_t m, int64_t k, const float* b, int64_t k2, int64_t n,
+                    float* out) {
+  Context* c;
+  NIMF_TRY(require_ctx(&c));
+  if (k2 != k)
+    return set_error(NIMF_ERR_SHAPE, "beMatmul: K = %lld but K2 = %lld", (long long)k,
+                     (long long)k2);
+  if (m < 0 || k < 0 || n < 0) return set_error(NIMF_ERR_SHAPE, "negative shape");
+  if (m == 0 || n == 0) return NIMF_OK;
+  if (!out || (k > 0 && (!a || !b))) return set_error(NIMF_ERR_ARG, "NULL array");
+  const size_t ba = (size_t)(m * k) * 4, bb = (size_t)(k * n) * 4, bc = (size_t)(m * n) * 4;
+  void *din, *dc;
+  NIMF_TRY(stage_in(ba + bb + 256, &din));
+  NIMF_TRY(stage_out(bc, &dc));
+  float* da = (float*)din;
+  float* db = (float*)((char*)din + ((ba + 255) / 256) * 256);
+  if (ba) NIMF_CUDA_TRY(cudaMemcpyAsync(da, a, ba, cudaMemcpyHostToDevice, c->stream));
+  if (bb) NIMF_CUDA_TRY(cudaMemcpyAsync(db, b, bb, cudaMemcpyHostToDevice, c->stream));
+  NIMF_TRY(f32_gemm(da, m, k, db, n, (float*)dc, c->stream));
+  NIMF_CUDA_TRY(cudaMemcpyAsync(out, dc, bc, cudaMemcpyDeviceToHost, c->stream));
+  NIMF_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  return NIMF_OK;
+}
+
+int nimf_matmul2_f32(const float* a1, int64_t m1, int64_t k1, const float* b1, int64_t k1b,
+                     int64_t n1, const float* a2, int64_t m2, int64_t k2, const float* b2,
+                     int64_t k2b, int64_t n2, float* out1, float* out2) {
+  NIMF_TRY(nimf_matmul_f32(a1, m1, k1, b1, k1b, n1, out1));
+  return nimf_matmul_f32(a2, m2, k2, b2, k2b, n2, out2);
+}
+
+// ------------------------------------------------------------------ CustomFloat / APF
+
+static int cf_check(int e, int m) {
+  if (e < 0 || m < 0) return set_error(NIMF_ERR_ARG, "negative exponent/mantissa bits");
+  if (1 + e + m > 64)
+    return set_error(NIMF_ERR_UNSUPPORTED,
+                     "CustomFloat e=%d m=%d: encodeArray/decodeArray support total_bits <= 64", e,
+                     m);
+  return NIMF_OK;
+}
+
+int nimf_cf_encode_dev(const float* x_dev, int64_t n, int e, int m, uint8_t* out_dev,
+                       void* stream) {
+  Context* c;
+  NIMF_TRY(require_ctx(&c));
+  NIMF_TRY(cf_check(e, m));
+  if (n < 0) return set_error(NIMF_ERR_SHAPE, "n < 0");
+  if (n == 0) return NIMF_OK;
+  if (!x_dev || !out_dev) return set_error(NIMF_ERR_ARG, "NULL buffer");
+  return cf_encode(x_dev, n, e, m, out_dev, stream ? (cudaStream_t)stream : c->stream);
+}
+
+int nimf_cf_decode_dev(const uint8_t* buf_dev, int64_t nbytes, int e, int m, float* out_dev,
+                       void* stream) {
+  Context* c;
+  NIMF_TRY(require_ctx(&c));
+  NIMF_TRY(cf_check(e, m));
+  const int item = (1 + e + m + 7) / 8;
+  if (nbytes < 0 || nbytes % item != 0)
+    return set_error(NIMF_ERR_SHAPE, "buffer of %lld bytes is not a multiple of itemSize %d",
+                     (long long)nbytes, item);
+  if (nbytes == 0) return NIMF_OK;
+  if (!buf_dev || !out_dev) return set_error(NIMF_ERR_ARG, "NULL buffer");
+  return cf_decode(buf_dev, nbytes / item, e, m, out_dev,
+                   stream ? (cudaStream_t)stream : c->stream);
+}
+
+int nimf_cf_encode(const float* x, int64_t n, int e, int m, uint8_t* out) {
+  Context* c;
+  NIMF_TRY(require_ctx(&c));
+  NIMF_TRY(cf_check(e, m));
+  if (n < 0) return set_error(NIMF_ERR_SHAPE, "n < 0");
+  if (n == 0) return NIMF_OK;
+  if (!x || !out) return set_error(NIMF_ERR_ARG, "NULL buffer");
+  const int item = (1 + e + m + 7) / 8;
+  void *dx, *dy;
+  NIMF_TRY(stage_in((size_t)n * 4, &dx));
+  NIMF_TRY(stage_out((size_t)n * item, &dy));
+  NIMF_CUDA_TRY(cudaMemcpyAsync(dx, x, (size_t)n * 4, cudaMemcpyHostToDevice, c->stream));
+  NIMF_TRY(cf_encode((const float*)dx, n, e, m, (uint8_t*)dy, c->stream));
+  NIMF_CUDA_TRY(cudaMemcpyAsync(out, dy, (size_t)n * item, cudaMemcpyDeviceToHost, c->stream));
+  NIMF_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  return NIMF_OK;
+}
+
+int nimf_cf_decode(const uint8_t* buf, int64_t nbytes, int e, int m, float* out) {
+  Context* c;
+  NIMF_TRY(require_ctx(&c));
+  NIMF_TRY(cf_check(e, m));
+  const int item = (1 + e + m + 7) / 8;
+  if (nbytes < 0 || nbytes % item != 0)
+    return set_error(NIMF_ERR_SHAPE, "buffer of %lld bytes is not a multiple of itemSize %d",
+                     (long long)nbytes, item);
+  if (nbytes == 0) return NIMF_OK;
+  if (!buf || !out) return set_error(NIMF_ERR_ARG, "NULL buffer");
+  const int64_t n = nbytes / item;
+  void *dx, *dy;
+  NIMF_TRY(stage_in((size_t)nbytes, &dx));
+  NIMF_TRY(stage_out((size_t)n * 4, &dy));
+  NIMF_CUDA_TRY(cudaMemcpyAsync(dx, buf, (size_t)nbytes, cudaMemcpyHostToDevice, c->stream));
+  NIMF_TRY(cf_decode((const uint8_t*)dx, n, e, m, (float*)dy, c->stream));
+  NIMF_CUDA_TRY(cudaMemcpyAsync(out, dy, (size_t)n * 4, cudaMemcpyDeviceToHost, c->stream));
+  NIMF_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  return NIMF_OK;
+}
+
+// customfloat.nim:149-198.  The reductions (min/max |x|, medians) run on the
+// device; the final integer formulas run here in double exactly as the
+// reference evaluates them.
+int nimf_cf_autoselect(const float* x, int64_t n, const float* grad, int64_t n_grad,
+                       double rel_error_tol, int exp_margin, int* exponent_bits,
+                       int* mantissa_bits) {
+  Context* c;
+  NIMF_TRY(require_ctx(&c));
+  if (n < 0 || n_grad < 0) return set_error(NIMF_ERR_SHAPE, "negative length");
+  if (!exponent_bits || !mantissa_bits) return set_error(NIMF_ERR_ARG, "NULL output");
+  if ((n > 0 && !x) || (n_grad > 0 && !grad)) return set_error(NIMF_ERR_ARG, "NULL input");
+  float mn = 0.f, mx = 0.f;
+  int found = 0;
+  void* dx = nullptr;
+  if (n > 0) {
+    NIMF_TRY(stage_in((size_t)n * 4, &dx));
+    NIMF_CUDA_TRY(cudaMemcpyAsync(dx, x, (size_t)n * 4, cudaMemcpyHostToDevice, c->stream));
+    NIMF_TRY(cf_absrange((const float*)dx, n, &mn, &mx, &found, c->stream));
+  }
+  // computeRequiredExponentBits (customfloat.nim:149-165)
+  int eb = 1;
+  if (found) {
+    const int64_t max_e = (int64_t)std::floor(std::log2((double)mx));
+    const int64_t min_e = (int64_t)std::floor(std::log2((double)mn));
+    const int64_t span = (max_e - min_e) + 2 * (int64_t)exp_margin + 2;
+    const int64_t r = (int64_t)std::ceil(std::log2((double)std::max<int64_t>(span, 2)));
+    eb = (int)std::max<int64_t>(1, r);
+  }
+  // computeRequiredMantissaBits (customfloat.nim:167-198)
+  int mb = 2;
+  if (found) {
+    const int64_t base = (int64_t)std::ceil(std::log2(1.0 / std::max(rel_error_tol, 1e-12)));
+    int64_t extra = 0;
+    if (n_grad > 0) {
+      float wmed = 0.f, gmed = 0.f;
+      int64_t nv = 0, ng = 0;
+      NIMF_TRY(cf_abs_median((const float*)dx, n, &wmed, &nv, c->stream));
+      void* dg;
+      NIMF_TRY(stage_out((size_t)n_grad * 4, &dg));
+      NIMF_CUDA_TRY(
+          cudaMemcpyAsync(dg, grad, (size_t)n_grad * 4, cudaMemcpyHostToDevice, c->stream));
+      NIMF_TRY(cf_abs_median((const float*)dg, n_grad, &gmed, &ng, c->stream));
+      if (ng > 0) {
+        wmed = std::max(wmed, 1e-12f);
+        const double ratio = (double)gmed / (double)wmed;
+        if (ratio > 0 && ratio < 1) {
+          const int64_t need = (int64_t)std::ceil(-std::log2(ratio));
+          extra = std::max<int64_t>(0, need - base);
+        }
+      }
+    }
+    mb = (int)std::min<int64_t>(23, std::max<int64_t>(2, base + extra));
+  }
+  *exponent_bits = eb;
+  *mantissa_bits = mb;
+  return NIMF_OK;
+}
+
+int nimf_apf_cast(const float* x, int64_t n, const float* grad, int64_t n_grad,
+                  double rel_error_tol, int exp_margin, int* exponent_bits, int* mantissa_bits,
+                  uint8_t* out) {
+  NIMF_TRY(nimf_cf_autoselect(x, n, grad, n_grad, rel_error_tol, exp_margin, exponent_bits,
+                              mantissa_bits));
+  return nimf_cf_encode(x, n, *exponent_bits, *mantissa_bits, out);
+}
+
+}  // extern "C"

@@ -1,0 +1,147 @@
+// nimf_internal.h -- host-side internals shared by the translation units of
+// libnimf_cuda.so (error reporting, the per-process device context, the
+// weight registry and the kernel launchers).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <memory>
+
+#include "../../include/nimf_cuda.h"
+
+namespace nimf {
+
+// ----------------------------------------------------------------- errors
+// Records `msg` as the calling thread's last error and returns `code`.
+int set_error(int code, const char* fmt, ...);
+
+#define NIMF_CUDA_TRY(expr)                                                                   \
+  do {                                                                                        \
+    cudaError_t e__ = (expr);                                                                 \
+    if (e__ != cudaSuccess)                                                                   \
+      return ::nimf::set_error(NIMF_ERR_CUDA, "%s failed: %s (%s:%d)", #expr,                \
+                               cudaGetErrorString(e__), __FILE__, __LINE__);                  \
+  } while (0)
+
+#define NIMF_TRY(expr)           \
+  do {                           \
+    int s__ = (expr);            \
+    if (s__ != NIMF_OK) return s__; \
+  } while (0)
+
+// ----------------------------------------------------------------- weights
+// Device copy of an int4 asymmetric per-group weight (N-shard of rows).
+//   fast layout (group_size % 64 == 0):
+//     frag : [n_rt][kq_total][32 lanes] uint4, word j of a lane = the
+//            mma.m16n8k16 A-fragment nibbles of k-tile 4*kq+j (see q4g.cu)
+//     sz   : [n_rt][groups][8] float4 {scale(r), zero(r), scale(r+8), zero(r+8)}
+//   generic layout (any other group size):
+//     raw  : the reference bytes [rows][ceil(K/2)], scales/zeros [rows][ngr]
+struct Q4GWeight {
+  int64_t rows = 0, k = 0, gs = 0, ngr = 0;
+  bool fast = false;
+  int64_t n_rt = 0, kq_total = 0, groups = 0;
+  void* frag = nullptr;   // uint4*
+  void* sz = nullptr;     // float4*
+  void* raw = nullptr;    // uint8_t*
+  void* scales = nullptr; // float*
+  void* zeros = nullptr;  // float*
+};
+
+// Device copy of an int8 weight: q [rows][K] int8, scales [1 or rows].
+struct I8Weight {
+  int64_t rows = 0, k = 0, n_scales = 0;
+  void* q = nullptr;
+  void* scales = nullptr;
+};
+
+// Device copy of a CustomFloat weight: item bytes [rows][K*item], optional
+// per-row scale.
+struct CFWeight {
+  int64_t rows = 0, k = 0;
+  int e = 0, m = 0, item = 0;
+  void* data = nullptr;
+  void* row_scales = nullptr;
+};
+
+// Device copy of an FP4 E2M1 block-16 weight.
+struct FP4Weight {
+  int64_t rows = 0, k = 0;
+  float tensor_scale = 1.0f;
+  void* packed = nullptr;  // [rows][ceil(K/2)]
+  void* bscale = nullptr;  // [rows][ceil(K/16)]
+};
+
+// Device copy of an fp32 weight stored [N][K] (transposed from beMatmul's b).
+struct F32Weight {
+  int64_t rows = 0, k = 0;
+  void* w = nullptr;
+};
+
+struct Weight {
+  int kind = -1;
+  int64_t device_bytes = 0;
+  Q4GWeight q4;
+  I8Weight i8;
+  CFWeight cf;
+  FP4Weight fp4;
+  F32Weight f32;
+  int64_t rows() const;
+  int64_t k() const;
+};
+
+// ----------------------------------------------------------------- context
+struct Context {
+  int device = -1;
+  int num_sms = 0;
+  cudaStream_t stream = nullptr;
+  // growable device staging buffers for the host-pointer entry points
+  void* stage_in = nullptr;
+  size_t stage_in_bytes = 0;
+  void* stage_out = nullptr;
+  size_t stage_out_bytes = 0;
+};
+
+Context* ctx();                        // nullptr before nimf_init
+int require_ctx(Context** out);        // NIMF_ERR_STATE if not initialised
+int stage_in(size_t bytes, void** p);  // grows the input staging buffer
+int stage_out(size_t bytes, void** p); // grows the output staging buffer
+int device_alloc(void** p, size_t bytes);
+void device_free(void* p);
+
+Weight* lookup(nimf_weight_t h);
+nimf_weight_t insert(std::unique_ptr<Weight> w);
+void free_weight_storage(Weight* w);
+
+// ----------------------------------------------------------------- launchers
+// All launchers validate their arguments, enqueue on `st` and return a status.
+int q4g_build(Weight* w, const uint8_t* wq_dev, const float* sc_dev, const float* zp_dev,
+              int64_t row_begin, int64_t rows, int64_t n_full, int64_t k, int64_t gs,
+              int64_t ngr, cudaStream_t st);
+int q4g_gemv(const Q4GWeight& w, const float* x, int64_t m, float* y, cudaStream_t st);
+int q4g_dequant(const Q4GWeight& w, float* out, cudaStream_t st);
+
+int i8_gemv(const I8Weight& w, const float* x, int64_t m, float* y, cudaStream_t st);
+int i8_dequant(const I8Weight& w, float* out, cudaStream_t st);
+
+int cf_encode(const float* x, int64_t n, int e, int m, uint8_t* out, cudaStream_t st);
+int cf_decode(const uint8_t* buf, int64_t n_items, int e, int m, float* out, cudaStream_t st);
+int cf_gemv(const CFWeight& w, const float* x, int64_t m, float* y, cudaStream_t st);
+int cf_dequant(const CFWeight& w, float* out, cudaStream_t st);
+// min / max of |x| over finite non-zero elements; returns found=0 when none.
+int cf_absrange(const float* x, int64_t n, float* min_abs, float* max_abs, int* found,
+                cudaStream_t st);
+// median (element n_valid/2 of the ascending order) of |x| over finite non-zero x.
+int cf_abs_median(const float* x, int64_t n, float* median, int64_t* n_valid, cudaStream_t st);
+
+int fp4_gemv(const FP4Weight& w, const float* x, int64_t m, float* y, cudaStream_t st);
+int fp4_dequant(const FP4Weight& w, float* out, cudaStream_t st);
+
+int f32_gemm(const float* a, int64_t m, int64_t k, const float* w_nk, int64_t n, float* c,
+             cudaStream_t st);
+int f32_transpose(const float* b_kn, int64_t k, int64_t n, float* w_nk, cudaStream_t st);
+
+}  // namespace nimf
