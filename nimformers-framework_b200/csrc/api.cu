@@ -41,6 +41,16 @@ int set_error(int code, const char* fmt, ...) {
 
 Context* ctx() { return g_ready ? &g_ctx : nullptr; }
 
+int check_device_error() {
+  if (g_ready && g_ctx.host_err && *g_ctx.host_err != 0) {
+    const int code = *g_ctx.host_err;
+    *g_ctx.host_err = 0;
+    return set_error(NIMF_ERR_TIMEOUT,
+                     "a kernel's bounded wait expired (code %d); its output is not valid", code);
+  }
+  return NIMF_OK;
+}
+
 int require_ctx(Context** out) {
   if (!g_ready) return set_error(NIMF_ERR_STATE, "nimf_init() has not been called");
   NIMF_CUDA_TRY(cudaSetDevice(g_ctx.device));
@@ -224,6 +234,11 @@ int nimf_init(int device) {
   g_ctx.device = device;
   g_ctx.num_sms = prop.multiProcessorCount;
   NIMF_CUDA_TRY(cudaStreamCreateWithFlags(&g_ctx.stream, cudaStreamNonBlocking));
+  void* he = nullptr;
+  NIMF_CUDA_TRY(cudaHostAlloc(&he, sizeof(int), cudaHostAllocMapped));
+  *(volatile int*)he = 0;
+  g_ctx.host_err = (volatile int*)he;
+  NIMF_CUDA_TRY(cudaHostGetDevicePointer((void**)&g_ctx.dev_err, he, 0));
   g_ready = true;
   return NIMF_OK;
 }
@@ -238,6 +253,7 @@ int nimf_shutdown(void) {
   g_q4_cache.clear();
   device_free(g_ctx.stage_in);
   device_free(g_ctx.stage_out);
+  if (g_ctx.host_err) cudaFreeHost((void*)g_ctx.host_err);
   cudaStreamDestroy(g_ctx.stream);
   g_ctx = Context();
   g_ready = false;
@@ -248,7 +264,8 @@ int nimf_sync(void) {
   Context* c;
   NIMF_TRY(require_ctx(&c));
   NIMF_CUDA_TRY(cudaStreamSynchronize(c->stream));
-  return NIMF_OK;
+  NIMF_CUDA_TRY(cudaDeviceSynchronize());
+  return check_device_error();
 }
 
 // ------------------------------------------------------------------ weights
@@ -460,7 +477,7 @@ int nimf_matmul_w(nimf_weight_t h, const float* x, int64_t m, float* y) {
   NIMF_TRY(matmul_dev(w, (const float*)dx, m, (float*)dy, c->stream));
   NIMF_CUDA_TRY(cudaMemcpyAsync(y, dy, (size_t)(m * rows) * 4, cudaMemcpyDeviceToHost, c->stream));
   NIMF_CUDA_TRY(cudaStreamSynchronize(c->stream));
-  return NIMF_OK;
+  return check_device_error();
 }
 
 int nimf_dequant_w(nimf_weight_t h, float* out_host) {

@@ -40,15 +40,9 @@ __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t
   return d;
 }
 
-// Unpacks the low nibble of each 16-bit half of `w` into a bf16x2 holding the
-// exact integers 0..15: 0x4300|n is bf16(128 + n), minus 128 (exact).
-__device__ __forceinline__ uint32_t nib2_to_bf16x2(uint32_t w) {
-  uint32_t v = lop3_and_or(w, 0x000F000Fu, 0x43004300u);
-  __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&v);
-  const __nv_bfloat162 bias = __floats2bfloat162_rn(128.0f, 128.0f);
-  h = __hsub2(h, bias);
-  return *reinterpret_cast<uint32_t*>(&h);
-}
+// The two bf16 halves of a bf16x2 word as floats (exact).
+__device__ __forceinline__ float bf16x2_lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf16x2_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
 
 // D += A(16x16 bf16, row) . B(16x8 bf16, col), fp32 accumulate.
 __device__ __forceinline__ void mma_bf16_16816(float* d, uint32_t a0, uint32_t a1, uint32_t a2,
@@ -103,6 +97,63 @@ __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
+}
+
+}  // namespace nimf
+
+namespace nimf {
+
+// ------------------------------------------------------------------ mbarrier / TMA bulk copies
+// Every wait is bounded: after kMaxSpin polls the caller records an error and
+// gives up instead of hanging the GPU.
+constexpr uint32_t kMaxSpin = 1u << 22;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* m, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(m)), "r"(count));
+}
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+// Arrive once and add `bytes` to the transaction count of the current phase.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* m, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(m)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* m) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(m)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* m, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_addr(m)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Waits for the phase with the given parity to complete; false on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t* m, uint32_t parity) {
+  for (uint32_t i = 0; i < kMaxSpin; ++i)
+    if (mbar_try_wait(m, parity)) return true;
+  return false;
+}
+// Global -> shared bulk copy (no multicast) completing on mbarrier `m`.
+// dst, src 16-byte aligned; bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* m) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(m))
+      : "memory");
+}
+// Named barrier over `threads` threads (a subset of the CTA).
+__device__ __forceinline__ void named_barrier(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 }  // namespace nimf

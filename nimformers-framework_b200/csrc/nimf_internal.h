@@ -103,7 +103,16 @@ struct Context {
   size_t stage_in_bytes = 0;
   void* stage_out = nullptr;
   size_t stage_out_bytes = 0;
+  // Host-mapped error word: kernels whose bounded waits expire set it to a
+  // non-zero code instead of hanging; blocking entry points and nimf_sync
+  // report it as NIMF_ERR_TIMEOUT and clear it.
+  volatile int* host_err = nullptr;
+  int* dev_err = nullptr;
 };
+
+// Returns NIMF_ERR_TIMEOUT (and clears the word) if a kernel reported an
+// expired wait since the last check.  Call after a stream synchronisation.
+int check_device_error();
 
 Context* ctx();                        // nullptr before nimf_init
 int require_ctx(Context** out);        // NIMF_ERR_STATE if not initialised
