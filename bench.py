@@ -3,8 +3,11 @@
 
 Workload (one step): y_r[M, N] = x[M, K] . W_r^T for R distinct int4 group-128
 asymmetric weights W_r (K=4096, N=12288, M=1; W ~ N(0, 0.02), quantised with
-the exporter's per-group rule), all resident in HBM.  R copies (> 3x L2 in
-total) rotate, so every step streams its weights from HBM.  With --gpus G the
+the exporter's per-group rule), all resident in HBM, issued as one grouped
+launch (nimf_matmul_w_group_dev: the weights share x, like fused projections).
+R copies (> 3x L2 in total) rotate, so every step streams its weights from
+HBM.  The same R GEMVs issued as R separate launches (PDL-chained in a CUDA
+graph) are reported as "single_launch".  With --gpus G the
 weight rows are N-sharded (each GPU holds 12288 rows of a 12288*G-row weight:
 per-GPU work is fixed, "weak" scaling) and the output slices are all-gathered
 over NCCL inside the step.
@@ -187,8 +190,14 @@ def run_ours(args, rank, world, local_rank):
     gathered = torch.empty(world, R, M, N_PER_GPU, device="cuda", dtype=torch.float32) if world > 1 else None
 
     stream = torch.cuda.Stream()
+    y_ptrs = [ys[r].data_ptr() for r in range(R)]
 
     def step(st):
+        nimf.Weight.matmul_group_dev(weights, x.data_ptr(), M, y_ptrs, st.cuda_stream)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered.view(-1), ys.view(-1))
+
+    def step_single(st):
         for r in range(R):
             weights[r].matmul_dev(x.data_ptr(), M, ys[r].data_ptr(), st.cuda_stream)
         if world > 1:
@@ -197,10 +206,14 @@ def run_ours(args, rank, world, local_rank):
     with torch.cuda.stream(stream):
         for _ in range(max(1, args.warmup)):
             step(stream)
+            step_single(stream)
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         step(stream)
+    graph1 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph1, stream=stream):
+        step_single(stream)
     torch.cuda.synchronize()
 
     # correctness spot check of one output against a host computation
@@ -241,15 +254,37 @@ def run_ours(args, rank, world, local_rank):
     bytes_step = R * algo_bytes(N_PER_GPU, K, M, GS) * world
     value = bytes_step / (ms_per_step * 1e-3) / 1e9
 
-    # kernel-level roofline: average duration of one GEMV launch in the region
+    # the same GEMVs as one launch each (PDL-chained in a graph)
+    for _ in range(args.warmup):
+        graph1.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s1, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s1.record()
+    for _ in range(args.steps):
+        graph1.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms1 = s1.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms1], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms1 = float(t.item())
+    single = {"value": bytes_step / (ms1 / args.steps * 1e-3) / 1e9, "unit": "GB/s",
+              "us_per_gemv": ms1 * 1e3 / (args.steps * R),
+              "note": "one launch per GEMV, PDL-chained in a CUDA graph"}
+
+    # kernel-level roofline: the grouped GEMV launch (one per step)
     pk, how = peaks()
-    per_launch_bytes = algo_bytes(N_PER_GPU, K, M, GS)
-    launch_s = ms * 1e-3 / (args.steps * R)
+    per_launch_bytes = R * algo_bytes(N_PER_GPU, K, M, GS)
+    launch_s = ms * 1e-3 / args.steps
     achieved = per_launch_bytes / launch_s / 1e9
     roofline = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                 "frac": achieved / pk["hbm_gbs"], "traffic": profile_traffic(),
-                "peak_source": how, "kernel": "q4g_gemv_kernel<1>",
-                "note": "launch duration = timed region / launches (back-to-back, PDL)"}
+                "peak_source": how, "kernel": "q4g_gemv_kernel<1,2> (grouped, %d weights)" % R,
+                "algorithmic_bytes_per_launch": per_launch_bytes,
+                "note": "launch duration = timed region / launches, CUDA events"}
 
     # end to end through the C ABI with host buffers (pinned), per step R calls
     xh = torch.randn(M, K, dtype=torch.float32).pin_memory()
@@ -259,9 +294,11 @@ def run_ours(args, rank, world, local_rank):
     xp = ctypes.c_void_p(xh.data_ptr())
     yps = [ctypes.c_void_p(yh[r].data_ptr()) for r in range(R)]
 
+    hs = (ctypes.c_uint64 * R)(*[w.handle for w in weights])
+    ypa = (ctypes.c_void_p * R)(*[yh[r].data_ptr() for r in range(R)])
+
     def e2e_step():
-        for r in range(R):
-            nimf.check(L.nimf_matmul_w(weights[r].handle, xp, M, yps[r]))
+        nimf.check(L.nimf_matmul_w_group(hs, R, xp, M, ypa))
 
     for _ in range(max(1, args.warmup)):
         e2e_step()
@@ -278,7 +315,7 @@ def run_ours(args, rank, world, local_rank):
         e2e_s = float(t.item())
     e2e = {"value": bytes_step / e2e_s / 1e9, "unit": "GB/s",
            "h2d_bytes_per_step": R * M * K * 4, "d2h_bytes_per_step": R * M * N_PER_GPU * 4,
-           "api": "nimf_matmul_w (host buffers, blocking, per weight)",
+           "api": "nimf_matmul_w_group (host buffers, blocking)",
            "note": "per-rank shard outputs; no host all-gather" if world > 1 else ""}
 
     cpu = None
@@ -288,6 +325,7 @@ def run_ours(args, rank, world, local_rank):
         cpu = {"value": rate, "unit": "GB/s", "cores": 1, "kind": "port", "sample": desc}
 
     graph.reset()
+    graph1.reset()
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
@@ -300,7 +338,8 @@ def run_ours(args, rank, world, local_rank):
                                  % (R, R * algo_bytes(N_PER_GPU, K, M, GS) / 1e6),
                            "parallelism": "N-shard x%d + NCCL all-gather" % world if world > 1 else "single GPU"},
                 "pct_of_hbm_peak": value / world / pk["hbm_gbs"],
-                "roofline": roofline, "e2e": e2e, "gpu_launches": args.steps * R,
+                "roofline": roofline, "e2e": e2e, "single_launch": single,
+                "gpu_launches": args.steps,
                 "clocks": clocks}
         if cpu is not None:
             line["cpu_baseline"] = cpu

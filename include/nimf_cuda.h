@@ -142,6 +142,19 @@ int nimf_matmul_w(nimf_weight_t w, const float* x, int64_t m, float* y);
 int nimf_matmul_w_dev(nimf_weight_t w, const float* x_dev, int64_t m, float* y_dev,
                       void* stream);
 
+/* Several weights with the same K applied to the same x, DEVICE buffers:
+ * y_devs[i][M][N_i] = x[M][K] . W_i^T.  int4 weights of one group size run as a
+ * single persistent launch that streams all their rows back to back (the
+ * fused q/k/v and gate/up projections of nim_inference.nim:506-508,818-819,
+ * which the reference issues as separate linearFastBias calls).  Other kinds
+ * are applied one after another. */
+int nimf_matmul_w_group_dev(const nimf_weight_t* handles, int count, const float* x_dev,
+                            int64_t m, float* const* y_devs, void* stream);
+
+/* HOST-buffer, blocking form of nimf_matmul_w_group_dev. */
+int nimf_matmul_w_group(const nimf_weight_t* handles, int count, const float* x, int64_t m,
+                        float* const* ys);
+
 /* Drop-in for beMatmulQ4 (backend.nim:93-110 -> gpubackend.nim:655-676):
  * same arguments, HOST arrays, out = float32 [M*N].  The packed weights are
  * cached on the device keyed by (wq pointer, bytes, K, N, group size), valid

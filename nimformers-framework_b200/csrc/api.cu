@@ -480,6 +480,76 @@ int nimf_matmul_w(nimf_weight_t h, const float* x, int64_t m, float* y) {
   return check_device_error();
 }
 
+int nimf_matmul_w_group_dev(const nimf_weight_t* handles, int count, const float* x_dev,
+                            int64_t m, float* const* y_devs, void* stream) {
+  Context* c;
+  NIMF_TRY(require_ctx(&c));
+  if (count < 0 || m < 0) return set_error(NIMF_ERR_SHAPE, "negative count or m");
+  if (count == 0 || m == 0) return NIMF_OK;
+  if (!handles || !y_devs) return set_error(NIMF_ERR_ARG, "NULL handle or output array");
+  cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+  std::vector<Weight*> ws((size_t)count);
+  bool all_q4 = true;
+  for (int i = 0; i < count; ++i) {
+    ws[i] = lookup(handles[i]);
+    if (!ws[i])
+      return set_error(NIMF_ERR_STATE, "unknown weight handle %llu", (unsigned long long)handles[i]);
+    if (ws[i]->k() != ws[0]->k())
+      return set_error(NIMF_ERR_SHAPE, "grouped matmul: weights have different K");
+    if (!y_devs[i] && ws[i]->rows() > 0) return set_error(NIMF_ERR_ARG, "NULL output %d", i);
+    all_q4 = all_q4 && ws[i]->kind == NIMF_KIND_INT4_ASYM && ws[i]->q4.gs == ws[0]->q4.gs &&
+             ws[i]->q4.fast == ws[0]->q4.fast;
+  }
+  if (!x_dev && ws[0]->k() > 0) return set_error(NIMF_ERR_ARG, "NULL x");
+  if (all_q4) {
+    std::vector<const Q4GWeight*> qs((size_t)count);
+    for (int i = 0; i < count; ++i) qs[i] = &ws[i]->q4;
+    return q4g_gemv_group(qs.data(), count, x_dev, m, y_devs, st);
+  }
+  for (int i = 0; i < count; ++i)
+    if (ws[i]->rows() > 0) NIMF_TRY(matmul_dev(ws[i], x_dev, m, y_devs[i], st));
+  return NIMF_OK;
+}
+
+int nimf_matmul_w_group(const nimf_weight_t* handles, int count, const float* x, int64_t m,
+                        float* const* ys) {
+  Context* c;
+  NIMF_TRY(require_ctx(&c));
+  if (count < 0 || m < 0) return set_error(NIMF_ERR_SHAPE, "negative count or m");
+  if (count == 0 || m == 0) return NIMF_OK;
+  if (!handles || !ys) return set_error(NIMF_ERR_ARG, "NULL handle or output array");
+  int64_t k = -1, total = 0;
+  std::vector<int64_t> rows((size_t)count);
+  for (int i = 0; i < count; ++i) {
+    Weight* w = lookup(handles[i]);
+    if (!w)
+      return set_error(NIMF_ERR_STATE, "unknown weight handle %llu", (unsigned long long)handles[i]);
+    if (k >= 0 && w->k() != k) return set_error(NIMF_ERR_SHAPE, "grouped matmul: different K");
+    k = w->k();
+    rows[i] = w->rows();
+    total += rows[i];
+  }
+  if (!x && k > 0) return set_error(NIMF_ERR_ARG, "NULL x");
+  void *dx, *dy;
+  NIMF_TRY(stage_in((size_t)(m * k) * 4, &dx));
+  NIMF_TRY(stage_out((size_t)(m * total) * 4, &dy));
+  std::vector<float*> yd((size_t)count);
+  int64_t off = 0;
+  for (int i = 0; i < count; ++i) {
+    yd[i] = (float*)dy + off;
+    off += m * rows[i];
+  }
+  if (m * k > 0)
+    NIMF_CUDA_TRY(cudaMemcpyAsync(dx, x, (size_t)(m * k) * 4, cudaMemcpyHostToDevice, c->stream));
+  NIMF_TRY(nimf_matmul_w_group_dev(handles, count, (const float*)dx, m, yd.data(), c->stream));
+  for (int i = 0; i < count; ++i)
+    if (rows[i] > 0)
+      NIMF_CUDA_TRY(cudaMemcpyAsync(ys[i], yd[i], (size_t)(m * rows[i]) * 4,
+                                    cudaMemcpyDeviceToHost, c->stream));
+  NIMF_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  return check_device_error();
+}
+
 int nimf_dequant_w(nimf_weight_t h, float* out_host) {
   Context* c;
   NIMF_TRY(require_ctx(&c));

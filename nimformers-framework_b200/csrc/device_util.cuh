@@ -1,5 +1,5 @@
 // device_util.cuh -- small sm_100a device helpers shared by the kernels:
-// streaming loads, tensor-core mma.sync wrappers, nibble -> bf16 unpacking,
+// streaming loads, tensor-core mma.sync wrappers (bf16, f16, s8),
 // fp32 -> bf16 hi/lo splitting and programmatic-dependent-launch controls.
 #pragma once
 
@@ -61,6 +61,16 @@ __device__ __forceinline__ void mma_f16_16816(float* d, uint32_t a0, uint32_t a1
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// D += A(16x32 s8, row) . B(32x8 s8, col), exact s32 accumulate.
+__device__ __forceinline__ void mma_s8_16832(int* d, uint32_t a0, uint32_t a1, uint32_t a2,
+                                             uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
@@ -136,10 +146,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* m, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Waits for the phase with the given parity to complete; false on timeout.
+// try_wait with a suspend-time hint: the thread sleeps until the phase
+// completes or about `ns` nanoseconds pass, instead of busy-polling.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* m, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_addr(m)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+// Waits for the phase with the given parity to complete; false on timeout
+// (bounded: kMaxSpin tries of at most ~1 us each).
 __device__ __forceinline__ bool mbar_wait(uint64_t* m, uint32_t parity) {
   for (uint32_t i = 0; i < kMaxSpin; ++i)
-    if (mbar_try_wait(m, parity)) return true;
+    if (mbar_try_wait_sleep(m, parity, 1000u)) return true;
   return false;
 }
 // Global -> shared bulk copy (no multicast) completing on mbarrier `m`.

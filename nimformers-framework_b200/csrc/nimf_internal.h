@@ -131,6 +131,10 @@ int q4g_build(Weight* w, const uint8_t* wq_dev, const float* sc_dev, const float
               int64_t row_begin, int64_t rows, int64_t n_full, int64_t k, int64_t gs,
               int64_t ngr, cudaStream_t st);
 int q4g_gemv(const Q4GWeight& w, const float* x, int64_t m, float* y, cudaStream_t st);
+// Several int4 weights with the same K and group size applied to the same x
+// in one persistent launch (their row tiles are streamed back to back).
+int q4g_gemv_group(const Q4GWeight* const* ws, int count, const float* x, int64_t m,
+                   float* const* ys, cudaStream_t st);
 int q4g_dequant(const Q4GWeight& w, float* out, cudaStream_t st);
 
 int i8_gemv(const I8Weight& w, const float* x, int64_t m, float* y, cudaStream_t st);

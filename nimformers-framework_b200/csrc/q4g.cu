@@ -57,11 +57,13 @@ constexpr int kMaxSplits = 8;                   // portable cluster size
 constexpr size_t kSmemBudget = (size_t)NIMF_Q4G_SMEM_KB * 1024;
 constexpr int kMaxTilesPerCluster = 48;         // partial-y rows a cluster keeps in shared memory
 
-// Slot s (0..7) of a fragment word holds row  g + 8*(s&1)  and
-// k-offset  2t + 8*((s>>1)&1) + ((s>>2)&1)  of the 16x16 tile.
-__device__ __forceinline__ int slot_row(int g, int s) { return g + ((s & 1) ? 8 : 0); }
-__device__ __forceinline__ int slot_k(int t, int s) {
-  return 2 * t + ((s & 2) ? 8 : 0) + ((s & 4) ? 1 : 0);
+// Fragment order of the packed weights (one uint4 per lane per 64-k quad):
+// word w = 2h + half of lane (g, t) covers k = 32h + 16*half + 4t + b (byte
+// b = 0..3); the low nibble of byte b is row g, the high nibble row g + 8.
+// Hence (w & 0x0F0F0F0F) and ((w >> 4) & 0x0F0F0F0F) are exactly the s8 A
+// fragments {row g, row g+8} x k[4t..4t+3] of mma.m16n8k32.
+__device__ __forceinline__ int nib_k(int w, int t, int b) {
+  return 32 * (w >> 1) + 16 * (w & 1) + 4 * t + b;
 }
 
 __global__ void q4g_repack_frag(const uint8_t* __restrict__ wq, int64_t bpr, int64_t rows,
@@ -76,21 +78,23 @@ __global__ void q4g_repack_frag(const uint8_t* __restrict__ wq, int64_t bpr, int
   const int g = lane >> 2, t = lane & 3;
   uint32_t words[4];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int64_t kt0 = (kq * 4 + j) * 16;
+  for (int wi = 0; wi < 4; ++wi) {
     uint32_t w = 0;
 #pragma unroll
-    for (int s = 0; s < 8; ++s) {
-      const int64_t row = rt * 16 + slot_row(g, s);
-      const int64_t col = kt0 + slot_k(t, s);
-      uint32_t nib = 0;
-      if (row < rows && col < k) {
-        const uint8_t b = wq[row * bpr + (col >> 1)];
-        nib = (col & 1) ? (uint32_t)(b >> 4) : (uint32_t)(b & 15);
+    for (int b = 0; b < 4; ++b) {
+      const int64_t col = kq * 64 + nib_k(wi, t, b);
+#pragma unroll
+      for (int hi = 0; hi < 2; ++hi) {
+        const int64_t row = rt * 16 + g + 8 * hi;
+        uint32_t nib = 0;
+        if (row < rows && col < k) {
+          const uint8_t byte = wq[row * bpr + (col >> 1)];
+          nib = (col & 1) ? (uint32_t)(byte >> 4) : (uint32_t)(byte & 15);
+        }
+        w |= nib << (8 * b + 4 * hi);
       }
-      w |= nib << (4 * s);
     }
-    words[j] = w;
+    words[wi] = w;
   }
   out[i] = make_uint4(words[0], words[1], words[2], words[3]);
 }
@@ -122,15 +126,14 @@ __global__ void q4g_dequant_frag(const uint4* __restrict__ frag, const float4* _
   const int64_t row = i / k, col = i % k;
   const int64_t rt = row >> 4;
   const int r = (int)(row & 15);
-  const int64_t kt = col >> 4;
-  const int kk = (int)(col & 15);
   const int g = r & 7, rhi = r >> 3;
-  const int t = (kk & 7) >> 1, khi = kk >> 3, kodd = kk & 1;
+  const int kk = (int)(col & 63);                 // k within the quad
+  const int h = kk >> 5, half = (kk >> 4) & 1, t = (kk & 15) >> 2, b = kk & 3;
   const int lane = g * 4 + t;
-  const int s = rhi + 2 * khi + 4 * kodd;
-  const uint4 v = frag[((rt * kq_total) + (kt >> 2)) * 32 + lane];
-  const uint32_t word = (&v.x)[kt & 3];
-  const uint32_t nib = (word >> (4 * s)) & 15u;
+  const uint4 v = frag[((rt * kq_total) + (col >> 6)) * 32 + lane];
+  const int wi = 2 * h + half;
+  const uint32_t word = wi == 0 ? v.x : (wi == 1 ? v.y : (wi == 2 ? v.z : v.w));
+  const uint32_t nib = (word >> (8 * b + 4 * rhi)) & 15u;
   const float4 p = sz[((rt * groups) + col / gs) * 8 + g];
   const float scale = rhi ? p.z : p.x;
   const float zero = rhi ? p.w : p.y;
@@ -150,14 +153,25 @@ __global__ void q4g_dequant_raw(const uint8_t* __restrict__ wq, const float* __r
   out[i] = __fmul_rn(__fsub_rn((float)nib, zp[row * ngr + g]), sc[row * ngr + g]);
 }
 
-struct GemvArgs {
+// One weight of a (grouped) launch: its row tiles occupy global row tiles
+// [rt_prefix[p], rt_prefix[p+1]) of the launch.
+constexpr int kMaxProblems = 16;
+struct GemvProblem {
   const uint4* frag;
   const float4* sz;
-  const float* x;
   float* y;
+  int64_t ldy;
+  int rows;
+};
+
+struct GemvArgs {
+  GemvProblem prob[kMaxProblems];
+  int rt_prefix[kMaxProblems + 1];
+  int nprob;
+  const float* x;
   int* err;            // host-mapped error word (1: a bounded wait expired)
-  int64_t ldx, ldy;
-  int m, k, rows, n_rt;
+  int64_t ldx;
+  int m, k, n_rt;      // n_rt: total row tiles of the launch
   int kq_total, groups;
   int gps;             // quantisation groups per k-split (the last split may have fewer)
   int n_clusters;      // clusters in the grid; cluster size = number of k-splits
@@ -172,47 +186,55 @@ struct GemvArgs {
 constexpr int kChunkQ = 8;
 constexpr int kIssuers = 4;  // producer lanes issuing stages round-robin
 
-template <int MODE>
-__host__ __device__ constexpr int xfrag_bytes() { return MODE == 1 ? 8 : 16; }
-
 // Shared-memory layout of one CTA:
-//   full/empty[kStages] mbarriers
-//   ring[ns][stage]          row-tile slices of the k-split
-//   xs   [k-tiles][cols][4]  compact B fragments of x (only columns that carry rows)
-//   sxs  [gps][2][8]         per-group sums of the bf16 hi / lo parts of x
-//   psum [2][M][64-k chunks] chunk sums used to build sxs
-//   part [tchunk*nchunk][16][8] per-unit partial y, then summed per row tile
+//   head: full/empty[kStages] mbarriers, cnt[kStages] arrival counters,
+//         xmax[8] (|x| maxima as float bits), zero pad (16 B)
+//   ring[ns][stage]   row-tile slices of this CTA's k-split (packed weights,
+//                     then the scale/zero pairs of their groups)
+//   xs    B fragments of the two s8 digits of x for the k-split:
+//         MODE 1: [k32 tiles][2M columns][4 lanes t] uint2 (d0 of row m in
+//                 column m, d1 in column M + m)
+//         MODE 2: [k32 tiles][M][4 lanes t] uint4 {d0 b0, d0 b1, d1 b0, d1 b1}
+//   sdi   [gps][16] int: per group, sums of the d0 (0..7) and d1 (8..15) digits
+//   part  split mode: [tchunk*ncn][16][8] per-unit partial y; direct mode (no
+//         k-split): [ns][ncn][16][8] per-stage slots summed into y in-CTA
 struct SmemLayout {
-  size_t ring, stage, xs, sxs, psum, part, total;
+  size_t ring, stage, xs, sdi, part, total;
 };
 
+constexpr size_t kHeadBytes = 2 * kStages * sizeof(uint64_t) + kStages * sizeof(int) + 64;
+
 __host__ __device__ inline SmemLayout q4g_smem_layout(int mode, int kqg, int gps, int m, int ns,
-                                                      int tchunk) {
+                                                      int tchunk, bool direct) {
   SmemLayout L;
   const int cg = kChunkQ / kqg;                       // groups per chunk
   const int nchunk = (gps + cg - 1) / cg;
   L.stage = (size_t)gps * kqg * 512 + (size_t)gps * 128;  // a row tile's k-split
-  L.ring = ((size_t)2 * kStages * sizeof(uint64_t) + 127) / 128 * 128;  // after the barriers
+  L.ring = (kHeadBytes + 127) / 128 * 128;
   L.xs = L.ring + L.stage * ns;
-  const int cols = mode == 1 ? 2 * m : m;             // B columns holding data
-  L.sxs = L.xs + (size_t)gps * kqg * 4 * cols * 4 * xfrag_bytes<1>() * (mode == 1 ? 1 : 2);
-  L.psum = L.sxs + (size_t)gps * 16 * sizeof(float);
-  const size_t nch = 2 * (((size_t)gps * kqg * 16 + 31) / 32);
-  L.part = L.psum + 2 * (size_t)m * nch * sizeof(float);
+  const size_t k32 = (size_t)gps * kqg * 2;
+  L.sdi = L.xs + k32 * (mode == 1 ? 2 * m * 4 * 8 : m * 4 * 16);
+  L.part = L.sdi + (size_t)gps * 16 * sizeof(int);
   L.part = (L.part + 15) & ~(size_t)15;
-  L.total = L.part + (size_t)tchunk * nchunk * 16 * 8 * sizeof(float);
+  L.total = L.part + (size_t)(direct ? ns : tchunk) * nchunk * 16 * 8 * sizeof(float);
   return L;
 }
 
 // One CTA = k-split `rank` of the row tiles of its cluster.  Warp kCons is the
-// producer (one lane streams units with bulk copies); consumer warp w handles
-// units (row tile i, chunk c) with (i * ncn + c) % kCons == w (ncn = nominal
-// chunks per row tile, the same on every rank); stage
-// i % ns of a row tile therefore always serves the same warps (ns is a multiple
-// of kCons / gcd(ncn, kCons)),
-// so no warp ever waits more than one phase ahead on a stage barrier.
-// MODE 1: M <= 4, one MMA per k-tile (hi parts of x in columns 0..3, lo in 4..7).
-// MODE 2: M <= 8, two MMAs per k-tile (hi and lo each in columns 0..7).
+// producer (lanes 0..kIssuers-1 stream row-tile slices with bulk copies);
+// consumer warp w takes the 512-k chunk units (row tile i, chunk c) with
+// (i * ncn + c) % kCons == w (ncn = nominal chunks per row tile, the same on
+// every rank); stage i % ns of a row tile therefore always serves the same
+// warps (ns is a multiple of kCons / gcd(ncn, kCons)), so no warp ever waits
+// more than one phase ahead on a stage barrier.
+//
+// Math: the nibbles (0..15, exact s8) multiply two s8 digits of x,
+// x ~= s_m (d0 + d1 / 256) with s_m = max|x_m| / 127 over the k-split, on the
+// s8 tensor cores (mma.m16n8k32, exact s32 sums); per group the fp32 epilogue
+// applies  sum_k (n - zp) sc x = sc s_m (A - zp D)  with A the MMA sum and D
+// the digit sum.  The weight values themselves are never rounded.
+// MODE 1: M <= 4, one MMA per 32 k (d0 in columns 0..3, d1 in 4..7).
+// MODE 2: M <= 8, two MMAs per 32 k (d0 and d1 each in columns 0..7).
 // KQG: k-quads (64 k) per quantisation group (group size 64 * KQG).
 template <int MODE, int KQG>
 __global__ void __launch_bounds__((kCons + 1) * 32, 1)
@@ -236,24 +258,30 @@ q4g_gemv_kernel(const GemvArgs a) {
   const int ncn = (a.gps + CG - 1) / CG;           // nominal chunks (same on every rank)
   const int nunits = nrt * ncn;
   const int NS = a.ns;
-  const int cols = MODE == 1 ? 2 * a.m : a.m;
+  const bool direct = nsplit == 1;  // no k-split: row tiles are finished in-CTA
 
-  const SmemLayout Ls = q4g_smem_layout(MODE, KQG, a.gps, a.m, NS, a.tchunk);
+  const SmemLayout Ls = q4g_smem_layout(MODE, KQG, a.gps, a.m, NS, a.tchunk, direct);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + kStages;
+  int* cnt = reinterpret_cast<int*>(empty + kStages);
+  unsigned* xmax = reinterpret_cast<unsigned*>(cnt + kStages);
+  const uint4* zpad = reinterpret_cast<const uint4*>(xmax + 8);
   unsigned char* ring = smem + Ls.ring;
   unsigned char* xs = smem + Ls.xs;
-  float* sxs = reinterpret_cast<float*>(smem + Ls.sxs);
-  float* psum = reinterpret_cast<float*>(smem + Ls.psum);
+  int* sdi = reinterpret_cast<int*>(smem + Ls.sdi);
   float* part = reinterpret_cast<float*>(smem + Ls.part);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], nchunk > 0 ? nchunk : 1);
+      mbar_init(&empty[s], direct ? 1 : (nchunk > 0 ? nchunk : 1));
+      cnt[s] = 0;
     }
     mbar_fence_init();
   }
+  if (threadIdx.x < 8) xmax[threadIdx.x] = 0u;
+  if (threadIdx.x < 4) reinterpret_cast<unsigned*>(xmax + 8)[threadIdx.x] = 0u;  // zero pad
+  for (int i = threadIdx.x; i < ng * 16; i += blockDim.x) sdi[i] = 0;
   __syncthreads();
 
   if (warp == kCons) {
@@ -261,7 +289,7 @@ q4g_gemv_kernel(const GemvArgs a) {
     // this runs without griddepcontrol.wait and overlaps the previous kernel.
     // Lanes 0..kIssuers-1 own the stages s = lane (mod kIssuers).
     griddep_launch_dependents();
-    if (lane < kIssuers) {
+    if (lane < kIssuers && ng > 0) {
       bool ok = true;
       const uint32_t wb = (uint32_t)ng * KQG * 512u, zb = (uint32_t)ng * 128u;
       int issued_last = -1;
@@ -271,12 +299,16 @@ q4g_gemv_kernel(const GemvArgs a) {
           ok = false;
           break;
         }
-        const int rt = rt0 + i;
+        const int grt = rt0 + i;
+        int p = 0;
+        while (p + 1 < a.nprob && grt >= a.rt_prefix[p + 1]) ++p;
+        const int rt = grt - a.rt_prefix[p];
         unsigned char* dst = ring + (size_t)s * Ls.stage;
         mbar_arrive_expect_tx(&full[s], wb + zb);
-        bulk_g2s(dst, a.frag + ((size_t)rt * a.kq_total + (size_t)g0 * KQG) * 32, wb, &full[s]);
-        bulk_g2s(dst + (size_t)a.gps * KQG * 512, a.sz + ((size_t)rt * a.groups + g0) * 8, zb,
+        bulk_g2s(dst, a.prob[p].frag + ((size_t)rt * a.kq_total + (size_t)g0 * KQG) * 32, wb,
                  &full[s]);
+        bulk_g2s(dst + (size_t)a.gps * KQG * 512,
+                 a.prob[p].sz + ((size_t)rt * a.groups + g0) * 8, zb, &full[s]);
         issued_last = i;
       }
       // drain: this lane's last copies land before the CTA may exit
@@ -288,103 +320,122 @@ q4g_gemv_kernel(const GemvArgs a) {
     }
     __syncwarp();
   } else {
-    // ---------------- consumers: stage x as compact B fragments + group sums
+    // ---------------- consumers: quantise x of the k-split into two s8 digits
     griddep_wait();  // x may be written by the previous kernel in the stream
-    {
-      const int kb0 = g0 * GS;
-      const int f4 = (ng * GS) >> 2;
-      const int f4p = (f4 + 31) & ~31;
-      const int nch = f4p >> 4;
-      uint32_t* xw = reinterpret_cast<uint32_t*>(xs);
-      constexpr int kUnroll = 4;
-      for (int it0 = threadIdx.x; it0 < a.m * f4p; it0 += kCons * 32 * kUnroll) {
-        float4 vv[kUnroll];
-#pragma unroll
-        for (int r = 0; r < kUnroll; ++r) {  // issue all loads first
-          const int it = it0 + r * kCons * 32;
-          const int mrow = it / f4p, f = it - mrow * f4p;
-          const int k = kb0 + 4 * f;
-          float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (it < a.m * f4p && f < f4) {
-            const float* xr = a.x + (size_t)mrow * a.ldx + k;
-            if (a.vec4 && k + 3 < a.k) {
-              v = __ldg(reinterpret_cast<const float4*>(xr));
-            } else {
-              v.x = k < a.k ? __ldg(xr) : 0.f;
-              v.y = k + 1 < a.k ? __ldg(xr + 1) : 0.f;
-              v.z = k + 2 < a.k ? __ldg(xr + 2) : 0.f;
-              v.w = k + 3 < a.k ? __ldg(xr + 3) : 0.f;
-            }
-          }
-          vv[r] = v;
-        }
-#pragma unroll
-        for (int r = 0; r < kUnroll; ++r) {
-          const int it = it0 + r * kCons * 32;
-          if (it >= a.m * f4p) break;  // uniform across the warp (f4p % 32 == 0)
-          const int mrow = it / f4p, f = it - mrow * f4p;
-          const float4 v = vv[r];
-          float sh = 0.f, sl = 0.f;
-          if (f < f4) {
-            uint32_t h01, l01, h23, l23;
-            split_bf16x2(v.x, v.y, h01, l01);
-            split_bf16x2(v.z, v.w, h23, l23);
-            sh = (bf16x2_lo(h01) + bf16x2_hi(h01)) + (bf16x2_lo(h23) + bf16x2_hi(h23));
-            sl = (bf16x2_lo(l01) + bf16x2_hi(l01)) + (bf16x2_lo(l23) + bf16x2_hi(l23));
-            // k offsets 4j..4j+3 of a 16-k tile feed lanes t = 2(j&1), 2(j&1)+1,
-            // fragment word j>>1 (k 0..7 -> b0, k 8..15 -> b1)
-            const int ktl = f >> 2, j = f & 3;
-            const int t0 = 2 * (j & 1), word = j >> 1;
-            if (MODE == 1) {
-              // compact columns: hi of row m at m, lo of row m at M + m
-              const size_t eh = ((size_t)ktl * cols + mrow) * 4 + t0;
-              const size_t el = ((size_t)ktl * cols + a.m + mrow) * 4 + t0;
-              xw[eh * 2 + word] = h01;
-              xw[(eh + 1) * 2 + word] = h23;
-              xw[el * 2 + word] = l01;
-              xw[(el + 1) * 2 + word] = l23;
-            } else {
-              const size_t e = ((size_t)ktl * cols + mrow) * 4 + t0;
-              xw[e * 4 + word] = h01;
-              xw[(e + 1) * 4 + word] = h23;
-              xw[e * 4 + 2 + word] = l01;
-              xw[(e + 1) * 4 + 2 + word] = l23;
-            }
-          }
-#pragma unroll
-          for (int o = 8; o > 0; o >>= 1) {
-            sh += __shfl_xor_sync(0xffffffffu, sh, o);
-            sl += __shfl_xor_sync(0xffffffffu, sl, o);
-          }
-          if ((lane & 15) == 0) {
-            psum[mrow * nch + (f >> 4)] = sh;
-            psum[(a.m + mrow) * nch + (f >> 4)] = sl;
-          }
+    const int kb0 = g0 * GS;
+    const int f4 = (ng * GS) >> 2;
+    const int f4p = (f4 + 31) & ~31;  // per-row item runs padded to whole warps
+    constexpr int kUnroll = 4;
+    const int nthr = kCons * 32;
+    auto load4 = [&](int it) -> float4 {
+      const int mrow = it / f4p, f = it - mrow * f4p;
+      const int k = kb0 + 4 * f;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (it < a.m * f4p && f < f4) {
+        const float* xr = a.x + (size_t)mrow * a.ldx + k;
+        if (a.vec4 && k + 3 < a.k) {
+          v = __ldg(reinterpret_cast<const float4*>(xr));
+        } else {
+          v.x = k < a.k ? __ldg(xr) : 0.f;
+          v.y = k + 1 < a.k ? __ldg(xr + 1) : 0.f;
+          v.z = k + 2 < a.k ? __ldg(xr + 2) : 0.f;
+          v.w = k + 3 < a.k ? __ldg(xr + 3) : 0.f;
         }
       }
-      named_barrier(1, kCons * 32);
-      for (int e = threadIdx.x; e < ng * 16; e += kCons * 32) {
-        const int gl = e >> 4, part_lo = (e >> 3) & 1, n = e & 7;
-        float s = 0.f;
-        if (n < a.m) {
-          const float* ps = psum + (part_lo * a.m + n) * nch + gl * KQG;
+      return v;
+    };
+    // pass 1: max |x| per row (a warp's 32 items always belong to one row)
+    for (int it0 = threadIdx.x; it0 < a.m * f4p; it0 += nthr * kUnroll) {
+      float4 vv[kUnroll];
 #pragma unroll
-          for (int c = 0; c < KQG; ++c) s += ps[c];
-        }
-        sxs[e] = s;
+      for (int r = 0; r < kUnroll; ++r) vv[r] = load4(it0 + r * nthr);
+#pragma unroll
+      for (int r = 0; r < kUnroll; ++r) {
+        const int it = it0 + r * nthr;
+        if (it >= a.m * f4p) break;  // uniform across the warp
+        float mx = fmaxf(fmaxf(fabsf(vv[r].x), fabsf(vv[r].y)), fmaxf(fabsf(vv[r].z), fabsf(vv[r].w)));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) atomicMax(&xmax[it / f4p], __float_as_uint(mx));
       }
-      named_barrier(1, kCons * 32);
     }
+    named_barrier(1, nthr);
+    // pass 2: digits d0 = rint(x / s), d1 = rint((x / s - d0) * 256), packed
+    // 4 k per word straight into the B fragment slots, and exact digit sums
+    const int cols = MODE == 1 ? 2 * a.m : a.m;
+    uint32_t* xw = reinterpret_cast<uint32_t*>(xs);
+    for (int it0 = threadIdx.x; it0 < a.m * f4p; it0 += nthr * kUnroll) {
+      float4 vv[kUnroll];
+#pragma unroll
+      for (int r = 0; r < kUnroll; ++r) vv[r] = load4(it0 + r * nthr);
+#pragma unroll
+      for (int r = 0; r < kUnroll; ++r) {
+        const int it = it0 + r * nthr;
+        if (it >= a.m * f4p) break;
+        const int mrow = it / f4p, f = it - mrow * f4p;
+        const float mxv = __uint_as_float(xmax[mrow]);
+        const float inv = mxv > 0.f ? 127.0f / mxv : 0.f;
+        const float xv[4] = {vv[r].x, vv[r].y, vv[r].z, vv[r].w};
+        uint32_t w0 = 0, w1 = 0;
+        int s0 = 0, s1 = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const float q = xv[b] * inv;
+          const int d0 = max(-127, min(127, __float2int_rn(q)));
+          const int d1 = max(-127, min(127, __float2int_rn((q - (float)d0) * 256.0f)));
+          w0 |= (uint32_t)(d0 & 0xFF) << (8 * b);
+          w1 |= (uint32_t)(d1 & 0xFF) << (8 * b);
+          s0 += d0;
+          s1 += d1;
+        }
+        if (f < f4) {
+          const int kt32 = f >> 3, j = f & 7;
+          const int half = j >> 2, tt = j & 3;
+          if (MODE == 1) {
+            xw[(((size_t)kt32 * cols + mrow) * 4 + tt) * 2 + half] = w0;
+            xw[(((size_t)kt32 * cols + a.m + mrow) * 4 + tt) * 2 + half] = w1;
+          } else {
+            xw[(((size_t)kt32 * cols + mrow) * 4 + tt) * 4 + half] = w0;
+            xw[(((size_t)kt32 * cols + mrow) * 4 + tt) * 4 + 2 + half] = w1;
+          }
+        }
+        // 64-k chunk sums over 16 lanes, then into the group's digit sums
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) {
+          s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+          s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+        }
+        if ((lane & 15) == 0 && f < f4) {
+          const int grp = (f >> 4) / KQG;
+          atomicAdd(&sdi[grp * 16 + mrow], s0);
+          atomicAdd(&sdi[grp * 16 + 8 + mrow], s1);
+        }
+      }
+    }
+    named_barrier(1, nthr);
     griddep_launch_dependents();
 
     // lane (n = g, t) carries B column n
     const int mcol = MODE == 1 ? (g & 3) : g;
     const bool bvalid = mcol < a.m;
-    const int ccol = MODE == 1 ? (g < 4 ? mcol : a.m + mcol) : mcol;  // compact column
-    const int sx_off = MODE == 1 ? (t < 2 ? 2 * t : 2 * t + 4) : 2 * t;
+    const int ccol = MODE == 1 ? (g < 4 ? mcol : a.m + mcol) : mcol;
+    const int sd_off = MODE == 1 ? (t < 2 ? 2 * t : 2 * t + 4) : 2 * t;
     const bool lane_has = MODE == 1 ? (t < 2) : true;
-    const uint2* xs2 = reinterpret_cast<const uint2*>(xs) + ccol * 4 + t;
-    const uint4* xs4 = reinterpret_cast<const uint4*>(xs) + ccol * 4 + t;
+    // digit scale of this lane's result columns 2t, 2t+1
+    float dsc[2], dsc2[2];
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const int m = MODE == 1 ? (t < 2 ? 2 * t + c : 2 * t - 4 + c) : 2 * t + c;
+      const float mxv = m < a.m ? __uint_as_float(xmax[m]) : 0.f;
+      const float sm = mxv / 127.0f;
+      dsc[c] = (MODE == 1 && t >= 2) ? sm * (1.0f / 256.0f) : sm;
+      dsc2[c] = sm * (1.0f / 256.0f);
+    }
+    // invalid columns read a zero pad (unconditional loads, no divergence)
+    const uint2* xs2 = bvalid ? reinterpret_cast<const uint2*>(xs) + ccol * 4 + t
+                              : reinterpret_cast<const uint2*>(zpad);
+    const uint4* xs4 = bvalid ? reinterpret_cast<const uint4*>(xs) + ccol * 4 + t : zpad;
+    const int xstride = bvalid ? cols * 4 : 0;
 
     for (int u = warp; u < nunits; u += kCons) {
       const int i = u / ncn, c = u - i * ncn;
@@ -400,13 +451,13 @@ q4g_gemv_kernel(const GemvArgs a) {
         const float4* szp =
             reinterpret_cast<const float4*>(st + (size_t)a.gps * KQG * 512 + (size_t)cg0 * 128) + g;
         // one accumulator set per group of the chunk: CG independent MMA chains
-        float acc[CG][4], acc2[MODE == 2 ? CG : 1][4];
+        int acc[CG][4], acc2[MODE == 2 ? CG : 1][4];
 #pragma unroll
         for (int gl = 0; gl < CG; ++gl)
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            acc[gl][q] = 0.f;
-            acc2[MODE == 2 ? gl : 0][q] = 0.f;
+            acc[gl][q] = 0;
+            acc2[MODE == 2 ? gl : 0][q] = 0;
           }
 #pragma unroll
         for (int gl = 0; gl < CG; ++gl) {
@@ -415,68 +466,110 @@ q4g_gemv_kernel(const GemvArgs a) {
             for (int qq = 0; qq < KQG; ++qq) {
               const int ql = gl * KQG + qq;                // quad within the chunk
               const uint4 w = wq[ql * 32];
-              const int kt0 = (cg0 * KQG + ql) * 4;        // k-tile within the CTA range
 #pragma unroll
-              for (int jj = 0; jj < 4; ++jj) {
-                const uint32_t word = jj == 0 ? w.x : (jj == 1 ? w.y : (jj == 2 ? w.z : w.w));
-                const uint32_t a0 = lop3_and_or(word, 0x000F000Fu, 0x43004300u);
-                const uint32_t a1 = lop3_and_or(word >> 4, 0x000F000Fu, 0x43004300u);
-                const uint32_t a2 = lop3_and_or(word >> 8, 0x000F000Fu, 0x43004300u);
-                const uint32_t a3 = lop3_and_or(word >> 12, 0x000F000Fu, 0x43004300u);
-                const int kt = kt0 + jj;
+              for (int h = 0; h < 2; ++h) {
+                const uint32_t wa = h == 0 ? w.x : w.z, wb = h == 0 ? w.y : w.w;
+                const uint32_t a0 = wa & 0x0F0F0F0Fu, a1 = (wa >> 4) & 0x0F0F0F0Fu;
+                const uint32_t a2 = wb & 0x0F0F0F0Fu, a3 = (wb >> 4) & 0x0F0F0F0Fu;
+                const int kt32 = (cg0 * KQG + ql) * 2 + h;  // k32 tile within the k-split
                 if (MODE == 1) {
-                  uint2 b = make_uint2(0u, 0u);
-                  if (bvalid) b = xs2[(size_t)kt * cols * 4];
-                  mma_bf16_16816(acc[gl], a0, a1, a2, a3, b.x, b.y);
+                  const uint2 b = xs2[(size_t)kt32 * xstride];
+                  mma_s8_16832(acc[gl], a0, a1, a2, a3, b.x, b.y);
                 } else {
-                  uint4 b = make_uint4(0u, 0u, 0u, 0u);
-                  if (bvalid) b = xs4[(size_t)kt * cols * 4];
-                  mma_bf16_16816(acc[gl], a0, a1, a2, a3, b.x, b.y);
-                  mma_bf16_16816(acc2[MODE == 2 ? gl : 0], a0, a1, a2, a3, b.z, b.w);
+                  const uint4 b = xs4[(size_t)kt32 * xstride];
+                  mma_s8_16832(acc[gl], a0, a1, a2, a3, b.x, b.y);
+                  mma_s8_16832(acc2[MODE == 2 ? gl : 0], a0, a1, a2, a3, b.z, b.w);
                 }
               }
             }
           }
         }
-        // per-group epilogues: sum_k (n - zp) x = acc - (128 + zp) sum_k x
+        // per-group epilogue: sum_k (n - zp) sc x = sc s (A - zp D)
 #pragma unroll
         for (int gl = 0; gl < CG; ++gl) {
           if (gl < ncg) {
             const float4 sp = szp[gl * 8];
-            const float zg = 128.0f + sp.y, zg8 = 128.0f + sp.w;
-            const int glc = cg0 + gl;                      // group within the CTA range
-            const float2 sx = *reinterpret_cast<const float2*>(&sxs[glc * 16 + sx_off]);
+            const int* sd = sdi + (cg0 + gl) * 16;
+            const float d0a = (float)sd[sd_off], d0b = (float)sd[sd_off + 1];
             if (MODE == 1) {
-              tot[0] = fmaf(sp.x, fmaf(-zg, sx.x, acc[gl][0]), tot[0]);
-              tot[1] = fmaf(sp.x, fmaf(-zg, sx.y, acc[gl][1]), tot[1]);
-              tot[2] = fmaf(sp.z, fmaf(-zg8, sx.x, acc[gl][2]), tot[2]);
-              tot[3] = fmaf(sp.z, fmaf(-zg8, sx.y, acc[gl][3]), tot[3]);
+              tot[0] = fmaf(sp.x * dsc[0], fmaf(-sp.y, d0a, (float)acc[gl][0]), tot[0]);
+              tot[1] = fmaf(sp.x * dsc[1], fmaf(-sp.y, d0b, (float)acc[gl][1]), tot[1]);
+              tot[2] = fmaf(sp.z * dsc[0], fmaf(-sp.w, d0a, (float)acc[gl][2]), tot[2]);
+              tot[3] = fmaf(sp.z * dsc[1], fmaf(-sp.w, d0b, (float)acc[gl][3]), tot[3]);
             } else {
-              const float2 sl = *reinterpret_cast<const float2*>(&sxs[glc * 16 + 8 + sx_off]);
               const int g2 = MODE == 2 ? gl : 0;
-              tot[0] = fmaf(sp.x, fmaf(-zg, sx.x, acc[gl][0]) + fmaf(-zg, sl.x, acc2[g2][0]), tot[0]);
-              tot[1] = fmaf(sp.x, fmaf(-zg, sx.y, acc[gl][1]) + fmaf(-zg, sl.y, acc2[g2][1]), tot[1]);
-              tot[2] = fmaf(sp.z, fmaf(-zg8, sx.x, acc[gl][2]) + fmaf(-zg8, sl.x, acc2[g2][2]), tot[2]);
-              tot[3] = fmaf(sp.z, fmaf(-zg8, sx.y, acc[gl][3]) + fmaf(-zg8, sl.y, acc2[g2][3]), tot[3]);
+              const float d1a = (float)sd[8 + sd_off], d1b = (float)sd[8 + sd_off + 1];
+              tot[0] += sp.x * (dsc[0] * fmaf(-sp.y, d0a, (float)acc[gl][0]) +
+                                dsc2[0] * fmaf(-sp.y, d1a, (float)acc2[g2][0]));
+              tot[1] += sp.x * (dsc[1] * fmaf(-sp.y, d0b, (float)acc[gl][1]) +
+                                dsc2[1] * fmaf(-sp.y, d1b, (float)acc2[g2][1]));
+              tot[2] += sp.z * (dsc[0] * fmaf(-sp.w, d0a, (float)acc[gl][2]) +
+                                dsc2[0] * fmaf(-sp.w, d1a, (float)acc2[g2][2]));
+              tot[3] += sp.z * (dsc[1] * fmaf(-sp.w, d0b, (float)acc[gl][3]) +
+                                dsc2[1] * fmaf(-sp.w, d1b, (float)acc2[g2][3]));
             }
           }
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
       if (MODE == 1) {
 #pragma unroll
         for (int q = 0; q < 4; ++q) tot[q] += __shfl_xor_sync(0xffffffffu, tot[q], 2);
       }
+      if (!direct) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        if (lane_has) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int r = g + ((q & 2) ? 8 : 0);
+            const int mm = 2 * t + (q & 1);
+            part[((size_t)u * 16 + r) * 8 + mm] = tot[q];
+          }
+        }
+        continue;
+      }
+      // direct mode: the row tile's last chunk-warp sums the chunk partials in
+      // chunk order (deterministic), writes y and releases the stage
+      float* red = part + ((size_t)s * ncn) * 128;
       if (lane_has) {
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int r = g + ((q & 2) ? 8 : 0);
           const int mm = 2 * t + (q & 1);
-          part[((size_t)u * 16 + r) * 8 + mm] = tot[q];
+          red[(size_t)c * 128 + r * 8 + mm] = tot[q];
+        }
+      }
+      __threadfence_block();
+      __syncwarp();
+      int old = 0;
+      if (lane == 0) old = atomicAdd(&cnt[s], 1);
+      old = __shfl_sync(0xffffffffu, old, 0);
+      if (old == nchunk - 1) {
+        __threadfence_block();
+        const int grt = rt0 + i;
+        int p = 0;
+        while (p + 1 < a.nprob && grt >= a.rt_prefix[p + 1]) ++p;
+        const int rbase = (grt - a.rt_prefix[p]) * 16;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int e = lane * 4 + q;
+          const int r = e >> 3, mm = e & 7;
+          float v = 0.f;
+          for (int c2 = 0; c2 < nchunk; ++c2) v += red[(size_t)c2 * 128 + e];
+          if (mm < a.m && rbase + r < a.prob[p].rows)
+            a.prob[p].y[(size_t)mm * a.prob[p].ldy + rbase + r] = v;
+        }
+        __syncwarp();
+        if (lane == 0) {
+          cnt[s] = 0;
+          mbar_arrive(&empty[s]);
         }
       }
     }
+  }
+  if (direct) {
+    __syncthreads();  // the producer's drain completes before the CTA exits
+    return;
   }
   // sum the chunks of each row tile locally (chunk order) into the now idle
   // ring, then over the cluster's k-splits (rank order): deterministic.
@@ -492,11 +585,14 @@ q4g_gemv_kernel(const GemvArgs a) {
   const int total = nrt * 128;
   for (int e = rank * blockDim.x + threadIdx.x; e < total; e += nsplit * blockDim.x) {
     const int mm = e & 7;
-    const int row = rt0 * 16 + (e >> 3);
-    if (mm >= a.m || row >= a.rows) continue;
+    const int grt = rt0 + (e >> 7);
+    int p = 0;
+    while (p + 1 < a.nprob && grt >= a.rt_prefix[p + 1]) ++p;
+    const int row = (grt - a.rt_prefix[p]) * 16 + ((e >> 3) & 15);
+    if (mm >= a.m || row >= a.prob[p].rows) continue;
     float s = 0.0f;
     for (int r = 0; r < nsplit; ++r) s += cluster.map_shared_rank(sums, r)[e];
-    a.y[(size_t)mm * a.ldy + row] = s;
+    a.prob[p].y[(size_t)mm * a.prob[p].ldy + row] = s;
   }
   cluster.sync();
 }
@@ -600,12 +696,37 @@ int q4g_dequant(const Q4GWeight& w, float* out, cudaStream_t st) {
 
 namespace {
 
-// Launches the GEMV over row tiles [rt_begin, rt_begin + n_rt) of w.
+// Ring stages of direct mode (no k-split) for this shape, 0 if it does not fit.
+inline int direct_ring_stages(int mode, int kqg, int groups, int mc) {
+  const SmemLayout L0 = q4g_smem_layout(mode, kqg, groups, mc, 0, 1, true);
+  if (L0.total >= kSmemBudget) return 0;
+  const int ncn = (groups + kChunkQ / kqg - 1) / (kChunkQ / kqg);
+  int gcdv = kCons, bb = ncn;
+  while (bb) { const int tmp = gcdv % bb; gcdv = bb; bb = tmp; }
+  const int period = std::max(kCons / gcdv, kIssuers);
+  int ns = (int)((kSmemBudget - L0.total) / (L0.stage + (size_t)ncn * 512));
+  ns = std::min(ns, kStages) / period * period;
+  return ns >= std::max(period, 4) ? ns : 0;
+}
+
+// A row-tile range of one weight inside a launch.
+struct Piece {
+  const Q4GWeight* w;
+  int64_t rt_begin;
+  int n_rt;
+  float* y;       // y of the whole weight (row 0)
+  int64_t ldy;
+};
+
+// Launches the GEMV over the given pieces (same K, group size and x).
 template <int MODE, int KQG>
-int launch_fast(const Q4GWeight& w, int64_t rt_begin, int n_rt, const float* x, int64_t ldx,
-                int mc, float* y, int64_t ldy, int num_sms, cudaStream_t st) {
+int launch_fast(const Piece* pcs, int npc, const float* x, int64_t ldx, int mc, int num_sms,
+                cudaStream_t st) {
   Context* c = ctx();
-  const int groups = (int)w.groups;
+  const Q4GWeight& w0 = *pcs[0].w;
+  const int groups = (int)w0.groups;
+  int n_rt = 0;
+  for (int i = 0; i < npc; ++i) n_rt += pcs[i].n_rt;
   const int slots = num_sms * kCtasPerSm;
   auto kern = q4g_gemv_kernel<MODE, KQG>;
   static int attr_dev = -1;
@@ -634,33 +755,41 @@ int launch_fast(const Q4GWeight& w, int64_t rt_begin, int n_rt, const float* x, 
     cudaGetLastError();
     attr_dev = c->device;
   }
-  // Pick the k-split count (= cluster size): feasible shared memory with at
-  // least kCons ring stages (row-tile slices); score = estimated time relative to
-  // a balanced full-GPU run (SM utilisation x row-tile balance).
+  // Pick the k-split count (= cluster size).  Without a k-split (direct mode)
+  // every row tile is finished inside one CTA and written straight to y, so
+  // it is preferred whenever a full-K row-tile slice fits the ring.  Otherwise
+  // choose s with feasible shared memory (>= one ring period of stages) and
+  // the best estimated time relative to a balanced full-GPU run.
   int best_s = -1, best_gps = 0, best_nclu = 1, best_ns = 0;
   double best_score = 1e30;
   for (int s = 1; s <= kMaxSplits; ++s) {
+#ifdef NIMF_Q4G_FORCE_SPLITS
+    if (s != NIMF_Q4G_FORCE_SPLITS) continue;
+#endif
     const int gps = (groups + s - 1) / s;
     const int ss = (groups + gps - 1) / gps;
     if (ss != s) continue;
+    const bool direct = ss == 1;
     const int act = (c && attr_dev == c->device) ? max_active[ss] : slots / ss;
     const int nclu = std::max(1, std::min(n_rt, act));
     const int tchunk = (n_rt + nclu - 1) / nclu;
-    const SmemLayout L0 = q4g_smem_layout(MODE, KQG, gps, mc, 0, tchunk);
+    if (!direct && tchunk > kMaxTilesPerCluster) continue;
+    const SmemLayout L0 = q4g_smem_layout(MODE, KQG, gps, mc, 0, tchunk, direct);
     if (L0.total >= kSmemBudget) continue;
-    const size_t stage = L0.stage;
-    // stage i % ns serves warps (i * nchunk + c) % kCons: keep ns a multiple of
+    const int ncn = (gps + kChunkQ / KQG - 1) / (kChunkQ / KQG);
+    const size_t per_stage = L0.stage + (direct ? (size_t)ncn * 512 : 0);
+    // stage i % ns serves warps (i * ncn + c) % kCons: keep ns a multiple of
     // that period so every stage always serves the same warps
-    const int nchunk = (gps + kChunkQ / KQG - 1) / (kChunkQ / KQG);
-    int gcdv = kCons, bb = nchunk;
+    int gcdv = kCons, bb = ncn;
     while (bb) { const int tmp = gcdv % bb; gcdv = bb; bb = tmp; }
     const int period = std::max(kCons / gcdv, kIssuers);
-    int ns = (int)((kSmemBudget - L0.total) / stage);
+    int ns = (int)((kSmemBudget - L0.total) / per_stage);
     ns = std::min(ns, kStages) / period * period;
-    if (ns < std::max(period, 4) || (size_t)ns * stage < (size_t)tchunk * 512) continue;
+    if (ns < std::max(period, 4) || (!direct && (size_t)ns * L0.stage < (size_t)tchunk * 512))
+      continue;
     const double util = std::min(1.0, (double)ss * nclu / slots);
     const double balance = (double)tchunk * nclu / n_rt;
-    const double score = balance / util;
+    const double score = direct ? 0.0 : balance / util;
     if (score < best_score - 1e-9) {
       best_score = score;
       best_s = ss;
@@ -670,25 +799,31 @@ int launch_fast(const Q4GWeight& w, int64_t rt_begin, int n_rt, const float* x, 
     }
   }
   if (best_s < 0)
-    return set_error(NIMF_ERR_UNSUPPORTED, "q4g gemv: K=%lld, M=%d does not fit the staging",
-                     (long long)w.k, mc);
+    return set_error(NIMF_ERR_UNSUPPORTED, "q4g gemv: K=%lld, M=%d (%d row tiles) does not fit",
+                     (long long)w0.k, mc, n_rt);
   const int s = best_s, gps = best_gps, n_clusters = best_nclu, ns = best_ns;
   const int tchunk = (n_rt + n_clusters - 1) / n_clusters;
-  const SmemLayout L = q4g_smem_layout(MODE, KQG, gps, mc, ns, tchunk);
+  const SmemLayout L = q4g_smem_layout(MODE, KQG, gps, mc, ns, tchunk, s == 1);
 
   GemvArgs a;
-  a.frag = (const uint4*)w.frag + (size_t)rt_begin * w.kq_total * 32;
-  a.sz = (const float4*)w.sz + (size_t)rt_begin * w.groups * 8;
+  a.nprob = npc;
+  a.rt_prefix[0] = 0;
+  for (int i = 0; i < npc; ++i) {
+    const Q4GWeight& w = *pcs[i].w;
+    a.prob[i].frag = (const uint4*)w.frag + (size_t)pcs[i].rt_begin * w.kq_total * 32;
+    a.prob[i].sz = (const float4*)w.sz + (size_t)pcs[i].rt_begin * w.groups * 8;
+    a.prob[i].y = pcs[i].y + pcs[i].rt_begin * 16;
+    a.prob[i].ldy = pcs[i].ldy;
+    a.prob[i].rows = (int)std::min<int64_t>((int64_t)pcs[i].n_rt * 16, w.rows - pcs[i].rt_begin * 16);
+    a.rt_prefix[i + 1] = a.rt_prefix[i] + pcs[i].n_rt;
+  }
   a.x = x;
-  a.y = y + rt_begin * 16;
   a.err = c ? c->dev_err : nullptr;
   a.ldx = ldx;
-  a.ldy = ldy;
   a.m = mc;
-  a.k = (int)w.k;
-  a.rows = (int)std::min<int64_t>((int64_t)n_rt * 16, w.rows - rt_begin * 16);
+  a.k = (int)w0.k;
   a.n_rt = n_rt;
-  a.kq_total = (int)w.kq_total;
+  a.kq_total = (int)w0.kq_total;
   a.groups = groups;
   a.gps = gps;
   a.n_clusters = n_clusters;
@@ -714,59 +849,99 @@ int launch_fast(const Q4GWeight& w, int64_t rt_begin, int n_rt, const float* x, 
   return NIMF_OK;
 }
 
-// Row tiles per launch are capped so a cluster holds at most kMaxTilesPerCluster
-// partial row tiles in shared memory.
+// Splits the concatenated row tiles of the weights into launches of at most
+// kMaxProblems pieces and a bounded number of row tiles per cluster.
 template <int MODE, int KQG>
-int launch_rows(const Q4GWeight& w, const float* x, int64_t ldx, int mc, float* y, int64_t ldy,
-                int num_sms, cudaStream_t st) {
-  const int64_t cap = (int64_t)kMaxTilesPerCluster * std::max(1, num_sms * kCtasPerSm / kMaxSplits);
-  for (int64_t r0 = 0; r0 < w.n_rt; r0 += cap) {
-    const int n = (int)std::min<int64_t>(cap, w.n_rt - r0);
-    NIMF_TRY((launch_fast<MODE, KQG>(w, r0, n, x, ldx, mc, y, ldy, num_sms, st)));
+int launch_rows(const Q4GWeight* const* ws, float* const* ys, int count, const float* x,
+                int64_t ldx, int mc, int64_t m0, int num_sms, cudaStream_t st) {
+  // Direct mode (no k-split) streams any number of row tiles; split mode keeps
+  // at most kMaxTilesPerCluster partial row tiles per cluster in shared memory.
+  const bool direct_fits = direct_ring_stages(MODE, KQG, (int)ws[0]->groups, mc) > 0;
+  const int64_t cap = direct_fits ? ((int64_t)1 << 40)
+                                  : (int64_t)kMaxTilesPerCluster *
+                                        std::max(1, num_sms * kCtasPerSm / kMaxSplits);
+  Piece pcs[kMaxProblems];
+  int npc = 0;
+  int64_t in_launch = 0;
+  for (int i = 0; i < count; ++i) {
+    const Q4GWeight& w = *ws[i];
+    for (int64_t r0 = 0; r0 < w.n_rt;) {
+      const int64_t n = std::min<int64_t>(w.n_rt - r0, cap - in_launch);
+      pcs[npc].w = &w;
+      pcs[npc].rt_begin = r0;
+      pcs[npc].n_rt = (int)n;
+      pcs[npc].y = ys[i] + m0 * w.rows;
+      pcs[npc].ldy = w.rows;
+      ++npc;
+      in_launch += n;
+      r0 += n;
+      if (npc == kMaxProblems || in_launch == cap) {
+        NIMF_TRY((launch_fast<MODE, KQG>(pcs, npc, x, ldx, mc, num_sms, st)));
+        npc = 0;
+        in_launch = 0;
+      }
+    }
   }
+  if (npc > 0) NIMF_TRY((launch_fast<MODE, KQG>(pcs, npc, x, ldx, mc, num_sms, st)));
   return NIMF_OK;
 }
 
 template <int MODE>
-int launch_mode(const Q4GWeight& w, const float* x, int64_t ldx, int mc, float* y, int64_t ldy,
-                int num_sms, cudaStream_t st) {
-  switch (w.gs) {
-    case 64: return launch_rows<MODE, 1>(w, x, ldx, mc, y, ldy, num_sms, st);
-    case 128: return launch_rows<MODE, 2>(w, x, ldx, mc, y, ldy, num_sms, st);
-    case 256: return launch_rows<MODE, 4>(w, x, ldx, mc, y, ldy, num_sms, st);
+int launch_mode(const Q4GWeight* const* ws, float* const* ys, int count, const float* x,
+                int64_t ldx, int mc, int64_t m0, int num_sms, cudaStream_t st) {
+  switch (ws[0]->gs) {
+    case 64: return launch_rows<MODE, 1>(ws, ys, count, x, ldx, mc, m0, num_sms, st);
+    case 128: return launch_rows<MODE, 2>(ws, ys, count, x, ldx, mc, m0, num_sms, st);
+    case 256: return launch_rows<MODE, 4>(ws, ys, count, x, ldx, mc, m0, num_sms, st);
   }
-  return set_error(NIMF_ERR_UNSUPPORTED, "q4g fast path: group size %lld", (long long)w.gs);
+  return set_error(NIMF_ERR_UNSUPPORTED, "q4g fast path: group size %lld", (long long)ws[0]->gs);
 }
 
 }  // namespace
 
-int q4g_gemv(const Q4GWeight& w, const float* x, int64_t m, float* y, cudaStream_t st) {
+int q4g_gemv_group(const Q4GWeight* const* ws, int count, const float* x, int64_t m,
+                   float* const* ys, cudaStream_t st) {
   Context* c = ctx();
   const int num_sms = c ? c->num_sms : 148;
-  if (m <= 0 || w.rows <= 0) return NIMF_OK;
-  if (w.k == 0) {
-    for (int64_t i = 0; i < m; ++i)
-      NIMF_CUDA_TRY(cudaMemsetAsync(y + i * w.rows, 0, (size_t)w.rows * sizeof(float), st));
+  if (m <= 0 || count <= 0) return NIMF_OK;
+  const Q4GWeight& w0 = *ws[0];
+  for (int i = 1; i < count; ++i)
+    if (ws[i]->k != w0.k || ws[i]->gs != w0.gs || ws[i]->fast != w0.fast)
+      return set_error(NIMF_ERR_SHAPE, "grouped GEMV: weights must share K and group size");
+  if (w0.k == 0) {
+    for (int i = 0; i < count; ++i)
+      if (ws[i]->rows > 0)
+        NIMF_CUDA_TRY(cudaMemsetAsync(ys[i], 0, (size_t)(m * ws[i]->rows) * sizeof(float), st));
     return NIMF_OK;
   }
   for (int64_t m0 = 0; m0 < m; m0 += 8) {
     const int mc = (int)std::min<int64_t>(8, m - m0);
-    const float* xc = x + m0 * w.k;
-    float* yc = y + m0 * w.rows;
-    if (w.fast) {
-      if (mc <= 4) NIMF_TRY(launch_mode<1>(w, xc, w.k, mc, yc, w.rows, num_sms, st));
-      else NIMF_TRY(launch_mode<2>(w, xc, w.k, mc, yc, w.rows, num_sms, st));
+    const float* xc = x + m0 * w0.k;
+    if (w0.fast) {
+      if (mc <= 4) NIMF_TRY(launch_mode<1>(ws, ys, count, xc, w0.k, mc, m0, num_sms, st));
+      else NIMF_TRY(launch_mode<2>(ws, ys, count, xc, w0.k, mc, m0, num_sms, st));
     } else {
-      const int block = 256;
-      const int64_t want = (w.rows * 32 + block - 1) / block;
-      const unsigned grid = (unsigned)std::min<int64_t>(want, (int64_t)num_sms * 16);
-      q4g_gemv_generic<<<grid, block, 0, st>>>((const uint8_t*)w.raw, (const float*)w.scales,
-                                               (const float*)w.zeros, w.rows, w.k, w.gs, w.ngr,
-                                               xc, w.k, mc, yc, w.rows);
-      NIMF_CUDA_TRY(cudaGetLastError());
+      for (int i = 0; i < count; ++i) {
+        const Q4GWeight& w = *ws[i];
+        if (w.rows == 0) continue;
+        const int block = 256;
+        const int64_t want = (w.rows * 32 + block - 1) / block;
+        const unsigned grid = (unsigned)std::min<int64_t>(want, (int64_t)num_sms * 16);
+        q4g_gemv_generic<<<grid, block, 0, st>>>((const uint8_t*)w.raw, (const float*)w.scales,
+                                                 (const float*)w.zeros, w.rows, w.k, w.gs, w.ngr,
+                                                 xc, w.k, mc, ys[i] + m0 * w.rows, w.rows);
+        NIMF_CUDA_TRY(cudaGetLastError());
+      }
     }
   }
   return NIMF_OK;
+}
+
+int q4g_gemv(const Q4GWeight& w, const float* x, int64_t m, float* y, cudaStream_t st) {
+  if (w.rows <= 0) return NIMF_OK;
+  const Q4GWeight* ws[1] = {&w};
+  float* ys[1] = {y};
+  return q4g_gemv_group(ws, 1, x, m, ys, st);
 }
 
 }  // namespace nimf

@@ -39,7 +39,8 @@ EXPORTS = [
     "nimf_init", "nimf_shutdown", "nimf_last_error", "nimf_device_count", "nimf_sync",
     "nimf_weight_register_q4g", "nimf_weight_register_i8", "nimf_weight_register_cf",
     "nimf_weight_register_fp4", "nimf_weight_register_f32", "nimf_weight_free",
-    "nimf_weight_info", "nimf_matmul_w", "nimf_matmul_w_dev", "nimf_matmul_q4",
+    "nimf_weight_info", "nimf_matmul_w", "nimf_matmul_w_dev", "nimf_matmul_w_group_dev",
+    "nimf_matmul_w_group", "nimf_matmul_q4",
     "nimf_weight_cache_clear", "nimf_matmul_f32", "nimf_matmul2_f32", "nimf_dequant_w",
     "nimf_cf_encode", "nimf_cf_decode", "nimf_cf_encode_dev", "nimf_cf_decode_dev",
     "nimf_cf_autoselect", "nimf_apf_cast",
@@ -82,6 +83,8 @@ def lib():
                              ctypes.POINTER(ctypes.c_int), ctypes.POINTER(i64)],
         "nimf_matmul_w": [ctypes.c_uint64, vp, i64, vp],
         "nimf_matmul_w_dev": [ctypes.c_uint64, vp, i64, vp, vp],
+        "nimf_matmul_w_group_dev": [vp, i32, vp, i64, vp, vp],
+        "nimf_matmul_w_group": [vp, i32, vp, i64, vp],
         "nimf_matmul_q4": [vp, vp, vp, vp, i64, i64, i64, i64, i64, vp],
         "nimf_weight_cache_clear": [],
         "nimf_matmul_f32": [vp, i64, i64, vp, i64, i64, vp],
@@ -361,6 +364,24 @@ class Weight:
         """Device pointers (ints), asynchronous on `stream` (int handle or None)."""
         check(lib().nimf_matmul_w_dev(self.handle, ctypes.c_void_p(x_ptr), M,
                                       ctypes.c_void_p(y_ptr), ctypes.c_void_p(stream or 0)))
+
+    @staticmethod
+    def matmul_group(weights, x, M):
+        """Weights sharing K applied to the same host x; returns a list of y."""
+        x = _arr(x, np.float32)
+        hs = (ctypes.c_uint64 * len(weights))(*[w.handle for w in weights])
+        ys = [np.empty(M * w.rows, np.float32) for w in weights]
+        yp = (ctypes.c_void_p * len(weights))(*[y.ctypes.data for y in ys])
+        check(lib().nimf_matmul_w_group(hs, len(weights), _ptr(x), M, yp))
+        return [y.reshape(M, w.rows) for y, w in zip(ys, weights)]
+
+    @staticmethod
+    def matmul_group_dev(weights, x_ptr, M, y_ptrs, stream=None):
+        """Device-pointer form (ints), asynchronous on `stream`."""
+        hs = (ctypes.c_uint64 * len(weights))(*[w.handle for w in weights])
+        yp = (ctypes.c_void_p * len(weights))(*y_ptrs)
+        check(lib().nimf_matmul_w_group_dev(hs, len(weights), ctypes.c_void_p(x_ptr), M, yp,
+                                            ctypes.c_void_p(stream or 0)))
 
     def dequant(self):
         out = np.empty(self.rows * self.k, np.float32)
