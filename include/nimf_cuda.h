@@ -214,6 +214,22 @@ int nimf_apf_cast(const float* x, int64_t n, const float* grad, int64_t n_grad,
                   double rel_error_tol, int exp_margin, int* exponent_bits,
                   int* mantissa_bits, uint8_t* out);
 
+/* Allocation-free form of nimf_cf_autoselect on device buffers.  No
+ * counterpart in the reference: it is for callers that cannot allocate device
+ * memory at the point of the call -- a host whose allocator owns the whole
+ * GPU memory and forbids other cudaMalloc calls, or code that must not add
+ * allocations while it runs.  x_dev / grad_dev are device pointers (grad_dev
+ * nullable, n_grad may be 0); the reductions run on `stream` (NULL: the
+ * library stream) and the call returns when the chosen format is known.
+ * Scratch lives in a fixed 8,200-byte device array inside the library, so it
+ * allocates nothing.  The first call on each device looks up that array's
+ * address (make it before any stream capture).  Limits: n and n_grad at most
+ * 2^31 - 1 (larger gives NIMF_ERR_SHAPE); calls that overlap on the GPU share
+ * the array and race, so issue them one at a time. */
+int nimf_cf_autoselect_dev_noalloc(const float* x_dev, int64_t n, const float* grad_dev,
+                                   int64_t n_grad, double rel_error_tol, int exp_margin,
+                                   int* exponent_bits, int* mantissa_bits, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

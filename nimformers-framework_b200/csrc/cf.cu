@@ -11,6 +11,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
+#include <cstdint>
 #include <vector>
 
 #include "device_util.cuh"
@@ -363,3 +365,156 @@ int cf_dequant(const CFWeight& w, float* out, cudaStream_t st) {
 }
 
 }  // namespace nimf
+
+// ---------------------------------------------------------------------------
+// Allocation-free APF format selection on device buffers.
+//
+// For callers that must not allocate device memory: code running while a
+// stream is being captured into a CUDA graph, or a host that hands the GPU's
+// whole memory to its own allocator and forbids any other cudaMalloc.  The
+// existing nimf_cf_autoselect stages x in buffers the library allocates and
+// keeps its reduction scratch in another allocated buffer; this variant reads
+// the caller's device buffers and keeps its scratch in the fixed array below.
+//
+// Scratch: g_noalloc_scratch holds 2 + 2048 32-bit words (8,200 bytes):
+// word 0 / 1 are the min / max of |x| (as float bits), words 2.. a radix
+// histogram.  Every GPU that loads the library holds it until the process
+// exits.  All calls share it, so calls that overlap on the GPU race; each call
+// clears what must start at zero before using it.  Element counts are limited
+// to 2^31 - 1 (the histogram counts are 32-bit).
+namespace nimf {
+namespace {
+
+constexpr int kNoAllocWords = 2 + 2048;
+constexpr int64_t kNoAllocMaxElems = 2147483647LL;
+static __device__ __align__(256) unsigned g_noalloc_scratch[kNoAllocWords];
+// Device address of g_noalloc_scratch, per device.  In host code the array's
+// name is only a host-side stand-in, never a device address.
+unsigned* g_noalloc_addr[64] = {};
+
+__global__ void noalloc_minmax_init(unsigned* s) {
+  s[0] = 0x7F800000u;
+  s[1] = 0u;
+}
+
+// Median of |v| over finite non-zero v (element n_valid/2 of the ascending
+// order), by three radix-histogram passes in the scratch histogram.
+int noalloc_abs_median(const float* v, int64_t n, unsigned* hist, float* median,
+                       int64_t* n_valid, cudaStream_t st) {
+  const int shifts[3] = {20, 9, 0};
+  const int widths[3] = {11, 11, 9};
+  unsigned prefix = 0;
+  int prefix_shift = 32;
+  int64_t want = -1, total = 0;
+  unsigned h[2048];
+  for (int pass = 0; pass < 3; ++pass) {
+    const int nb = 1 << widths[pass];
+    NIMF_CUDA_TRY(cudaMemsetAsync(hist, 0, nb * sizeof(unsigned), st));
+    radix_hist_kernel<<<grid_for(n, 256), 256, 0, st>>>(v, n, shifts[pass], widths[pass], prefix,
+                                                        prefix_shift, hist);
+    NIMF_CUDA_TRY(cudaGetLastError());
+    NIMF_CUDA_TRY(cudaMemcpyAsync(h, hist, nb * sizeof(unsigned), cudaMemcpyDeviceToHost, st));
+    NIMF_CUDA_TRY(cudaStreamSynchronize(st));
+    if (pass == 0) {
+      for (int i = 0; i < nb; ++i) total += h[i];
+      *n_valid = total;
+      if (total == 0) {
+        *median = 0.0f;
+        return NIMF_OK;
+      }
+      want = total / 2;
+    }
+    int64_t acc = 0;
+    int sel = nb - 1;
+    for (int i = 0; i < nb; ++i) {
+      if (acc + h[i] > want) {
+        sel = i;
+        break;
+      }
+      acc += h[i];
+    }
+    want -= acc;
+    prefix = (prefix << widths[pass]) | (unsigned)sel;
+    prefix_shift = shifts[pass];
+  }
+  *median = __builtin_bit_cast(float, prefix);
+  return NIMF_OK;
+}
+
+}  // namespace
+}  // namespace nimf
+
+using namespace nimf;
+
+extern "C" int nimf_cf_autoselect_dev_noalloc(const float* x_dev, int64_t n,
+                                              const float* grad_dev, int64_t n_grad,
+                                              double rel_error_tol, int exp_margin,
+                                              int* exponent_bits, int* mantissa_bits,
+                                              void* stream) {
+  Context* c;
+  NIMF_TRY(require_ctx(&c));
+  if (n < 0 || n_grad < 0) return set_error(NIMF_ERR_SHAPE, "negative length");
+  if (n > kNoAllocMaxElems || n_grad > kNoAllocMaxElems)
+    return set_error(NIMF_ERR_SHAPE,
+                     "nimf_cf_autoselect_dev_noalloc: at most %lld elements per buffer "
+                     "(its fixed scratch keeps 32-bit counts); got %lld and %lld",
+                     (long long)kNoAllocMaxElems, (long long)n, (long long)n_grad);
+  if (!exponent_bits || !mantissa_bits) return set_error(NIMF_ERR_ARG, "NULL output");
+  if ((n > 0 && !x_dev) || (n_grad > 0 && !grad_dev)) return set_error(NIMF_ERR_ARG, "NULL input");
+  if (c->device < 0 || c->device >= 64) return set_error(NIMF_ERR_STATE, "device index");
+  // One-time set-up on this device (the device is current): the array's
+  // device address.  Make the first call before any stream capture.
+  if (!g_noalloc_addr[c->device]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess)
+      return set_error(NIMF_ERR_CUDA, "cudaGetSymbolAddress(scratch) failed: %s",
+                       cudaGetErrorString(e));
+    g_noalloc_addr[c->device] = (unsigned*)p;
+  }
+  unsigned* scratch = g_noalloc_addr[c->device];
+  cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+
+  float mn = 0.f, mx = 0.f;
+  bool found = false;
+  if (n > 0) {
+    noalloc_minmax_init<<<1, 1, 0, st>>>(scratch);
+    absrange_kernel<<<grid_for(n, 256), 256, 0, st>>>(x_dev, n, scratch);
+    NIMF_CUDA_TRY(cudaGetLastError());
+    unsigned r[2];
+    NIMF_CUDA_TRY(cudaMemcpyAsync(r, scratch, sizeof(r), cudaMemcpyDeviceToHost, st));
+    NIMF_CUDA_TRY(cudaStreamSynchronize(st));
+    found = r[1] != 0u;
+    mn = __builtin_bit_cast(float, r[0]);
+    mx = __builtin_bit_cast(float, r[1]);
+  }
+  // computeRequiredExponentBits / computeRequiredMantissaBits
+  // (customfloat.nim:149-198), evaluated in double as the reference does.
+  int eb = 1, mb = 2;
+  if (found) {
+    const int64_t max_e = (int64_t)std::floor(std::log2((double)mx));
+    const int64_t min_e = (int64_t)std::floor(std::log2((double)mn));
+    const int64_t span = (max_e - min_e) + 2 * (int64_t)exp_margin + 2;
+    eb = (int)std::max<int64_t>(1, (int64_t)std::ceil(std::log2((double)std::max<int64_t>(span, 2))));
+    const int64_t base = (int64_t)std::ceil(std::log2(1.0 / std::max(rel_error_tol, 1e-12)));
+    int64_t extra = 0;
+    if (n_grad > 0) {
+      float wmed = 0.f, gmed = 0.f;
+      int64_t nv = 0, ngv = 0;
+      NIMF_TRY(noalloc_abs_median(x_dev, n, scratch + 2, &wmed, &nv, st));
+      NIMF_TRY(noalloc_abs_median(grad_dev, n_grad, scratch + 2, &gmed, &ngv, st));
+      if (ngv > 0) {
+        wmed = std::max(wmed, 1e-12f);
+        const double ratio = (double)gmed / (double)wmed;
+        if (ratio > 0 && ratio < 1) {
+          const int64_t need = (int64_t)std::ceil(-std::log2(ratio));
+          extra = std::max<int64_t>(0, need - base);
+        }
+      }
+    }
+    mb = (int)std::min<int64_t>(23, std::max<int64_t>(2, base + extra));
+  }
+  *exponent_bits = eb;
+  *mantissa_bits = mb;
+  return NIMF_OK;
+}

@@ -43,7 +43,7 @@ EXPORTS = [
     "nimf_matmul_w_group", "nimf_matmul_q4",
     "nimf_weight_cache_clear", "nimf_matmul_f32", "nimf_matmul2_f32", "nimf_dequant_w",
     "nimf_cf_encode", "nimf_cf_decode", "nimf_cf_encode_dev", "nimf_cf_decode_dev",
-    "nimf_cf_autoselect", "nimf_apf_cast",
+    "nimf_cf_autoselect", "nimf_apf_cast", "nimf_cf_autoselect_dev_noalloc",
 ]
 
 
@@ -98,6 +98,9 @@ def lib():
                                ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)],
         "nimf_apf_cast": [vp, i64, vp, i64, ctypes.c_double, i32, ctypes.POINTER(ctypes.c_int),
                           ctypes.POINTER(ctypes.c_int), vp],
+        "nimf_cf_autoselect_dev_noalloc": [vp, i64, vp, i64, ctypes.c_double, i32,
+                                           ctypes.POINTER(ctypes.c_int),
+                                           ctypes.POINTER(ctypes.c_int), vp],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
