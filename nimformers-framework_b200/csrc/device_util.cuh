@@ -165,6 +165,34 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* m, uint32_t parity) {
     if (mbar_try_wait_sleep(m, parity, 1000u)) return true;
   return false;
 }
+// Non-blocking test of the phase with the given parity.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* m, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_addr(m)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait with a chosen polling style: HINT > 0 try_wait with a
+// suspend-time hint of HINT ns, HINT == 0 try_wait with the system's limit,
+// HINT < 0 test_wait with a sleep of about -HINT ns between polls.
+template <int HINT>
+__device__ __forceinline__ bool mbar_wait_t(uint64_t* m, uint32_t parity) {
+  for (uint32_t i = 0; i < kMaxSpin; ++i) {
+    if (HINT > 0) {
+      if (mbar_try_wait_sleep(m, parity, (uint32_t)HINT)) return true;
+    } else if (HINT == 0) {
+      if (mbar_try_wait(m, parity)) return true;
+    } else {
+      if (mbar_test_wait(m, parity)) return true;
+      __nanosleep((unsigned)(-HINT));
+    }
+  }
+  return false;
+}
 // Global -> shared bulk copy (no multicast) completing on mbarrier `m`.
 // dst, src 16-byte aligned; bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* m) {

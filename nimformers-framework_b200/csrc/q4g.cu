@@ -184,11 +184,24 @@ struct GemvArgs {
 // then the scale/zero pairs of its groups), moved by two bulk copies.  It is
 // consumed as chunks of kChunkQ k-quads (512 k), one chunk per warp-unit.
 constexpr int kChunkQ = 8;
-constexpr int kIssuers = 4;  // producer lanes issuing stages round-robin
+#ifndef NIMF_Q4G_ISSUERS
+#define NIMF_Q4G_ISSUERS 4
+#endif
+constexpr int kIssuers = NIMF_Q4G_ISSUERS;  // producer lanes issuing stages round-robin
+#ifndef NIMF_Q4G_PWAIT
+#define NIMF_Q4G_PWAIT -32
+#endif
+#ifndef NIMF_Q4G_CWAIT
+#define NIMF_Q4G_CWAIT 1000
+#endif
+// Wait styles (mbar_wait_t) of the producer lanes and of the consumer warps.
+// The producer's lanes diverge, so they poll instead of sleeping in try_wait.
+constexpr int kProdWait = NIMF_Q4G_PWAIT;
+constexpr int kConsWait = NIMF_Q4G_CWAIT;
 
 // Shared-memory layout of one CTA:
-//   head: full/empty[kStages] mbarriers, cnt[kStages] arrival counters,
-//         xmax[8] (|x| maxima as float bits), zero pad (16 B)
+//   head: full/empty/merged/pfull[kStages] mbarriers,
+//         xmax[8] (|x| maxima as float bits), zero pad (16 B), problem table
 //   ring[ns][stage]   row-tile slices of this CTA's k-split (packed weights,
 //                     then the scale/zero pairs of their groups)
 //   xs    B fragments of the two s8 digits of x for the k-split:
@@ -202,7 +215,11 @@ struct SmemLayout {
   size_t ring, stage, xs, sdi, part, total;
 };
 
-constexpr size_t kHeadBytes = 2 * kStages * sizeof(uint64_t) + kStages * sizeof(int) + 64;
+// + the launch's problem table copied to shared memory (pointers, y strides,
+// rows, row-tile prefix): dynamic indexing into kernel parameters is slow
+constexpr size_t kBarBytes = 4 * kStages * sizeof(uint64_t) + 64;
+constexpr size_t kTabBytes = 3 * kMaxProblems * 8 + kMaxProblems * 8 + kMaxProblems * 4 + 80;
+constexpr size_t kHeadBytes = kBarBytes + kTabBytes;
 
 __host__ __device__ inline SmemLayout q4g_smem_layout(int mode, int kqg, int gps, int m, int ns,
                                                       int tchunk, bool direct) {
@@ -237,7 +254,7 @@ __host__ __device__ inline SmemLayout q4g_smem_layout(int mode, int kqg, int gps
 // MODE 2: M <= 8, two MMAs per 32 k (d0 and d1 each in columns 0..7).
 // KQG: k-quads (64 k) per quantisation group (group size 64 * KQG).
 template <int MODE, int KQG>
-__global__ void __launch_bounds__((kCons + 1) * 32, 1)
+__global__ void __launch_bounds__((kCons + 2) * 32, 1)
 q4g_gemv_kernel(const GemvArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr int GS = 64 * KQG;
@@ -263,9 +280,21 @@ q4g_gemv_kernel(const GemvArgs a) {
   const SmemLayout Ls = q4g_smem_layout(MODE, KQG, a.gps, a.m, NS, a.tchunk, direct);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + kStages;
-  int* cnt = reinterpret_cast<int*>(empty + kStages);
-  unsigned* xmax = reinterpret_cast<unsigned*>(cnt + kStages);
+  uint64_t* merged = empty + kStages;  // direct mode: the stage's partial slots are free again
+  uint64_t* pfull = merged + kStages;  // direct mode: all chunk partials of the stage written
+  unsigned* xmax = reinterpret_cast<unsigned*>(pfull + kStages);
   const uint4* zpad = reinterpret_cast<const uint4*>(xmax + 8);
+  const uint4** tfrag = reinterpret_cast<const uint4**>(smem + kBarBytes);
+  const float4** tsz = reinterpret_cast<const float4**>(tfrag + kMaxProblems);
+  float** ty = reinterpret_cast<float**>(smem + kBarBytes + 2 * kMaxProblems * 8);
+  int64_t* tldy = reinterpret_cast<int64_t*>(ty + kMaxProblems);
+  int* trows = reinterpret_cast<int*>(tldy + kMaxProblems);
+  int* tpref = trows + kMaxProblems;
+  // problem of global row tile grt (problems are few; p only grows with grt)
+  auto prob_of = [&](int grt, int p) {
+    while (p + 1 < a.nprob && grt >= tpref[p + 1]) ++p;
+    return p;
+  };
   unsigned char* ring = smem + Ls.ring;
   unsigned char* xs = smem + Ls.xs;
   int* sdi = reinterpret_cast<int*>(smem + Ls.sdi);
@@ -274,11 +303,21 @@ q4g_gemv_kernel(const GemvArgs a) {
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], direct ? 1 : (nchunk > 0 ? nchunk : 1));
-      cnt[s] = 0;
+      mbar_init(&empty[s], nchunk > 0 ? nchunk : 1);
+      mbar_init(&merged[s], 1);
+      mbar_init(&pfull[s], nchunk > 0 ? nchunk : 1);
     }
     mbar_fence_init();
   }
+  if (threadIdx.x < a.nprob) {
+    const int i = threadIdx.x;
+    tfrag[i] = a.prob[i].frag;
+    tsz[i] = a.prob[i].sz;
+    ty[i] = a.prob[i].y;
+    tldy[i] = a.prob[i].ldy;
+    trows[i] = a.prob[i].rows;
+  }
+  if (threadIdx.x <= a.nprob) tpref[threadIdx.x] = a.rt_prefix[threadIdx.x];
   if (threadIdx.x < 8) xmax[threadIdx.x] = 0u;
   if (threadIdx.x < 4) reinterpret_cast<unsigned*>(xmax + 8)[threadIdx.x] = 0u;  // zero pad
   for (int i = threadIdx.x; i < ng * 16; i += blockDim.x) sdi[i] = 0;
@@ -293,32 +332,80 @@ q4g_gemv_kernel(const GemvArgs a) {
       bool ok = true;
       const uint32_t wb = (uint32_t)ng * KQG * 512u, zb = (uint32_t)ng * 128u;
       int issued_last = -1;
+      int pp = 0;
       for (int i = lane; i < nrt; i += kIssuers) {
         const int s = i % NS;
-        if (i >= NS && !mbar_wait(&empty[s], ((i / NS) - 1) & 1)) {
+        if (i >= NS && !mbar_wait_t<kProdWait>(&empty[s], ((i / NS) - 1) & 1)) {
           ok = false;
           break;
         }
         const int grt = rt0 + i;
-        int p = 0;
-        while (p + 1 < a.nprob && grt >= a.rt_prefix[p + 1]) ++p;
-        const int rt = grt - a.rt_prefix[p];
+        pp = prob_of(grt, pp);
+        const int p = pp;
+        const int rt = grt - tpref[p];
         unsigned char* dst = ring + (size_t)s * Ls.stage;
         mbar_arrive_expect_tx(&full[s], wb + zb);
-        bulk_g2s(dst, a.prob[p].frag + ((size_t)rt * a.kq_total + (size_t)g0 * KQG) * 32, wb,
+        bulk_g2s(dst, tfrag[p] + ((size_t)rt * a.kq_total + (size_t)g0 * KQG) * 32, wb,
                  &full[s]);
         bulk_g2s(dst + (size_t)a.gps * KQG * 512,
-                 a.prob[p].sz + ((size_t)rt * a.groups + g0) * 8, zb, &full[s]);
+                 tsz[p] + ((size_t)rt * a.groups + g0) * 8, zb, &full[s]);
         issued_last = i;
       }
       // drain: this lane's last copies land before the CTA may exit
       if (ok) {
         for (int i = issued_last; i >= 0 && i > issued_last - NS; i -= kIssuers)
-          if (!mbar_wait(&full[i % NS], (i / NS) & 1)) ok = false;
+          if (!mbar_wait_t<kProdWait>(&full[i % NS], (i / NS) & 1)) ok = false;
       }
       if (!ok && a.err) atomicExch(a.err, 1);
     }
     __syncwarp();
+  } else if (warp == kCons + 1) {
+    // ---------------- merger (direct mode): sums each row tile's chunk
+    // partials in chunk order (deterministic), writes y and frees the
+    // stage's partial slots for the next round
+    if (direct) {
+      griddep_wait();  // y may be read or written by the previous kernel
+      int pp = 0;
+      for (int i = 0; i < nrt; ++i) {
+        const int s = i % NS;
+        if (!mbar_wait_t<kConsWait>(&pfull[s], (i / NS) & 1)) {
+          if (lane == 0 && a.err) atomicExch(a.err, 1);
+          break;
+        }
+        const float* red = part + ((size_t)s * ncn) * 128;
+        // lane sums elements 4 lane .. 4 lane + 3: row lane / 2, columns
+        // 4 (lane & 1) .. 4 (lane & 1) + 3
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int c2 = 0; c2 < nchunk; ++c2) {
+          const float4 e4 = reinterpret_cast<const float4*>(red + (size_t)c2 * 128)[lane];
+          v.x += e4.x;
+          v.y += e4.y;
+          v.z += e4.z;
+          v.w += e4.w;
+        }
+        if (MODE == 1) {
+          // columns 4..7 hold the d1 parts of x rows 0..3: add them to 0..3
+          v.x += __shfl_xor_sync(0xffffffffu, v.x, 1);
+          v.y += __shfl_xor_sync(0xffffffffu, v.y, 1);
+          v.z += __shfl_xor_sync(0xffffffffu, v.z, 1);
+          v.w += __shfl_xor_sync(0xffffffffu, v.w, 1);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&merged[s]);
+        const int grt = rt0 + i;
+        pp = prob_of(grt, pp);
+        const int rbase = (grt - tpref[pp]) * 16;
+        const int r = lane >> 1, m0 = (lane & 1) * 4;
+        if ((MODE == 2 || (lane & 1) == 0) && rbase + r < trows[pp]) {
+          float* yp = ty[pp] + rbase + r;
+          const int64_t ld = tldy[pp];
+          if (m0 < a.m) yp[(size_t)m0 * ld] = v.x;
+          if (m0 + 1 < a.m) yp[(size_t)(m0 + 1) * ld] = v.y;
+          if (m0 + 2 < a.m) yp[(size_t)(m0 + 2) * ld] = v.z;
+          if (m0 + 3 < a.m) yp[(size_t)(m0 + 3) * ld] = v.w;
+        }
+      }
+    }
   } else {
     // ---------------- consumers: quantise x of the k-split into two s8 digits
     griddep_wait();  // x may be written by the previous kernel in the stream
@@ -443,13 +530,28 @@ q4g_gemv_kernel(const GemvArgs a) {
       const int s = i % NS;
       const int cg0 = c * CG, ncg = min(CG, ng - cg0);
       float tot[4] = {0.f, 0.f, 0.f, 0.f};
-      if (!mbar_wait(&full[s], (i / NS) & 1)) {
+      if (!mbar_wait_t<kConsWait>(&full[s], (i / NS) & 1)) {
         if (lane == 0 && a.err) atomicExch(a.err, 1);
       } else {
+        // load the chunk (weights and its groups' scales) into registers and
+        // give the ring slot back at once: the producer refills it while
+        // this warp computes
         const unsigned char* st = ring + (size_t)s * Ls.stage;
         const uint4* wq = reinterpret_cast<const uint4*>(st + (size_t)c * kChunkQ * 512) + lane;
         const float4* szp =
             reinterpret_cast<const float4*>(st + (size_t)a.gps * KQG * 512 + (size_t)cg0 * 128) + g;
+        uint4 wr[kChunkQ];
+        float4 sr[CG];
+#pragma unroll
+        for (int gl = 0; gl < CG; ++gl) {
+          if (gl < ncg) {
+#pragma unroll
+            for (int qq = 0; qq < KQG; ++qq) wr[gl * KQG + qq] = wq[(gl * KQG + qq) * 32];
+            sr[gl] = szp[gl * 8];
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
         // one accumulator set per group of the chunk: CG independent MMA chains
         int acc[CG][4], acc2[MODE == 2 ? CG : 1][4];
 #pragma unroll
@@ -465,7 +567,7 @@ q4g_gemv_kernel(const GemvArgs a) {
 #pragma unroll
             for (int qq = 0; qq < KQG; ++qq) {
               const int ql = gl * KQG + qq;                // quad within the chunk
-              const uint4 w = wq[ql * 32];
+              const uint4 w = wr[ql];
 #pragma unroll
               for (int h = 0; h < 2; ++h) {
                 const uint32_t wa = h == 0 ? w.x : w.z, wb = h == 0 ? w.y : w.w;
@@ -488,7 +590,7 @@ q4g_gemv_kernel(const GemvArgs a) {
 #pragma unroll
         for (int gl = 0; gl < CG; ++gl) {
           if (gl < ncg) {
-            const float4 sp = szp[gl * 8];
+            const float4 sp = sr[gl];
             const int* sd = sdi + (cg0 + gl) * 16;
             const float d0a = (float)sd[sd_off], d0b = (float)sd[sd_off + 1];
             if (MODE == 1) {
@@ -511,13 +613,11 @@ q4g_gemv_kernel(const GemvArgs a) {
           }
         }
       }
-      if (MODE == 1) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) tot[q] += __shfl_xor_sync(0xffffffffu, tot[q], 2);
-      }
       if (!direct) {
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
+        if (MODE == 1) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) tot[q] += __shfl_xor_sync(0xffffffffu, tot[q], 2);
+        }
         if (lane_has) {
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
@@ -528,43 +628,23 @@ q4g_gemv_kernel(const GemvArgs a) {
         }
         continue;
       }
-      // direct mode: the row tile's last chunk-warp sums the chunk partials in
-      // chunk order (deterministic), writes y and releases the stage
+      // direct mode: hand the chunk's partial (all 8 MMA columns) to the
+      // merger warp.  The stage's partial slots are reused by the next round
+      // of the same stage: wait until the merger has read the previous one.
       float* red = part + ((size_t)s * ncn) * 128;
-      if (lane_has) {
+      if (i >= NS && !mbar_wait_t<kConsWait>(&merged[s], ((i / NS) - 1) & 1)) {
+        if (lane == 0 && a.err) atomicExch(a.err, 1);
+        continue;
+      }
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int r = g + ((q & 2) ? 8 : 0);
-          const int mm = 2 * t + (q & 1);
-          red[(size_t)c * 128 + r * 8 + mm] = tot[q];
-        }
+      for (int q = 0; q < 4; ++q) {
+        const int r = g + ((q & 2) ? 8 : 0);
+        const int mm = 2 * t + (q & 1);
+        red[(size_t)c * 128 + r * 8 + mm] = tot[q];
       }
       __threadfence_block();
       __syncwarp();
-      int old = 0;
-      if (lane == 0) old = atomicAdd(&cnt[s], 1);
-      old = __shfl_sync(0xffffffffu, old, 0);
-      if (old == nchunk - 1) {
-        __threadfence_block();
-        const int grt = rt0 + i;
-        int p = 0;
-        while (p + 1 < a.nprob && grt >= a.rt_prefix[p + 1]) ++p;
-        const int rbase = (grt - a.rt_prefix[p]) * 16;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int e = lane * 4 + q;
-          const int r = e >> 3, mm = e & 7;
-          float v = 0.f;
-          for (int c2 = 0; c2 < nchunk; ++c2) v += red[(size_t)c2 * 128 + e];
-          if (mm < a.m && rbase + r < a.prob[p].rows)
-            a.prob[p].y[(size_t)mm * a.prob[p].ldy + rbase + r] = v;
-        }
-        __syncwarp();
-        if (lane == 0) {
-          cnt[s] = 0;
-          mbar_arrive(&empty[s]);
-        }
-      }
+      if (lane == 0) mbar_arrive(&pfull[s]);
     }
   }
   if (direct) {
@@ -586,13 +666,12 @@ q4g_gemv_kernel(const GemvArgs a) {
   for (int e = rank * blockDim.x + threadIdx.x; e < total; e += nsplit * blockDim.x) {
     const int mm = e & 7;
     const int grt = rt0 + (e >> 7);
-    int p = 0;
-    while (p + 1 < a.nprob && grt >= a.rt_prefix[p + 1]) ++p;
-    const int row = (grt - a.rt_prefix[p]) * 16 + ((e >> 3) & 15);
-    if (mm >= a.m || row >= a.prob[p].rows) continue;
+    const int p = prob_of(grt, 0);
+    const int row = (grt - tpref[p]) * 16 + ((e >> 3) & 15);
+    if (mm >= a.m || row >= trows[p]) continue;
     float s = 0.0f;
     for (int r = 0; r < nsplit; ++r) s += cluster.map_shared_rank(sums, r)[e];
-    a.prob[p].y[(size_t)mm * a.prob[p].ldy + row] = s;
+    ty[p][(size_t)mm * tldy[p] + row] = s;
   }
   cluster.sync();
 }
@@ -696,6 +775,19 @@ int q4g_dequant(const Q4GWeight& w, float* out, cudaStream_t st) {
 
 namespace {
 
+// Stage counts must be multiples of both the stage->warp period and the
+// issuer count, so that every ring slot keeps the same consumer warps and the
+// same producer lane.
+inline int lcm_int(int a, int b) {
+  int x = a, y = b;
+  while (y) {
+    const int t2 = x % y;
+    x = y;
+    y = t2;
+  }
+  return a / x * b;
+}
+
 // Ring stages of direct mode (no k-split) for this shape, 0 if it does not fit.
 inline int direct_ring_stages(int mode, int kqg, int groups, int mc) {
   const SmemLayout L0 = q4g_smem_layout(mode, kqg, groups, mc, 0, 1, true);
@@ -703,7 +795,7 @@ inline int direct_ring_stages(int mode, int kqg, int groups, int mc) {
   const int ncn = (groups + kChunkQ / kqg - 1) / (kChunkQ / kqg);
   int gcdv = kCons, bb = ncn;
   while (bb) { const int tmp = gcdv % bb; gcdv = bb; bb = tmp; }
-  const int period = std::max(kCons / gcdv, kIssuers);
+  const int period = lcm_int(kCons / gcdv, kIssuers);
   int ns = (int)((kSmemBudget - L0.total) / (L0.stage + (size_t)ncn * 512));
   ns = std::min(ns, kStages) / period * period;
   return ns >= std::max(period, 4) ? ns : 0;
@@ -739,7 +831,7 @@ int launch_fast(const Piece* pcs, int npc, const float* x, int64_t ldx, int mc, 
     for (int cs = 1; cs <= kMaxSplits; ++cs) {
       cudaLaunchConfig_t q = {};
       q.gridDim = dim3((unsigned)(cs * 64), 1, 1);
-      q.blockDim = dim3((kCons + 1) * 32, 1, 1);
+      q.blockDim = dim3((kCons + 2) * 32, 1, 1);
       q.dynamicSmemBytes = kSmemBudget;
       cudaLaunchAttribute at[1];
       at[0].id = cudaLaunchAttributeClusterDimension;
@@ -782,7 +874,7 @@ int launch_fast(const Piece* pcs, int npc, const float* x, int64_t ldx, int mc, 
     // that period so every stage always serves the same warps
     int gcdv = kCons, bb = ncn;
     while (bb) { const int tmp = gcdv % bb; gcdv = bb; bb = tmp; }
-    const int period = std::max(kCons / gcdv, kIssuers);
+    const int period = lcm_int(kCons / gcdv, kIssuers);
     int ns = (int)((kSmemBudget - L0.total) / per_stage);
     ns = std::min(ns, kStages) / period * period;
     if (ns < std::max(period, 4) || (!direct && (size_t)ns * L0.stage < (size_t)tchunk * 512))
@@ -833,7 +925,7 @@ int launch_fast(const Piece* pcs, int npc, const float* x, int64_t ldx, int mc, 
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(n_clusters * s), 1, 1);
-  cfg.blockDim = dim3((kCons + 1) * 32, 1, 1);
+  cfg.blockDim = dim3((kCons + 2) * 32, 1, 1);
   cfg.dynamicSmemBytes = L.total;
   cfg.stream = st;
   cudaLaunchAttribute attrs[2];
