@@ -174,15 +174,17 @@ struct GemvArgs {
   int m, k, n_rt;      // n_rt: total row tiles of the launch
   int kq_total, groups;
   int gps;             // quantisation groups per k-split (the last split may have fewer)
+  int kbg, nkb;        // groups per ring stage (k-block) and k-blocks per row tile
   int n_clusters;      // clusters in the grid; cluster size = number of k-splits
   int tchunk;          // max row tiles per cluster (sizes the partial-y buffers)
   int ns;              // stages in the weight ring (a multiple of kCons)
   int vec4;            // x rows 16-byte aligned
 };
 
-// A stage holds one row tile's slice of this CTA's k-split (packed weights,
-// then the scale/zero pairs of its groups), moved by two bulk copies.  It is
-// consumed as chunks of kChunkQ k-quads (512 k), one chunk per warp-unit.
+// A stage holds one k-block of a row tile's slice of this CTA's k-split
+// (packed weights, then the scale/zero pairs of its groups), moved by two bulk
+// copies; a row tile spans nkb stages.  A stage is consumed as chunks of
+// kChunkQ k-quads (512 k), one chunk per warp-unit.
 constexpr int kChunkQ = 8;
 #ifndef NIMF_Q4G_ISSUERS
 #define NIMF_Q4G_ISSUERS 4
@@ -202,15 +204,15 @@ constexpr int kConsWait = NIMF_Q4G_CWAIT;
 // Shared-memory layout of one CTA:
 //   head: full/empty/merged/pfull[kStages] mbarriers,
 //         xmax[8] (|x| maxima as float bits), zero pad (16 B), problem table
-//   ring[ns][stage]   row-tile slices of this CTA's k-split (packed weights,
-//                     then the scale/zero pairs of their groups)
+//   ring[ns][stage]   k-blocks of row tiles (packed weights, then the
+//                     scale/zero pairs of their groups)
 //   xs    B fragments of the two s8 digits of x for the k-split:
 //         MODE 1: [k32 tiles][2M columns][4 lanes t] uint2 (d0 of row m in
 //                 column m, d1 in column M + m)
 //         MODE 2: [k32 tiles][M][4 lanes t] uint4 {d0 b0, d0 b1, d1 b0, d1 b1}
 //   sdi   [gps][16] int: per group, sums of the d0 (0..7) and d1 (8..15) digits
-//   part  split mode: [tchunk*ncn][16][8] per-unit partial y; direct mode (no
-//         k-split): [ns][ncn][16][8] per-stage slots summed into y in-CTA
+//   part  split mode: [tchunk*ncs][16][8] per-unit partial y; direct mode (no
+//         k-split): [ns][ncs][16][8] per-stage slots summed into y in-CTA
 struct SmemLayout {
   size_t ring, stage, xs, sdi, part, total;
 };
@@ -221,12 +223,12 @@ constexpr size_t kBarBytes = 4 * kStages * sizeof(uint64_t) + 64;
 constexpr size_t kTabBytes = 3 * kMaxProblems * 8 + kMaxProblems * 8 + kMaxProblems * 4 + 80;
 constexpr size_t kHeadBytes = kBarBytes + kTabBytes;
 
-__host__ __device__ inline SmemLayout q4g_smem_layout(int mode, int kqg, int gps, int m, int ns,
-                                                      int tchunk, bool direct) {
+__host__ __device__ inline SmemLayout q4g_smem_layout(int mode, int kqg, int gps, int kbg, int m,
+                                                      int ns, int tchunk, bool direct) {
   SmemLayout L;
   const int cg = kChunkQ / kqg;                       // groups per chunk
-  const int nchunk = (gps + cg - 1) / cg;
-  L.stage = (size_t)gps * kqg * 512 + (size_t)gps * 128;  // a row tile's k-split
+  const int nchunk = (kbg + cg - 1) / cg;             // chunks per stage
+  L.stage = (size_t)kbg * kqg * 512 + (size_t)kbg * 128;  // one k-block
   L.ring = (kHeadBytes + 127) / 128 * 128;
   L.xs = L.ring + L.stage * ns;
   const size_t k32 = (size_t)gps * kqg * 2;
@@ -239,11 +241,12 @@ __host__ __device__ inline SmemLayout q4g_smem_layout(int mode, int kqg, int gps
 
 // One CTA = k-split `rank` of the row tiles of its cluster.  Warp kCons is the
 // producer (lanes 0..kIssuers-1 stream row-tile slices with bulk copies);
-// consumer warp w takes the 512-k chunk units (row tile i, chunk c) with
-// (i * ncn + c) % kCons == w (ncn = nominal chunks per row tile, the same on
-// every rank); stage i % ns of a row tile therefore always serves the same
-// warps (ns is a multiple of kCons / gcd(ncn, kCons)), so no warp ever waits
-// more than one phase ahead on a stage barrier.
+// consumer warp w takes the 512-k chunk units (stage q, chunk c) with
+// (q * ncs + c) % kCons == w (ncs = nominal chunks per stage, the same on
+// every rank); ring slot q % ns therefore always serves the same warps (ns is
+// a multiple of kCons / gcd(ncs, kCons)), so no warp ever waits more than one
+// phase ahead on a stage barrier.  In direct mode (no k-split) warp kCons + 1
+// sums the chunk partials of each row tile's stages and writes y.
 //
 // Math: the nibbles (0..15, exact s8) multiply two s8 digits of x,
 // x ~= s_m (d0 + d1 / 256) with s_m = max|x_m| / 127 over the k-split, on the
@@ -271,13 +274,18 @@ q4g_gemv_kernel(const GemvArgs a) {
   const int nrt = base + (cid < rem ? 1 : 0);
   const int g0 = rank * a.gps;
   const int ng = max(0, min(a.gps, a.groups - g0));
-  const int nchunk = (ng + CG - 1) / CG;          // chunks this rank actually has
-  const int ncn = (a.gps + CG - 1) / CG;           // nominal chunks (same on every rank)
-  const int nunits = nrt * ncn;
-  const int NS = a.ns;
   const bool direct = nsplit == 1;  // no k-split: row tiles are finished in-CTA
+  const int nkb = a.nkb;
+  const int ncs = (a.kbg + CG - 1) / CG;           // nominal chunks per stage (every rank)
+  // split mode has one stage per row tile; its last rank may have fewer chunks
+  const int nchunk = direct ? ncs : (ng + CG - 1) / CG;
+  const int nstg = nrt * nkb;                      // stages of this CTA
+  const int nunits = nstg * ncs;
+  // groups of k-block kb (the last k-block may have fewer)
+  auto kb_groups = [&](int kb) { return max(0, min(a.kbg, ng - kb * a.kbg)); };
+  const int NS = a.ns;
 
-  const SmemLayout Ls = q4g_smem_layout(MODE, KQG, a.gps, a.m, NS, a.tchunk, direct);
+  const SmemLayout Ls = q4g_smem_layout(MODE, KQG, a.gps, a.kbg, a.m, NS, a.tchunk, direct);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + kStages;
   uint64_t* merged = empty + kStages;  // direct mode: the stage's partial slots are free again
@@ -330,31 +338,33 @@ q4g_gemv_kernel(const GemvArgs a) {
     griddep_launch_dependents();
     if (lane < kIssuers && ng > 0) {
       bool ok = true;
-      const uint32_t wb = (uint32_t)ng * KQG * 512u, zb = (uint32_t)ng * 128u;
       int issued_last = -1;
       int pp = 0;
-      for (int i = lane; i < nrt; i += kIssuers) {
-        const int s = i % NS;
-        if (i >= NS && !mbar_wait_t<kProdWait>(&empty[s], ((i / NS) - 1) & 1)) {
+      for (int q = lane; q < nstg; q += kIssuers) {
+        const int s = q % NS;
+        if (q >= NS && !mbar_wait_t<kProdWait>(&empty[s], ((q / NS) - 1) & 1)) {
           ok = false;
           break;
         }
+        const int i = q / nkb, kb = q - i * nkb;
+        const int ngk = kb_groups(kb), gk0 = g0 + kb * a.kbg;
+        const uint32_t wb = (uint32_t)ngk * KQG * 512u, zb = (uint32_t)ngk * 128u;
         const int grt = rt0 + i;
         pp = prob_of(grt, pp);
         const int p = pp;
         const int rt = grt - tpref[p];
         unsigned char* dst = ring + (size_t)s * Ls.stage;
         mbar_arrive_expect_tx(&full[s], wb + zb);
-        bulk_g2s(dst, tfrag[p] + ((size_t)rt * a.kq_total + (size_t)g0 * KQG) * 32, wb,
+        bulk_g2s(dst, tfrag[p] + ((size_t)rt * a.kq_total + (size_t)gk0 * KQG) * 32, wb,
                  &full[s]);
-        bulk_g2s(dst + (size_t)a.gps * KQG * 512,
-                 tsz[p] + ((size_t)rt * a.groups + g0) * 8, zb, &full[s]);
-        issued_last = i;
+        bulk_g2s(dst + (size_t)a.kbg * KQG * 512,
+                 tsz[p] + ((size_t)rt * a.groups + gk0) * 8, zb, &full[s]);
+        issued_last = q;
       }
       // drain: this lane's last copies land before the CTA may exit
       if (ok) {
-        for (int i = issued_last; i >= 0 && i > issued_last - NS; i -= kIssuers)
-          if (!mbar_wait_t<kProdWait>(&full[i % NS], (i / NS) & 1)) ok = false;
+        for (int q = issued_last; q >= 0 && q > issued_last - NS; q -= kIssuers)
+          if (!mbar_wait_t<kProdWait>(&full[q % NS], (q / NS) & 1)) ok = false;
       }
       if (!ok && a.err) atomicExch(a.err, 1);
     }
@@ -366,32 +376,37 @@ q4g_gemv_kernel(const GemvArgs a) {
     if (direct) {
       griddep_wait();  // y may be read or written by the previous kernel
       int pp = 0;
-      for (int i = 0; i < nrt; ++i) {
-        const int s = i % NS;
-        if (!mbar_wait_t<kConsWait>(&pfull[s], (i / NS) & 1)) {
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int q = 0; q < nstg; ++q) {
+        const int s = q % NS;
+        const int i = q / nkb, kb = q - i * nkb;
+        if (!mbar_wait_t<kConsWait>(&pfull[s], (q / NS) & 1)) {
           if (lane == 0 && a.err) atomicExch(a.err, 1);
           break;
         }
-        const float* red = part + ((size_t)s * ncn) * 128;
-        // lane sums elements 4 lane .. 4 lane + 3: row lane / 2, columns
-        // 4 (lane & 1) .. 4 (lane & 1) + 3
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int c2 = 0; c2 < nchunk; ++c2) {
+        const float* red = part + ((size_t)s * ncs) * 128;
+        // lane sums elements 4 lane .. 4 lane + 3 (row lane / 2, columns
+        // 4 (lane & 1) .. 4 (lane & 1) + 3) over the row tile's stages and
+        // chunks in order (unused chunks hold zeros)
+        if (kb == 0) v = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int c2 = 0; c2 < ncs; ++c2) {
           const float4 e4 = reinterpret_cast<const float4*>(red + (size_t)c2 * 128)[lane];
           v.x += e4.x;
           v.y += e4.y;
           v.z += e4.z;
           v.w += e4.w;
         }
-        if (MODE == 1) {
-          // columns 4..7 hold the d1 parts of x rows 0..3: add them to 0..3
-          v.x += __shfl_xor_sync(0xffffffffu, v.x, 1);
-          v.y += __shfl_xor_sync(0xffffffffu, v.y, 1);
-          v.z += __shfl_xor_sync(0xffffffffu, v.z, 1);
-          v.w += __shfl_xor_sync(0xffffffffu, v.w, 1);
-        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&merged[s]);
+        if (kb != nkb - 1) continue;
+        float4 o = v;
+        if (MODE == 1) {
+          // columns 4..7 hold the d1 parts of x rows 0..3: add them to 0..3
+          o.x += __shfl_xor_sync(0xffffffffu, o.x, 1);
+          o.y += __shfl_xor_sync(0xffffffffu, o.y, 1);
+          o.z += __shfl_xor_sync(0xffffffffu, o.z, 1);
+          o.w += __shfl_xor_sync(0xffffffffu, o.w, 1);
+        }
         const int grt = rt0 + i;
         pp = prob_of(grt, pp);
         const int rbase = (grt - tpref[pp]) * 16;
@@ -399,10 +414,10 @@ q4g_gemv_kernel(const GemvArgs a) {
         if ((MODE == 2 || (lane & 1) == 0) && rbase + r < trows[pp]) {
           float* yp = ty[pp] + rbase + r;
           const int64_t ld = tldy[pp];
-          if (m0 < a.m) yp[(size_t)m0 * ld] = v.x;
-          if (m0 + 1 < a.m) yp[(size_t)(m0 + 1) * ld] = v.y;
-          if (m0 + 2 < a.m) yp[(size_t)(m0 + 2) * ld] = v.z;
-          if (m0 + 3 < a.m) yp[(size_t)(m0 + 3) * ld] = v.w;
+          if (m0 < a.m) yp[(size_t)m0 * ld] = o.x;
+          if (m0 + 1 < a.m) yp[(size_t)(m0 + 1) * ld] = o.y;
+          if (m0 + 2 < a.m) yp[(size_t)(m0 + 2) * ld] = o.z;
+          if (m0 + 3 < a.m) yp[(size_t)(m0 + 3) * ld] = o.w;
         }
       }
     }
@@ -525,33 +540,41 @@ q4g_gemv_kernel(const GemvArgs a) {
     const int xstride = bvalid ? cols * 4 : 0;
 
     for (int u = warp; u < nunits; u += kCons) {
-      const int i = u / ncn, c = u - i * ncn;
+      const int q = u / ncs, c = u - q * ncs;
       if (c >= nchunk) continue;  // the last k-split may have fewer chunks
-      const int s = i % NS;
-      const int cg0 = c * CG, ncg = min(CG, ng - cg0);
+      const int s = q % NS;
+      const int kb = q % nkb;
+      // chunks past the end of a short last k-block (direct mode) still take
+      // part in the stage's barriers, with no groups (their partial is zero)
+      const int cg0 = c * CG, ncg = max(0, min(CG, kb_groups(kb) - cg0));
+      const int gb = kb * a.kbg + cg0;  // first group of the chunk in the k-split
       float tot[4] = {0.f, 0.f, 0.f, 0.f};
-      if (!mbar_wait_t<kConsWait>(&full[s], (i / NS) & 1)) {
+      if (!mbar_wait_t<kConsWait>(&full[s], (q / NS) & 1)) {
         if (lane == 0 && a.err) atomicExch(a.err, 1);
       } else {
-        // load the chunk (weights and its groups' scales) into registers and
-        // give the ring slot back at once: the producer refills it while
-        // this warp computes
+        // MODE 1 (group size >= 128) loads the chunk (weights and scales) into
+        // registers and gives the ring slot back at once, so the producer
+        // refills it while this warp computes; MODE 2 (two accumulator sets)
+        // has no registers to spare and reads the slot in place.
+        constexpr bool kStaged = MODE == 1 && KQG >= 2;
         const unsigned char* st = ring + (size_t)s * Ls.stage;
         const uint4* wq = reinterpret_cast<const uint4*>(st + (size_t)c * kChunkQ * 512) + lane;
         const float4* szp =
-            reinterpret_cast<const float4*>(st + (size_t)a.gps * KQG * 512 + (size_t)cg0 * 128) + g;
-        uint4 wr[kChunkQ];
-        float4 sr[CG];
+            reinterpret_cast<const float4*>(st + (size_t)a.kbg * KQG * 512 + (size_t)cg0 * 128) + g;
+        uint4 wr[kStaged ? kChunkQ : 1];
+        float4 sr[kStaged ? CG : 1];
+        if (kStaged) {
 #pragma unroll
-        for (int gl = 0; gl < CG; ++gl) {
-          if (gl < ncg) {
+          for (int gl = 0; gl < CG; ++gl) {
+            if (gl < ncg) {
 #pragma unroll
-            for (int qq = 0; qq < KQG; ++qq) wr[gl * KQG + qq] = wq[(gl * KQG + qq) * 32];
-            sr[gl] = szp[gl * 8];
+              for (int qq = 0; qq < KQG; ++qq) wr[gl * KQG + qq] = wq[(gl * KQG + qq) * 32];
+              sr[gl] = szp[gl * 8];
+            }
           }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[s]);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
         // one accumulator set per group of the chunk: CG independent MMA chains
         int acc[CG][4], acc2[MODE == 2 ? CG : 1][4];
 #pragma unroll
@@ -567,13 +590,13 @@ q4g_gemv_kernel(const GemvArgs a) {
 #pragma unroll
             for (int qq = 0; qq < KQG; ++qq) {
               const int ql = gl * KQG + qq;                // quad within the chunk
-              const uint4 w = wr[ql];
+              const uint4 w = kStaged ? wr[kStaged ? ql : 0] : wq[ql * 32];
 #pragma unroll
               for (int h = 0; h < 2; ++h) {
                 const uint32_t wa = h == 0 ? w.x : w.z, wb = h == 0 ? w.y : w.w;
                 const uint32_t a0 = wa & 0x0F0F0F0Fu, a1 = (wa >> 4) & 0x0F0F0F0Fu;
                 const uint32_t a2 = wb & 0x0F0F0F0Fu, a3 = (wb >> 4) & 0x0F0F0F0Fu;
-                const int kt32 = (cg0 * KQG + ql) * 2 + h;  // k32 tile within the k-split
+                const int kt32 = (gb * KQG + ql) * 2 + h;  // k32 tile within the k-split
                 if (MODE == 1) {
                   const uint2 b = xs2[(size_t)kt32 * xstride];
                   mma_s8_16832(acc[gl], a0, a1, a2, a3, b.x, b.y);
@@ -590,8 +613,8 @@ q4g_gemv_kernel(const GemvArgs a) {
 #pragma unroll
         for (int gl = 0; gl < CG; ++gl) {
           if (gl < ncg) {
-            const float4 sp = sr[gl];
-            const int* sd = sdi + (cg0 + gl) * 16;
+            const float4 sp = kStaged ? sr[kStaged ? gl : 0] : szp[gl * 8];
+            const int* sd = sdi + (gb + gl) * 16;
             const float d0a = (float)sd[sd_off], d0b = (float)sd[sd_off + 1];
             if (MODE == 1) {
               tot[0] = fmaf(sp.x * dsc[0], fmaf(-sp.y, d0a, (float)acc[gl][0]), tot[0]);
@@ -612,6 +635,10 @@ q4g_gemv_kernel(const GemvArgs a) {
             }
           }
         }
+        if (!kStaged) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[s]);
+        }
       }
       if (!direct) {
         if (MODE == 1) {
@@ -631,8 +658,8 @@ q4g_gemv_kernel(const GemvArgs a) {
       // direct mode: hand the chunk's partial (all 8 MMA columns) to the
       // merger warp.  The stage's partial slots are reused by the next round
       // of the same stage: wait until the merger has read the previous one.
-      float* red = part + ((size_t)s * ncn) * 128;
-      if (i >= NS && !mbar_wait_t<kConsWait>(&merged[s], ((i / NS) - 1) & 1)) {
+      float* red = part + ((size_t)s * ncs) * 128;
+      if (q >= NS && !mbar_wait_t<kConsWait>(&merged[s], ((q / NS) - 1) & 1)) {
         if (lane == 0 && a.err) atomicExch(a.err, 1);
         continue;
       }
@@ -658,7 +685,7 @@ q4g_gemv_kernel(const GemvArgs a) {
   for (int e = threadIdx.x; e < nrt * 128; e += blockDim.x) {
     const int i = e >> 7, r = e & 127;
     float s = 0.f;
-    for (int c = 0; c < nchunk; ++c) s += part[((size_t)(i * ncn + c)) * 128 + r];
+    for (int c = 0; c < nchunk; ++c) s += part[((size_t)(i * ncs + c)) * 128 + r];
     sums[e] = s;
   }
   cluster.sync();
@@ -788,17 +815,40 @@ inline int lcm_int(int a, int b) {
   return a / x * b;
 }
 
-// Ring stages of direct mode (no k-split) for this shape, 0 if it does not fit.
-inline int direct_ring_stages(int mode, int kqg, int groups, int mc) {
-  const SmemLayout L0 = q4g_smem_layout(mode, kqg, groups, mc, 0, 1, true);
+// Ring stages for stages of kbg groups and the given fixed shared memory, 0 if
+// fewer than one period (and at least 4) fit.
+inline int ring_stages(const SmemLayout& L0, int kqg, int kbg, bool direct) {
   if (L0.total >= kSmemBudget) return 0;
-  const int ncn = (groups + kChunkQ / kqg - 1) / (kChunkQ / kqg);
-  int gcdv = kCons, bb = ncn;
-  while (bb) { const int tmp = gcdv % bb; gcdv = bb; bb = tmp; }
+  const int ncs = (kbg + kChunkQ / kqg - 1) / (kChunkQ / kqg);
+  int gcdv = kCons, bb = ncs;
+  while (bb) {
+    const int tmp = gcdv % bb;
+    gcdv = bb;
+    bb = tmp;
+  }
   const int period = lcm_int(kCons / gcdv, kIssuers);
-  int ns = (int)((kSmemBudget - L0.total) / (L0.stage + (size_t)ncn * 512));
+  const size_t per_stage = L0.stage + (direct ? (size_t)ncs * 512 : 0);
+  int ns = (int)((kSmemBudget - L0.total) / per_stage);
   ns = std::min(ns, kStages) / period * period;
   return ns >= std::max(period, 4) ? ns : 0;
+}
+
+// Direct mode (no k-split): x of the whole K in shared memory, row tiles cut
+// into k-blocks of about 36 KB of weights.  False if it does not fit.
+inline bool plan_direct(int mode, int kqg, int groups, int mc, int* kbg, int* nkb, int* ns) {
+  const int cg = kChunkQ / kqg;
+  int kmax = (36864 / (kqg * 512 + 128)) / cg * cg;
+  if (kmax < cg) kmax = cg;
+  const int nb = (groups + kmax - 1) / kmax;
+  const int per = (groups + nb - 1) / nb;
+  const int kb = (per + cg - 1) / cg * cg;
+  const SmemLayout L0 = q4g_smem_layout(mode, kqg, groups, kb, mc, 0, 1, true);
+  const int n = ring_stages(L0, kqg, kb, true);
+  if (n == 0) return false;
+  *kbg = kb;
+  *nkb = (groups + kb - 1) / kb;
+  *ns = n;
+  return true;
 }
 
 // A row-tile range of one weight inside a launch.
@@ -847,47 +897,46 @@ int launch_fast(const Piece* pcs, int npc, const float* x, int64_t ldx, int mc, 
     cudaGetLastError();
     attr_dev = c->device;
   }
-  // Pick the k-split count (= cluster size).  Without a k-split (direct mode)
-  // every row tile is finished inside one CTA and written straight to y, so
-  // it is preferred whenever a full-K row-tile slice fits the ring.  Otherwise
-  // choose s with feasible shared memory (>= one ring period of stages) and
-  // the best estimated time relative to a balanced full-GPU run.
-  int best_s = -1, best_gps = 0, best_nclu = 1, best_ns = 0;
+  // Pick direct mode or a k-split count (= cluster size) by the estimated
+  // weight bytes of the busiest CTA (in units of 16 rows x one group); split
+  // mode pays for its cluster reduction with a 25% penalty.
+  int best_s = -1, best_gps = 0, best_nclu = 1, best_ns = 0, best_kbg = 0, best_nkb = 1;
   double best_score = 1e30;
-  for (int s = 1; s <= kMaxSplits; ++s) {
+  {
+    int kbg, nkb, ns;
+    if (plan_direct(MODE, KQG, groups, mc, &kbg, &nkb, &ns)) {
+      best_s = 1;
+      best_gps = groups;
+      best_nclu = std::max(1, std::min(n_rt, slots));
+      best_ns = ns;
+      best_kbg = kbg;
+      best_nkb = nkb;
+      best_score = (double)((n_rt + best_nclu - 1) / best_nclu) * groups;
+    }
+  }
+  for (int s = 2; s <= kMaxSplits; ++s) {
 #ifdef NIMF_Q4G_FORCE_SPLITS
     if (s != NIMF_Q4G_FORCE_SPLITS) continue;
 #endif
     const int gps = (groups + s - 1) / s;
     const int ss = (groups + gps - 1) / gps;
     if (ss != s) continue;
-    const bool direct = ss == 1;
     const int act = (c && attr_dev == c->device) ? max_active[ss] : slots / ss;
     const int nclu = std::max(1, std::min(n_rt, act));
     const int tchunk = (n_rt + nclu - 1) / nclu;
-    if (!direct && tchunk > kMaxTilesPerCluster) continue;
-    const SmemLayout L0 = q4g_smem_layout(MODE, KQG, gps, mc, 0, tchunk, direct);
-    if (L0.total >= kSmemBudget) continue;
-    const int ncn = (gps + kChunkQ / KQG - 1) / (kChunkQ / KQG);
-    const size_t per_stage = L0.stage + (direct ? (size_t)ncn * 512 : 0);
-    // stage i % ns serves warps (i * ncn + c) % kCons: keep ns a multiple of
-    // that period so every stage always serves the same warps
-    int gcdv = kCons, bb = ncn;
-    while (bb) { const int tmp = gcdv % bb; gcdv = bb; bb = tmp; }
-    const int period = lcm_int(kCons / gcdv, kIssuers);
-    int ns = (int)((kSmemBudget - L0.total) / per_stage);
-    ns = std::min(ns, kStages) / period * period;
-    if (ns < std::max(period, 4) || (!direct && (size_t)ns * L0.stage < (size_t)tchunk * 512))
-      continue;
-    const double util = std::min(1.0, (double)ss * nclu / slots);
-    const double balance = (double)tchunk * nclu / n_rt;
-    const double score = direct ? 0.0 : balance / util;
+    if (tchunk > kMaxTilesPerCluster) continue;
+    const SmemLayout L0 = q4g_smem_layout(MODE, KQG, gps, gps, mc, 0, tchunk, false);
+    const int ns = ring_stages(L0, KQG, gps, false);
+    if (ns == 0 || (size_t)ns * L0.stage < (size_t)tchunk * 512) continue;
+    const double score = 1.25 * tchunk * gps;
     if (score < best_score - 1e-9) {
       best_score = score;
       best_s = ss;
       best_gps = gps;
       best_nclu = nclu;
       best_ns = ns;
+      best_kbg = gps;
+      best_nkb = 1;
     }
   }
   if (best_s < 0)
@@ -895,7 +944,7 @@ int launch_fast(const Piece* pcs, int npc, const float* x, int64_t ldx, int mc, 
                      (long long)w0.k, mc, n_rt);
   const int s = best_s, gps = best_gps, n_clusters = best_nclu, ns = best_ns;
   const int tchunk = (n_rt + n_clusters - 1) / n_clusters;
-  const SmemLayout L = q4g_smem_layout(MODE, KQG, gps, mc, ns, tchunk, s == 1);
+  const SmemLayout L = q4g_smem_layout(MODE, KQG, gps, best_kbg, mc, ns, tchunk, s == 1);
 
   GemvArgs a;
   a.nprob = npc;
@@ -918,6 +967,8 @@ int launch_fast(const Piece* pcs, int npc, const float* x, int64_t ldx, int mc, 
   a.kq_total = (int)w0.kq_total;
   a.groups = groups;
   a.gps = gps;
+  a.kbg = best_kbg;
+  a.nkb = best_nkb;
   a.n_clusters = n_clusters;
   a.tchunk = tchunk;
   a.ns = ns;
@@ -948,7 +999,8 @@ int launch_rows(const Q4GWeight* const* ws, float* const* ys, int count, const f
                 int64_t ldx, int mc, int64_t m0, int num_sms, cudaStream_t st) {
   // Direct mode (no k-split) streams any number of row tiles; split mode keeps
   // at most kMaxTilesPerCluster partial row tiles per cluster in shared memory.
-  const bool direct_fits = direct_ring_stages(MODE, KQG, (int)ws[0]->groups, mc) > 0;
+  int kbg, nkb, nsd;
+  const bool direct_fits = plan_direct(MODE, KQG, (int)ws[0]->groups, mc, &kbg, &nkb, &nsd);
   const int64_t cap = direct_fits ? ((int64_t)1 << 40)
                                   : (int64_t)kMaxTilesPerCluster *
                                         std::max(1, num_sms * kCtasPerSm / kMaxSplits);
