@@ -204,6 +204,104 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+# 7B-shape decoder stack (32 layers, d_model 4096, 32 heads x 128, SiLU-gated
+# FFN 11008, vocab 32000), int4 group-128 weights: the matmul path of one
+# decode step = per layer q/k/v (one grouped launch), o, gate/up (one grouped
+# launch), down; then lm_head.
+D7, F7, V7, L7 = 4096, 11008, 32000, 32
+
+
+def decode7b_bytes(batch):
+    """Weight + activation bytes one decode step streams (algorithmic)."""
+    per_layer = (algo_bytes(3 * D7, D7, batch, GS) + algo_bytes(D7, D7, batch, GS)
+                 + algo_bytes(2 * F7, D7, batch, GS) + algo_bytes(D7, F7, batch, GS))
+    return L7 * per_layer + algo_bytes(V7, D7, batch, GS)
+
+
+def run_decode_7b(nimf, torch, steps, warmup):
+    """tok/s of the 7B-shape int4 decode matmul path on one GPU, batch 1 and 8.
+
+    Weights are synthetic int4 codes (seeded random bytes) with group scales
+    and zeros of the magnitude N(0, 0.02) weights quantise to; every layer has
+    its own device copy, so each step streams all 3.7 GB from HBM.  The
+    activation glue between projections (norms, attention, SiLU) is not on
+    this path; each projection reads the previous one's output."""
+    import numpy as np
+    rng = np.random.default_rng(4)
+
+    def make(n, k):
+        ngr = k // GS
+        p = rng.integers(0, 256, size=n * (k // 2), dtype=np.uint8)
+        sc = rng.uniform(0.002, 0.004, size=n * ngr).astype(np.float32)
+        zp = rng.uniform(6.0, 9.0, size=n * ngr).astype(np.float32)
+        return p, sc, zp
+
+    shapes = {"q": (D7, D7), "o": (D7, D7), "gu": (F7, D7), "down": (D7, F7), "head": (V7, D7)}
+    host = {kname: make(*nk) for kname, nk in shapes.items()}
+    layers = []
+    for _ in range(L7):
+        q, k, v = [nimf.Weight.q4g(*host["q"], D7, D7, GS) for _ in range(3)]
+        o = nimf.Weight.q4g(*host["o"], D7, D7, GS)
+        gate, up = [nimf.Weight.q4g(*host["gu"], F7, D7, GS) for _ in range(2)]
+        down = nimf.Weight.q4g(*host["down"], D7, F7, GS)
+        layers.append((q, k, v, o, gate, up, down))
+    head = nimf.Weight.q4g(*host["head"], V7, D7, GS)
+    out = {}
+    try:
+        for batch in (1, 8):
+            dev = torch.device("cuda")
+            x = torch.randn(batch, D7, device=dev)
+            qkv = torch.empty(3, batch, D7, device=dev)
+            att = torch.empty(batch, D7, device=dev)
+            gu = torch.empty(2, batch, F7, device=dev)
+            dn = torch.empty(batch, D7, device=dev)
+            logits = torch.empty(batch, V7, device=dev)
+            stream = torch.cuda.Stream()
+
+            def step(st):
+                h = x
+                for (q, k, v, o, gate, up, down) in layers:
+                    nimf.Weight.matmul_group_dev([q, k, v], h.data_ptr(), batch,
+                                                 [qkv[i].data_ptr() for i in range(3)], st)
+                    o.matmul_dev(qkv[0].data_ptr(), batch, att.data_ptr(), st)
+                    nimf.Weight.matmul_group_dev([gate, up], att.data_ptr(), batch,
+                                                 [gu[0].data_ptr(), gu[1].data_ptr()], st)
+                    down.matmul_dev(gu[0].data_ptr(), batch, dn.data_ptr(), st)
+                    h = dn
+                head.matmul_dev(dn.data_ptr(), batch, logits.data_ptr(), st)
+
+            with torch.cuda.stream(stream):
+                step(stream.cuda_stream)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                step(stream.cuda_stream)
+            for _ in range(warmup):
+                graph.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(steps):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / steps
+            graph.reset()
+            out["batch%d" % batch] = {
+                "tok_s": batch / (ms * 1e-3), "ms_per_step": ms,
+                "gb_s": decode7b_bytes(batch) / (ms * 1e-3) / 1e9,
+                "bytes_per_step": decode7b_bytes(batch)}
+    finally:
+        for lw in layers:
+            for w in lw:
+                w.free()
+        head.free()
+    out["launches_per_step"] = 4 * L7 + 1
+    out["note"] = ("matmul path only (grouped q/k/v and gate/up), one CUDA graph per step, "
+                   "synthetic int4-g128 weights, %d timed steps" % steps)
+    return out
+
+
 def run_ours(args, rank, world, local_rank):
     import numpy as np
     import torch
@@ -214,7 +312,7 @@ def run_ours(args, rank, world, local_rank):
     nimf.init(local_rank)
     R = args.copies
     n_total = N_PER_GPU * world
-    r0, r1 = rank * N_PER_GPU, (rank + 1) * N_PER_GPU
+    r0, r1 = nimf.shard_rows(n_total, world, rank)   # N_PER_GPU rows per rank
 
     # synthetic weights: the same quantised matrix on every rank's shard rows
     w = (np.random.default_rng(0).standard_normal((N_PER_GPU, K)) * 0.02).astype(np.float32)
@@ -365,6 +463,9 @@ def run_ours(args, rank, world, local_rank):
 
     graph.reset()
     graph1.reset()
+    decode = None
+    if world == 1 and args.decode_steps > 0:
+        decode = run_decode_7b(nimf, torch, args.decode_steps, max(3, args.warmup // 4))
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
@@ -377,6 +478,8 @@ def run_ours(args, rank, world, local_rank):
                 "clocks": clocks}
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if decode is not None:
+            line["decode_7b"] = decode
         print(json.dumps(line), flush=True)
     for wt in weights:
         wt.free()
@@ -390,6 +493,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--copies", type=int, default=14)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--decode-steps", type=int, default=200,
+                    help="timed steps of the 7B-shape decode measurement (0: skip)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 

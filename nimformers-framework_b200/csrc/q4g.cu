@@ -834,21 +834,25 @@ inline int ring_stages(const SmemLayout& L0, int kqg, int kbg, bool direct) {
 }
 
 // Direct mode (no k-split): x of the whole K in shared memory, row tiles cut
-// into k-blocks of about 36 KB of weights.  False if it does not fit.
+// into k-blocks of about 36 KB of weights (18 or 9 KB when x leaves too little
+// room for a ring of the larger ones).  False if it does not fit.
 inline bool plan_direct(int mode, int kqg, int groups, int mc, int* kbg, int* nkb, int* ns) {
   const int cg = kChunkQ / kqg;
-  int kmax = (36864 / (kqg * 512 + 128)) / cg * cg;
-  if (kmax < cg) kmax = cg;
-  const int nb = (groups + kmax - 1) / kmax;
-  const int per = (groups + nb - 1) / nb;
-  const int kb = (per + cg - 1) / cg * cg;
-  const SmemLayout L0 = q4g_smem_layout(mode, kqg, groups, kb, mc, 0, 1, true);
-  const int n = ring_stages(L0, kqg, kb, true);
-  if (n == 0) return false;
-  *kbg = kb;
-  *nkb = (groups + kb - 1) / kb;
-  *ns = n;
-  return true;
+  for (int target = 36864; target >= 9216; target /= 2) {
+    int kmax = (target / (kqg * 512 + 128)) / cg * cg;
+    if (kmax < cg) kmax = cg;
+    const int nb = (groups + kmax - 1) / kmax;
+    const int per = (groups + nb - 1) / nb;
+    const int kb = (per + cg - 1) / cg * cg;
+    const SmemLayout L0 = q4g_smem_layout(mode, kqg, groups, kb, mc, 0, 1, true);
+    const int n = ring_stages(L0, kqg, kb, true);
+    if (n == 0) continue;
+    *kbg = kb;
+    *nkb = (groups + kb - 1) / kb;
+    *ns = n;
+    return true;
+  }
+  return false;
 }
 
 // A row-tile range of one weight inside a launch.

@@ -402,6 +402,27 @@ class Weight:
             self.handle = 0
 
 
+# ------------------------------------------------------------ N-sharding
+def shard_rows(n, world, rank, align=16):
+    """Row range [r0, r1) of output channels held by `rank` of `world` GPUs.
+
+    Rows are the reference's output channels (W[N][K], nimformer.nim:90), so a
+    shard is a contiguous run of packed rows and of scale/zero rows; shards are
+    whole 16-row tiles except the last, and sizes differ by at most one tile.
+    """
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("rank %d of world %d" % (rank, world))
+    tiles = (n + align - 1) // align
+    t0, t1 = tiles * rank // world, tiles * (rank + 1) // world
+    return min(n, t0 * align), min(n, t1 * align)
+
+
+def gather_shards(parts, m):
+    """Reassembles y[m][N] from the ranks' shard outputs y_r[m][n_r] (rank
+    order), as an all-gather of the shards followed by a column concatenation."""
+    return np.concatenate([np.asarray(p, np.float32).reshape(m, -1) for p in parts], axis=1)
+
+
 # ------------------------------------------------------------ host quantiser
 def quantize_int4_per_group(w, group_size=128):
     """export_to_nimq.py:363-395 quantize_int4_asymmetric_per_group, vectorised.
