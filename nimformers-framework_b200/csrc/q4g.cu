@@ -1047,6 +1047,9 @@ int launch_mode(const Q4GWeight* const* ws, float* const* ys, int count, const f
 
 }  // namespace
 
+// Rows of x above which the tensor-core GEMM replaces the GEMV.
+constexpr int64_t kTcMinRows = 16;
+
 int q4g_gemv_group(const Q4GWeight* const* ws, int count, const float* x, int64_t m,
                    float* const* ys, cudaStream_t st) {
   Context* c = ctx();
@@ -1061,6 +1064,17 @@ int q4g_gemv_group(const Q4GWeight* const* ws, int count, const float* x, int64_
       if (ws[i]->rows > 0)
         NIMF_CUDA_TRY(cudaMemsetAsync(ys[i], 0, (size_t)(m * ws[i]->rows) * sizeof(float), st));
     return NIMF_OK;
+  }
+  // prefill-sized x: one tensor-core GEMM per weight (the weights are read
+  // once per 128 rows of x instead of once per 8)
+  if (m > kTcMinRows) {
+    bool tc = true;
+    for (int i = 0; i < count; ++i) tc = tc && (ws[i]->rows == 0 || q4g_tc_supported(*ws[i]));
+    if (tc) {
+      for (int i = 0; i < count; ++i)
+        if (ws[i]->rows > 0) NIMF_TRY(q4g_gemm_tc(*ws[i], x, m, ys[i], st));
+      return NIMF_OK;
+    }
   }
   for (int64_t m0 = 0; m0 < m; m0 += 8) {
     const int mc = (int)std::min<int64_t>(8, m - m0);

@@ -1,0 +1,83 @@
+"""int4 group-quantised weights times a prefill-sized x (more than 16 rows):
+the tcgen05 tensor-core GEMM, through the C ABI, against the reference path.
+
+Bar: max|y - y_ref| / max|y_ref| <= 1e-3 (fp32 accumulate) against
+cpuDequantMatmulQ4Fallback + cpuMatmul (gpubackend.nim:628-653) at sizes the
+C restatement finishes quickly, and against the bit-exact dequantised weights
+times x in float64 at prefill sizes.
+"""
+import numpy as np
+import pytest
+
+import pyoracle as O
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+
+
+def rel_err(y, ref):
+    y, ref = np.asarray(y, np.float64), np.asarray(ref, np.float64)
+    return float(np.max(np.abs(y - ref)) / max(np.max(np.abs(ref)), 1e-30))
+
+
+def quantized(n, k, gs, seed):
+    w = (np.random.default_rng(seed).standard_normal((n, k)) * 0.02).astype(np.float32)
+    p, s, z = O.quantize_int4_asym_per_group(w, gs)
+    return p, s, z, (k + gs - 1) // gs
+
+
+@pytest.mark.parametrize("n,k,gs,m", [(64, 4096, 128, 17), (200, 1000, 128, 64),
+                                      (256, 512, 64, 130), (37, 640, 128, 33),
+                                      (128, 256, 64, 128), (48, 512, 256, 40)])
+def test_prefill_matches_reference_path(nimf_gpu, n, k, gs, m):
+    p, s, z, ngr = quantized(n, k, gs, seed=n + m)
+    x = np.random.default_rng(m).standard_normal((m, k)).astype(np.float32)
+    w = nimf_gpu.Weight.q4g(p, s, z, n, k, gs, ngr)
+    y = w.matmul(x, m)
+    y2 = w.matmul(x, m)
+    w.free()
+    assert np.array_equal(y.view(np.uint32), y2.view(np.uint32))  # deterministic
+    ref = O.dequant_matmul_q4(x, p, s, z, m, k, n, gs, ngr)
+    assert rel_err(y, ref) <= TOL
+
+
+@pytest.mark.parametrize("n,k,m", [(4096, 4096, 512), (11008, 4096, 128), (4096, 11008, 256)])
+def test_prefill_config_shapes(nimf_gpu, n, k, m):
+    """7B-shape prefill projections (512 prompt tokens split in row tiles)."""
+    gs = 128
+    p, s, z, ngr = quantized(n, k, gs, seed=3)
+    x = np.random.default_rng(4).standard_normal((m, k)).astype(np.float32)
+    w = nimf_gpu.Weight.q4g(p, s, z, n, k, gs)
+    y = w.matmul(x, m)
+    w.free()
+    wd = O.dequantize_int4_asym(p, s, z, n, k, gs).astype(np.float64)
+    ref = x.astype(np.float64) @ wd.T
+    assert rel_err(y, ref) <= TOL
+
+
+def test_prefill_grouped_and_rows_of_x_beyond_tiles(nimf_gpu):
+    k, gs, m = 1024, 128, 200
+    shapes = [256, 48, 129]
+    ws, qs = [], []
+    for i, n in enumerate(shapes):
+        p, s, z, ngr = quantized(n, k, gs, seed=40 + i)
+        qs.append((p, s, z, ngr, n))
+        ws.append(nimf_gpu.Weight.q4g(p, s, z, n, k, gs))
+    x = np.random.default_rng(7).standard_normal((m, k)).astype(np.float32)
+    ys = nimf_gpu.Weight.matmul_group(ws, x, m)
+    for w, y, (p, s, z, ngr, n) in zip(ws, ys, qs):
+        ref = O.dequant_matmul_q4(x, p, s, z, m, k, n, gs, ngr)
+        assert rel_err(y, ref) <= TOL
+        w.free()
+
+
+def test_prefill_zero_and_large_x(nimf_gpu):
+    n, k, gs, m = 64, 512, 128, 40
+    p, s, z, ngr = quantized(n, k, gs, seed=9)
+    w = nimf_gpu.Weight.q4g(p, s, z, n, k, gs)
+    assert np.all(w.matmul(np.zeros((m, k), np.float32), m) == 0.0)
+    x = np.random.default_rng(2).standard_normal((m, k)).astype(np.float32) * 1e4
+    x[5] = 0.0
+    ref = O.dequant_matmul_q4(x, p, s, z, m, k, n, gs, ngr)
+    assert rel_err(w.matmul(x, m), ref) <= TOL
+    w.free()
