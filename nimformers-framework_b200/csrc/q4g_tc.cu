@@ -1,32 +1,33 @@
 // q4g_tc.cu -- int4 group-quantised weights (quant.nim:131-167) times a
-// prefill-sized x (M >= 33 rows) on the 5th-generation tensor cores:
-// tcgen05.mma kind::i8 with the accumulators in tensor memory (TMEM).
+// prefill-sized x (more than 16 rows) on the 5th-generation tensor cores:
+// tcgen05.mma kind::f16 with fp32 accumulators in tensor memory (TMEM).
 //
-// The arithmetic is the decode GEMV's, on 128 x 128 tiles:
-//   x[m][k] ~= s[m][g] (d0 + d1 / 256), two signed 8-bit digits per element
-//   with one scale per (row of x, quantisation group g), and the weights'
-//   nibbles n[c][k] (0..15) exact as unsigned bytes.  Per group
-//     sum_k (n - zp) sc x = sc s ((A0 + A1 / 256) - zp D),
-//   A0 / A1 the integer dot products of the nibbles with d0 / d1 (exact s32
-//   tensor-core sums) and D the group's digit sum.  The weights themselves
-//   are never rounded; x carries a relative error below 2^-16 of its group
-//   maximum.
+// Per quantisation group g of a channel c (scale sc, zero point zp):
+//   y[r][c] += sc * (D[c][r] - zp * S[r][g]),
+//   D[c][r] = sum_{k in g} nib[c][k] * xh[r][k],   S[r][g] = sum_{k in g} xh[r][k]
+// with nib the raw nibbles (0..15, exact in fp16) and xh = fp16(x * 2^e_r),
+// x rounded once to fp16 after a per-row power-of-two scale that puts the
+// row's largest magnitude in [128, 256); y is multiplied by 2^-e_r at the end.
+// The weights are never rounded; the only approximation is x's fp16 rounding
+// (relative 2^-11 per element).
 //
-// One CTA computes y[128 rows of x][128 output channels]:
-//   D[channel][j] = sum_k nib[channel][k] * B[j][k],  j < 128: d0 of x row j,
-//                                                     j >= 128: d1 of row j-128
-// as one M=128, N=256, K=32 MMA per 32 k.  Per quantisation group the
-// accumulators go to one of two TMEM buffers (2 x 256 columns) and epilogue
-// warps apply the group's scales while the tensor core fills the other one.
+// One CTA computes y[128 rows of x][128 output channels], one M=128
+// (channels) x N=npad (x rows of this tile, rounded up to 16) x K=16 MMA per
+// 16 k.  Operand A (the nibbles as fp16) lives in TMEM, written by unpack
+// warps with tcgen05.st (no generic-to-async proxy fence on the critical
+// path); operand B (xh) comes from shared memory in the canonical K-major
+// layout.  Per group the accumulators go to one of two TMEM buffers and the
+// epilogue warps apply sc and zp while the tensor core fills the other one.
 //
-// Warps: 0 producer (bulk copies of x digits and packed weights, before
-// griddepcontrol.wait only what does not depend on the previous kernel),
-// 1 TMEM owner and MMA issuer, 2-3 unpack the weights' nibbles into the MMA's
-// canonical K-major byte layout, 4-11 epilogue (warp e reads TMEM lanes
-// 32 (e % 4) .. + 31 = output channels, for x rows 64 ((e - 4) / 4) .. + 63).
+// Warps: 0 producer (bulk copy of the prepared x tile and its group sums, a
+// tensor-map load of the packed weights), 1 TMEM owner and MMA issuer, 2-5
+// unpack (thread = output channel = TMEM lane), 6-21 epilogue (warp w reads
+// TMEM lanes 32 (w % 4) .. + 31 = output channels, for x rows
+// 32 ((w - 6) / 4) .. + 31).
 // Every wait is bounded; on expiry the kernel records an error, lets the
 // other roles run out and still frees its TMEM.
 #include <cuda.h>
+#include <cuda_fp16.h>
 
 #include <algorithm>
 
@@ -39,9 +40,10 @@ namespace {
 
 constexpr int kTcRows = 128;      // x rows per CTA tile
 constexpr int kTcChan = 128;      // output channels per CTA tile (8 row tiles)
-constexpr int kTcStages = 4;      // x-digit / packed-weight ring
-constexpr int kTcEpi = 4;         // ring of per-group x scales for the epilogue
-constexpr int kTcThreads = 12 * 32;
+constexpr int kTcEpi = 16;        // ring of per-group x scales for the epilogue
+constexpr int kTcA = 4;           // unpacked weight tiles in TMEM
+constexpr int kTcEpiWarps = 16;   // 4 TMEM lane quarters x 4 row quarters
+constexpr int kTcThreads = (6 + kTcEpiWarps) * 32;
 constexpr uint32_t kTmemCols = 512;
 #ifndef NIMF_TC_WAIT
 #define NIMF_TC_WAIT 0
@@ -69,18 +71,32 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
-// generic-proxy shared-memory writes -> visible to the tensor core's reads
-__device__ __forceinline__ void fence_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-// D (TMEM) (+)= A (smem, u8) x B^T (smem, s8), M=128 N=256 K=32
-__device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
-                                        uint32_t idesc, uint32_t accumulate) {
+// D (TMEM, f32) (+)= A (TMEM, f16, K-major) x B^T (smem, f16), M=128, K=16
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc,
+                                           uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u)
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %5, %5, %5}, p;\n}" ::"r"(
+          tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u)
       : "memory");
+}
+// 32 consecutive columns of this thread's TMEM lane <- registers
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 // mbarrier arrive once every earlier tcgen05 operation of this thread is done
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -89,17 +105,14 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
           smem_addr(bar))
       : "memory");
 }
-// 32 consecutive columns of this thread's TMEM lane
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+// 16 consecutive columns of this thread's TMEM lane
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
         "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() {
@@ -128,66 +141,96 @@ __device__ __forceinline__ uint64_t smem_desc(const void* p, uint32_t lbo, uint3
   return d;
 }
 
-// Instruction descriptor: s32 accumulate, A u8, B s8, both K-major,
-// N = 256, M = 128.
-constexpr uint32_t kIdescI8 = (2u << 4) | (0u << 7) | (1u << 10) | ((256u >> 3) << 17) |
-                              ((128u >> 4) << 24);
+// Instruction descriptor: f32 accumulate, A and B f16, both K-major,
+// M = 128 (output channels); N (x rows, a multiple of 16) is or-ed in.
+constexpr uint32_t kIdescF16 = (1u << 4) | (0u << 7) | (0u << 10) | ((128u >> 4) << 24);
+__host__ __device__ constexpr uint32_t idesc_n(int n) { return kIdescF16 | ((uint32_t)(n >> 3) << 17); }
+
+// fp16x2 fused multiply-add
+__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
 
 // Byte offset of (row r, k) in a K-major canonical tile with `kbytes` of K.
 __host__ __device__ __forceinline__ uint32_t canon_off(int r, int k, int kbytes) {
   return (uint32_t)((r >> 3) * (kbytes * 8) + (k >> 4) * 128 + (r & 7) * 16 + (k & 15));
 }
 
-// x preparation, one CTA per (128-row tile mt, group g), thread = row:
-//   [d0: 128 x gs bytes][d1: 128 x gs bytes] in the canonical layout,
-//   then s[128] (digit scale) and dz[128] (d0 sum + d1 sum / 256) as floats.
-// Rows past m are zero.
+// Per-row power-of-two scale of x: scale[r] = 2^e, inv[r] = 2^-e with the
+// row's largest finite magnitude times 2^e in [128, 256) (e = 0 for a zero
+// row; |e| <= 126 keeps both factors finite).  One warp per row.
+__global__ void q4g_tc_rowscale(const float* __restrict__ x, int64_t ldx, int m, int k,
+                                float* __restrict__ scale, float* __restrict__ inv) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  griddep_wait();  // x may be written by the previous kernel in the stream
+  if (row < m) {
+    const float* xr = x + (size_t)row * ldx;
+    float mx = 0.f;
+    for (int i = lane; i < k; i += 32) {
+      const float v = fabsf(__ldg(xr + i));
+      if (v <= 3.402823466e38f) mx = fmaxf(mx, v);  // skips inf and NaN
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) {
+      int ex = 0;
+      if (mx > 0.f) frexpf(mx, &ex);  // mx = f 2^ex, f in [0.5, 1)
+      const int e = mx > 0.f ? max(-126, min(126, 8 - ex)) : 0;
+      scale[row] = ldexpf(1.0f, e);
+      inv[row] = ldexpf(1.0f, -e);
+    }
+  }
+  griddep_launch_dependents();
+}
+
+// x tile preparation, one CTA per (kTcRows-row tile mt, group g), thread = row:
+//   [xh: kTcRows x gs fp16 in the canonical K-major layout][S: kTcRows floats]
+// xh holds fp16(x * scale[row]) in the MMA's K order: within every aligned
+// 4 k the positions hold k offsets 0, 2, 1, 3 (the order in which the unpack
+// warps pair a fragment word's nibbles).  S[row] is the fp32 sum of the
+// row's fp16 values in the group.  Rows past m and k past K are zero.
 __global__ void q4g_tc_prep_x(const float* __restrict__ x, int64_t ldx, int m, int k, int gs,
-                              int groups, unsigned char* __restrict__ out) {
+                              int groups, const float* __restrict__ scale,
+                              unsigned char* __restrict__ out) {
   const int mt = blockIdx.x / groups, g = blockIdx.x - (blockIdx.x / groups) * groups;
   const int r = threadIdx.x;
   const int row = mt * kTcRows + r;
-  const size_t plane = (size_t)kTcRows * gs;
-  unsigned char* base = out + (size_t)blockIdx.x * (2 * plane + 2 * kTcRows * 4);
-  float* sv = reinterpret_cast<float*>(base + 2 * plane);
-  float* dz = sv + kTcRows;
-  griddep_wait();  // x may be written by the previous kernel in the stream
+  const size_t tile = (size_t)kTcRows * gs * 2;
+  unsigned char* base = out + (size_t)blockIdx.x * (tile + kTcRows * 4);
+  griddep_wait();  // scale comes from the previous kernel
   const bool rv = row < m;
+  const float sf = rv ? __ldg(scale + row) : 0.f;
   const float* xr = x + (size_t)(rv ? row : 0) * ldx + (size_t)g * gs;
   const int kvalid = rv ? max(0, min(gs, k - g * gs)) : 0;
-  float mx = 0.f;
-  for (int i = 0; i < gs; ++i) {
-    const float v = i < kvalid ? __ldg(xr + i) : 0.f;
-    mx = fmaxf(mx, fabsf(v));
-  }
-  const float inv = mx > 0.f ? 127.0f / mx : 0.f;
-  int s0 = 0, s1 = 0;
-  for (int c = 0; c < gs; c += 16) {
-    uint32_t w0[4], w1[4];
+  const bool vec = kvalid == gs && ((ldx & 3) == 0) && ((reinterpret_cast<uintptr_t>(xr) & 15) == 0);
+  float sum = 0.f;
+  for (int c = 0; c < gs; c += 8) {
+    float v[8];
+    if (vec) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(xr + c));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(xr + c + 4));
+      v[0] = a.x; v[1] = a.z; v[2] = a.y; v[3] = a.w;
+      v[4] = b.x; v[5] = b.z; v[6] = b.y; v[7] = b.w;
+    } else {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint32_t a = 0, b = 0;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int i = c + 4 * q + e;
-        const float v = i < kvalid ? __ldg(xr + i) : 0.f;
-        const float t = v * inv;
-        const int d0 = max(-127, min(127, __float2int_rn(t)));
-        const int d1 = max(-127, min(127, __float2int_rn((t - (float)d0) * 256.0f)));
-        a |= (uint32_t)(d0 & 0xFF) << (8 * e);
-        b |= (uint32_t)(d1 & 0xFF) << (8 * e);
-        s0 += d0;
-        s1 += d1;
+      for (int j = 0; j < 8; ++j) {
+        const int i = c + (j & 4) + ((j & 1) << 1) + ((j >> 1) & 1);  // 0,2,1,3 within 4
+        v[j] = i < kvalid ? __ldg(xr + i) : 0.f;
       }
-      w0[q] = a;
-      w1[q] = b;
     }
-    *reinterpret_cast<uint4*>(base + canon_off(r, c, gs)) = make_uint4(w0[0], w0[1], w0[2], w0[3]);
-    *reinterpret_cast<uint4*>(base + plane + canon_off(r, c, gs)) =
-        make_uint4(w1[0], w1[1], w1[2], w1[3]);
+    uint32_t h[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const __half2 p = __floats2half2_rn(v[2 * j] * sf, v[2 * j + 1] * sf);
+      const float2 q = __half22float2(p);
+      sum += q.x + q.y;
+      h[j] = *reinterpret_cast<const uint32_t*>(&p);
+    }
+    *reinterpret_cast<uint4*>(base + canon_off(r, 2 * c, 2 * gs)) = make_uint4(h[0], h[1], h[2], h[3]);
   }
-  sv[r] = mx * (1.0f / 127.0f);
-  dz[r] = (float)s0 + (float)s1 * (1.0f / 256.0f);
+  reinterpret_cast<float*>(base + tile)[r] = sum;
   griddep_launch_dependents();
 }
 
@@ -195,6 +238,7 @@ struct TcArgs {
   const uint4* frag;     // weight fragments, row tile 0
   const float4* sz;      // scale/zero pairs, row tile 0
   const unsigned char* xp;  // prepared x, [mt][g]
+  const float* xinv;     // per-row 2^-e of x's scale
   float* y;
   int64_t ldy;
   int m, rows, n_rt, kq_total, groups;
@@ -205,16 +249,22 @@ struct TcArgs {
 template <int KQG>
 struct TcLayout {
   static constexpr int GS = 64 * KQG;
-  static constexpr int DBYTES = 2 * kTcRows * GS;                    // digit planes d0, d1
-  static constexpr int EBYTES = 2 * kTcRows * 4;                     // s and dz
-  static constexpr int XBYTES = DBYTES + EBYTES;                     // one prepared group
+  static constexpr int XB = kTcRows * GS * 2;                        // xh tile
+  static constexpr int SB = kTcRows * 4;                             // group sums
+  static constexpr int XBYTES = XB + SB;                             // one prepared group
   static constexpr int WBYTES = 8 * KQG * 512;                       // packed weights
-  static constexpr int ABYTES = kTcChan * GS;                        // unpacked nibbles
+  static constexpr int STAGES = KQG == 1 ? 8 : 4;
   static constexpr int XOFF = 1024;                                  // after the barriers
-  static constexpr int WOFF = XOFF + kTcStages * DBYTES;
-  static constexpr int EOFF = WOFF + kTcStages * WBYTES;
-  static constexpr int AOFF = (EOFF + kTcEpi * EBYTES + 1023) / 1024 * 1024;
-  static constexpr int TOTAL = AOFF + 2 * ABYTES;
+  static constexpr int WOFF = XOFF + STAGES * XB;
+  static constexpr int EOFF = WOFF + STAGES * WBYTES;
+  static constexpr int TOTAL = EOFF + kTcEpi * SB;
+  // TMEM columns: accumulators [0, 2 kTcRows) (two buffers), then kTcA
+  // unpacked weight tiles (2 fp16 of K per column, padded to the 32 columns
+  // one tcgen05.st writes)
+  static constexpr uint32_t ACOL = 2 * kTcRows;
+  static constexpr uint32_t AW = GS / 2 < 32 ? 32 : GS / 2;
+  static_assert(ACOL + kTcA * AW <= kTmemCols, "TMEM columns");
+  static_assert(TOTAL <= 227 * 1024, "shared memory");
 };
 
 // wmap: the weight fragments as a 2-D tensor of 4-byte elements, one row per
@@ -224,16 +274,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     q4g_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap wmap) {
   using L = TcLayout<KQG>;
   constexpr int GS = L::GS;
-  constexpr int KSTEPS = GS / 32;
+  constexpr int KSTEPS = GS / 16;
+  constexpr int NS = L::STAGES;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = smem_raw;
   uint64_t* sfull = reinterpret_cast<uint64_t*>(smem);    // producer -> MMA, unpack
-  uint64_t* sempty = sfull + kTcStages;                    // MMA + 2 unpack warps -> producer
-  uint64_t* efull = sempty + kTcStages;                    // producer -> epilogue
-  uint64_t* eempty = efull + kTcEpi;                       // 8 epilogue warps -> producer
-  uint64_t* afull = eempty + kTcEpi;                       // [2] unpack -> MMA
-  uint64_t* aempty = afull + 2;                            // [2] MMA -> unpack
-  uint64_t* tfull = aempty + 2;                            // [2] MMA -> epilogue
+  uint64_t* sempty = sfull + NS;                           // MMA + 4 unpack warps -> producer
+  uint64_t* efull = sempty + NS;                           // producer -> epilogue
+  uint64_t* eempty = efull + kTcEpi;                       // epilogue warps -> producer
+  uint64_t* afull = eempty + kTcEpi;                       // [kTcA] unpack -> MMA
+  uint64_t* aempty = afull + kTcA;                         // [kTcA] MMA -> unpack
+  uint64_t* tfull = aempty + kTcA;                         // [2] MMA -> epilogue
   uint64_t* tempty = tfull + 2;                            // [2] epilogue -> MMA
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   int* failed = reinterpret_cast<int*>(tmem_slot + 1);
@@ -243,21 +294,26 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int G = a.groups;
   const int rt0 = nt * 8;
   const int nrt = max(0, min(8, a.n_rt - rt0));
+  // x rows of this tile, rounded up to the MMA's N granule
+  const int nrows = min(kTcRows, a.m - mt * kTcRows);
+  const int npad = (nrows + 15) & ~15;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kTcStages; ++s) {
+    for (int s = 0; s < NS; ++s) {
       mbar_init(&sfull[s], 1);
-      mbar_init(&sempty[s], 1 + 2);
+      mbar_init(&sempty[s], 1 + 4);
     }
     for (int s = 0; s < kTcEpi; ++s) {
       mbar_init(&efull[s], 1);
-      mbar_init(&eempty[s], 8);
+      mbar_init(&eempty[s], kTcEpiWarps);
+    }
+    for (int b = 0; b < kTcA; ++b) {
+      mbar_init(&afull[b], 4);
+      mbar_init(&aempty[b], 1);
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&afull[b], 2);
-      mbar_init(&aempty[b], 1);
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 8);
+      mbar_init(&tempty[b], kTcEpiWarps);
     }
     *failed = 0;
     mbar_fence_init();
@@ -277,16 +333,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   auto stop = [&]() { return *reinterpret_cast<volatile int*>(failed) != 0; };
 
   if (warp == 0) {
-    // ---------------- producer: per group, x digits, x scales and the 8 row
-    // tiles' packed nibbles (one tensor-map box; rows past the weight read 0)
+    // ---------------- producer: per group, the x tile's npad rows, their
+    // group sums and the 8 row tiles' packed nibbles (one tensor-map box;
+    // rows past the weight read 0)
+    const uint32_t xbytes = (uint32_t)npad * GS * 2, sbytes = (uint32_t)npad * 4;
     int last = -1;
     for (int g = 0; g < G; ++g) {
-      const int s = g % kTcStages, es = g % kTcEpi;
+      const int s = g % NS, es = g % kTcEpi;
       // lane 0 decides for the warp, so its lanes leave the loop together
       int ok = 1;
       if (lane == 0)
-        ok = (!stop() &&
-              (g < kTcStages || mbar_wait_t<kTcWait>(&sempty[s], ((g / kTcStages) - 1) & 1)) &&
+        ok = (!stop() && (g < NS || mbar_wait_t<kTcWait>(&sempty[s], ((g / NS) - 1) & 1)) &&
               (g < kTcEpi || mbar_wait_t<kTcWait>(&eempty[es], ((g / kTcEpi) - 1) & 1)))
                  ? 1
                  : 0;
@@ -295,62 +352,75 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (lane == 0 && !stop()) fail(3);
         break;
       }
-      unsigned char* xs = smem + L::XOFF + s * L::DBYTES;
+      unsigned char* xs = smem + L::XOFF + s * L::XB;
       unsigned char* ws = smem + L::WOFF + s * L::WBYTES;
-      unsigned char* ep = smem + L::EOFF + es * L::EBYTES;
+      unsigned char* ep = smem + L::EOFF + es * L::SB;
       if (lane == 0) {
-        mbar_arrive_expect_tx(&sfull[s], L::DBYTES + L::WBYTES);
-        mbar_arrive_expect_tx(&efull[es], L::EBYTES);
+        mbar_arrive_expect_tx(&sfull[s], xbytes + L::WBYTES);
+        mbar_arrive_expect_tx(&efull[es], sbytes);
         if (g == 0) griddep_wait();  // the prepared x comes from the previous kernel
       }
       __syncwarp();
       const unsigned char* src = a.xp + ((size_t)mt * G + g) * L::XBYTES;
-      if (lane == 0) bulk_g2s(xs, src, L::DBYTES, &sfull[s]);
-      if (lane == 1) bulk_g2s(ep, src + L::DBYTES, L::EBYTES, &efull[es]);
+      if (lane == 0) bulk_g2s(xs, src, xbytes, &sfull[s]);
+      if (lane == 1) bulk_g2s(ep, src + L::XB, sbytes, &efull[es]);
       if (lane == 2) tma_load_2d(ws, &wmap, g * KQG * 128, rt0, &sfull[s]);
       last = g;
     }
     // the last copies land before the CTA may exit
     if (lane == 0 && last >= 0) {
-      for (int g = max(0, last - kTcStages + 1); g <= last; ++g)
-        if (!mbar_wait_t<kTcWait>(&sfull[g % kTcStages], (g / kTcStages) & 1)) fail(3);
+      for (int g = max(0, last - NS + 1); g <= last; ++g)
+        if (!mbar_wait_t<kTcWait>(&sfull[g % NS], (g / NS) & 1)) fail(3);
       for (int g = max(0, last - kTcEpi + 1); g <= last; ++g)
         if (!mbar_wait_t<kTcWait>(&efull[g % kTcEpi], (g / kTcEpi) & 1)) fail(3);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer (one thread)
     if (lane == 0) {
+      const uint32_t idesc = idesc_n(npad);
       for (int g = 0; g < G; ++g) {
-        const int s = g % kTcStages, b = g & 1;
-        if (stop() || !mbar_wait_t<kTcWait>(&sfull[s], (g / kTcStages) & 1) ||
-            !mbar_wait_t<kTcWait>(&afull[b], (g >> 1) & 1) ||
+        const int s = g % NS, b = g & 1, ab = g % kTcA;
+        if (stop() || !mbar_wait_t<kTcWait>(&sfull[s], (g / NS) & 1) ||
+            !mbar_wait_t<kTcWait>(&afull[ab], (g / kTcA) & 1) ||
             (g >= 2 && !mbar_wait_t<kTcWait>(&tempty[b], ((g >> 1) - 1) & 1))) {
           fail(4);
           break;
         }
         tc_fence_after();
-        const unsigned char* at = smem + L::AOFF + b * L::ABYTES;
-        const unsigned char* bt = smem + L::XOFF + s * L::DBYTES;
-        const uint32_t td = tmem + (uint32_t)b * 256u;
+        const unsigned char* bt = smem + L::XOFF + s * L::XB;
+        const uint32_t td = tmem + (uint32_t)b * kTcRows;
+        const uint32_t ta = tmem + L::ACOL + (uint32_t)ab * L::AW;
 #pragma unroll
         for (int kk = 0; kk < KSTEPS; ++kk)
-          umma_i8(td, smem_desc(at + kk * 256, 128, GS * 8), smem_desc(bt + kk * 256, 128, GS * 8),
-                  kIdescI8, kk > 0 ? 1u : 0u);
-        umma_commit(&aempty[b]);
+          umma_f16_ts(td, ta + (uint32_t)kk * 8u, smem_desc(bt + kk * 256, 128, GS * 2 * 8), idesc,
+                      kk > 0 ? 1u : 0u);
+        umma_commit(&aempty[ab]);
         umma_commit(&tfull[b]);
         umma_commit(&sempty[s]);
       }
     }
     __syncwarp();
-  } else if (warp < 4) {
-    // ---------------- unpack: packed nibbles (fragment order) -> u8 canonical
-    const int ut = threadIdx.x - 64;  // 0..63
+  } else if (warp < 6) {
+    // ---------------- unpack: packed nibbles (fragment order) -> fp16 rows of
+    // A in TMEM.  Thread = output channel r (TMEM lane; a warp owns lanes
+    // 32 (warp % 4) .. + 31); rows g8 and g8 + 8 of a row tile share a
+    // fragment word (low / high nibble of each byte).  Word wi of fragment
+    // lane (g8, t) of quad qq holds k = qq*64 + 16 wi + 4 t + b, b = 0..3;
+    // its column pair (qq*32 + wi*8 + 2t, + 1) holds k offsets (0, 2), (1, 3).
+    const int r = (warp & 3) * 32 + lane;
+    const int rl = r >> 4, g8 = r & 7, rot = g8 >> 1;
+    const bool hi = (r & 8) != 0;
+    const uint32_t mask = hi ? 0x00F000F0u : 0x000F000Fu;
+    // (0x6400 | n) = 1024 + n and (0x6400 | n << 4) = 1024 + 16 n in fp16:
+    // one exact fma.f16x2 gives n
+    const uint32_t hmul = hi ? 0x2C002C00u : 0x3C003C00u;  // 1/16 : 1
+    const uint32_t hadd = hi ? 0xD400D400u : 0xE400E400u;  // -64 : -1024
     for (int g = 0; g < G; ++g) {
-      const int s = g % kTcStages, b = g & 1;
+      const int s = g % NS, ab = g % kTcA;
       int ok = 1;
       if (lane == 0)
-        ok = (!stop() && mbar_wait_t<kTcWait>(&sfull[s], (g / kTcStages) & 1) &&
-              (g < 2 || mbar_wait_t<kTcWait>(&aempty[b], ((g >> 1) - 1) & 1)))
+        ok = (!stop() && mbar_wait_t<kTcWait>(&sfull[s], (g / NS) & 1) &&
+              (g < kTcA || mbar_wait_t<kTcWait>(&aempty[ab], ((g / kTcA) - 1) & 1)))
                  ? 1
                  : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -358,46 +428,71 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (lane == 0) fail(5);
         break;
       }
+      tc_fence_after();
       const uint4* wsrc = reinterpret_cast<const uint4*>(smem + L::WOFF + s * L::WBYTES);
-      unsigned char* at = smem + L::AOFF + b * L::ABYTES;
-      for (int i = ut; i < nrt * KQG * 32; i += 64) {
-        const int rl = i / (KQG * 32), qq = (i / 32) % KQG, ln = i & 31;
-        const int gq = ln >> 2, t = ln & 3;
-        const uint4 w = wsrc[i];
-        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+      const uint32_t ta = tmem + ((uint32_t)((warp & 3) * 32) << 16) + L::ACOL + (uint32_t)ab * L::AW;
 #pragma unroll
-        for (int wi = 0; wi < 4; ++wi) {
-          const int kloc = qq * 64 + 32 * (wi >> 1) + 16 * (wi & 1) + 4 * t;
-          const uint32_t lo = words[wi] & 0x0F0F0F0Fu, hi = (words[wi] >> 4) & 0x0F0F0F0Fu;
-          *reinterpret_cast<uint32_t*>(at + canon_off(rl * 16 + gq, kloc, GS)) = lo;
-          *reinterpret_cast<uint32_t*>(at + canon_off(rl * 16 + 8 + gq, kloc, GS)) = hi;
+      for (int qq = 0; qq < KQG; ++qq) {
+        // load j reads fragment lane (g8, (j + rot) & 3): the 8 g8 of a warp
+        // then hit 8 different 16-byte bank groups
+        uint4 u[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          u[j] = make_uint4(0u, 0u, 0u, 0u);
+          if (rl < nrt) u[j] = wsrc[(rl * KQG + qq) * 32 + g8 * 4 + ((j + rot) & 3)];
         }
+        // back to fragment order: u[t] <- u[(t - rot) & 3]
+        if (rot & 1) {
+          const uint4 t3 = u[3];
+          u[3] = u[2];
+          u[2] = u[1];
+          u[1] = u[0];
+          u[0] = t3;
+        }
+        if (rot & 2) {
+          const uint4 t0 = u[0], t1 = u[1];
+          u[0] = u[2];
+          u[1] = u[3];
+          u[2] = t0;
+          u[3] = t1;
+        }
+        uint32_t col[32];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const uint32_t wv[4] = {u[t].x, u[t].y, u[t].z, u[t].w};
+#pragma unroll
+          for (int wi = 0; wi < 4; ++wi) {
+            col[wi * 8 + 2 * t] = hfma2((wv[wi] & mask) | 0x64006400u, hmul, hadd);
+            col[wi * 8 + 2 * t + 1] = hfma2(((wv[wi] >> 8) & mask) | 0x64006400u, hmul, hadd);
+          }
+        }
+        tmem_st32(ta + (uint32_t)qq * 32u, col);
       }
-      fence_async_smem();
+      tmem_wait_st();
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&afull[b]);
+        mbar_arrive(&afull[ab]);
         mbar_arrive(&sempty[s]);
       }
     }
   } else {
-    // ---------------- epilogue: thread = output channel (TMEM lane), 64 x rows
-    const int e = warp - 4;
-    const int quad = e & 3, half = e >> 2;
+    // ---------------- epilogue: thread = output channel (TMEM lane), 32 x rows
+    const int quad = warp & 3, rq = (warp - 6) >> 2;
     const int ch = quad * 32 + lane;              // channel within the tile
     const int rt = rt0 + (ch >> 4), r16 = ch & 15;
     const bool cvalid = rt < a.n_rt && rt * 16 + r16 < a.rows;
+    const bool active = rq * 32 < npad;           // warp-uniform
     const float4* szp = a.sz + ((size_t)min(rt, a.n_rt - 1) * a.groups) * 8 + (r16 & 7);
-    float acc[64];
+    float acc[32];
 #pragma unroll
-    for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+    for (int i = 0; i < 32; ++i) acc[i] = 0.f;
     griddep_wait();
     for (int g = 0; g < G; ++g) {
       const int es = g % kTcEpi, b = g & 1;
       const float4 zz = __ldg(szp + (size_t)g * 8);
-      // y += sc s / 256 ((256 A0 + A1) - 256 zp dz): one conversion per element
-      const float sc = ((r16 >> 3) ? zz.z : zz.x) * (1.0f / 256.0f);
-      const float zp = ((r16 >> 3) ? zz.w : zz.y) * 256.0f;
+      const float sc = (r16 >> 3) ? zz.z : zz.x;
+      const float nzp = -((r16 >> 3) ? zz.w : zz.y);
       int ok = 1;
       if (lane == 0)
         ok = (!stop() && mbar_wait_t<kTcWait>(&tfull[b], (g >> 1) & 1) &&
@@ -410,43 +505,40 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         break;
       }
       tc_fence_after();
-      const float4* sv4 = reinterpret_cast<const float4*>(smem + L::EOFF + es * L::EBYTES);
-      const float4* dz4 = sv4 + kTcRows / 4;
-      const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)b * 256u;
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t c0[32], c1[32];
-        const int j0 = half * 64 + c * 32;  // first x row of this chunk
-        tmem_ld32(tl + (uint32_t)j0, c0);
-        tmem_ld32(tl + 128u + (uint32_t)j0, c1);
+      uint32_t d0[16], d1[16];
+      if (active) {
+        const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)b * kTcRows + rq * 32;
+        tmem_ld16(tl, d0);
+        tmem_ld16(tl + 16u, d1);
         tmem_wait_ld();
-        if (c == 1) {
-          // both chunks are in registers: the buffer may be refilled
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[b]);
-        }
+      }
+      // the buffer may be refilled
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[b]);
+      if (active) {
+        const float4* s4 = reinterpret_cast<const float4*>(smem + L::EOFF + es * L::SB) + rq * 8;
 #pragma unroll
         for (int i4 = 0; i4 < 8; ++i4) {
-          const float4 s4 = sv4[(j0 >> 2) + i4], d4 = dz4[(j0 >> 2) + i4];
-          const float sv[4] = {s4.x, s4.y, s4.z, s4.w}, dv[4] = {d4.x, d4.y, d4.z, d4.w};
+          const float4 sv = s4[i4];
+          const float sa[4] = {sv.x, sv.y, sv.z, sv.w};
 #pragma unroll
-          for (int e4 = 0; e4 < 4; ++e4) {
-            const int i = i4 * 4 + e4;
-            const float u = (float)((int)c0[i] * 256 + (int)c1[i]);
-            acc[c * 32 + i] = fmaf(sc * sv[e4], fmaf(-zp, dv[e4], u), acc[c * 32 + i]);
+          for (int e = 0; e < 4; ++e) {
+            const int i = i4 * 4 + e;
+            const float d = __uint_as_float(i < 16 ? d0[i & 15] : d1[i & 15]);
+            acc[i] = fmaf(sc, fmaf(nzp, sa[e], d), acc[i]);
           }
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&eempty[es]);
     }
-    if (cvalid && !stop()) {
+    if (cvalid && active && !stop()) {
       const int n = rt * 16 + r16;
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const int row = mt * kTcRows + half * 64 + i;
-        if (row < a.m) a.y[(size_t)row * a.ldy + n] = acc[i];
+      for (int i = 0; i < 32; ++i) {
+        const int row = mt * kTcRows + rq * 32 + i;
+        if (row < a.m) a.y[(size_t)row * a.ldy + n] = acc[i] * __ldg(a.xinv + row);
       }
     }
   }
@@ -528,8 +620,13 @@ int launch_tc(const Q4GWeight& w, const float* x, int64_t ldx, int m, float* y, 
   const int G = (int)w.groups;
   const int mts = (m + kTcRows - 1) / kTcRows;
   const int nts = (int)((w.rows + kTcChan - 1) / kTcChan);
+  // scratch: the prepared tiles, then scale[m] and inv[m]
+  const size_t tiles = ((size_t)mts * G * L::XBYTES + 255) & ~(size_t)255;
+  const size_t mpad = (size_t)mts * kTcRows;
   unsigned char* xp = nullptr;
-  NIMF_TRY(prep_buffer((size_t)mts * G * L::XBYTES, st, &xp));
+  NIMF_TRY(prep_buffer(tiles + 2 * mpad * sizeof(float), st, &xp));
+  float* scale = reinterpret_cast<float*>(xp + tiles);
+  float* inv = scale + mpad;
   static int attr_dev = -1;
   auto kern = q4g_tc_kernel<KQG>;
   if (c && attr_dev != c->device) {
@@ -541,17 +638,28 @@ int launch_tc(const Q4GWeight& w, const float* x, int64_t ldx, int m, float* y, 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   {
     cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((m + 7) / 8), 1, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    NIMF_CUDA_TRY(cudaLaunchKernelEx(&cfg, q4g_tc_rowscale, x, ldx, m, (int)w.k, scale, inv));
+  }
+  {
+    cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(mts * G), 1, 1);
     cfg.blockDim = dim3(kTcRows, 1, 1);
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    NIMF_CUDA_TRY(cudaLaunchKernelEx(&cfg, q4g_tc_prep_x, x, ldx, m, (int)w.k, 64 * KQG, G, xp));
+    NIMF_CUDA_TRY(cudaLaunchKernelEx(&cfg, q4g_tc_prep_x, x, ldx, m, (int)w.k, L::GS, G,
+                                     (const float*)scale, xp));
   }
   TcArgs a;
   a.frag = (const uint4*)w.frag;
   a.sz = (const float4*)w.sz;
   a.xp = xp;
+  a.xinv = inv;
   a.y = y;
   a.ldy = ldy;
   a.m = m;
