@@ -202,6 +202,15 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       "l"(src), "r"(bytes), "r"(smem_addr(m))
       : "memory");
 }
+// True in exactly one active lane of a converged warp.  Issuing tcgen05.mma
+// and bulk copies under this predicate from a converged warp keeps their
+// operands warp-uniform; issuing them from a lane-divergent branch measured
+// 2-3x slower per instruction.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile("{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}" : "=r"(pred));
+  return pred != 0;
+}
 // Named barrier over `threads` threads (a subset of the CTA).
 __device__ __forceinline__ void named_barrier(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

@@ -43,6 +43,7 @@ int set_error(int code, const char* fmt, ...);
 struct Q4GWeight {
   int64_t rows = 0, k = 0, gs = 0, ngr = 0;
   bool fast = false;
+  bool tc_zp_ok = false;  // every zero point finite with |zp| < 60000 (tensor-core GEMM)
   int64_t n_rt = 0, kq_total = 0, groups = 0;
   void* frag = nullptr;   // uint4*
   void* sz = nullptr;     // float4*

@@ -115,6 +115,16 @@ __global__ void q4g_repack_sz(const float* __restrict__ sc, const float* __restr
   out[i] = v;
 }
 
+// *bad = 1 if a zero point is not finite or |zp| >= 60000 (the tensor-core
+// GEMM carries zp + 64 as two fp16 parts).
+__global__ void q4g_zp_range(const float* __restrict__ zp, int64_t ngr, int64_t rows,
+                             int* __restrict__ bad) {
+  const int64_t n = rows * ngr;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    if (!(fabsf(zp[i]) < 60000.0f)) *bad = 1;
+}
+
 // out[r][c] = (float(nib) - zp) * sc with the reference's two roundings
 // (quant.nim:162: lut[k] = (float32(k) - zp) * sc), read back from the
 // fragment layout.
@@ -770,6 +780,23 @@ int q4g_build(Weight* wt, const uint8_t* wq_dev, const float* sc_dev, const floa
       q4g_repack_sz<<<grid1d(nsz, 256), 256, 0, st>>>(scs, zps, ngr, rows, w.groups, nsz,
                                                       (float4*)w.sz);
     NIMF_CUDA_TRY(cudaGetLastError());
+    w.tc_zp_ok = false;
+    if (rows * ngr > 0) {
+      int* bad = nullptr;
+      NIMF_TRY(device_alloc((void**)&bad, sizeof(int)));
+      int hb = 0;
+      cudaError_t e = cudaMemsetAsync(bad, 0, sizeof(int), st);
+      if (e == cudaSuccess) {
+        const int64_t n = rows * ngr;
+        q4g_zp_range<<<(unsigned)std::min<int64_t>((n + 255) / 256, 1024), 256, 0, st>>>(zps, ngr, rows, bad);
+        e = cudaGetLastError();
+      }
+      if (e == cudaSuccess) e = cudaMemcpyAsync(&hb, bad, sizeof(int), cudaMemcpyDeviceToHost, st);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+      device_free(bad);
+      NIMF_CUDA_TRY(e);
+      w.tc_zp_ok = hb == 0;
+    }
   } else {
     const size_t nb = (size_t)(rows * bpr);
     const size_t ns = (size_t)(rows * ngr) * sizeof(float);

@@ -3,27 +3,31 @@
 // tcgen05.mma kind::f16 with fp32 accumulators in tensor memory (TMEM).
 //
 // Per quantisation group g of a channel c (scale sc, zero point zp):
-//   y[r][c] += sc * (D[c][r] - zp * S[r][g]),
-//   D[c][r] = sum_{k in g} nib[c][k] * xh[r][k],   S[r][g] = sum_{k in g} xh[r][k]
-// with nib the raw nibbles (0..15, exact in fp16) and xh = fp16(x * 2^e_r),
-// x rounded once to fp16 after a per-row power-of-two scale that puts the
-// row's largest magnitude in [128, 256); y is multiplied by 2^-e_r at the end.
-// The weights are never rounded; the only approximation is x's fp16 rounding
-// (relative 2^-11 per element).
+//   y[r][c] += sc * D[c][r],
+//   D[c][r] = sum_{k in g} (64 + nib[c][k]) * xh[r][k] - (64 + zp) * S[r][g]
+//           = sum_{k in g} (nib[c][k] - zp) * xh[r][k],
+// with nib the raw nibbles, xh = fp16(x * 2^e_r) (x rounded once to fp16
+// after a per-row power-of-two scale that puts the row's largest magnitude
+// in [128, 256)) and S[r][g] the fp32 sum of the row's xh in the group.  The
+// tensor core computes all of D: 64 + nib is exact in fp16, and the
+// zero-point term is one more K=16 step whose operands split 64 + zp and S
+// into two fp16 parts each (hi + lo, 22 significant bits), giving
+// zh*Sh + zh*Sl + zl*Sh.  y is multiplied by 2^-e_r at the end.  The only
+// approximation is x's fp16 rounding (relative 2^-11 per element).
 //
-// One CTA computes y[128 rows of x][128 output channels], one M=128
-// (channels) x N=npad (x rows of this tile, rounded up to 16) x K=16 MMA per
-// 16 k.  Operand A (the nibbles as fp16) lives in TMEM, written by unpack
-// warps with tcgen05.st (no generic-to-async proxy fence on the critical
-// path); operand B (xh) comes from shared memory in the canonical K-major
-// layout.  Per group the accumulators go to one of two TMEM buffers and the
-// epilogue warps apply sc and zp while the tensor core fills the other one.
+// One CTA computes y[128 rows of x][128 output channels], M=128 (channels) x
+// N=npad (x rows of the tile, rounded up to 16) x K=16 MMAs.  Operand A lives
+// in TMEM, written by unpack warps with tcgen05.st (no generic-to-async proxy
+// fence on the critical path); operand B comes from shared memory in the
+// canonical K-major layout.  Per group the accumulators go to one of two
+// TMEM buffers and the epilogue warps add sc * D while the tensor core fills
+// the other one.  The MMA and producer warps stay converged and issue from
+// one elected lane.
 //
-// Warps: 0 producer (bulk copy of the prepared x tile and its group sums, a
-// tensor-map load of the packed weights), 1 TMEM owner and MMA issuer, 2-5
-// unpack (thread = output channel = TMEM lane), 6-21 epilogue (warp w reads
-// TMEM lanes 32 (w % 4) .. + 31 = output channels, for x rows
-// 32 ((w - 6) / 4) .. + 31).
+// Warps: 0 producer (bulk copy of the prepared x tile, tensor-map load of the
+// packed weights), 1 TMEM owner and MMA issuer, 2-5 unpack (thread = output
+// channel = TMEM lane), 6-21 epilogue (warp w reads TMEM lanes 32 (w % 4) ..
+// + 31 = output channels, for x rows 32 ((w - 6) / 4) .. + 31).
 // Every wait is bounded; on expiry the kernel records an error, lets the
 // other roles run out and still frees its TMEM.
 #include <cuda.h>
@@ -40,8 +44,6 @@ namespace {
 
 constexpr int kTcRows = 128;      // x rows per CTA tile
 constexpr int kTcChan = 128;      // output channels per CTA tile (8 row tiles)
-constexpr int kTcEpi = 16;        // ring of per-group x scales for the epilogue
-constexpr int kTcA = 4;           // unpacked weight tiles in TMEM
 constexpr int kTcEpiWarps = 16;   // 4 TMEM lane quarters x 4 row quarters
 constexpr int kTcThreads = (6 + kTcEpiWarps) * 32;
 constexpr uint32_t kTmemCols = 512;
@@ -79,6 +81,13 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, ui
       " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %5, %5, %5}, p;\n}" ::"r"(
           tmem_d),
       "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u)
+      : "memory");
+}
+// 8 consecutive columns of this thread's TMEM lane <- registers
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
       : "memory");
 }
 // 32 consecutive columns of this thread's TMEM lane <- registers
@@ -146,12 +155,6 @@ __device__ __forceinline__ uint64_t smem_desc(const void* p, uint32_t lbo, uint3
 constexpr uint32_t kIdescF16 = (1u << 4) | (0u << 7) | (0u << 10) | ((128u >> 4) << 24);
 __host__ __device__ constexpr uint32_t idesc_n(int n) { return kIdescF16 | ((uint32_t)(n >> 3) << 17); }
 
-// fp16x2 fused multiply-add
-__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
-  uint32_t d;
-  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
-}
 
 // Byte offset of (row r, k) in a K-major canonical tile with `kbytes` of K.
 __host__ __device__ __forceinline__ uint32_t canon_off(int r, int k, int kbytes) {
@@ -185,20 +188,22 @@ __global__ void q4g_tc_rowscale(const float* __restrict__ x, int64_t ldx, int m,
   griddep_launch_dependents();
 }
 
-// x tile preparation, one CTA per (kTcRows-row tile mt, group g), thread = row:
-//   [xh: kTcRows x gs fp16 in the canonical K-major layout][S: kTcRows floats]
-// xh holds fp16(x * scale[row]) in the MMA's K order: within every aligned
-// 4 k the positions hold k offsets 0, 2, 1, 3 (the order in which the unpack
-// warps pair a fragment word's nibbles).  S[row] is the fp32 sum of the
-// row's fp16 values in the group.  Rows past m and k past K are zero.
+// x tile preparation, one CTA per (kTcRows-row tile mt, group g), thread = row.
+// Each row is RB = 2 gs + 32 bytes of K-major fp16 in the canonical layout:
+//   gs values fp16(x * scale[row]) in the MMA's K order (within every aligned
+//   4 k the positions hold k offsets 0, 2, 1, 3: the order in which the
+//   unpack warps pair a fragment word's nibbles), then the zero-point step
+//   [Sh, Sl, Sh, 0 x 13] with S the fp32 sum of the row's fp16 values,
+//   Sh = fp16(S), Sl = fp16(S - Sh).
+// Rows past m and k past K are zero.
 __global__ void q4g_tc_prep_x(const float* __restrict__ x, int64_t ldx, int m, int k, int gs,
                               int groups, const float* __restrict__ scale,
                               unsigned char* __restrict__ out) {
   const int mt = blockIdx.x / groups, g = blockIdx.x - (blockIdx.x / groups) * groups;
   const int r = threadIdx.x;
   const int row = mt * kTcRows + r;
-  const size_t tile = (size_t)kTcRows * gs * 2;
-  unsigned char* base = out + (size_t)blockIdx.x * (tile + kTcRows * 4);
+  const int rb = 2 * gs + 32;
+  unsigned char* base = out + (size_t)blockIdx.x * kTcRows * rb;
   griddep_wait();  // scale comes from the previous kernel
   const bool rv = row < m;
   const float sf = rv ? __ldg(scale + row) : 0.f;
@@ -228,9 +233,13 @@ __global__ void q4g_tc_prep_x(const float* __restrict__ x, int64_t ldx, int m, i
       sum += q.x + q.y;
       h[j] = *reinterpret_cast<const uint32_t*>(&p);
     }
-    *reinterpret_cast<uint4*>(base + canon_off(r, 2 * c, 2 * gs)) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(base + canon_off(r, 2 * c, rb)) = make_uint4(h[0], h[1], h[2], h[3]);
   }
-  reinterpret_cast<float*>(base + tile)[r] = sum;
+  const __half sh = __float2half_rn(sum);
+  const __half sl = __float2half_rn(sum - __half2float(sh));
+  const uint32_t hs = __half_as_ushort(sh), ls = __half_as_ushort(sl);
+  *reinterpret_cast<uint4*>(base + canon_off(r, 2 * gs, rb)) = make_uint4(hs | (ls << 16), hs, 0u, 0u);
+  *reinterpret_cast<uint4*>(base + canon_off(r, 2 * gs + 16, rb)) = make_uint4(0u, 0u, 0u, 0u);
   griddep_launch_dependents();
 }
 
@@ -245,25 +254,25 @@ struct TcArgs {
   int* err;
 };
 
-// Shared memory (offsets from the 1024-aligned base)
+// Shared memory (offsets from the 1024-aligned base) and TMEM columns
 template <int KQG>
 struct TcLayout {
   static constexpr int GS = 64 * KQG;
-  static constexpr int XB = kTcRows * GS * 2;                        // xh tile
-  static constexpr int SB = kTcRows * 4;                             // group sums
-  static constexpr int XBYTES = XB + SB;                             // one prepared group
+  static constexpr int RB = 2 * GS + 32;                             // bytes per x row
+  static constexpr int XB = kTcRows * RB;                            // one prepared x tile
   static constexpr int WBYTES = 8 * KQG * 512;                       // packed weights
   static constexpr int STAGES = KQG == 1 ? 8 : 4;
   static constexpr int XOFF = 1024;                                  // after the barriers
   static constexpr int WOFF = XOFF + STAGES * XB;
-  static constexpr int EOFF = WOFF + STAGES * WBYTES;
-  static constexpr int TOTAL = EOFF + kTcEpi * SB;
-  // TMEM columns: accumulators [0, 2 kTcRows) (two buffers), then kTcA
-  // unpacked weight tiles (2 fp16 of K per column, padded to the 32 columns
-  // one tcgen05.st writes)
+  static constexpr int TOTAL = WOFF + STAGES * WBYTES;
+  static constexpr int KSTEPS = GS / 16 + 1;                         // + zero-point step
+  // TMEM: accumulators [0, 2 kTcRows) (two buffers), then ABUF unpacked
+  // weight tiles of AW columns (2 fp16 of K per column; the last 8 hold the
+  // zero-point step)
   static constexpr uint32_t ACOL = 2 * kTcRows;
-  static constexpr uint32_t AW = GS / 2 < 32 ? 32 : GS / 2;
-  static_assert(ACOL + kTcA * AW <= kTmemCols, "TMEM columns");
+  static constexpr uint32_t AW = GS / 2 + 8;
+  static constexpr int ABUF = (int)((kTmemCols - ACOL) / AW) < 4 ? (int)((kTmemCols - ACOL) / AW) : 4;
+  static_assert(ABUF >= 2, "TMEM columns");
   static_assert(TOTAL <= 227 * 1024, "shared memory");
 };
 
@@ -274,17 +283,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     q4g_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap wmap) {
   using L = TcLayout<KQG>;
   constexpr int GS = L::GS;
-  constexpr int KSTEPS = GS / 16;
-  constexpr int NS = L::STAGES;
+  constexpr int NS = L::STAGES, NA = L::ABUF;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = smem_raw;
   uint64_t* sfull = reinterpret_cast<uint64_t*>(smem);    // producer -> MMA, unpack
   uint64_t* sempty = sfull + NS;                           // MMA + 4 unpack warps -> producer
-  uint64_t* efull = sempty + NS;                           // producer -> epilogue
-  uint64_t* eempty = efull + kTcEpi;                       // epilogue warps -> producer
-  uint64_t* afull = eempty + kTcEpi;                       // [kTcA] unpack -> MMA
-  uint64_t* aempty = afull + kTcA;                         // [kTcA] MMA -> unpack
-  uint64_t* tfull = aempty + kTcA;                         // [2] MMA -> epilogue
+  uint64_t* afull = sempty + NS;                           // [NA] unpack -> MMA
+  uint64_t* aempty = afull + NA;                           // [NA] MMA -> unpack
+  uint64_t* tfull = aempty + NA;                           // [2] MMA -> epilogue
   uint64_t* tempty = tfull + 2;                            // [2] epilogue -> MMA
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   int* failed = reinterpret_cast<int*>(tmem_slot + 1);
@@ -303,11 +309,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&sfull[s], 1);
       mbar_init(&sempty[s], 1 + 4);
     }
-    for (int s = 0; s < kTcEpi; ++s) {
-      mbar_init(&efull[s], 1);
-      mbar_init(&eempty[s], kTcEpiWarps);
-    }
-    for (int b = 0; b < kTcA; ++b) {
+    for (int b = 0; b < NA; ++b) {
       mbar_init(&afull[b], 4);
       mbar_init(&aempty[b], 1);
     }
@@ -333,20 +335,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   auto stop = [&]() { return *reinterpret_cast<volatile int*>(failed) != 0; };
 
   if (warp == 0) {
-    // ---------------- producer: per group, the x tile's npad rows, their
-    // group sums and the 8 row tiles' packed nibbles (one tensor-map box;
-    // rows past the weight read 0)
-    const uint32_t xbytes = (uint32_t)npad * GS * 2, sbytes = (uint32_t)npad * 4;
+    // ---------------- producer: per group, the x tile's npad rows and the 8
+    // row tiles' packed nibbles (one tensor-map box; rows past the weight
+    // read 0)
+    const uint32_t xbytes = (uint32_t)npad * L::RB;
     int last = -1;
     for (int g = 0; g < G; ++g) {
-      const int s = g % NS, es = g % kTcEpi;
+      const int s = g % NS;
       // lane 0 decides for the warp, so its lanes leave the loop together
       int ok = 1;
       if (lane == 0)
-        ok = (!stop() && (g < NS || mbar_wait_t<kTcWait>(&sempty[s], ((g / NS) - 1) & 1)) &&
-              (g < kTcEpi || mbar_wait_t<kTcWait>(&eempty[es], ((g / kTcEpi) - 1) & 1)))
-                 ? 1
-                 : 0;
+        ok = (!stop() && (g < NS || mbar_wait_t<kTcWait>(&sempty[s], ((g / NS) - 1) & 1))) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) {
         if (lane == 0 && !stop()) fail(3);
@@ -354,52 +353,55 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       unsigned char* xs = smem + L::XOFF + s * L::XB;
       unsigned char* ws = smem + L::WOFF + s * L::WBYTES;
-      unsigned char* ep = smem + L::EOFF + es * L::SB;
-      if (lane == 0) {
+      const unsigned char* src = a.xp + ((size_t)mt * G + g) * L::XB;
+      if (g == 0) griddep_wait();  // the prepared x comes from the previous kernel
+      if (elect_one()) {
         mbar_arrive_expect_tx(&sfull[s], xbytes + L::WBYTES);
-        mbar_arrive_expect_tx(&efull[es], sbytes);
-        if (g == 0) griddep_wait();  // the prepared x comes from the previous kernel
+        bulk_g2s(xs, src, xbytes, &sfull[s]);
+        tma_load_2d(ws, &wmap, g * KQG * 128, rt0, &sfull[s]);
       }
       __syncwarp();
-      const unsigned char* src = a.xp + ((size_t)mt * G + g) * L::XBYTES;
-      if (lane == 0) bulk_g2s(xs, src, xbytes, &sfull[s]);
-      if (lane == 1) bulk_g2s(ep, src + L::XB, sbytes, &efull[es]);
-      if (lane == 2) tma_load_2d(ws, &wmap, g * KQG * 128, rt0, &sfull[s]);
       last = g;
     }
     // the last copies land before the CTA may exit
     if (lane == 0 && last >= 0) {
       for (int g = max(0, last - NS + 1); g <= last; ++g)
         if (!mbar_wait_t<kTcWait>(&sfull[g % NS], (g / NS) & 1)) fail(3);
-      for (int g = max(0, last - kTcEpi + 1); g <= last; ++g)
-        if (!mbar_wait_t<kTcWait>(&efull[g % kTcEpi], (g / kTcEpi) & 1)) fail(3);
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer (one thread)
-    if (lane == 0) {
-      const uint32_t idesc = idesc_n(npad);
-      for (int g = 0; g < G; ++g) {
-        const int s = g % NS, b = g & 1, ab = g % kTcA;
-        if (stop() || !mbar_wait_t<kTcWait>(&sfull[s], (g / NS) & 1) ||
-            !mbar_wait_t<kTcWait>(&afull[ab], (g / kTcA) & 1) ||
-            (g >= 2 && !mbar_wait_t<kTcWait>(&tempty[b], ((g >> 1) - 1) & 1))) {
-          fail(4);
-          break;
-        }
-        tc_fence_after();
-        const unsigned char* bt = smem + L::XOFF + s * L::XB;
-        const uint32_t td = tmem + (uint32_t)b * kTcRows;
-        const uint32_t ta = tmem + L::ACOL + (uint32_t)ab * L::AW;
+    // ---------------- MMA issuer: the converged warp computes the operands,
+    // one elected lane issues
+    const uint32_t idesc = idesc_n(npad);
+    const uint64_t bdesc0 = smem_desc(smem + L::XOFF, 128, L::RB * 8);
+    for (int g = 0; g < G; ++g) {
+      const int s = g % NS, b = g & 1, ab = g % NA;
+      int ok = 1;
+      if (lane == 0)
+        ok = (!stop() && mbar_wait_t<kTcWait>(&sfull[s], (g / NS) & 1) &&
+              mbar_wait_t<kTcWait>(&afull[ab], (g / NA) & 1) &&
+              (g < 2 || mbar_wait_t<kTcWait>(&tempty[b], ((g >> 1) - 1) & 1)))
+                 ? 1
+                 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        if (lane == 0) fail(4);
+        break;
+      }
+      tc_fence_after();
+      // descriptor start address in 16-byte units: stage offset, 256 B per k step
+      const uint64_t bd = bdesc0 + (uint64_t)((s * L::XB) >> 4);
+      const uint32_t td = tmem + (uint32_t)b * kTcRows;
+      const uint32_t ta = tmem + L::ACOL + (uint32_t)ab * L::AW;
 #pragma unroll
-        for (int kk = 0; kk < KSTEPS; ++kk)
-          umma_f16_ts(td, ta + (uint32_t)kk * 8u, smem_desc(bt + kk * 256, 128, GS * 2 * 8), idesc,
-                      kk > 0 ? 1u : 0u);
+      for (int kk = 0; kk < L::KSTEPS; ++kk)
+        if (elect_one()) umma_f16_ts(td, ta + (uint32_t)kk * 8u, bd + (uint64_t)(kk * 16), idesc, kk > 0 ? 1u : 0u);
+      if (elect_one()) {
         umma_commit(&aempty[ab]);
         umma_commit(&tfull[b]);
         umma_commit(&sempty[s]);
       }
+      __syncwarp();
     }
-    __syncwarp();
   } else if (warp < 6) {
     // ---------------- unpack: packed nibbles (fragment order) -> fp16 rows of
     // A in TMEM.  Thread = output channel r (TMEM lane; a warp owns lanes
@@ -407,20 +409,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // fragment word (low / high nibble of each byte).  Word wi of fragment
     // lane (g8, t) of quad qq holds k = qq*64 + 16 wi + 4 t + b, b = 0..3;
     // its column pair (qq*32 + wi*8 + 2t, + 1) holds k offsets (0, 2), (1, 3).
+    // A nibble n moved to fp16 mantissa bits 4..7 under exponent 2^6 reads
+    // 64 + n.
     const int r = (warp & 3) * 32 + lane;
     const int rl = r >> 4, g8 = r & 7, rot = g8 >> 1;
     const bool hi = (r & 8) != 0;
-    const uint32_t mask = hi ? 0x00F000F0u : 0x000F000Fu;
-    // (0x6400 | n) = 1024 + n and (0x6400 | n << 4) = 1024 + 16 n in fp16:
-    // one exact fma.f16x2 gives n
-    const uint32_t hmul = hi ? 0x2C002C00u : 0x3C003C00u;  // 1/16 : 1
-    const uint32_t hadd = hi ? 0xD400D400u : 0xE400E400u;  // -64 : -1024
+    const int sh0 = hi ? 0 : 4, sh1 = hi ? 8 : 4;  // bytes 0, 2: left; bytes 1, 3: right
+    const int rt = min(rt0 + rl, a.n_rt - 1);
+    const float4* szp = a.sz + (size_t)rt * a.groups * 8 + g8;
     for (int g = 0; g < G; ++g) {
-      const int s = g % NS, ab = g % kTcA;
+      const int s = g % NS, ab = g % NA;
+      const float4 zz = __ldg(szp + (size_t)g * 8);
       int ok = 1;
       if (lane == 0)
         ok = (!stop() && mbar_wait_t<kTcWait>(&sfull[s], (g / NS) & 1) &&
-              (g < kTcA || mbar_wait_t<kTcWait>(&aempty[ab], ((g / kTcA) - 1) & 1)))
+              (g < NA || mbar_wait_t<kTcWait>(&aempty[ab], ((g / NA) - 1) & 1)))
                  ? 1
                  : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -462,11 +465,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const uint32_t wv[4] = {u[t].x, u[t].y, u[t].z, u[t].w};
 #pragma unroll
           for (int wi = 0; wi < 4; ++wi) {
-            col[wi * 8 + 2 * t] = hfma2((wv[wi] & mask) | 0x64006400u, hmul, hadd);
-            col[wi * 8 + 2 * t + 1] = hfma2(((wv[wi] >> 8) & mask) | 0x64006400u, hmul, hadd);
+            col[wi * 8 + 2 * t] = ((wv[wi] << sh0) & 0x00F000F0u) | 0x54005400u;
+            col[wi * 8 + 2 * t + 1] = ((wv[wi] >> sh1) & 0x00F000F0u) | 0x54005400u;
           }
         }
         tmem_st32(ta + (uint32_t)qq * 32u, col);
+      }
+      {
+        // zero-point step: (-zh, -zh), (-zl, 0) against (Sh, Sl), (Sh, 0)
+        const float z = (hi ? zz.w : zz.y) + 64.0f;
+        const __half zh = __float2half_rn(z);
+        const __half zl = __float2half_rn(z - __half2float(zh));
+        const uint32_t nzh = (uint32_t)__half_as_ushort(zh) ^ 0x8000u;
+        const uint32_t nzl = (uint32_t)__half_as_ushort(zl) ^ 0x8000u;
+        const uint32_t zc[8] = {nzh | (nzh << 16), nzl, 0u, 0u, 0u, 0u, 0u, 0u};
+        tmem_st8(ta + (uint32_t)(GS / 2), zc);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -489,16 +502,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (int i = 0; i < 32; ++i) acc[i] = 0.f;
     griddep_wait();
     for (int g = 0; g < G; ++g) {
-      const int es = g % kTcEpi, b = g & 1;
+      const int b = g & 1;
       const float4 zz = __ldg(szp + (size_t)g * 8);
       const float sc = (r16 >> 3) ? zz.z : zz.x;
-      const float nzp = -((r16 >> 3) ? zz.w : zz.y);
       int ok = 1;
-      if (lane == 0)
-        ok = (!stop() && mbar_wait_t<kTcWait>(&tfull[b], (g >> 1) & 1) &&
-              mbar_wait_t<kTcWait>(&efull[es], (g / kTcEpi) & 1))
-                 ? 1
-                 : 0;
+      if (lane == 0) ok = (!stop() && mbar_wait_t<kTcWait>(&tfull[b], (g >> 1) & 1)) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) {
         if (lane == 0) fail(6);
@@ -517,21 +525,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[b]);
       if (active) {
-        const float4* s4 = reinterpret_cast<const float4*>(smem + L::EOFF + es * L::SB) + rq * 8;
 #pragma unroll
-        for (int i4 = 0; i4 < 8; ++i4) {
-          const float4 sv = s4[i4];
-          const float sa[4] = {sv.x, sv.y, sv.z, sv.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int i = i4 * 4 + e;
-            const float d = __uint_as_float(i < 16 ? d0[i & 15] : d1[i & 15]);
-            acc[i] = fmaf(sc, fmaf(nzp, sa[e], d), acc[i]);
-          }
+        for (int i = 0; i < 16; ++i) {
+          acc[i] = fmaf(sc, __uint_as_float(d0[i]), acc[i]);
+          acc[16 + i] = fmaf(sc, __uint_as_float(d1[i]), acc[16 + i]);
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&eempty[es]);
     }
     if (cvalid && active && !stop()) {
       const int n = rt * 16 + r16;
@@ -544,7 +543,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
   // every role is done; outstanding MMAs finished before the last tfull
   // phase, which the epilogue waited for (or the kernel failed, in which case
-  // the MMA thread waits here for its own last commit)
+  // the MMA warp waits here for its own last commit)
   __syncthreads();
   if (warp == 1) {
     if (lane == 0 && stop() && G > 0) mbar_wait_t<kTcWait>(&tfull[(G - 1) & 1], ((G - 1) >> 1) & 1);
@@ -621,7 +620,7 @@ int launch_tc(const Q4GWeight& w, const float* x, int64_t ldx, int m, float* y, 
   const int mts = (m + kTcRows - 1) / kTcRows;
   const int nts = (int)((w.rows + kTcChan - 1) / kTcChan);
   // scratch: the prepared tiles, then scale[m] and inv[m]
-  const size_t tiles = ((size_t)mts * G * L::XBYTES + 255) & ~(size_t)255;
+  const size_t tiles = ((size_t)mts * G * L::XB + 255) & ~(size_t)255;
   const size_t mpad = (size_t)mts * kTcRows;
   unsigned char* xp = nullptr;
   NIMF_TRY(prep_buffer(tiles + 2 * mpad * sizeof(float), st, &xp));
@@ -683,9 +682,10 @@ int launch_tc(const Q4GWeight& w, const float* x, int64_t ldx, int m, float* y, 
 
 }  // namespace
 
-// Group sizes 64 and 128 (256 would need more shared memory than a CTA has).
+// Group sizes 64 and 128 (256 would need more shared memory than a CTA has),
+// zero points within the fp16 split (others use the CUDA-core path).
 bool q4g_tc_supported(const Q4GWeight& w) {
-  return w.fast && (w.gs == 64 || w.gs == 128) && w.rows > 0 && w.k > 0;
+  return w.fast && w.tc_zp_ok && (w.gs == 64 || w.gs == 128) && w.rows > 0 && w.k > 0;
 }
 
 int q4g_gemm_tc(const Q4GWeight& w, const float* x, int64_t m, float* y, cudaStream_t st) {
