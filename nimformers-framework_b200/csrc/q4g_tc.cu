@@ -163,83 +163,107 @@ __host__ __device__ __forceinline__ uint32_t canon_off(int r, int k, int kbytes)
 
 // Per-row power-of-two scale of x: scale[r] = 2^e, inv[r] = 2^-e with the
 // row's largest finite magnitude times 2^e in [128, 256) (e = 0 for a zero
-// row; |e| <= 126 keeps both factors finite).  One warp per row.
+// row; |e| <= 126 keeps both factors finite).  One 128-thread block per row.
 __global__ void q4g_tc_rowscale(const float* __restrict__ x, int64_t ldx, int m, int k,
                                 float* __restrict__ scale, float* __restrict__ inv) {
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  __shared__ float part[4];
+  const int row = blockIdx.x;
   griddep_wait();  // x may be written by the previous kernel in the stream
-  if (row < m) {
-    const float* xr = x + (size_t)row * ldx;
-    float mx = 0.f;
-    for (int i = lane; i < k; i += 32) {
-      const float v = fabsf(__ldg(xr + i));
-      if (v <= 3.402823466e38f) mx = fmaxf(mx, v);  // skips inf and NaN
+  const float* xr = x + (size_t)row * ldx;
+  float mx = 0.f;
+  auto take = [&](float v) {
+    v = fabsf(v);
+    if (v <= 3.402823466e38f) mx = fmaxf(mx, v);  // skips inf and NaN
+  };
+  if (((ldx & 3) == 0) && ((reinterpret_cast<uintptr_t>(xr) & 15) == 0)) {
+    const float4* x4 = reinterpret_cast<const float4*>(xr);
+    const int k4 = k >> 2;
+    for (int i = threadIdx.x; i < k4; i += blockDim.x) {
+      const float4 v = __ldg(x4 + i);
+      take(v.x);
+      take(v.y);
+      take(v.z);
+      take(v.w);
     }
+    for (int i = (k4 << 2) + threadIdx.x; i < k; i += blockDim.x) take(__ldg(xr + i));
+  } else {
+    for (int i = threadIdx.x; i < k; i += blockDim.x) take(__ldg(xr + i));
+  }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if (lane == 0) {
-      int ex = 0;
-      if (mx > 0.f) frexpf(mx, &ex);  // mx = f 2^ex, f in [0.5, 1)
-      const int e = mx > 0.f ? max(-126, min(126, 8 - ex)) : 0;
-      scale[row] = ldexpf(1.0f, e);
-      inv[row] = ldexpf(1.0f, -e);
-    }
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mx = fmaxf(fmaxf(part[0], part[1]), fmaxf(part[2], part[3]));
+    int ex = 0;
+    if (mx > 0.f) frexpf(mx, &ex);  // mx = f 2^ex, f in [0.5, 1)
+    const int e = mx > 0.f ? max(-126, min(126, 8 - ex)) : 0;
+    scale[row] = ldexpf(1.0f, e);
+    inv[row] = ldexpf(1.0f, -e);
   }
   griddep_launch_dependents();
 }
 
-// x tile preparation, one CTA per (kTcRows-row tile mt, group g), thread = row.
-// Each row is RB = 2 gs + 32 bytes of K-major fp16 in the canonical layout:
+// x tile preparation.  Each prepared tile (mt, g) holds kTcRows rows of
+// RB = 2 gs + 32 bytes of K-major fp16 in the canonical layout:
 //   gs values fp16(x * scale[row]) in the MMA's K order (within every aligned
 //   4 k the positions hold k offsets 0, 2, 1, 3: the order in which the
 //   unpack warps pair a fragment word's nibbles), then the zero-point step
 //   [Sh, Sl, Sh, 0 x 13] with S the fp32 sum of the row's fp16 values,
 //   Sh = fp16(S), Sl = fp16(S - Sh).
-// Rows past m and k past K are zero.
-__global__ void q4g_tc_prep_x(const float* __restrict__ x, int64_t ldx, int m, int k, int gs,
-                              int groups, const float* __restrict__ scale,
-                              unsigned char* __restrict__ out) {
-  const int mt = blockIdx.x / groups, g = blockIdx.x - (blockIdx.x / groups) * groups;
-  const int r = threadIdx.x;
-  const int row = mt * kTcRows + r;
+// Rows past m and k past K are zero.  Thread = (row, 8 consecutive k); the
+// gs / 8 threads of a row are consecutive lanes.  Block = 256 threads =
+// 2048 / gs rows of one tile and group; grid = (tiles x kTcRows / rows per
+// block, groups).
+__global__ void __launch_bounds__(256) q4g_tc_prep_x(const float* __restrict__ x, int64_t ldx,
+                                                     int m, int k, int gs,
+                                                     const float* __restrict__ scale,
+                                                     unsigned char* __restrict__ out) {
+  const int cg = gs >> 3;                       // threads per row (8 or 16)
+  const int rpb = 256 / cg;                     // rows per block
+  const int g = blockIdx.y, groups = gridDim.y;
+  const int grow = blockIdx.x * rpb + (int)threadIdx.x / cg;  // row over all tiles
+  const int c8 = (int)threadIdx.x % cg;
+  const int mt = grow / kTcRows, r = grow % kTcRows;
   const int rb = 2 * gs + 32;
-  unsigned char* base = out + (size_t)blockIdx.x * kTcRows * rb;
+  unsigned char* base = out + ((size_t)mt * groups + g) * kTcRows * rb;
   griddep_wait();  // scale comes from the previous kernel
-  const bool rv = row < m;
-  const float sf = rv ? __ldg(scale + row) : 0.f;
-  const float* xr = x + (size_t)(rv ? row : 0) * ldx + (size_t)g * gs;
-  const int kvalid = rv ? max(0, min(gs, k - g * gs)) : 0;
-  const bool vec = kvalid == gs && ((ldx & 3) == 0) && ((reinterpret_cast<uintptr_t>(xr) & 15) == 0);
-  float sum = 0.f;
-  for (int c = 0; c < gs; c += 8) {
-    float v[8];
-    if (vec) {
-      const float4 a = __ldg(reinterpret_cast<const float4*>(xr + c));
-      const float4 b = __ldg(reinterpret_cast<const float4*>(xr + c + 4));
-      v[0] = a.x; v[1] = a.z; v[2] = a.y; v[3] = a.w;
-      v[4] = b.x; v[5] = b.z; v[6] = b.y; v[7] = b.w;
-    } else {
+  const bool rv = grow < m;
+  const float sf = rv ? __ldg(scale + grow) : 0.f;
+  const int c = c8 * 8;
+  const float* xr = x + (size_t)(rv ? grow : 0) * ldx + (size_t)g * gs + c;
+  const int kvalid = rv ? max(0, min(8, k - g * gs - c)) : 0;
+  float v[8];
+  if (kvalid == 8 && ((reinterpret_cast<uintptr_t>(xr) & 15) == 0)) {
+    const float4 p = __ldg(reinterpret_cast<const float4*>(xr));
+    const float4 q = __ldg(reinterpret_cast<const float4*>(xr + 4));
+    v[0] = p.x; v[1] = p.z; v[2] = p.y; v[3] = p.w;
+    v[4] = q.x; v[5] = q.z; v[6] = q.y; v[7] = q.w;
+  } else {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int i = c + (j & 4) + ((j & 1) << 1) + ((j >> 1) & 1);  // 0,2,1,3 within 4
-        v[j] = i < kvalid ? __ldg(xr + i) : 0.f;
-      }
+    for (int j = 0; j < 8; ++j) {
+      const int i = (j & 4) + ((j & 1) << 1) + ((j >> 1) & 1);  // 0,2,1,3 within 4
+      v[j] = i < kvalid ? __ldg(xr + i) : 0.f;
     }
-    uint32_t h[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const __half2 p = __floats2half2_rn(v[2 * j] * sf, v[2 * j + 1] * sf);
-      const float2 q = __half22float2(p);
-      sum += q.x + q.y;
-      h[j] = *reinterpret_cast<const uint32_t*>(&p);
-    }
-    *reinterpret_cast<uint4*>(base + canon_off(r, 2 * c, rb)) = make_uint4(h[0], h[1], h[2], h[3]);
   }
-  const __half sh = __float2half_rn(sum);
-  const __half sl = __float2half_rn(sum - __half2float(sh));
-  const uint32_t hs = __half_as_ushort(sh), ls = __half_as_ushort(sl);
-  *reinterpret_cast<uint4*>(base + canon_off(r, 2 * gs, rb)) = make_uint4(hs | (ls << 16), hs, 0u, 0u);
-  *reinterpret_cast<uint4*>(base + canon_off(r, 2 * gs + 16, rb)) = make_uint4(0u, 0u, 0u, 0u);
+  uint32_t h[4];
+  float sum = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const __half2 p = __floats2half2_rn(v[2 * j] * sf, v[2 * j + 1] * sf);
+    const float2 q = __half22float2(p);
+    sum += q.x + q.y;
+    h[j] = *reinterpret_cast<const uint32_t*>(&p);
+  }
+  *reinterpret_cast<uint4*>(base + canon_off(r, 2 * c, rb)) = make_uint4(h[0], h[1], h[2], h[3]);
+  for (int o = cg >> 1; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if (c8 == 0) {
+    const __half sh = __float2half_rn(sum);
+    const __half sl = __float2half_rn(sum - __half2float(sh));
+    const uint32_t hs = __half_as_ushort(sh), ls = __half_as_ushort(sl);
+    *reinterpret_cast<uint4*>(base + canon_off(r, 2 * gs, rb)) = make_uint4(hs | (ls << 16), hs, 0u, 0u);
+    *reinterpret_cast<uint4*>(base + canon_off(r, 2 * gs + 16, rb)) = make_uint4(0u, 0u, 0u, 0u);
+  }
   griddep_launch_dependents();
 }
 
@@ -637,8 +661,8 @@ int launch_tc(const Q4GWeight& w, const float* x, int64_t ldx, int m, float* y, 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)((m + 7) / 8), 1, 1);
-    cfg.blockDim = dim3(256, 1, 1);
+    cfg.gridDim = dim3((unsigned)m, 1, 1);
+    cfg.blockDim = dim3(128, 1, 1);
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
@@ -646,12 +670,12 @@ int launch_tc(const Q4GWeight& w, const float* x, int64_t ldx, int m, float* y, 
   }
   {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(mts * G), 1, 1);
-    cfg.blockDim = dim3(kTcRows, 1, 1);
+    cfg.gridDim = dim3((unsigned)(mpad * L::GS / 2048), (unsigned)G, 1);
+    cfg.blockDim = dim3(256, 1, 1);
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    NIMF_CUDA_TRY(cudaLaunchKernelEx(&cfg, q4g_tc_prep_x, x, ldx, m, (int)w.k, L::GS, G,
+    NIMF_CUDA_TRY(cudaLaunchKernelEx(&cfg, q4g_tc_prep_x, x, ldx, m, (int)w.k, L::GS,
                                      (const float*)scale, xp));
   }
   TcArgs a;
