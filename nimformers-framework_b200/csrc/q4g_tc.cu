@@ -25,9 +25,10 @@
 // one elected lane.
 //
 // Warps: 0 producer (bulk copy of the prepared x tile, tensor-map load of the
-// packed weights), 1 TMEM owner and MMA issuer, 2-5 unpack (thread = output
-// channel = TMEM lane), 6-21 epilogue (warp w reads TMEM lanes 32 (w % 4) ..
-// + 31 = output channels, for x rows 32 ((w - 6) / 4) .. + 31).
+// packed weights), 1 TMEM owner and MMA issuer, 2-9 unpack in two sets of 4
+// taking alternate groups (thread = output channel = TMEM lane), 10-17
+// epilogue (warp w reads TMEM lanes 32 (w % 4) .. + 31 = output channels,
+// for x rows 64 ((w - 10) / 4) .. + 63).
 // Every wait is bounded; on expiry the kernel records an error, lets the
 // other roles run out and still frees its TMEM.
 #include <cuda.h>
@@ -44,8 +45,13 @@ namespace {
 
 constexpr int kTcRows = 128;      // x rows per CTA tile
 constexpr int kTcChan = 128;      // output channels per CTA tile (8 row tiles)
-constexpr int kTcEpiWarps = 16;   // 4 TMEM lane quarters x 4 row quarters
-constexpr int kTcThreads = (6 + kTcEpiWarps) * 32;
+constexpr int kTcUnpWarps = 8;    // two sets of 4 (TMEM lane quarters), alternate groups
+constexpr int kTcEpiWarps = 8;    // 4 TMEM lane quarters x 2 row halves
+constexpr int kTcEpi0 = 2 + kTcUnpWarps;   // first epilogue warp
+constexpr int kTcThreads = (kTcEpi0 + kTcEpiWarps) * 32;
+#ifndef NIMF_TC_ROTATE
+#define NIMF_TC_ROTATE 1
+#endif
 constexpr uint32_t kTmemCols = 512;
 #ifndef NIMF_TC_WAIT
 #define NIMF_TC_WAIT 0
@@ -426,7 +432,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       __syncwarp();
     }
-  } else if (warp < 6) {
+  } else if (warp < kTcEpi0) {
     // ---------------- unpack: packed nibbles (fragment order) -> fp16 rows of
     // A in TMEM.  Thread = output channel r (TMEM lane; a warp owns lanes
     // 32 (warp % 4) .. + 31); rows g8 and g8 + 8 of a row tile share a
@@ -436,12 +442,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // A nibble n moved to fp16 mantissa bits 4..7 under exponent 2^6 reads
     // 64 + n.
     const int r = (warp & 3) * 32 + lane;
-    const int rl = r >> 4, g8 = r & 7, rot = g8 >> 1;
+    const int uset = (warp - 2) >> 2;
+    const int rl = r >> 4, g8 = r & 7, rot = NIMF_TC_ROTATE ? (g8 >> 1) : 0;
     const bool hi = (r & 8) != 0;
     const int sh0 = hi ? 0 : 4, sh1 = hi ? 8 : 4;  // bytes 0, 2: left; bytes 1, 3: right
     const int rt = min(rt0 + rl, a.n_rt - 1);
     const float4* szp = a.sz + (size_t)rt * a.groups * 8 + g8;
-    for (int g = 0; g < G; ++g) {
+    for (int g = uset; g < G; g += 2) {
       const int s = g % NS, ab = g % NA;
       const float4 zz = __ldg(szp + (size_t)g * 8);
       int ok = 1;
@@ -469,14 +476,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (rl < nrt) u[j] = wsrc[(rl * KQG + qq) * 32 + g8 * 4 + ((j + rot) & 3)];
         }
         // back to fragment order: u[t] <- u[(t - rot) & 3]
-        if (rot & 1) {
+        if (NIMF_TC_ROTATE && (rot & 1)) {
           const uint4 t3 = u[3];
           u[3] = u[2];
           u[2] = u[1];
           u[1] = u[0];
           u[0] = t3;
         }
-        if (rot & 2) {
+        if (NIMF_TC_ROTATE && (rot & 2)) {
           const uint4 t0 = u[0], t1 = u[1];
           u[0] = u[2];
           u[1] = u[3];
@@ -514,16 +521,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     }
   } else {
-    // ---------------- epilogue: thread = output channel (TMEM lane), 32 x rows
-    const int quad = warp & 3, rq = (warp - 6) >> 2;
+    // ---------------- epilogue: thread = output channel (TMEM lane), 64 x rows
+    const int quad = warp & 3, rh = (warp - kTcEpi0) >> 2;
     const int ch = quad * 32 + lane;              // channel within the tile
     const int rt = rt0 + (ch >> 4), r16 = ch & 15;
     const bool cvalid = rt < a.n_rt && rt * 16 + r16 < a.rows;
-    const bool active = rq * 32 < npad;           // warp-uniform
+    const bool act0 = rh * 64 < npad, act1 = rh * 64 + 32 < npad;  // warp-uniform
     const float4* szp = a.sz + ((size_t)min(rt, a.n_rt - 1) * a.groups) * 8 + (r16 & 7);
-    float acc[32];
+    float acc[64];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+    for (int i = 0; i < 64; ++i) acc[i] = 0.f;
     griddep_wait();
     for (int g = 0; g < G; ++g) {
       const int b = g & 1;
@@ -537,30 +544,31 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         break;
       }
       tc_fence_after();
-      uint32_t d0[16], d1[16];
-      if (active) {
-        const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)b * kTcRows + rq * 32;
-        tmem_ld16(tl, d0);
-        tmem_ld16(tl + 16u, d1);
-        tmem_wait_ld();
+      const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)b * kTcRows + rh * 64;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (h == 0 ? act0 : act1) {
+          uint32_t d0[16], d1[16];
+          tmem_ld16(tl + h * 32, d0);
+          tmem_ld16(tl + h * 32 + 16u, d1);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            acc[h * 32 + i] = fmaf(sc, __uint_as_float(d0[i]), acc[h * 32 + i]);
+            acc[h * 32 + 16 + i] = fmaf(sc, __uint_as_float(d1[i]), acc[h * 32 + 16 + i]);
+          }
+        }
       }
       // the buffer may be refilled
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[b]);
-      if (active) {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          acc[i] = fmaf(sc, __uint_as_float(d0[i]), acc[i]);
-          acc[16 + i] = fmaf(sc, __uint_as_float(d1[i]), acc[16 + i]);
-        }
-      }
     }
-    if (cvalid && active && !stop()) {
+    if (cvalid && act0 && !stop()) {
       const int n = rt * 16 + r16;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int row = mt * kTcRows + rq * 32 + i;
+      for (int i = 0; i < 64; ++i) {
+        const int row = mt * kTcRows + rh * 64 + i;
         if (row < a.m) a.y[(size_t)row * a.ldy + n] = acc[i] * __ldg(a.xinv + row);
       }
     }
