@@ -302,6 +302,88 @@ def run_decode_7b(nimf, torch, steps, warmup):
     return out
 
 
+def prefill7b_flops(tokens):
+    """Multiply-add FLOPs of one 7B layer's projections for `tokens` rows."""
+    return 2 * tokens * (4 * D7 * D7 + 3 * F7 * D7)
+
+
+def run_prefill_7b(nimf, torch, steps, warmup, tokens=512, copies=4):
+    """TFLOP/s of the 7B-shape int4 prefill projections (tensor-core GEMM).
+
+    One step runs `copies` layers (distinct weight copies, 4 x 0.1 GB, more
+    than L2) of grouped q/k/v, o, grouped gate/up and down on x[tokens, 4096],
+    captured in one CUDA graph; weights are synthetic int4-g128 codes with
+    group scales and zeros as in the decode measurement.  Attention, norms and
+    the LM head are not on this path."""
+    import numpy as np
+    rng = np.random.default_rng(5)
+
+    def make(n, k):
+        ngr = k // GS
+        p = rng.integers(0, 256, size=n * (k // 2), dtype=np.uint8)
+        sc = rng.uniform(0.002, 0.004, size=n * ngr).astype(np.float32)
+        zp = rng.uniform(6.0, 9.0, size=n * ngr).astype(np.float32)
+        return p, sc, zp
+
+    hq, hg, hd = make(D7, D7), make(F7, D7), make(D7, F7)
+    layers = []
+    for _ in range(copies):
+        q, k, v, o = [nimf.Weight.q4g(*hq, D7, D7, GS) for _ in range(4)]
+        gate, up = [nimf.Weight.q4g(*hg, F7, D7, GS) for _ in range(2)]
+        down = nimf.Weight.q4g(*hd, D7, F7, GS)
+        layers.append((q, k, v, o, gate, up, down))
+    try:
+        dev = torch.device("cuda")
+        x = torch.randn(tokens, D7, device=dev)
+        qkv = torch.empty(3, tokens, D7, device=dev)
+        att = torch.empty(tokens, D7, device=dev)
+        gu = torch.empty(2, tokens, F7, device=dev)
+        dn = torch.empty(tokens, D7, device=dev)
+        stream = torch.cuda.Stream()
+
+        def step(st):
+            for (q, k, v, o, gate, up, down) in layers:
+                nimf.Weight.matmul_group_dev([q, k, v], x.data_ptr(), tokens,
+                                             [qkv[i].data_ptr() for i in range(3)], st)
+                o.matmul_dev(qkv[0].data_ptr(), tokens, att.data_ptr(), st)
+                nimf.Weight.matmul_group_dev([gate, up], att.data_ptr(), tokens,
+                                             [gu[0].data_ptr(), gu[1].data_ptr()], st)
+                down.matmul_dev(gu[0].data_ptr(), tokens, dn.data_ptr(), st)
+
+        with torch.cuda.stream(stream):
+            step(stream.cuda_stream)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step(stream.cuda_stream)
+        for _ in range(warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        graph.reset()
+    finally:
+        for lw in layers:
+            for w in lw:
+                w.free()
+    per_layer = ms / copies
+    tflops = prefill7b_flops(tokens) / (per_layer * 1e-3) / 1e12
+    pk, kind = peaks()
+    peak = float(pk.get("bf16_tflops", 1590.0)) if kind == "measured" else 1590.0
+    return {"tokens": tokens, "ms_per_layer": per_layer, "tflop_s": tflops,
+            "frac_of_bf16_peak": tflops / peak, "bf16_peak_tflop_s": peak,
+            "peak_source": kind,
+            "matmul_tok_s_32_layers": tokens / (32 * per_layer * 1e-3),
+            "launches_per_layer": 4 * 3,
+            "note": ("x prepared once per call (row scale + fp16 tiles) then one tcgen05 GEMM "
+                     "launch per call; %d layer copies per step, %d timed steps" % (copies, steps))}
+
+
 def run_ours(args, rank, world, local_rank):
     import numpy as np
     import torch
@@ -466,6 +548,9 @@ def run_ours(args, rank, world, local_rank):
     decode = None
     if world == 1 and args.decode_steps > 0:
         decode = run_decode_7b(nimf, torch, args.decode_steps, max(3, args.warmup // 4))
+    prefill = None
+    if world == 1 and args.prefill_steps > 0:
+        prefill = run_prefill_7b(nimf, torch, args.prefill_steps, 3)
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
@@ -480,6 +565,8 @@ def run_ours(args, rank, world, local_rank):
             line["cpu_baseline"] = cpu
         if decode is not None:
             line["decode_7b"] = decode
+        if prefill is not None:
+            line["prefill_7b"] = prefill
         print(json.dumps(line), flush=True)
     for wt in weights:
         wt.free()
@@ -495,6 +582,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--decode-steps", type=int, default=200,
                     help="timed steps of the 7B-shape decode measurement (0: skip)")
+    ap.add_argument("--prefill-steps", type=int, default=20,
+                    help="timed steps of the 7B-shape prefill measurement (0: skip)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 

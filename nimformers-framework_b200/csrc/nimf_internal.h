@@ -141,6 +141,8 @@ int q4g_dequant(const Q4GWeight& w, float* out, cudaStream_t st);
 // the weight's group size has a tensor-core kernel.
 bool q4g_tc_supported(const Q4GWeight& w);
 int q4g_gemm_tc(const Q4GWeight& w, const float* x, int64_t m, float* y, cudaStream_t st);
+int q4g_gemm_tc_group(const Q4GWeight* const* ws, int count, const float* x, int64_t m,
+                      float* const* ys, cudaStream_t st);
 
 int i8_gemv(const I8Weight& w, const float* x, int64_t m, float* y, cudaStream_t st);
 int i8_dequant(const I8Weight& w, float* out, cudaStream_t st);

@@ -1096,10 +1096,27 @@ int q4g_gemv_group(const Q4GWeight* const* ws, int count, const float* x, int64_
   // once per 128 rows of x instead of once per 8)
   if (m > kTcMinRows) {
     bool tc = true;
-    for (int i = 0; i < count; ++i) tc = tc && (ws[i]->rows == 0 || q4g_tc_supported(*ws[i]));
+    int64_t gs0 = 0;
+    for (int i = 0; i < count; ++i) {
+      if (ws[i]->rows == 0) continue;
+      if (gs0 == 0) gs0 = ws[i]->gs;
+      tc = tc && q4g_tc_supported(*ws[i]) && ws[i]->gs == gs0;
+    }
     if (tc) {
-      for (int i = 0; i < count; ++i)
-        if (ws[i]->rows > 0) NIMF_TRY(q4g_gemm_tc(*ws[i], x, m, ys[i], st));
+      // weights with rows share one x preparation and one launch per 4
+      const Q4GWeight* tw[64];
+      float* ty[64];
+      int n = 0;
+      for (int i = 0; i < count; ++i) {
+        if (ws[i]->rows <= 0) continue;
+        tw[n] = ws[i];
+        ty[n] = ys[i];
+        if (++n == 64) {
+          NIMF_TRY(q4g_gemm_tc_group(tw, n, x, m, ty, st));
+          n = 0;
+        }
+      }
+      if (n > 0) NIMF_TRY(q4g_gemm_tc_group(tw, n, x, m, ty, st));
       return NIMF_OK;
     }
   }

@@ -273,15 +273,28 @@ __global__ void __launch_bounds__(256) q4g_tc_prep_x(const float* __restrict__ x
   griddep_launch_dependents();
 }
 
-struct TcArgs {
-  const uint4* frag;     // weight fragments, row tile 0
+// One launch covers up to kTcMaxW weights that share x (a grouped call):
+// CTA column blockIdx.x belongs to weight i for nt0[i] <= blockIdx.x < nt0[i+1].
+constexpr int kTcMaxW = 4;
+struct TcW {
   const float4* sz;      // scale/zero pairs, row tile 0
+  float* y;              // [m][ldy]
+  int64_t ldy;
+  int rows, n_rt;
+};
+struct TcArgs {
+  TcW w[kTcMaxW];
+  int nt0[kTcMaxW];
+  int nw;
   const unsigned char* xp;  // prepared x, [mt][g]
   const float* xinv;     // per-row 2^-e of x's scale
-  float* y;
-  int64_t ldy;
-  int m, rows, n_rt, kq_total, groups;
+  int m, groups;
   int* err;
+};
+// the weights' fragments as 2-D tensors of 4-byte elements, one row per row
+// tile (kq_total * 128 elements); box = 8 row tiles x one group
+struct TcMaps {
+  CUtensorMap m[kTcMaxW];
 };
 
 // Shared memory (offsets from the 1024-aligned base) and TMEM columns
@@ -306,11 +319,9 @@ struct TcLayout {
   static_assert(TOTAL <= 227 * 1024, "shared memory");
 };
 
-// wmap: the weight fragments as a 2-D tensor of 4-byte elements, one row per
-// row tile (kq_total * 128 elements); its box is 8 row tiles x one group.
 template <int KQG>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    q4g_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap wmap) {
+    q4g_tc_kernel(const TcArgs a, const __grid_constant__ TcMaps maps) {
   using L = TcLayout<KQG>;
   constexpr int GS = L::GS;
   constexpr int NS = L::STAGES, NA = L::ABUF;
@@ -326,10 +337,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   int* failed = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nt = blockIdx.x, mt = blockIdx.y;
+  int wsel = 0;
+  for (int i = 1; i < a.nw; ++i)
+    if ((int)blockIdx.x >= a.nt0[i]) wsel = i;
+  const TcW W = a.w[wsel];
+  const CUtensorMap* wmap = &maps.m[wsel];
+  const int nt = (int)blockIdx.x - a.nt0[wsel], mt = blockIdx.y;
   const int G = a.groups;
   const int rt0 = nt * 8;
-  const int nrt = max(0, min(8, a.n_rt - rt0));
+  const int nrt = max(0, min(8, W.n_rt - rt0));
   // x rows of this tile, rounded up to the MMA's N granule
   const int nrows = min(kTcRows, a.m - mt * kTcRows);
   const int npad = (nrows + 15) & ~15;
@@ -388,7 +404,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (elect_one()) {
         mbar_arrive_expect_tx(&sfull[s], xbytes + L::WBYTES);
         bulk_g2s(xs, src, xbytes, &sfull[s]);
-        tma_load_2d(ws, &wmap, g * KQG * 128, rt0, &sfull[s]);
+        tma_load_2d(ws, wmap, g * KQG * 128, rt0, &sfull[s]);
       }
       __syncwarp();
       last = g;
@@ -446,8 +462,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int rl = r >> 4, g8 = r & 7, rot = NIMF_TC_ROTATE ? (g8 >> 1) : 0;
     const bool hi = (r & 8) != 0;
     const int sh0 = hi ? 0 : 4, sh1 = hi ? 8 : 4;  // bytes 0, 2: left; bytes 1, 3: right
-    const int rt = min(rt0 + rl, a.n_rt - 1);
-    const float4* szp = a.sz + (size_t)rt * a.groups * 8 + g8;
+    const int rt = min(rt0 + rl, W.n_rt - 1);
+    const float4* szp = W.sz + (size_t)rt * a.groups * 8 + g8;
     for (int g = uset; g < G; g += 2) {
       const int s = g % NS, ab = g % NA;
       const float4 zz = __ldg(szp + (size_t)g * 8);
@@ -525,9 +541,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int quad = warp & 3, rh = (warp - kTcEpi0) >> 2;
     const int ch = quad * 32 + lane;              // channel within the tile
     const int rt = rt0 + (ch >> 4), r16 = ch & 15;
-    const bool cvalid = rt < a.n_rt && rt * 16 + r16 < a.rows;
+    const bool cvalid = rt < W.n_rt && rt * 16 + r16 < W.rows;
     const bool act0 = rh * 64 < npad, act1 = rh * 64 + 32 < npad;  // warp-uniform
-    const float4* szp = a.sz + ((size_t)min(rt, a.n_rt - 1) * a.groups) * 8 + (r16 & 7);
+    const float4* szp = W.sz + ((size_t)min(rt, W.n_rt - 1) * a.groups) * 8 + (r16 & 7);
     float acc[64];
 #pragma unroll
     for (int i = 0; i < 64; ++i) acc[i] = 0.f;
@@ -569,7 +585,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
       for (int i = 0; i < 64; ++i) {
         const int row = mt * kTcRows + rh * 64 + i;
-        if (row < a.m) a.y[(size_t)row * a.ldy + n] = acc[i] * __ldg(a.xinv + row);
+        if (row < a.m) W.y[(size_t)row * W.ldy + n] = acc[i] * __ldg(a.xinv + row);
       }
     }
   }
@@ -644,13 +660,14 @@ int weight_tensor_map(const Q4GWeight& w, int kqg, CUtensorMap* tm) {
 }
 
 template <int KQG>
-int launch_tc(const Q4GWeight& w, const float* x, int64_t ldx, int m, float* y, int64_t ldy,
+int launch_tc(const Q4GWeight* const* ws, int count, const float* x, int m, float* const* ys,
               cudaStream_t st) {
   using L = TcLayout<KQG>;
   Context* c = ctx();
-  const int G = (int)w.groups;
+  const Q4GWeight& w0 = *ws[0];
+  const int G = (int)w0.groups;
+  const int64_t ldx = w0.k;
   const int mts = (m + kTcRows - 1) / kTcRows;
-  const int nts = (int)((w.rows + kTcChan - 1) / kTcChan);
   // scratch: the prepared tiles, then scale[m] and inv[m]
   const size_t tiles = ((size_t)mts * G * L::XB + 255) & ~(size_t)255;
   const size_t mpad = (size_t)mts * kTcRows;
@@ -674,7 +691,7 @@ int launch_tc(const Q4GWeight& w, const float* x, int64_t ldx, int m, float* y, 
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    NIMF_CUDA_TRY(cudaLaunchKernelEx(&cfg, q4g_tc_rowscale, x, ldx, m, (int)w.k, scale, inv));
+    NIMF_CUDA_TRY(cudaLaunchKernelEx(&cfg, q4g_tc_rowscale, x, ldx, m, (int)w0.k, scale, inv));
   }
   {
     cudaLaunchConfig_t cfg = {};
@@ -683,32 +700,43 @@ int launch_tc(const Q4GWeight& w, const float* x, int64_t ldx, int m, float* y, 
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    NIMF_CUDA_TRY(cudaLaunchKernelEx(&cfg, q4g_tc_prep_x, x, ldx, m, (int)w.k, L::GS,
+    NIMF_CUDA_TRY(cudaLaunchKernelEx(&cfg, q4g_tc_prep_x, x, ldx, m, (int)w0.k, L::GS,
                                      (const float*)scale, xp));
   }
-  TcArgs a;
-  a.frag = (const uint4*)w.frag;
-  a.sz = (const float4*)w.sz;
-  a.xp = xp;
-  a.xinv = inv;
-  a.y = y;
-  a.ldy = ldy;
-  a.m = m;
-  a.rows = (int)w.rows;
-  a.n_rt = (int)w.n_rt;
-  a.kq_total = (int)w.kq_total;
-  a.groups = G;
-  a.err = c ? c->dev_err : nullptr;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)nts, (unsigned)mts, 1);
-  cfg.blockDim = dim3(kTcThreads, 1, 1);
-  cfg.dynamicSmemBytes = L::TOTAL;
-  cfg.stream = st;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  CUtensorMap wmap;
-  NIMF_TRY(weight_tensor_map(w, KQG, &wmap));
-  NIMF_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a, wmap));
+  // one launch per kTcMaxW weights, all reading the same prepared x
+  for (int i0 = 0; i0 < count; i0 += kTcMaxW) {
+    TcArgs a = {};
+    TcMaps maps;
+    int nts = 0;
+    a.nw = 0;
+    for (int i = i0; i < count && i < i0 + kTcMaxW; ++i) {
+      const Q4GWeight& w = *ws[i];
+      TcW& t = a.w[a.nw];
+      t.sz = (const float4*)w.sz;
+      t.y = ys[i];
+      t.ldy = w.rows;
+      t.rows = (int)w.rows;
+      t.n_rt = (int)w.n_rt;
+      a.nt0[a.nw] = nts;
+      NIMF_TRY(weight_tensor_map(w, KQG, &maps.m[a.nw]));
+      nts += (int)((w.rows + kTcChan - 1) / kTcChan);
+      ++a.nw;
+    }
+    for (int i = a.nw; i < kTcMaxW; ++i) a.nt0[i] = nts;
+    a.xp = xp;
+    a.xinv = inv;
+    a.m = m;
+    a.groups = G;
+    a.err = c ? c->dev_err : nullptr;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)nts, (unsigned)mts, 1);
+    cfg.blockDim = dim3(kTcThreads, 1, 1);
+    cfg.dynamicSmemBytes = L::TOTAL;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    NIMF_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a, maps));
+  }
   return NIMF_OK;
 }
 
@@ -720,14 +748,26 @@ bool q4g_tc_supported(const Q4GWeight& w) {
   return w.fast && w.tc_zp_ok && (w.gs == 64 || w.gs == 128) && w.rows > 0 && w.k > 0;
 }
 
-int q4g_gemm_tc(const Q4GWeight& w, const float* x, int64_t m, float* y, cudaStream_t st) {
-  if (m <= 0 || w.rows <= 0) return NIMF_OK;
+// ws[0..count) share x (same K and group size, all q4g_tc_supported, rows > 0)
+int q4g_gemm_tc_group(const Q4GWeight* const* ws, int count, const float* x, int64_t m,
+                      float* const* ys, cudaStream_t st) {
+  if (m <= 0 || count <= 0) return NIMF_OK;
   if (m > 0x7fffffff / 2) return set_error(NIMF_ERR_SHAPE, "prefill GEMM: M = %lld", (long long)m);
-  switch (w.gs) {
-    case 64: return launch_tc<1>(w, x, w.k, (int)m, y, w.rows, st);
-    case 128: return launch_tc<2>(w, x, w.k, (int)m, y, w.rows, st);
+  for (int i = 1; i < count; ++i)
+    if (ws[i]->gs != ws[0]->gs || ws[i]->k != ws[0]->k)
+      return set_error(NIMF_ERR_SHAPE, "prefill GEMM: grouped weights differ in K or group size");
+  switch (ws[0]->gs) {
+    case 64: return launch_tc<1>(ws, count, x, (int)m, ys, st);
+    case 128: return launch_tc<2>(ws, count, x, (int)m, ys, st);
   }
-  return set_error(NIMF_ERR_UNSUPPORTED, "prefill GEMM: group size %lld", (long long)w.gs);
+  return set_error(NIMF_ERR_UNSUPPORTED, "prefill GEMM: group size %lld", (long long)ws[0]->gs);
+}
+
+int q4g_gemm_tc(const Q4GWeight& w, const float* x, int64_t m, float* y, cudaStream_t st) {
+  if (w.rows <= 0) return NIMF_OK;
+  const Q4GWeight* ws[1] = {&w};
+  float* ys[1] = {y};
+  return q4g_gemm_tc_group(ws, 1, x, m, ys, st);
 }
 
 }  // namespace nimf

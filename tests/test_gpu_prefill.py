@@ -81,3 +81,54 @@ def test_prefill_zero_and_large_x(nimf_gpu):
     ref = O.dequant_matmul_q4(x, p, s, z, m, k, n, gs, ngr)
     assert rel_err(w.matmul(x, m), ref) <= TOL
     w.free()
+
+
+def test_prefill_group_of_six_shares_one_x_preparation(nimf_gpu):
+    """More weights than one launch takes (four): two launches, one prepared x."""
+    k, gs, m = 512, 64, 150
+    shapes = [128, 64, 200, 16, 130, 256]
+    ws, qs = [], []
+    for i, n in enumerate(shapes):
+        p, s, z, ngr = quantized(n, k, gs, seed=60 + i)
+        qs.append((p, s, z, ngr))
+        ws.append(nimf_gpu.Weight.q4g(p, s, z, n, k, gs))
+    x = np.random.default_rng(8).standard_normal((m, k)).astype(np.float32)
+    ys = nimf_gpu.Weight.matmul_group(ws, x, m)
+    for w, y, (p, s, z, ngr), n in zip(ws, ys, qs, shapes):
+        ref = O.dequant_matmul_q4(x, p, s, z, m, k, n, gs, ngr)
+        assert rel_err(y, ref) <= TOL
+        w.free()
+
+
+def test_prefill_mixed_group_sizes_in_one_call(nimf_gpu):
+    """Weights of different group sizes sharing x run as one call each."""
+    k, m = 512, 48
+    specs = [(96, 64), (80, 128)]
+    ws, qs = [], []
+    for i, (n, gs) in enumerate(specs):
+        p, s, z, ngr = quantized(n, k, gs, seed=70 + i)
+        qs.append((p, s, z, ngr, n, gs))
+        ws.append(nimf_gpu.Weight.q4g(p, s, z, n, k, gs))
+    x = np.random.default_rng(9).standard_normal((m, k)).astype(np.float32)
+    ys = nimf_gpu.Weight.matmul_group(ws, x, m)
+    for w, y, (p, s, z, ngr, n, gs) in zip(ws, ys, qs):
+        ref = O.dequant_matmul_q4(x, p, s, z, m, k, n, gs, ngr)
+        assert rel_err(y, ref) <= TOL
+        w.free()
+
+
+def test_prefill_zero_points_outside_fp16_split(nimf_gpu):
+    """A weight whose zero points do not fit the split-fp16 zero-point step
+    (|zp| >= 60000) is computed on the CUDA-core path, still to the bar."""
+    n, k, gs, m = 64, 256, 128, 40
+    rng = np.random.default_rng(12)
+    p = rng.integers(0, 256, size=n * k // 2, dtype=np.uint8)
+    s = rng.uniform(1e-6, 2e-6, size=n * 2).astype(np.float32)
+    z = rng.uniform(6.0, 9.0, size=n * 2).astype(np.float32)
+    z[5] = -70000.0
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    w = nimf_gpu.Weight.q4g(p, s, z, n, k, gs)
+    y = w.matmul(x, m)
+    w.free()
+    ref = O.dequant_matmul_q4(x, p, s, z, m, k, n, gs, 2)
+    assert rel_err(y, ref) <= TOL
