@@ -274,7 +274,7 @@ __global__ void __launch_bounds__(256) q4g_tc_prep_x(const float* __restrict__ x
 }
 
 // One launch covers up to kTcMaxW weights that share x (a grouped call):
-// CTA column blockIdx.x belongs to weight i for nt0[i] <= blockIdx.x < nt0[i+1].
+// channel tile blockIdx.y belongs to weight i for nt0[i] <= blockIdx.y < nt0[i+1].
 constexpr int kTcMaxW = 4;
 struct TcW {
   const float4* sz;      // scale/zero pairs, row tile 0
@@ -337,12 +337,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   int* failed = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // blockIdx.x = x tile (fastest, so the CTAs reading one weight tile run
+  // together and it comes from DRAM once), blockIdx.y = channel tile
   int wsel = 0;
   for (int i = 1; i < a.nw; ++i)
-    if ((int)blockIdx.x >= a.nt0[i]) wsel = i;
+    if ((int)blockIdx.y >= a.nt0[i]) wsel = i;
   const TcW W = a.w[wsel];
   const CUtensorMap* wmap = &maps.m[wsel];
-  const int nt = (int)blockIdx.x - a.nt0[wsel], mt = blockIdx.y;
+  const int nt = (int)blockIdx.y - a.nt0[wsel], mt = blockIdx.x;
   const int G = a.groups;
   const int rt0 = nt * 8;
   const int nrt = max(0, min(8, W.n_rt - rt0));
@@ -668,6 +670,7 @@ int launch_tc(const Q4GWeight* const* ws, int count, const float* x, int m, floa
   const int G = (int)w0.groups;
   const int64_t ldx = w0.k;
   const int mts = (m + kTcRows - 1) / kTcRows;
+  if (G > 65535) return set_error(NIMF_ERR_SHAPE, "prefill GEMM: %d groups (max 65535)", G);
   // scratch: the prepared tiles, then scale[m] and inv[m]
   const size_t tiles = ((size_t)mts * G * L::XB + 255) & ~(size_t)255;
   const size_t mpad = (size_t)mts * kTcRows;
@@ -722,6 +725,8 @@ int launch_tc(const Q4GWeight* const* ws, int count, const float* x, int m, floa
       nts += (int)((w.rows + kTcChan - 1) / kTcChan);
       ++a.nw;
     }
+    if (nts > 65535)
+      return set_error(NIMF_ERR_SHAPE, "prefill GEMM: %d channel tiles in one launch (max 65535)", nts);
     for (int i = a.nw; i < kTcMaxW; ++i) a.nt0[i] = nts;
     a.xp = xp;
     a.xinv = inv;
@@ -729,7 +734,7 @@ int launch_tc(const Q4GWeight* const* ws, int count, const float* x, int m, floa
     a.groups = G;
     a.err = c ? c->dev_err : nullptr;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)nts, (unsigned)mts, 1);
+    cfg.gridDim = dim3((unsigned)mts, (unsigned)nts, 1);
     cfg.blockDim = dim3(kTcThreads, 1, 1);
     cfg.dynamicSmemBytes = L::TOTAL;
     cfg.stream = st;
