@@ -1,30 +1,31 @@
 // q4g.cu -- int4 asymmetric per-group weights (QuantTensor kind 3 with
 // groupSize > 0, quant.nim:131-167) on sm_100a: device repack, bit-exact
-// dequantisation and the decode GEMV y[M][N] = x[M][K] . W^T.
+// dequantisation and the decode GEMV y[M][N] = x[M][K] . W^T (M <= 16; more
+// rows go to the tensor-core GEMM in q4g_tc.cu).
 //
 // GEMV design (memory-bound: 0.5 B of weight per multiply-add):
-//   * Weights are repacked once at registration into mma.sync m16n8k16
+//   * Weights are repacked once at registration into mma.sync m16n8k32
 //     A-fragment order: for row tile rt (16 output rows) and k-quad kq (64 k),
-//     lane L of a warp owns one uint4 whose word j holds the 8 nibbles that
-//     lane needs for k-tile 4*kq+j.  A warp therefore streams 512 contiguous
-//     bytes per 128-bit load, and unpacking is 1 SHF + 4 LOP3 + 4 bf16 SUB
-//     per 8 nibbles (0x4300|n == bf16(128+n)).
-//   * The nibbles (exact small integers in bf16) multiply x on the tensor
-//     cores.  x is split into bf16 hi + lo parts (~2^-17 relative), so the
-//     products carry fp32-class accuracy; for M <= 4 the hi and lo parts sit
-//     in columns [0,4) and [4,8) of the same n=8 MMA, for M <= 8 they take
-//     two MMAs.
-//   * The asymmetric zero point is applied once per group by the algebra
-//     sum_k (n_k - zp) s x_k = s (sum_k n_k x_k - zp sum_k x_k); the per-group
-//     sums of x are computed in the CTA prologue.  Only the GEMV accumulation
-//     is refactored; the dequantised weights themselves (q4g_dequant below)
-//     are bit-identical to the reference.
-//   * Split-K over a thread-block cluster: the CTAs of one row band each take
-//     a range of groups, stage their slice of x (as ready-to-use B fragments)
-//     and their scales/zeros in shared memory, and reduce the partial y
-//     through distributed shared memory in rank order (deterministic).
-//   * Programmatic dependent launch: weights are prefetched before
-//     griddepcontrol.wait, so back-to-back GEMVs overlap prologue and tail.
+//     lane (g, t) of a warp owns one uint4 whose word 2h + half holds, in
+//     byte b, the nibbles of k = 32h + 16half + 4t + b for rows g (low
+//     nibble) and g + 8 (high nibble).  A row tile's quads are one
+//     contiguous range, streamed by bulk copies.
+//   * Persistent kernel, one CTA per SM: a producer warp fills an mbarrier
+//     ring with cp.async.bulk copies (before griddepcontrol.wait, so the next
+//     launch's weights stream while the previous kernel drains), 16 consumer
+//     warps and a merge warp.
+//   * x is quantised per CTA into two signed 8-bit digits,
+//     x ~= s (d0 + d1 / 256) with s = max|x| / 127; consumers unpack the
+//     nibbles with two masks and run mma.sync m16n8k32 s8 against the digits,
+//     so the dot products are exact integers.  Per group the fp32 epilogue
+//     applies sc s (A - zp D) with D the exact digit sum: the algebra of
+//     sum_k (n_k - zp) sc x_k.  The dequantised weights themselves
+//     (q4g_dequant below) are bit-identical to the reference.
+//   * The merge warp sums chunk partials of a row tile in a fixed order and
+//     writes y (deterministic).
+//   * Row tiles are cut into k-blocks of about 36 KB (direct mode); when
+//     there are too few row tiles for the SMs, CTAs of a thread-block cluster
+//     split K and reduce through distributed shared memory in rank order.
 #include <cooperative_groups.h>
 
 #include <algorithm>
