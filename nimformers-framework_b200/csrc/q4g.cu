@@ -457,19 +457,35 @@ q4g_gemv_kernel(const GemvArgs a) {
       }
       return v;
     };
-    // pass 1: max |x| per row (a warp's 32 items always belong to one row)
-    for (int it0 = threadIdx.x; it0 < a.m * f4p; it0 += nthr * kUnroll) {
+    const int total = a.m * f4p;
+    // pass 1: max |x| per row (a warp's 32 items always belong to one row).
+    // The first kCache items of every thread are loaded at once and kept in
+    // registers for pass 2; only a larger x is read a second time.
+    constexpr int kCache = MODE == 1 ? 8 : (KQG == 1 ? 0 : 4);
+    float4 cache[kCache > 0 ? kCache : 1];
+#pragma unroll
+    for (int r = 0; r < kCache; ++r) cache[r] = load4(threadIdx.x + r * nthr);
+    auto row_max = [&](const float4& v, int it) {
+      float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      if (lane == 0) atomicMax(&xmax[it / f4p], __float_as_uint(mx));
+    };
+#pragma unroll
+    for (int r = 0; r < kCache; ++r) {
+      const int it = threadIdx.x + r * nthr;
+      if (it - lane >= total) break;  // uniform across the warp (total is a multiple of 32)
+      row_max(cache[r], it);
+    }
+    for (int it0 = threadIdx.x + kCache * nthr; it0 - lane < total; it0 += nthr * kUnroll) {
       float4 vv[kUnroll];
 #pragma unroll
       for (int r = 0; r < kUnroll; ++r) vv[r] = load4(it0 + r * nthr);
 #pragma unroll
       for (int r = 0; r < kUnroll; ++r) {
         const int it = it0 + r * nthr;
-        if (it >= a.m * f4p) break;  // uniform across the warp
-        float mx = fmaxf(fmaxf(fabsf(vv[r].x), fabsf(vv[r].y)), fmaxf(fabsf(vv[r].z), fabsf(vv[r].w)));
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        if (lane == 0) atomicMax(&xmax[it / f4p], __float_as_uint(mx));
+        if (it - lane >= total) break;
+        row_max(vv[r], it);
       }
     }
     named_barrier(1, nthr);
@@ -477,52 +493,61 @@ q4g_gemv_kernel(const GemvArgs a) {
     // 4 k per word straight into the B fragment slots, and exact digit sums
     const int cols = MODE == 1 ? 2 * a.m : a.m;
     uint32_t* xw = reinterpret_cast<uint32_t*>(xs);
-    for (int it0 = threadIdx.x; it0 < a.m * f4p; it0 += nthr * kUnroll) {
+    auto digits = [&](const float4& v, int it) {
+      const int mrow = it / f4p, f = it - mrow * f4p;
+      const float mxv = __uint_as_float(xmax[mrow]);
+      const float inv = mxv > 0.f ? 127.0f / mxv : 0.f;
+      const float xv[4] = {v.x, v.y, v.z, v.w};
+      uint32_t w0 = 0, w1 = 0;
+      int s0 = 0, s1 = 0;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const float q = xv[b] * inv;
+        const int d0 = max(-127, min(127, __float2int_rn(q)));
+        const int d1 = max(-127, min(127, __float2int_rn((q - (float)d0) * 256.0f)));
+        w0 |= (uint32_t)(d0 & 0xFF) << (8 * b);
+        w1 |= (uint32_t)(d1 & 0xFF) << (8 * b);
+        s0 += d0;
+        s1 += d1;
+      }
+      if (f < f4) {
+        const int kt32 = f >> 3, j = f & 7;
+        const int half = j >> 2, tt = j & 3;
+        if (MODE == 1) {
+          xw[(((size_t)kt32 * cols + mrow) * 4 + tt) * 2 + half] = w0;
+          xw[(((size_t)kt32 * cols + a.m + mrow) * 4 + tt) * 2 + half] = w1;
+        } else {
+          xw[(((size_t)kt32 * cols + mrow) * 4 + tt) * 4 + half] = w0;
+          xw[(((size_t)kt32 * cols + mrow) * 4 + tt) * 4 + 2 + half] = w1;
+        }
+      }
+      // 64-k chunk sums over 16 lanes, then into the group's digit sums
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) {
+        s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+      }
+      if ((lane & 15) == 0 && f < f4) {
+        const int grp = (f >> 4) / KQG;
+        atomicAdd(&sdi[grp * 16 + mrow], s0);
+        atomicAdd(&sdi[grp * 16 + 8 + mrow], s1);
+      }
+    };
+#pragma unroll
+    for (int r = 0; r < kCache; ++r) {
+      const int it = threadIdx.x + r * nthr;
+      if (it - lane >= total) break;
+      digits(cache[r], it);
+    }
+    for (int it0 = threadIdx.x + kCache * nthr; it0 - lane < total; it0 += nthr * kUnroll) {
       float4 vv[kUnroll];
 #pragma unroll
       for (int r = 0; r < kUnroll; ++r) vv[r] = load4(it0 + r * nthr);
 #pragma unroll
       for (int r = 0; r < kUnroll; ++r) {
         const int it = it0 + r * nthr;
-        if (it >= a.m * f4p) break;
-        const int mrow = it / f4p, f = it - mrow * f4p;
-        const float mxv = __uint_as_float(xmax[mrow]);
-        const float inv = mxv > 0.f ? 127.0f / mxv : 0.f;
-        const float xv[4] = {vv[r].x, vv[r].y, vv[r].z, vv[r].w};
-        uint32_t w0 = 0, w1 = 0;
-        int s0 = 0, s1 = 0;
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          const float q = xv[b] * inv;
-          const int d0 = max(-127, min(127, __float2int_rn(q)));
-          const int d1 = max(-127, min(127, __float2int_rn((q - (float)d0) * 256.0f)));
-          w0 |= (uint32_t)(d0 & 0xFF) << (8 * b);
-          w1 |= (uint32_t)(d1 & 0xFF) << (8 * b);
-          s0 += d0;
-          s1 += d1;
-        }
-        if (f < f4) {
-          const int kt32 = f >> 3, j = f & 7;
-          const int half = j >> 2, tt = j & 3;
-          if (MODE == 1) {
-            xw[(((size_t)kt32 * cols + mrow) * 4 + tt) * 2 + half] = w0;
-            xw[(((size_t)kt32 * cols + a.m + mrow) * 4 + tt) * 2 + half] = w1;
-          } else {
-            xw[(((size_t)kt32 * cols + mrow) * 4 + tt) * 4 + half] = w0;
-            xw[(((size_t)kt32 * cols + mrow) * 4 + tt) * 4 + 2 + half] = w1;
-          }
-        }
-        // 64-k chunk sums over 16 lanes, then into the group's digit sums
-#pragma unroll
-        for (int o = 8; o > 0; o >>= 1) {
-          s0 += __shfl_xor_sync(0xffffffffu, s0, o);
-          s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-        }
-        if ((lane & 15) == 0 && f < f4) {
-          const int grp = (f >> 4) / KQG;
-          atomicAdd(&sdi[grp * 16 + mrow], s0);
-          atomicAdd(&sdi[grp * 16 + 8 + mrow], s1);
-        }
+        if (it - lane >= total) break;
+        digits(vv[r], it);
       }
     }
     named_barrier(1, nthr);
