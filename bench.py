@@ -384,6 +384,178 @@ def run_prefill_7b(nimf, torch, steps, warmup, tokens=512, copies=4):
                      "launch per call; %d layer copies per step, %d timed steps" % (copies, steps))}
 
 
+def graph_ms(torch, fn, steps, warmup):
+    """Milliseconds per replay of fn() captured in a CUDA graph (CUDA events on
+    the capturing stream, after warm-up replays)."""
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        fn(stream.cuda_stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        fn(stream.cuda_stream)
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    graph.reset()
+    return ms
+
+
+def run_formats(nimf, torch, steps):
+    """The other quantised formats at their config shapes, on one GPU:
+      * FP4 E2M1 block-16 and fp8 (CustomFloat(4,3) codes with a per-channel
+        fp32 scale) GEMV/GEMM, K=8192, N=28672, M in {1, 16, 128, 512};
+        W ~ N(0, 0.015) with 0.1% of entries x20, seed 2; two weight copies
+        alternate so every call streams its weight from HBM (each > L2);
+      * APF / CustomFloat encode and decode of 64M fp32 ~ N(0,1) with 1% x50
+        outliers (seed 3) for E4M3, E5M10 and the auto-selected format, and
+        the allocation-free auto-selection itself;
+      * the int8 layer x[1,1024] . W[1024,1024] (per-tensor quant.nim scale).
+    GB/s counts algorithmic bytes (SURVEY-style per-call figures); TFLOP/s
+    counts 2 M N K."""
+    import ctypes
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pyoracle as O
+    pk, how = peaks()
+    hbm = float(pk["hbm_gbs"])
+    out = {"peak_hbm_gbs": hbm, "peak_source": how}
+    dev = torch.device("cuda")
+    L = nimf.lib()
+
+    # ---- config 3: FP4 / fp8 at K=8192, N=28672
+    n3, k3 = 28672, 8192
+    rng = np.random.default_rng(2)
+    w = (rng.standard_normal((n3, k3), dtype=np.float32) * np.float32(0.015))
+    idx = rng.choice(w.size, w.size // 1000, replace=False)
+    w.flat[idx] *= 20
+    ts = float(np.abs(w).max()) / (6 * 448)
+    rs = (np.abs(w).max(axis=1) / 224.0).astype(np.float32)
+    # quantise row blocks on parallel threads (the C oracle releases the GIL)
+    from concurrent.futures import ThreadPoolExecutor
+    nblk = 32
+    bounds = [n3 * i // nblk for i in range(nblk + 1)]
+    with ThreadPoolExecutor(max_workers=min(nblk, os.cpu_count() or 1)) as ex:
+        q4 = list(ex.map(lambda i: O.quantize_fp4_block16(w[bounds[i]:bounds[i + 1]], ts),
+                         range(nblk)))
+        e8 = list(ex.map(lambda i: O.cf_encode(w[bounds[i]:bounds[i + 1]]
+                                               / rs[bounds[i]:bounds[i + 1], None], 4, 3),
+                         range(nblk)))
+    p4 = np.concatenate([a for a, _ in q4])
+    b4 = np.concatenate([b for _, b in q4])
+    e8 = np.concatenate(e8)
+    del w, q4
+    cf43 = nimf.newCustomFloat(4, 3)
+    fmts = {
+        "fp4_e2m1_b16": (lambda: nimf.Weight.fp4(p4, b4, ts, n3, k3),
+                         n3 * k3 // 2 + n3 * k3 // 16 + 4),
+        "fp8_e4m3_rowscale": (lambda: nimf.Weight.cf(e8, cf43, n3, k3, row_scales=rs),
+                              n3 * k3 + 4 * n3),
+    }
+    res3 = {}
+    for name, (mk, wbytes) in fmts.items():
+        ws = [mk(), mk()]
+        try:
+            for m in (1, 16, 128, 512):
+                x = torch.randn(m, k3, device=dev)
+                y = torch.empty(m, n3, device=dev)
+
+                def step(st):
+                    for wt in ws:
+                        wt.matmul_dev(x.data_ptr(), m, y.data_ptr(), st)
+
+                ms = graph_ms(torch, step, max(3, steps if m <= 16 else steps // 8), 3) / len(ws)
+                nbytes = wbytes + 4 * m * k3 + 4 * m * n3
+                gbs = nbytes / (ms * 1e-3) / 1e9
+                res3["%s_m%d" % (name, m)] = {
+                    "us": ms * 1e3, "gb_s": gbs, "frac_of_hbm": gbs / hbm,
+                    "tflop_s": 2.0 * m * n3 * k3 / (ms * 1e-3) / 1e12,
+                    "algorithmic_bytes": nbytes}
+        finally:
+            for wt in ws:
+                wt.free()
+    del p4, b4, e8
+    out["config3_k8192_n28672"] = res3
+
+    # ---- config 4: APF encode / decode, 64M elements
+    n4 = 1 << 26
+    rng = np.random.default_rng(3)
+    xa = rng.standard_normal(n4, dtype=np.float32)
+    oi = rng.choice(n4, n4 // 100, replace=False)
+    xa[oi] *= 50
+    xd = torch.from_numpy(xa).to(dev)
+    eb, mb = ctypes.c_int(), ctypes.c_int()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    nimf.check(L.nimf_cf_autoselect_dev_noalloc(ctypes.c_void_p(xd.data_ptr()), n4, None, 0,
+                                                1e-3, 1, ctypes.byref(eb), ctypes.byref(mb), None))
+    auto_s = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    reps = 5
+    for _ in range(reps):
+        nimf.check(L.nimf_cf_autoselect_dev_noalloc(ctypes.c_void_p(xd.data_ptr()), n4, None, 0,
+                                                    1e-3, 1, ctypes.byref(eb), ctypes.byref(mb),
+                                                    None))
+    auto_s = (time.perf_counter() - t0) / reps
+    res4 = {"auto_selected": "e%dm%d" % (eb.value, mb.value),
+            "autoselect_ms": auto_s * 1e3, "autoselect_gb_s": 4 * n4 / auto_s / 1e9}
+    for e, m in ((4, 3), (5, 10), (eb.value, mb.value)):
+        item = (1 + e + m + 7) // 8
+        enc = torch.empty(n4 * item, dtype=torch.uint8, device=dev)
+        dec = torch.empty(n4, dtype=torch.float32, device=dev)
+        ep = ctypes.c_void_p(enc.data_ptr())
+
+        def encode(st, e=e, m=m, ep=ep):
+            nimf.check(L.nimf_cf_encode_dev(ctypes.c_void_p(xd.data_ptr()), n4, e, m, ep,
+                                            ctypes.c_void_p(st)))
+
+        def decode(st, e=e, m=m, ep=ep, item=item):
+            nimf.check(L.nimf_cf_decode_dev(ep, n4 * item, e, m, ctypes.c_void_p(dec.data_ptr()),
+                                            ctypes.c_void_p(st)))
+
+        ms_e = graph_ms(torch, encode, max(3, steps // 4), 3)
+        ms_d = graph_ms(torch, decode, max(3, steps // 4), 3)
+        nb = n4 * (4 + item)
+        res4["e%dm%d" % (e, m)] = {
+            "item_bytes": item,
+            "encode_gb_s": nb / (ms_e * 1e-3) / 1e9, "encode_frac_of_hbm": nb / (ms_e * 1e-3) / 1e9 / hbm,
+            "decode_gb_s": nb / (ms_d * 1e-3) / 1e9, "decode_frac_of_hbm": nb / (ms_d * 1e-3) / 1e9 / hbm,
+            "encode_us": ms_e * 1e3, "decode_us": ms_d * 1e3}
+        del enc, dec
+    del xd
+    out["config4_apf_64m"] = res4
+
+    # ---- config 1: int8 layer
+    rng = np.random.default_rng(0)
+    x1 = rng.standard_normal((1, 1024)).astype(np.float32)
+    w1 = (rng.standard_normal((1024, 1024)) * 0.02).astype(np.float32)
+    q1, s1 = O.quantize_int8(w1)
+    h1 = nimf.Weight.i8(q1, s1, 1024, 1024)
+    try:
+        xd1 = torch.from_numpy(x1).to(dev)
+        yd1 = torch.empty(1, 1024, device=dev)
+        ms1 = graph_ms(torch, lambda st: h1.matmul_dev(xd1.data_ptr(), 1, yd1.data_ptr(), st),
+                       max(3, steps), 3)
+        h1.matmul(x1, 1)
+        t0 = time.perf_counter()
+        for _ in range(200):
+            h1.matmul(x1, 1)
+        e2e_us = (time.perf_counter() - t0) / 200 * 1e6
+    finally:
+        h1.free()
+    out["config1_int8_1024"] = {"us_device": ms1 * 1e3, "us_e2e_host_buffers": e2e_us,
+                                "gb_s": 1056772 / (ms1 * 1e-3) / 1e9,
+                                "note": "launch-bound: 1 MB of weight"}
+    return out
+
+
 def run_ours(args, rank, world, local_rank):
     import numpy as np
     import torch
@@ -551,6 +723,9 @@ def run_ours(args, rank, world, local_rank):
     prefill = None
     if world == 1 and args.prefill_steps > 0:
         prefill = run_prefill_7b(nimf, torch, args.prefill_steps, 3)
+    formats = None
+    if world == 1 and args.format_steps > 0:
+        formats = run_formats(nimf, torch, args.format_steps)
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
@@ -567,6 +742,8 @@ def run_ours(args, rank, world, local_rank):
             line["decode_7b"] = decode
         if prefill is not None:
             line["prefill_7b"] = prefill
+        if formats is not None:
+            line["formats"] = formats
         print(json.dumps(line), flush=True)
     for wt in weights:
         wt.free()
@@ -584,6 +761,8 @@ def main():
                     help="timed steps of the 7B-shape decode measurement (0: skip)")
     ap.add_argument("--prefill-steps", type=int, default=20,
                     help="timed steps of the 7B-shape prefill measurement (0: skip)")
+    ap.add_argument("--format-steps", type=int, default=40,
+                    help="timed steps of the FP4/fp8/APF/int8 measurements (0: skip)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 

@@ -135,6 +135,7 @@ void free_weight_storage(Weight* w) {
   device_free(w->fp4.packed);
   device_free(w->fp4.bscale);
   device_free(w->f32.w);
+  fw_free(&w->fw);
   w->q4 = Q4GWeight();
   w->i8 = I8Weight();
   w->cf = CFWeight();
@@ -174,6 +175,11 @@ static int check_rows(int64_t n, int64_t row_begin, int64_t row_end) {
   return NIMF_OK;
 }
 
+static int64_t fw_bytes(const FWLayout& L) {
+  if (L.fmt < 0) return 0;
+  return L.n_rt * L.ntk * 512 + (L.fmt == FW_FP4 ? L.n_rt * L.ntk * 64 : 0);
+}
+
 static int finish_register(std::unique_ptr<Weight> w, nimf_weight_t* out) {
   NIMF_CUDA_TRY(cudaStreamSynchronize(g_ctx.stream));
   NIMF_CUDA_TRY(cudaGetLastError());
@@ -185,9 +191,12 @@ static int finish_register(std::unique_ptr<Weight> w, nimf_weight_t* out) {
 static int matmul_dev(Weight* w, const float* x, int64_t m, float* y, cudaStream_t st) {
   switch (w->kind) {
     case NIMF_KIND_INT4_ASYM: return q4g_gemv(w->q4, x, m, y, st);
-    case NIMF_KIND_INT8: return i8_gemv(w->i8, x, m, y, st);
-    case NIMF_KIND_CUSTOM_FLOAT: return cf_gemv(w->cf, x, m, y, st);
-    case NIMF_KIND_FP4_E2M1: return fp4_gemv(w->fp4, x, m, y, st);
+    case NIMF_KIND_INT8:
+      return w->fw.fmt >= 0 ? fw_gemv(w->fw, x, m, y, st) : i8_gemv(w->i8, x, m, y, st);
+    case NIMF_KIND_CUSTOM_FLOAT:
+      return w->fw.fmt >= 0 ? fw_gemv(w->fw, x, m, y, st) : cf_gemv(w->cf, x, m, y, st);
+    case NIMF_KIND_FP4_E2M1:
+      return w->fw.fmt >= 0 ? fw_gemv(w->fw, x, m, y, st) : fp4_gemv(w->fp4, x, m, y, st);
     case NIMF_KIND_F32: return f32_gemm(x, m, w->f32.k, (const float*)w->f32.w, w->f32.rows, y, st);
   }
   return set_error(NIMF_ERR_UNSUPPORTED, "weight kind %d has no matmul path", w->kind);
@@ -251,6 +260,7 @@ int nimf_shutdown(void) {
   for (auto& kv : g_weights) free_weight_storage(kv.second.get());
   g_weights.clear();
   g_q4_cache.clear();
+  fw_release_scratch();
   device_free(g_ctx.stage_in);
   device_free(g_ctx.stage_out);
   if (g_ctx.host_err) cudaFreeHost((void*)g_ctx.host_err);
@@ -332,6 +342,15 @@ int nimf_weight_register_i8(const int8_t* q, const float* scales, int64_t n_scal
   NIMF_CUDA_TRY(cudaMemcpyAsync(d.scales, n_scales == 1 ? scales : scales + row_begin,
                                 (size_t)d.n_scales * 4, cudaMemcpyHostToDevice, c->stream));
   w->device_bytes = rows * k + d.n_scales * 4;
+  {
+    int st = fw_build(&w->fw, FW_I8, d.q, nullptr, d.n_scales == 1 ? nullptr : (const float*)d.scales,
+                      n_scales == 1 ? scales[0] : 1.0f, rows, k, c->stream);
+    if (st != NIMF_OK) {
+      free_weight_storage(w.get());
+      return st;
+    }
+    w->device_bytes += fw_bytes(w->fw);
+  }
   return finish_register(std::move(w), out);
 }
 
@@ -368,6 +387,19 @@ int nimf_weight_register_cf(const uint8_t* data, int e, int m, const float* row_
                                   cudaMemcpyHostToDevice, c->stream));
     w->device_bytes += rows * 4;
   }
+  // one-byte E4M3 / E5M2 codes that decode exactly like OCP FP8: tensor-core GEMV
+  if (item == 1 && ((e == 4 && m == 3) || (e == 5 && m == 2))) {
+    int64_t special = 0;
+    int st = fw_count_special_codes((const uint8_t*)d.data, rows * k, m, &special, c->stream);
+    if (st == NIMF_OK && special == 0)
+      st = fw_build(&w->fw, e == 4 ? FW_E4M3 : FW_E5M2, d.data, nullptr,
+                    (const float*)d.row_scales, 1.0f, rows, k, c->stream);
+    if (st != NIMF_OK) {
+      free_weight_storage(w.get());
+      return st;
+    }
+    w->device_bytes += fw_bytes(w->fw);
+  }
   return finish_register(std::move(w), out);
 }
 
@@ -397,6 +429,14 @@ int nimf_weight_register_fp4(const uint8_t* packed, const uint8_t* block_scales,
     NIMF_CUDA_TRY(cudaMemcpyAsync(d.bscale, block_scales + row_begin * nb, (size_t)(rows * nb),
                                   cudaMemcpyHostToDevice, c->stream));
   w->device_bytes = rows * bpr + rows * nb;
+  {
+    int st = fw_build(&w->fw, FW_FP4, d.packed, d.bscale, nullptr, tensor_scale, rows, k, c->stream);
+    if (st != NIMF_OK) {
+      free_weight_storage(w.get());
+      return st;
+    }
+    w->device_bytes += fw_bytes(w->fw);
+  }
   return finish_register(std::move(w), out);
 }
 
@@ -563,9 +603,17 @@ int nimf_dequant_w(nimf_weight_t h, float* out_host) {
   float* o = (float*)d;
   switch (w->kind) {
     case NIMF_KIND_INT4_ASYM: NIMF_TRY(q4g_dequant(w->q4, o, c->stream)); break;
-    case NIMF_KIND_INT8: NIMF_TRY(i8_dequant(w->i8, o, c->stream)); break;
-    case NIMF_KIND_CUSTOM_FLOAT: NIMF_TRY(cf_dequant(w->cf, o, c->stream)); break;
-    case NIMF_KIND_FP4_E2M1: NIMF_TRY(fp4_dequant(w->fp4, o, c->stream)); break;
+    // formats with a tensor-core copy are read back from it, so the bit-exact
+    // check covers the layout the GEMV streams
+    case NIMF_KIND_INT8:
+      NIMF_TRY(w->fw.fmt >= 0 ? fw_dequant(w->fw, o, c->stream) : i8_dequant(w->i8, o, c->stream));
+      break;
+    case NIMF_KIND_CUSTOM_FLOAT:
+      NIMF_TRY(w->fw.fmt >= 0 ? fw_dequant(w->fw, o, c->stream) : cf_dequant(w->cf, o, c->stream));
+      break;
+    case NIMF_KIND_FP4_E2M1:
+      NIMF_TRY(w->fw.fmt >= 0 ? fw_dequant(w->fw, o, c->stream) : fp4_dequant(w->fp4, o, c->stream));
+      break;
     case NIMF_KIND_F32:
       NIMF_TRY(f32_transpose((const float*)w->f32.w, w->f32.k, w->f32.rows, o, c->stream));
       break;

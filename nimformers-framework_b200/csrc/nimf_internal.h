@@ -52,6 +52,18 @@ struct Q4GWeight {
   void* zeros = nullptr;  // float*
 };
 
+// Tensor-core GEMV layout of a byte-coded float weight (fw.cu): int8, one-byte
+// CustomFloat E4M3 / E5M2 whose codes decode exactly like OCP FP8, FP4 E2M1.
+enum { FW_I8 = 0, FW_E4M3 = 1, FW_E5M2 = 2, FW_FP4 = 3 };
+struct FWLayout {
+  int fmt = -1;                    // FW_*; -1: no fast layout (generic kernels)
+  int64_t rows = 0, k = 0, n_rt = 0, ntk = 0;
+  void* frag = nullptr;            // uint4 [n_rt][ntk][32]
+  void* sfrag = nullptr;           // FP4: uint2 [n_rt][ntk][8] block scales
+  const float* rscale = nullptr;   // per-row output scale (not owned), or
+  float uscale = 1.0f;             // one scale for every row
+};
+
 // Device copy of an int8 weight: q [rows][K] int8, scales [1 or rows].
 struct I8Weight {
   int64_t rows = 0, k = 0, n_scales = 0;
@@ -90,6 +102,7 @@ struct Weight {
   CFWeight cf;
   FP4Weight fp4;
   F32Weight f32;
+  FWLayout fw;  // int8 / CustomFloat / FP4: tensor-core GEMV copy of the codes
   int64_t rows() const;
   int64_t k() const;
 };
@@ -156,6 +169,18 @@ int cf_absrange(const float* x, int64_t n, float* min_abs, float* max_abs, int* 
                 cudaStream_t st);
 // median (element n_valid/2 of the ascending order) of |x| over finite non-zero x.
 int cf_abs_median(const float* x, int64_t n, float* median, int64_t* n_valid, cudaStream_t st);
+
+// Byte-coded float weights on the tensor cores (fw.cu).  fw_build repacks the
+// reference codes (raw_dev) into L; the *_special_codes count tells whether a
+// one-byte CustomFloat weight decodes exactly like OCP FP8 (count 0).
+int fw_build(FWLayout* L, int fmt, const void* raw_dev, const void* bscale_dev,
+             const float* rscale_dev, float uscale, int64_t rows, int64_t k, cudaStream_t st);
+int fw_count_special_codes(const uint8_t* d, int64_t n, int mbits, int64_t* count,
+                           cudaStream_t st);
+void fw_free(FWLayout* L);
+void fw_release_scratch();
+int fw_gemv(const FWLayout& L, const float* x, int64_t m, float* y, cudaStream_t st);
+int fw_dequant(const FWLayout& L, float* out, cudaStream_t st);
 
 int fp4_gemv(const FP4Weight& w, const float* x, int64_t m, float* y, cudaStream_t st);
 int fp4_dequant(const FP4Weight& w, float* out, cudaStream_t st);
