@@ -187,16 +187,22 @@ static int finish_register(std::unique_ptr<Weight> w, nimf_weight_t* out) {
   return NIMF_OK;
 }
 
+// Byte-coded float weights: decode GEMV for up to 16 rows of x, the
+// tensor-core GEMM for prompts.
+static int fw_matmul(const FWLayout& L, const float* x, int64_t m, float* y, cudaStream_t st) {
+  return m > 16 ? fw_gemm_tc(L, x, m, y, st) : fw_gemv(L, x, m, y, st);
+}
+
 // Runs the kernel path of a weight on device buffers.
 static int matmul_dev(Weight* w, const float* x, int64_t m, float* y, cudaStream_t st) {
   switch (w->kind) {
     case NIMF_KIND_INT4_ASYM: return q4g_gemv(w->q4, x, m, y, st);
     case NIMF_KIND_INT8:
-      return w->fw.fmt >= 0 ? fw_gemv(w->fw, x, m, y, st) : i8_gemv(w->i8, x, m, y, st);
+      return w->fw.fmt >= 0 ? fw_matmul(w->fw, x, m, y, st) : i8_gemv(w->i8, x, m, y, st);
     case NIMF_KIND_CUSTOM_FLOAT:
-      return w->fw.fmt >= 0 ? fw_gemv(w->fw, x, m, y, st) : cf_gemv(w->cf, x, m, y, st);
+      return w->fw.fmt >= 0 ? fw_matmul(w->fw, x, m, y, st) : cf_gemv(w->cf, x, m, y, st);
     case NIMF_KIND_FP4_E2M1:
-      return w->fw.fmt >= 0 ? fw_gemv(w->fw, x, m, y, st) : fp4_gemv(w->fp4, x, m, y, st);
+      return w->fw.fmt >= 0 ? fw_matmul(w->fw, x, m, y, st) : fp4_gemv(w->fp4, x, m, y, st);
     case NIMF_KIND_F32: return f32_gemm(x, m, w->f32.k, (const float*)w->f32.w, w->f32.rows, y, st);
   }
   return set_error(NIMF_ERR_UNSUPPORTED, "weight kind %d has no matmul path", w->kind);

@@ -154,6 +154,9 @@ int q4g_dequant(const Q4GWeight& w, float* out, cudaStream_t st);
 // the weight's group size has a tensor-core kernel.
 bool q4g_tc_supported(const Q4GWeight& w);
 int q4g_gemm_tc(const Q4GWeight& w, const float* x, int64_t m, float* y, cudaStream_t st);
+// Per-device scratch of the tensor-core GEMMs' prepared x (grown outside
+// stream capture; calls using it are ordered on one stream).
+int tc_prep_buffer(size_t bytes, cudaStream_t st, unsigned char** out);
 int q4g_gemm_tc_group(const Q4GWeight* const* ws, int count, const float* x, int64_t m,
                       float* const* ys, cudaStream_t st);
 
@@ -181,6 +184,8 @@ void fw_free(FWLayout* L);
 void fw_release_scratch();
 int fw_gemv(const FWLayout& L, const float* x, int64_t m, float* y, cudaStream_t st);
 int fw_dequant(const FWLayout& L, float* out, cudaStream_t st);
+// Prefill GEMM of a byte-coded float weight on tcgen05 (fw_tc.cu).
+int fw_gemm_tc(const FWLayout& L, const float* x, int64_t m, float* y, cudaStream_t st);
 
 int fp4_gemv(const FP4Weight& w, const float* x, int64_t m, float* y, cudaStream_t st);
 int fp4_dequant(const FP4Weight& w, float* out, cudaStream_t st);

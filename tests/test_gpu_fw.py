@@ -167,3 +167,21 @@ def test_config3_full_size_properties(nimf_gpu):
                                   512, k)
     assert rel_err(y[:, rows], O.gemv_f64(x, wd)) <= TOL
     h.free()
+
+
+@pytest.mark.parametrize("fmt", ["fp8", "fp4", "i8_channel", "i8_tensor"])
+def test_prefill_tensor_core_gemm(nimf_gpu, fmt):
+    """More than 16 rows of x run on the tcgen05 GEMM (x rounded once to fp16
+    after a per-row power-of-two scale; measured error about 3e-4 of max|y|):
+    K=8192 as in the FP4 / fp8 config, 384 of its rows, prompts of 128 and 512
+    rows and a ragged 200 (a partial x tile)."""
+    n, k = 384, 8192
+    w = config3_weights(n, k, seed=12)
+    h, wd = MAKERS[fmt](nimf_gpu, w)
+    rng = np.random.default_rng(13)
+    for m in (128, 200, 512):
+        x = rng.standard_normal((m, k)).astype(np.float32)
+        y = h.matmul(x, m)
+        assert rel_err(y, O.gemv_f64(x, wd)) <= TOL, (fmt, m)
+        assert np.array_equal(h.matmul(x, m).view(np.uint32), y.view(np.uint32))
+    h.free()
