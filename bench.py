@@ -218,16 +218,25 @@ def decode7b_bytes(batch):
     return L7 * per_layer + algo_bytes(V7, D7, batch, GS)
 
 
-def run_decode_7b(nimf, torch, steps, warmup):
-    """tok/s of the 7B-shape int4 decode matmul path on one GPU, batch 1 and 8.
+def run_decode_7b(nimf, torch, steps, warmup, rank=0, world=1):
+    """tok/s of the 7B-shape int4 decode matmul path, batch 1 and 8.
 
     Weights are synthetic int4 codes (seeded random bytes) with group scales
     and zeros of the magnitude N(0, 0.02) weights quantise to; every layer has
     its own device copy, so each step streams all 3.7 GB from HBM.  The
     activation glue between projections (norms, attention, SiLU) is not on
-    this path; each projection reads the previous one's output."""
+    this path; each projection reads the previous one's output.
+
+    With world > 1 GPUs every projection is N-sharded (rank r holds rows
+    nimf.shard_rows(N, world, r) of every weight, 3.7 GB / world per GPU) and
+    each projection group's outputs are all-gathered over NCCL inside the
+    captured step, then laid out as the next projection's x [batch][N].
+    Step time is the max over ranks."""
     import numpy as np
     rng = np.random.default_rng(4)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
 
     def make(n, k):
         ngr = k // GS
@@ -238,24 +247,40 @@ def run_decode_7b(nimf, torch, steps, warmup):
 
     shapes = {"q": (D7, D7), "o": (D7, D7), "gu": (F7, D7), "down": (D7, F7), "head": (V7, D7)}
     host = {kname: make(*nk) for kname, nk in shapes.items()}
+
+    def reg(kname):
+        n, k = shapes[kname]
+        return nimf.Weight.q4g(*host[kname], n, k, GS, rows=nimf.shard_rows(n, world, rank))
+
     layers = []
     for _ in range(L7):
-        q, k, v = [nimf.Weight.q4g(*host["q"], D7, D7, GS) for _ in range(3)]
-        o = nimf.Weight.q4g(*host["o"], D7, D7, GS)
-        gate, up = [nimf.Weight.q4g(*host["gu"], F7, D7, GS) for _ in range(2)]
-        down = nimf.Weight.q4g(*host["down"], D7, F7, GS)
+        q, k, v = [reg("q") for _ in range(3)]
+        o = reg("o")
+        gate, up = [reg("gu") for _ in range(2)]
+        down = reg("down")
         layers.append((q, k, v, o, gate, up, down))
-    head = nimf.Weight.q4g(*host["head"], V7, D7, GS)
+    head = reg("head")
+    nd, nf, nv = D7 // world, F7 // world, V7 // world   # equal shards at 1/2/4/8 GPUs
     out = {}
     try:
         for batch in (1, 8):
             dev = torch.device("cuda")
             x = torch.randn(batch, D7, device=dev)
-            qkv = torch.empty(3, batch, D7, device=dev)
-            att = torch.empty(batch, D7, device=dev)
-            gu = torch.empty(2, batch, F7, device=dev)
-            dn = torch.empty(batch, D7, device=dev)
-            logits = torch.empty(batch, V7, device=dev)
+            qkv = torch.empty(3, batch, nd, device=dev)
+            att = torch.empty(batch, nd, device=dev)
+            gu = torch.empty(2, batch, nf, device=dev)
+            dn = torch.empty(batch, nd, device=dev)
+            logits = torch.empty(batch, nv, device=dev)
+            if world > 1:
+                g_qkv = torch.empty(world, 3, batch, nd, device=dev)
+                g_att = torch.empty(world, batch, nd, device=dev)
+                g_gu = torch.empty(world, 2, batch, nf, device=dev)
+                g_dn = torch.empty(world, batch, nd, device=dev)
+                g_log = torch.empty(world, batch, nv, device=dev)
+                x_o = torch.empty(batch, D7, device=dev)     # full q output
+                x_gu = torch.empty(batch, D7, device=dev)    # full o output
+                x_dn = torch.empty(batch, F7, device=dev)    # full gate output
+                x_l = torch.empty(batch, D7, device=dev)     # full down output
             stream = torch.cuda.Stream()
 
             def step(st):
@@ -263,12 +288,33 @@ def run_decode_7b(nimf, torch, steps, warmup):
                 for (q, k, v, o, gate, up, down) in layers:
                     nimf.Weight.matmul_group_dev([q, k, v], h.data_ptr(), batch,
                                                  [qkv[i].data_ptr() for i in range(3)], st)
-                    o.matmul_dev(qkv[0].data_ptr(), batch, att.data_ptr(), st)
-                    nimf.Weight.matmul_group_dev([gate, up], att.data_ptr(), batch,
+                    xo = qkv[0]
+                    if world > 1:
+                        dist.all_gather_into_tensor(g_qkv.view(-1), qkv.view(-1))
+                        x_o.copy_(g_qkv[:, 0].permute(1, 0, 2).reshape(batch, D7))
+                        xo = x_o
+                    o.matmul_dev(xo.data_ptr(), batch, att.data_ptr(), st)
+                    xg = att
+                    if world > 1:
+                        dist.all_gather_into_tensor(g_att.view(-1), att.view(-1))
+                        x_gu.copy_(g_att.permute(1, 0, 2).reshape(batch, D7))
+                        xg = x_gu
+                    nimf.Weight.matmul_group_dev([gate, up], xg.data_ptr(), batch,
                                                  [gu[0].data_ptr(), gu[1].data_ptr()], st)
-                    down.matmul_dev(gu[0].data_ptr(), batch, dn.data_ptr(), st)
+                    xd = gu[0]
+                    if world > 1:
+                        dist.all_gather_into_tensor(g_gu.view(-1), gu.view(-1))
+                        x_dn.copy_(g_gu[:, 0].permute(1, 0, 2).reshape(batch, F7))
+                        xd = x_dn
+                    down.matmul_dev(xd.data_ptr(), batch, dn.data_ptr(), st)
                     h = dn
-                head.matmul_dev(dn.data_ptr(), batch, logits.data_ptr(), st)
+                    if world > 1:
+                        dist.all_gather_into_tensor(g_dn.view(-1), dn.view(-1))
+                        x_l.copy_(g_dn.permute(1, 0, 2).reshape(batch, D7))
+                        h = x_l
+                head.matmul_dev(h.data_ptr(), batch, logits.data_ptr(), st)
+                if world > 1:
+                    dist.all_gather_into_tensor(g_log.view(-1), logits.view(-1))
 
             with torch.cuda.stream(stream):
                 step(stream.cuda_stream)
@@ -279,6 +325,8 @@ def run_decode_7b(nimf, torch, steps, warmup):
             for _ in range(warmup):
                 graph.replay()
             torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
             for _ in range(steps):
@@ -286,7 +334,13 @@ def run_decode_7b(nimf, torch, steps, warmup):
             e1.record()
             torch.cuda.synchronize()
             ms = e0.elapsed_time(e1) / steps
+            if world > 1:
+                t = torch.tensor([ms], device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                ms = float(t.item())
+                dist.barrier()
             graph.reset()
+            del graph
             out["batch%d" % batch] = {
                 "tok_s": batch / (ms * 1e-3), "ms_per_step": ms,
                 "gb_s": decode7b_bytes(batch) / (ms * 1e-3) / 1e9,
@@ -297,8 +351,14 @@ def run_decode_7b(nimf, torch, steps, warmup):
                 w.free()
         head.free()
     out["launches_per_step"] = 4 * L7 + 1
+    out["n_gpus"] = world
+    if world > 1:
+        out["all_gathers_per_step"] = 4 * L7 + 1
     out["note"] = ("matmul path only (grouped q/k/v and gate/up), one CUDA graph per step, "
-                   "synthetic int4-g128 weights, %d timed steps" % steps)
+                   "synthetic int4-g128 weights, %d timed steps%s" % (
+                       steps, "" if world == 1 else
+                       "; N-sharded over %d GPUs, NCCL all-gather after every projection group, "
+                       "step time = max over ranks" % world))
     return out
 
 
@@ -718,8 +778,8 @@ def run_ours(args, rank, world, local_rank):
     graph.reset()
     graph1.reset()
     decode = None
-    if world == 1 and args.decode_steps > 0:
-        decode = run_decode_7b(nimf, torch, args.decode_steps, max(3, args.warmup // 4))
+    if args.decode_steps > 0:
+        decode = run_decode_7b(nimf, torch, args.decode_steps, max(3, args.warmup // 4), rank, world)
     prefill = None
     if world == 1 and args.prefill_steps > 0:
         prefill = run_prefill_7b(nimf, torch, args.prefill_steps, 3)

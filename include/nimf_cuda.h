@@ -182,6 +182,47 @@ int nimf_matmul2_f32(const float* a1, int64_t m1, int64_t k1, const float* b1, i
  * quant.nim:162), so a bit-exact comparison with dequantizeTensor is possible. */
 int nimf_dequant_w(nimf_weight_t w, float* out_host);
 
+/* ------------------------------------------------------------ .nimq state dicts */
+
+/* One tensor record of a NIMQ2 stream (quant.nim:386-409 readQuantTensor).
+ * The pointers point into the caller's buffer; scales and zeros are
+ * n_scales little-endian float32 values that may be unaligned. */
+typedef struct {
+  const char* name;
+  int64_t name_len;
+  int kind;                /* QuantKind ordinal, quant.nim:12-20 */
+  int ndims;
+  int64_t dims[8];
+  int64_t n_scales;
+  const uint8_t* scales;
+  const uint8_t* zeros;
+  int64_t group_size;
+  int exponent_bits, mantissa_bits;
+  const uint8_t* data;
+  int64_t data_len;
+} nimf_nimq_tensor;
+
+/* loadQuantStateDict (quant.nim:429-448) on a stream held in memory: checks
+ * the "NIMQ2" magic (NIMF_ERR_ARG otherwise) and that every record lies
+ * inside [buf, buf + len) (NIMF_ERR_SHAPE otherwise); returns the 5
+ * architecture integers (arch may be NULL) and the tensor count.  Host only:
+ * needs neither nimf_init nor a device. */
+int nimf_nimq_parse(const uint8_t* buf, int64_t len, int32_t* arch, int64_t* count);
+
+/* Record `index` of the stream (host only). */
+int nimf_nimq_get(const uint8_t* buf, int64_t len, int64_t index, nimf_nimq_tensor* out);
+
+/* Uploads rows [row_begin, row_end) of record `index`, a 2-D weight W[N][K]
+ * (row = output channel, nimformer.nim:90), as a device-resident weight:
+ * kind 1 int8 (scale[0], as dequantizeInt8), kind 2 / 3 int4 with rows of
+ * ceil(K/2) bytes as dequantizeTensorTransposed reads them (quant.nim:270-330;
+ * per group, per row or per tensor), kinds 4-7 CustomFloat codes, kind 0 raw
+ * fp32 (whole tensor only, registered as beMatmul's b = W^T).  Replaces
+ * setQuantWeight's host copy and per-forward dequantisation
+ * (nimformer.nim:94-133): the packed codes go from the file to HBM once. */
+int nimf_nimq_register(const uint8_t* buf, int64_t len, int64_t index, int64_t row_begin,
+                       int64_t row_end, nimf_weight_t* out);
+
 /* ------------------------------------------------------------ CustomFloat / APF */
 
 /* beCustomfloatEncode (backend.nim:177-178 -> customfloat.nim:125-129):

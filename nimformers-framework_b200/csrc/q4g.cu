@@ -268,7 +268,7 @@ __host__ __device__ inline SmemLayout q4g_smem_layout(int mode, int kqg, int gps
 // MODE 2: M <= 8, two MMAs per 32 k (d0 and d1 each in columns 0..7).
 // KQG: k-quads (64 k) per quantisation group (group size 64 * KQG).
 template <int MODE, int KQG>
-__global__ void __launch_bounds__((kCons + 2) * 32, 1)
+__global__ void __launch_bounds__((kCons + 2) * 32, kCtasPerSm)
 q4g_gemv_kernel(const GemvArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr int GS = 64 * KQG;

@@ -44,6 +44,7 @@ EXPORTS = [
     "nimf_weight_cache_clear", "nimf_matmul_f32", "nimf_matmul2_f32", "nimf_dequant_w",
     "nimf_cf_encode", "nimf_cf_decode", "nimf_cf_encode_dev", "nimf_cf_decode_dev",
     "nimf_cf_autoselect", "nimf_apf_cast", "nimf_cf_autoselect_dev_noalloc",
+    "nimf_nimq_parse", "nimf_nimq_get", "nimf_nimq_register",
 ]
 
 
@@ -101,6 +102,9 @@ def lib():
         "nimf_cf_autoselect_dev_noalloc": [vp, i64, vp, i64, ctypes.c_double, i32,
                                            ctypes.POINTER(ctypes.c_int),
                                            ctypes.POINTER(ctypes.c_int), vp],
+        "nimf_nimq_parse": [vp, i64, vp, ctypes.POINTER(i64)],
+        "nimf_nimq_get": [vp, i64, i64, ctypes.POINTER(NimqTensor)],
+        "nimf_nimq_register": [vp, i64, i64, i64, i64, u64p],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -110,6 +114,17 @@ def lib():
     L.nimf_last_error.restype = ctypes.c_char_p
     _lib = L
     return L
+
+
+class NimqTensor(ctypes.Structure):
+    """nimf_nimq_tensor: one record of a NIMQ2 stream (quant.nim:386-409)."""
+    _fields_ = [("name", ctypes.c_void_p), ("name_len", ctypes.c_int64),
+                ("kind", ctypes.c_int), ("ndims", ctypes.c_int),
+                ("dims", ctypes.c_int64 * 8), ("n_scales", ctypes.c_int64),
+                ("scales", ctypes.c_void_p), ("zeros", ctypes.c_void_p),
+                ("group_size", ctypes.c_int64), ("exponent_bits", ctypes.c_int),
+                ("mantissa_bits", ctypes.c_int), ("data", ctypes.c_void_p),
+                ("data_len", ctypes.c_int64)]
 
 
 def check(status):
@@ -403,6 +418,59 @@ class Weight:
 
 
 # ------------------------------------------------------------ N-sharding
+# ------------------------------------------------------------ quant.nim I/O
+class QuantStateDict:
+    """A NIMQ2 state dict held in memory (quant.nim:429-448 loadQuantStateDict):
+    `arch` (5 ints) and `tensors`, a list of (name, info) in file order where
+    info has kind, shape, group_size, exponentBits, mantissaBits and numpy
+    views of scales, zero_point and data.  `register(i, rows)` uploads tensor
+    i as a device-resident Weight without a host dequantisation."""
+
+    def __init__(self, raw):
+        self.raw = np.frombuffer(bytes(raw), np.uint8)
+        L = lib()
+        arch = (ctypes.c_int32 * 5)()
+        count = ctypes.c_int64()
+        check(L.nimf_nimq_parse(_ptr(self.raw), self.raw.size, arch, ctypes.byref(count)))
+        self.arch = list(arch)
+        base = self.raw.ctypes.data
+        self.tensors = []
+        for i in range(count.value):
+            t = NimqTensor()
+            check(L.nimf_nimq_get(_ptr(self.raw), self.raw.size, i, ctypes.byref(t)))
+            off = lambda p: (p or base) - base
+            name = self.raw[off(t.name):off(t.name) + t.name_len].tobytes().decode()
+            info = {"kind": t.kind, "shape": [t.dims[j] for j in range(t.ndims)],
+                    "group_size": t.group_size, "exponentBits": t.exponent_bits,
+                    "mantissaBits": t.mantissa_bits,
+                    "scales": self.raw[off(t.scales):off(t.scales) + 4 * t.n_scales].view(np.float32),
+                    "zero_point": self.raw[off(t.zeros):off(t.zeros) + 4 * t.n_scales].view(np.float32),
+                    "data": self.raw[off(t.data):off(t.data) + t.data_len]}
+            self.tensors.append((name, info))
+
+    def index(self, name):
+        for i, (nm, _) in enumerate(self.tensors):
+            if nm == name:
+                return i
+        raise KeyError(name)
+
+    def register(self, i, rows=None):
+        _, info = self.tensors[i]
+        n = info["shape"][0] if info["shape"] else 0
+        r0, r1 = rows if rows is not None else (0, n)
+        return Weight._reg(lib().nimf_nimq_register, _ptr(self.raw), self.raw.size, i, r0, r1)
+
+
+def loadQuantStateDict(path_or_bytes):
+    """quant.nim:429-448: (arch, [(name, info)]) plus the QuantStateDict."""
+    raw = path_or_bytes
+    if isinstance(path_or_bytes, (str, os.PathLike)):
+        with open(path_or_bytes, "rb") as f:
+            raw = f.read()
+    sd = QuantStateDict(raw)
+    return sd.arch, sd.tensors, sd
+
+
 def shard_rows(n, world, rank, align=16):
     """Row range [r0, r1) of output channels held by `rank` of `world` GPUs.
 

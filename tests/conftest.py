@@ -20,3 +20,12 @@ def nimf_gpu():
     import nimf
     nimf.init(0)
     yield nimf
+
+
+@pytest.fixture(scope="session")
+def nimf_mod():
+    """The host mirror with the library loaded but no device bound (host-only
+    entry points such as the .nimq reader)."""
+    import nimf
+    nimf.lib()
+    return nimf
