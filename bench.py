@@ -616,6 +616,40 @@ def run_formats(nimf, torch, steps):
     return out
 
 
+def run_ncu_case(name):
+    """Small fixed workloads for ncu captures (one GPU, a few GB at most): each
+    case runs three warm-up rounds and one final round, every round one launch
+    per case, so `-s` / `-c` select the final round.
+      fw: an FP4 E2M1 block-16 weight and a one-byte CustomFloat(4,3) weight
+          with per-row scales, both 28672 x 8192 (random codes), at M = 1 and 1
+          (GEMV), 16 (GEMV), 17 and 128 (tcgen05 GEMM) and 512."""
+    import numpy as np
+    import torch
+    import nimf
+    if name != "fw":
+        raise SystemExit("unknown --ncu-case %s" % name)
+    nimf.init(0)
+    n3, k3 = 28672, 8192
+    rng = np.random.default_rng(2)
+    packed = rng.integers(0, 256, size=n3 * k3 // 2, dtype=np.uint8)
+    bs = rng.integers(0x20, 0x48, size=n3 * k3 // 16, dtype=np.uint8)
+    h4 = nimf.Weight.fp4(packed, bs, 1e-3, n3, k3)
+    codes = rng.integers(0, 0x78, size=n3 * k3, dtype=np.uint8)  # no inf codes
+    codes[(codes & 0x78) == 0] = 0                                # no exponent-0 mantissas
+    h8 = nimf.Weight.cf(codes, nimf.newCustomFloat(4, 3), n3, k3,
+                        row_scales=np.ones(n3, np.float32))
+    cases = [(h4, 1), (h8, 1), (h8, 16), (h8, 17), (h4, 128), (h8, 512)]
+    xs = {m: torch.randn(m, k3, device="cuda") for _, m in cases}
+    ys = {m: torch.empty(m, n3, device="cuda") for _, m in cases}
+    for _ in range(4):
+        for h, m in cases:
+            h.matmul_dev(xs[m].data_ptr(), m, ys[m].data_ptr())
+        torch.cuda.synchronize()
+    h4.free()
+    h8.free()
+    print("ncu case %s done" % name)
+
+
 def run_ours(args, rank, world, local_rank):
     import numpy as np
     import torch
@@ -823,7 +857,12 @@ def main():
                     help="timed steps of the 7B-shape prefill measurement (0: skip)")
     ap.add_argument("--format-steps", type=int, default=40,
                     help="timed steps of the FP4/fp8/APF/int8 measurements (0: skip)")
+    ap.add_argument("--ncu-case", default=None,
+                    help="run one small fixed workload for an ncu capture and exit (fw)")
     args = ap.parse_args()
+    if args.ncu_case:
+        run_ncu_case(args.ncu_case)
+        return
     args.warmup = max(3, args.warmup)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
