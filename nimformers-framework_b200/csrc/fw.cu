@@ -105,16 +105,25 @@ template <int FMT>
 __device__ __forceinline__ void tile_a(const uint4& w, uint32_t sw, int j, uint32_t (&a)[4]) {
   const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
   if (FMT == FW_FP4) {
-    const uint32_t v = wd[j];
     // block scales of rows g and g+8 for this subtile, broadcast per row
     const uint32_t s2 = cvt_e4m3x2(sw);
     uint32_t sg, sg8;
     asm("prmt.b32 %0, %1, %1, 0x1010;" : "=r"(sg) : "r"(s2));
     asm("prmt.b32 %0, %1, %1, 0x3232;" : "=r"(sg8) : "r"(s2));
-    a[0] = hmul2_u(cvt_e2m1x2(v), sg);
-    a[1] = hmul2_u(cvt_e2m1x2(v >> 8), sg8);
-    a[2] = hmul2_u(cvt_e2m1x2(v >> 16), sg);
-    a[3] = hmul2_u(cvt_e2m1x2(v >> 24), sg8);
+    // the word's four bytes (registers a0..a3 of the subtile) are split once
+    uint32_t c[4];
+    asm("{ .reg .b8 b0, b1, b2, b3;\n"
+        "  mov.b32 {b0, b1, b2, b3}, %4;\n"
+        "  cvt.rn.f16x2.e2m1x2 %0, b0;\n"
+        "  cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+        "  cvt.rn.f16x2.e2m1x2 %2, b2;\n"
+        "  cvt.rn.f16x2.e2m1x2 %3, b3; }"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(wd[j]));
+    a[0] = hmul2_u(c[0], sg);
+    a[1] = hmul2_u(c[1], sg8);
+    a[2] = hmul2_u(c[2], sg);
+    a[3] = hmul2_u(c[3], sg8);
   } else {
     const uint32_t w0 = wd[2 * j], w1 = wd[2 * j + 1];
     if (FMT == FW_I8) {
@@ -331,9 +340,22 @@ __global__ void __launch_bounds__(kFwThreads, 1) fw_gemv_kernel(const FwArgs a) 
         if (j < nt) sv[j] = ldg_stream2(ss + (size_t)j * 8);
     }
   };
+  // the chunk after the next one is pulled into L2 by one bulk prefetch, so
+  // the register loads of the next chunk find their lines in L2
+  auto prefetch_chunk = [&](int c) {
+    const int rl = c / cpr, ch = c - rl * cpr;
+    const int kt = kt0 + ch * kChunkTiles;
+    const int nt = min(kChunkTiles, kt0 + nkt - kt);
+    const size_t tile0 = (size_t)(rt0 + rl) * a.ntk + kt;
+    if (lane == 0) {
+      bulk_prefetch_l2(a.frag + tile0 * 32, (uint32_t)nt * 512u);
+      if (FMT == FW_FP4) bulk_prefetch_l2(a.sfrag + tile0 * 8, (uint32_t)nt * 64u);
+    }
+  };
   uint4 wv[kChunkTiles], nv[kChunkTiles];
   uint2 sv[kChunkTiles], nsv[kChunkTiles];
   griddep_launch_dependents();
+  if (c0 + 1 < c1) prefetch_chunk(c0 + 1);
   if (c0 < c1) load_chunk(c0, wv, sv);
 
   if (threadIdx.x < 16) xmax[threadIdx.x] = 0u;
@@ -447,6 +469,7 @@ __global__ void __launch_bounds__(kFwThreads, 1) fw_gemv_kernel(const FwArgs a) 
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[q][e] = 0.f;
     }
+    if (c + 2 < c1) prefetch_chunk(c + 2);
     if (c + 1 < c1) load_chunk(c + 1, nv, nsv);
     const int nt = min(kChunkTiles, nkt - ch * kChunkTiles);
 #pragma unroll
