@@ -523,7 +523,7 @@ def run_formats(nimf, torch, steps):
     for name, (mk, wbytes) in fmts.items():
         ws = [mk(), mk()]
         try:
-            for m in (1, 16, 128, 512):
+            for m in (1, 4, 8, 16, 17, 128, 512):
                 x = torch.randn(m, k3, device=dev)
                 y = torch.empty(m, n3, device=dev)
 

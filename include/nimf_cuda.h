@@ -116,6 +116,21 @@ int nimf_weight_register_fp4(const uint8_t* packed, const uint8_t* block_scales,
                              float tensor_scale, int64_t n, int64_t k, int64_t row_begin,
                              int64_t row_end, nimf_weight_t* out);
 
+/* GPTQ-native int4 checkpoint tensors as export_to_nimq.py:219-254
+ * (dequantize_gptq_linear) reads them: qweight int32 [in_features/8][out],
+ * nibble k % 8 of qweight[k/8][n]; qzeros int32 [n_groups][out/8], nibble
+ * n % 8; scales fp16 bits [n_groups][out]; g_idx int32 [in_features].
+ * w[n][k] = (nib - ((z + 1) & 15)) * float(scale), bit-identical to the
+ * reference, without its fp32 round-trip.  Groups must hold equal numbers of
+ * input features (the last may hold fewer); act-order g_idx is supported by
+ * storing k grouped and gathering x through the permutation at each call.
+ * Output channels [row_begin, row_end) are uploaded.  Resulting weights
+ * behave as int4 group weights (nimf_weight_info reports kind 3). */
+int nimf_weight_register_gptq(const int32_t* qweight, const int32_t* qzeros,
+                              const uint16_t* scales_f16, const int32_t* g_idx,
+                              int64_t in_features, int64_t out_features, int64_t n_groups,
+                              int64_t row_begin, int64_t row_end, nimf_weight_t* out);
+
 /* Raw float32 weights given as beMatmul's b operand [K][N] row-major
  * (backend.nim:87, gpubackend.nim:584). */
 int nimf_weight_register_f32(const float* b_kn, int64_t k, int64_t n, nimf_weight_t* out);

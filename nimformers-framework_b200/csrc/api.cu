@@ -136,6 +136,9 @@ void free_weight_storage(Weight* w) {
   device_free(w->fp4.bscale);
   device_free(w->f32.w);
   fw_free(&w->fw);
+  device_free(w->kperm);
+  w->kperm = nullptr;
+  w->kperm_host.clear();
   w->q4 = Q4GWeight();
   w->i8 = I8Weight();
   w->cf = CFWeight();
@@ -187,14 +190,20 @@ static int finish_register(std::unique_ptr<Weight> w, nimf_weight_t* out) {
   return NIMF_OK;
 }
 
-// Byte-coded float weights: decode GEMV for up to 16 rows of x, the
-// tensor-core GEMM for prompts.
+// Byte-coded float weights: decode GEMV for up to 8 rows of x, the tcgen05
+// GEMM above (at K=8192, N=28672 the GEMM takes 145 us for 17 rows where the
+// GEMV takes 200 us for 16 and 93 us for 8).
 static int fw_matmul(const FWLayout& L, const float* x, int64_t m, float* y, cudaStream_t st) {
-  return m > 16 ? fw_gemm_tc(L, x, m, y, st) : fw_gemv(L, x, m, y, st);
+  return m > 8 ? fw_gemm_tc(L, x, m, y, st) : fw_gemv(L, x, m, y, st);
 }
 
 // Runs the kernel path of a weight on device buffers.
 static int matmul_dev(Weight* w, const float* x, int64_t m, float* y, cudaStream_t st) {
+  if (w->kperm && m > 0 && w->k() > 0) {
+    const float* xg = nullptr;
+    NIMF_TRY(gather_cols(x, m, w->k(), (const int32_t*)w->kperm, &xg, st));
+    x = xg;
+  }
   switch (w->kind) {
     case NIMF_KIND_INT4_ASYM: return q4g_gemv(w->q4, x, m, y, st);
     case NIMF_KIND_INT8:
@@ -267,6 +276,7 @@ int nimf_shutdown(void) {
   g_weights.clear();
   g_q4_cache.clear();
   fw_release_scratch();
+  release_perm_buffer();
   device_free(g_ctx.stage_in);
   device_free(g_ctx.stage_out);
   if (g_ctx.host_err) cudaFreeHost((void*)g_ctx.host_err);
@@ -544,7 +554,7 @@ int nimf_matmul_w_group_dev(const nimf_weight_t* handles, int count, const float
       return set_error(NIMF_ERR_SHAPE, "grouped matmul: weights have different K");
     if (!y_devs[i] && ws[i]->rows() > 0) return set_error(NIMF_ERR_ARG, "NULL output %d", i);
     all_q4 = all_q4 && ws[i]->kind == NIMF_KIND_INT4_ASYM && ws[i]->q4.gs == ws[0]->q4.gs &&
-             ws[i]->q4.fast == ws[0]->q4.fast;
+             ws[i]->q4.fast == ws[0]->q4.fast && !ws[i]->kperm;
   }
   if (!x_dev && ws[0]->k() > 0) return set_error(NIMF_ERR_ARG, "NULL x");
   if (all_q4) {
@@ -627,6 +637,16 @@ int nimf_dequant_w(nimf_weight_t h, float* out_host) {
   }
   NIMF_CUDA_TRY(cudaMemcpyAsync(out_host, o, (size_t)n * 4, cudaMemcpyDeviceToHost, c->stream));
   NIMF_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  if (!w->kperm_host.empty()) {
+    // stored column j is input feature kperm[j]: back to the reference order
+    const int64_t k = w->k();
+    std::vector<float> row((size_t)k);
+    for (int64_t r = 0; r < w->rows(); ++r) {
+      float* o_r = out_host + r * k;
+      std::copy(o_r, o_r + k, row.begin());
+      for (int64_t j = 0; j < k; ++j) o_r[w->kperm_host[(size_t)j]] = row[(size_t)j];
+    }
+  }
   return NIMF_OK;
 }
 

@@ -1,4 +1,4 @@
-// fw_tc.cu -- prefill GEMM (x with more than 16 rows) of the byte-coded float
+// fw_tc.cu -- GEMM (x with more than 8 rows) of the byte-coded float
 // weights (int8, one-byte CustomFloat E4M3 / E5M2, FP4 E2M1 block-16) on the
 // 5th-generation tensor cores: tcgen05.mma kind::f16, fp32 accumulators in
 // tensor memory (TMEM).

@@ -9,6 +9,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <memory>
+#include <vector>
 
 #include "../../include/nimf_cuda.h"
 
@@ -103,6 +104,10 @@ struct Weight {
   FP4Weight fp4;
   F32Weight f32;
   FWLayout fw;  // int8 / CustomFloat / FP4: tensor-core GEMV copy of the codes
+  // act-order GPTQ weights: stored column j holds input feature kperm[j]
+  // (device int32 [K]; x is gathered through it before each matmul)
+  void* kperm = nullptr;
+  std::vector<int32_t> kperm_host;
   int64_t rows() const;
   int64_t k() const;
 };
@@ -186,6 +191,12 @@ int fw_gemv(const FWLayout& L, const float* x, int64_t m, float* y, cudaStream_t
 int fw_dequant(const FWLayout& L, float* out, cudaStream_t st);
 // Prefill GEMM of a byte-coded float weight on tcgen05 (fw_tc.cu).
 int fw_gemm_tc(const FWLayout& L, const float* x, int64_t m, float* y, cudaStream_t st);
+
+// x[m][k] gathered through a column permutation into a per-device scratch
+// buffer (gptq.cu); *out points at the gathered rows.
+int gather_cols(const float* x, int64_t m, int64_t k, const int32_t* perm, const float** out,
+                cudaStream_t st);
+void release_perm_buffer();
 
 int fp4_gemv(const FP4Weight& w, const float* x, int64_t m, float* y, cudaStream_t st);
 int fp4_dequant(const FP4Weight& w, float* out, cudaStream_t st);

@@ -44,7 +44,7 @@ EXPORTS = [
     "nimf_weight_cache_clear", "nimf_matmul_f32", "nimf_matmul2_f32", "nimf_dequant_w",
     "nimf_cf_encode", "nimf_cf_decode", "nimf_cf_encode_dev", "nimf_cf_decode_dev",
     "nimf_cf_autoselect", "nimf_apf_cast", "nimf_cf_autoselect_dev_noalloc",
-    "nimf_nimq_parse", "nimf_nimq_get", "nimf_nimq_register",
+    "nimf_nimq_parse", "nimf_nimq_get", "nimf_nimq_register", "nimf_weight_register_gptq",
 ]
 
 
@@ -105,6 +105,7 @@ def lib():
         "nimf_nimq_parse": [vp, i64, vp, ctypes.POINTER(i64)],
         "nimf_nimq_get": [vp, i64, i64, ctypes.POINTER(NimqTensor)],
         "nimf_nimq_register": [vp, i64, i64, i64, i64, u64p],
+        "nimf_weight_register_gptq": [vp, vp, vp, vp, i64, i64, i64, i64, i64, u64p],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -363,6 +364,19 @@ class Weight:
         b = np.ascontiguousarray(block_scales, dtype=np.uint8).ravel()
         return cls._reg(lib().nimf_weight_register_fp4, _ptr(p), _ptr(b), float(tensor_scale), N,
                         K, r0, r1)
+
+    @classmethod
+    def gptq(cls, qweight, qzeros, scales_f16, g_idx, rows=None):
+        """GPTQ-native tensors (export_to_nimq.py:219-254 layout): qweight
+        int32 [K/8][N], qzeros int32 [G][N/8], scales float16 [G][N], g_idx [K]."""
+        qw = np.ascontiguousarray(qweight, dtype=np.int32)
+        qz = np.ascontiguousarray(qzeros, dtype=np.int32)
+        sc = np.ascontiguousarray(scales_f16, dtype=np.float16).view(np.uint16)
+        gi = np.ascontiguousarray(g_idx, dtype=np.int32)
+        K, N = qw.shape[0] * 8, qw.shape[1]
+        r0, r1 = rows if rows is not None else (0, N)
+        return cls._reg(lib().nimf_weight_register_gptq, _ptr(qw), _ptr(qz), _ptr(sc), _ptr(gi),
+                        K, N, sc.shape[0], r0, r1)
 
     @classmethod
     def f32(cls, b_kn, K, N):

@@ -7,7 +7,8 @@ CustomFloat, the FP4 format definition for FP4); matmul outputs meet
 max|y - y_ref| / max|y_ref| <= 1e-3 against float64 sums of the dequantised
 weights.  Shapes cover every x-row mode (M <= 4, <= 8, <= 16, chunks of 16),
 ragged rows and k, k-splits through the scratch buffer, and the config-3
-shape K=8192 (a row slice of N=28672; the full N at the end)."""
+shape K=8192 (a row slice of N=28672; the full N at the end).  Up to 8 rows
+of x run on the mma.sync GEMV, more on the tcgen05 GEMM."""
 import numpy as np
 import pytest
 
@@ -85,14 +86,15 @@ def test_ragged_shapes_all_modes(nimf_gpu, fmt, n, k):
 
 @pytest.mark.parametrize("fmt", ["fp8", "fp4", "i8_channel"])
 def test_config3_k8192_row_slice(nimf_gpu, fmt):
-    """K=8192 as in the FP4 / fp8 config, 1024 of its 28672 rows, M in {1, 16}
-    (M=16 splits k four ways through the scratch partials)."""
+    """K=8192 as in the FP4 / fp8 config, 1024 of its 28672 rows, M in {1, 8, 16}
+    (M=8 splits k two ways through the scratch partials; M=16 runs on the
+    tcgen05 GEMM)."""
     n, k = 1024, 8192
     w = config3_weights(n, k)
     h, wd = MAKERS[fmt](nimf_gpu, w)
     assert np.array_equal(h.dequant().view(np.uint32), wd.view(np.uint32))
     rng = np.random.default_rng(7)
-    for m in (1, 16):
+    for m in (1, 8, 16):
         x = rng.standard_normal((m, k)).astype(np.float32)
         y = h.matmul(x, m)
         assert rel_err(y, O.gemv_f64(x, wd)) <= TOL
