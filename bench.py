@@ -362,6 +362,103 @@ def run_decode_7b(nimf, torch, steps, warmup, rank=0, world=1):
     return out
 
 
+def run_decode_7b_full(nimf, torch, steps, warmup, pos=512, max_seq=640, layers=L7):
+    """tok/s of one whole 7B-shape decode step at batch 1 with the glue on the
+    device: per layer RMSNorm, fused q/k/v GEMV, RoPE on q and k (one launch),
+    KV-cache append + attention over pos + 1 positions (32 heads x 128), o GEMV,
+    residual add fused with the next RMSNorm, fused gate/up GEMV, SwiGLU, down
+    GEMV, residual add fused with the next layer's (or the final) RMSNorm; then
+    the lm_head GEMV (nim_inference.nim:847-921's order).  One CUDA graph per step; synthetic int4-g128 weights, random
+    norm weights and KV caches (fp32, 32 x 2 x 32 x 640 x 128)."""
+    import ctypes
+    import numpy as np
+    rng = np.random.default_rng(6)
+    L = nimf.lib()
+    H, HD = 32, 128
+
+    def make(n, k):
+        ngr = k // GS
+        p = rng.integers(0, 256, size=n * (k // 2), dtype=np.uint8)
+        sc = rng.uniform(0.002, 0.004, size=n * ngr).astype(np.float32)
+        zp = rng.uniform(6.0, 9.0, size=n * ngr).astype(np.float32)
+        return p, sc, zp
+
+    hq, hg, hd, hh = make(D7, D7), make(F7, D7), make(D7, F7), make(V7, D7)
+    dev = torch.device("cuda")
+    nlayers = layers
+    layers = []
+    for _ in range(nlayers):
+        q, k, v, o = [nimf.Weight.q4g(*hq, D7, D7, GS) for _ in range(4)]
+        gate, up = [nimf.Weight.q4g(*hg, F7, D7, GS) for _ in range(2)]
+        down = nimf.Weight.q4g(*hd, D7, F7, GS)
+        n1 = torch.rand(D7, device=dev) + 0.5
+        n2 = torch.rand(D7, device=dev) + 0.5
+        kc = torch.randn(H * max_seq * HD, device=dev)
+        vc = torch.randn(H * max_seq * HD, device=dev)
+        layers.append((q, k, v, o, gate, up, down, n1, n2, kc, vc))
+    head = nimf.Weight.q4g(*hh, V7, D7, GS)
+    nf = torch.rand(D7, device=dev) + 0.5
+    half = HD // 2
+    inv = 1.0 / np.power(np.float32(10000.0), np.arange(half, dtype=np.float32) / np.float32(half))
+    ang = np.arange(max_seq, dtype=np.float32)[:, None] * inv[None, :].astype(np.float32)
+    cos_t = torch.from_numpy(np.cos(ang).astype(np.float32)).to(dev)
+    sin_t = torch.from_numpy(np.sin(ang).astype(np.float32)).to(dev)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+    x0 = torch.randn(1, D7, device=dev)
+    x = torch.empty(1, D7, device=dev)
+    h = torch.empty(1, D7, device=dev)
+    xn = torch.empty(1, D7, device=dev)
+    qkv = torch.empty(3, 1, D7, device=dev)
+    att = torch.empty(1, D7, device=dev)
+    ao = torch.empty(1, D7, device=dev)
+    gu = torch.empty(2, 1, F7, device=dev)
+    act = torch.empty(1, F7, device=dev)
+    dn = torch.empty(1, D7, device=dev)
+    logits = torch.empty(1, V7, device=dev)
+    scale = float(np.float32(1.0) / np.sqrt(np.float32(HD)))
+
+    def step(st):
+        sp = ctypes.c_void_p(st)
+        x.copy_(x0)   # the same token every replay
+        nimf.check(L.nimf_rmsnorm_dev(P(x), P(layers[0][7]), 1, D7, ctypes.c_float(1e-6), P(xn), sp))
+        for li, (q, k, v, o, gate, up, down, n1, n2, kc, vc) in enumerate(layers):
+            nimf.Weight.matmul_group_dev([q, k, v], xn.data_ptr(), 1,
+                                         [qkv[i].data_ptr() for i in range(3)], st)
+            # q and k are adjacent in qkv: one launch rotates both (2 H heads)
+            nimf.check(L.nimf_rope_dev(P(qkv[0]), 1, 1, 2 * H, HD, pos, P(cos_t), P(sin_t), max_seq, sp))
+            nimf.check(L.nimf_attention_decode_dev(P(qkv[0]), P(qkv[1]), P(qkv[2]), P(kc), P(vc),
+                                                   H, H, HD, max_seq, pos, ctypes.c_float(scale),
+                                                   P(att), sp))
+            o.matmul_dev(att.data_ptr(), 1, ao.data_ptr(), st)
+            # h = x + attention output, xn = RMSNorm(h)
+            nimf.check(L.nimf_add_rmsnorm_dev(P(x), P(ao), P(n2), 1, D7, ctypes.c_float(1e-6),
+                                              P(h), P(xn), sp))
+            nimf.Weight.matmul_group_dev([gate, up], xn.data_ptr(), 1,
+                                         [gu[0].data_ptr(), gu[1].data_ptr()], st)
+            nimf.check(L.nimf_swiglu_dev(P(gu[0]), P(gu[1]), F7, P(act), sp))
+            down.matmul_dev(act.data_ptr(), 1, dn.data_ptr(), st)
+            # x = h + FFN output, xn = the next layer's (or the final) RMSNorm of x
+            nxt = layers[li + 1][7] if li + 1 < len(layers) else nf
+            nimf.check(L.nimf_add_rmsnorm_dev(P(h), P(dn), P(nxt), 1, D7, ctypes.c_float(1e-6),
+                                              P(x), P(xn), sp))
+        head.matmul_dev(xn.data_ptr(), 1, logits.data_ptr(), st)
+
+    try:
+        ms = graph_ms(torch, step, steps, warmup)
+    finally:
+        for lw in layers:
+            for w in lw[:7]:
+                w.free()
+        head.free()
+    kv_bytes = nlayers * 2 * H * (pos + 1) * HD * 4
+    return {"tok_s": 1.0 / (ms * 1e-3), "ms_per_step": ms, "position": pos,
+            "weight_bytes_per_step": decode7b_bytes(1), "kv_bytes_per_step": kv_bytes,
+            "gb_s": (decode7b_bytes(1) + kv_bytes) / (ms * 1e-3) / 1e9,
+            "launches_per_step": nlayers * 9 + 2,
+            "note": ("batch 1, whole decode step on the device (glue + int4-g128 matmuls), one "
+                     "CUDA graph, KV caches fp32 [32 heads][640][128] per layer, %d timed steps" % steps)}
+
+
 def prefill7b_flops(tokens):
     """Multiply-add FLOPs of one 7B layer's projections for `tokens` rows."""
     return 2 * tokens * (4 * D7 * D7 + 3 * F7 * D7)
@@ -620,12 +717,19 @@ def run_ncu_case(name):
     """Small fixed workloads for ncu captures (one GPU, a few GB at most): each
     case runs three warm-up rounds and one final round, every round one launch
     per case, so `-s` / `-c` select the final round.
+      decode_step: the whole-step 7B decode of run_decode_7b_full with 2 layers
+          (graph replays: 2 warm-up, 2 timed);
       fw: an FP4 E2M1 block-16 weight and a one-byte CustomFloat(4,3) weight
           with per-row scales, both 28672 x 8192 (random codes), at M = 1 and 1
           (GEMV), 16 (GEMV), 17 and 128 (tcgen05 GEMM) and 512."""
     import numpy as np
     import torch
     import nimf
+    if name == "decode_step":
+        nimf.init(0)
+        run_decode_7b_full(nimf, torch, 2, 2, layers=2)
+        print("ncu case %s done" % name)
+        return
     if name != "fw":
         raise SystemExit("unknown --ncu-case %s" % name)
     nimf.init(0)
@@ -814,6 +918,9 @@ def run_ours(args, rank, world, local_rank):
     decode = None
     if args.decode_steps > 0:
         decode = run_decode_7b(nimf, torch, args.decode_steps, max(3, args.warmup // 4), rank, world)
+    decode_full = None
+    if world == 1 and args.decode_steps > 0:
+        decode_full = run_decode_7b_full(nimf, torch, max(5, args.decode_steps // 2), 3)
     prefill = None
     if world == 1 and args.prefill_steps > 0:
         prefill = run_prefill_7b(nimf, torch, args.prefill_steps, 3)
@@ -834,6 +941,8 @@ def run_ours(args, rank, world, local_rank):
             line["cpu_baseline"] = cpu
         if decode is not None:
             line["decode_7b"] = decode
+        if decode_full is not None:
+            line["decode_7b_full_step"] = decode_full
         if prefill is not None:
             line["prefill_7b"] = prefill
         if formats is not None:

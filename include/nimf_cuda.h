@@ -197,6 +197,49 @@ int nimf_matmul2_f32(const float* a1, int64_t m1, int64_t k1, const float* b1, i
  * quant.nim:162), so a bit-exact comparison with dequantizeTensor is possible. */
 int nimf_dequant_w(nimf_weight_t w, float* out_host);
 
+/* ------------------------------------------------------------ decode glue */
+/* The steps between the linears of a Llama-style decode step
+ * (nim_inference.nim), on DEVICE buffers and asynchronous on `stream`, so the
+ * activations stay in HBM across the quantised matmuls.  Products and sums the
+ * reference rounds separately are rounded separately; reductions run in a
+ * tree order. */
+
+/* RMSNormL.forward (nim_inference.nim:143-200, rmsNormPrep :114-140):
+ * y[r][c] = (x[r][c] * inv_r) * w[c], inv_r = 1 / sqrt(sum_c x^2 / cols + eps). */
+int nimf_rmsnorm_dev(const float* x, const float* w, int64_t rows, int64_t cols, float eps,
+                     float* y, void* stream);
+
+/* beAdd (backend.nim) as the residual connections of TransformerBlockLlama
+ * use it (nim_inference.nim:847-875): out = a + b. */
+int nimf_add_dev(const float* a, const float* b, int64_t n, float* out, void* stream);
+
+/* The residual add and the next RMSNorm in one launch: h = a + b (the
+ * residual stream, TransformerBlockLlama.forward nim_inference.nim:847-875),
+ * then y = RMSNorm(h) as nimf_rmsnorm_dev.  h may alias a. */
+int nimf_add_rmsnorm_dev(const float* a, const float* b, const float* w, int64_t rows,
+                         int64_t cols, float eps, float* h, float* y, void* stream);
+
+/* SwiGLUL.forward gating (nim_inference.nim:336-356): out = (g * sigmoid(g)) * up,
+ * sigmoid = 1 / (1 + exp(-g)) (vendor/bybylang/gpubackend.nim:111-114). */
+int nimf_swiglu_dev(const float* gate, const float* up, int64_t n, float* out, void* stream);
+
+/* applyRoPEInplace (nim_inference.nim:261-330) on data [B][T][H][D] in place:
+ * rotate-half with the caller's tables cos_t / sin_t [max_seq][D/2] built as
+ * newRoPEL does (:246-259); position of token t is pos_offset + t. */
+int nimf_rope_dev(float* data, int64_t B, int64_t T, int64_t H, int64_t D, int64_t pos_offset,
+                  const float* cos_t, const float* sin_t, int64_t max_seq, void* stream);
+
+/* One decode token of GQAAttention.forwardDecode (nim_inference.nim:624-748):
+ * appends k_new / v_new [HKV][D] at row `pos` of the caches [HKV][max_seq][D]
+ * (appendKV :404-426), then for each query head h of H (KV head h / (H/HKV)):
+ * scores over the pos + 1 cached rows of (q * scale) . K^T, softmax
+ * (vendor/bybylang/gpubackend.nim:236-250), out[h] = P . V.  D a multiple of 32,
+ * at most 256.  Internal partial buffers grow on first use (make the first
+ * call with a given size before any stream capture). */
+int nimf_attention_decode_dev(const float* q, const float* k_new, const float* v_new,
+                              float* k_cache, float* v_cache, int64_t H, int64_t HKV, int64_t D,
+                              int64_t max_seq, int64_t pos, float scale, float* out, void* stream);
+
 /* ------------------------------------------------------------ .nimq state dicts */
 
 /* One tensor record of a NIMQ2 stream (quant.nim:386-409 readQuantTensor).

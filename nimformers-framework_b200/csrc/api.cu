@@ -277,6 +277,7 @@ int nimf_shutdown(void) {
   g_q4_cache.clear();
   fw_release_scratch();
   release_perm_buffer();
+  release_attn_buffer();
   device_free(g_ctx.stage_in);
   device_free(g_ctx.stage_out);
   if (g_ctx.host_err) cudaFreeHost((void*)g_ctx.host_err);

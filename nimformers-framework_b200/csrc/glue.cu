@@ -1,0 +1,438 @@
+// glue.cu -- the element-wise and attention steps between the linears of a
+// Llama-style decode step (nim_inference.nim), kept on the device so that the
+// activations never return to the host between the quantised matmuls:
+//   RMSNorm          nim_inference.nim:114-200 (rmsNormPrep + forward)
+//   residual add     beAdd (backend.nim) as used by TransformerBlockLlama
+//   SwiGLU gating    nim_inference.nim:336-356, sigmoid as gpubackend.nim:111-114
+//   RoPE             nim_inference.nim:261-330 (rotate-half, caller's tables)
+//   decode attention nim_inference.nim:624-748 with appendKV :404-426 and
+//                    softmax as gpubackend.nim:236-250
+// Every product and sum that the reference rounds separately is rounded
+// separately here (__fmul_rn / __fadd_rn, no contraction); reductions (row
+// sums, dot products, softmax sums) run in a tree order instead of the
+// reference's sequential order.
+#include <algorithm>
+
+#include "device_util.cuh"
+#include "nimf_internal.h"
+
+namespace nimf {
+
+namespace {
+
+__device__ __forceinline__ float block_sum(float v, float* sh) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) sh[w] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int i = 0; i < nw; ++i) t += sh[i];
+  return t;
+}
+
+__device__ __forceinline__ float block_max(float v, float* sh) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) sh[w] = v;
+  __syncthreads();
+  float t = sh[0];
+  for (int i = 1; i < nw; ++i) t = fmaxf(t, sh[i]);
+  return t;
+}
+
+// y = (x * inv) * w with inv = 1 / sqrt(sum x^2 / cols + eps); one block per
+// row.  With a residual (r != nullptr) x is first replaced by x + r, written
+// to h (the residual stream), and normalised.
+__global__ void rmsnorm_kernel(const float* __restrict__ x0, const float* __restrict__ r,
+                               float* __restrict__ h, const float* __restrict__ w, int64_t cols,
+                               float eps, float* __restrict__ y) {
+  __shared__ float sh[32];
+  griddep_launch_dependents();
+  griddep_wait();
+  const int64_t off = (int64_t)blockIdx.x * cols;
+  if (r) {
+    for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) h[off + c] = __fadd_rn(x0[off + c], r[off + c]);
+    __syncthreads();  // each thread reads back only what it wrote; the fence orders it for the block
+  }
+  const float* xr = (r ? h : x0) + off;
+  float* yr = y + off;
+  float s4[4] = {0.f, 0.f, 0.f, 0.f};
+  const int64_t step = blockDim.x;
+  int64_t c = threadIdx.x;
+  for (; c + 3 * step < cols; c += 4 * step) {
+    const float v0 = xr[c], v1 = xr[c + step], v2 = xr[c + 2 * step], v3 = xr[c + 3 * step];
+    s4[0] = __fadd_rn(s4[0], __fmul_rn(v0, v0));
+    s4[1] = __fadd_rn(s4[1], __fmul_rn(v1, v1));
+    s4[2] = __fadd_rn(s4[2], __fmul_rn(v2, v2));
+    s4[3] = __fadd_rn(s4[3], __fmul_rn(v3, v3));
+  }
+  for (; c < cols; c += step) s4[0] = __fadd_rn(s4[0], __fmul_rn(xr[c], xr[c]));
+  float s = __fadd_rn(__fadd_rn(s4[0], s4[1]), __fadd_rn(s4[2], s4[3]));
+  s = block_sum(s, sh);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)cols), eps)));
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) yr[c] = __fmul_rn(__fmul_rn(xr[c], inv), w[c]);
+}
+
+__global__ void add_kernel(const float* __restrict__ a, const float* __restrict__ b, int64_t n,
+                           float* __restrict__ out) {
+  griddep_launch_dependents();
+  griddep_wait();
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = __fadd_rn(a[i], b[i]);
+}
+
+__global__ void swiglu_kernel(const float* __restrict__ g, const float* __restrict__ u, int64_t n,
+                              float* __restrict__ out) {
+  griddep_launch_dependents();
+  griddep_wait();
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g[i])));
+    out[i] = __fmul_rn(__fmul_rn(g[i], sig), u[i]);
+  }
+}
+
+// one thread per (b, t, h, i < D/2) pair of elements
+__global__ void rope_kernel(float* __restrict__ d, int64_t T, int64_t H, int64_t D, int64_t npairs,
+                            int64_t pos_offset, const float* __restrict__ cos_t,
+                            const float* __restrict__ sin_t) {
+  griddep_launch_dependents();
+  griddep_wait();
+  const int64_t half = D / 2;
+  for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < npairs; p += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = p % half, bth = p / half;
+    const int64_t t = (bth / H) % T;
+    const int64_t base = bth * D;
+    const int64_t pos = pos_offset + t;
+    const float c = cos_t[pos * half + i], s = sin_t[pos * half + i];
+    const float x1 = d[base + i], x2 = d[base + i + half];
+    d[base + i] = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(-x2, s));
+    d[base + i + half] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+  }
+}
+
+// appendKV: row pos of every KV head; one thread per element
+__global__ void kv_append_kernel(const float* __restrict__ k_new, const float* __restrict__ v_new,
+                                 float* __restrict__ kc, float* __restrict__ vc, int64_t HKV,
+                                 int64_t D, int64_t max_seq, int64_t pos) {
+  griddep_launch_dependents();
+  griddep_wait();
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < HKV * D; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t h = i / D, dd = i - h * D;
+    kc[(h * max_seq + pos) * D + dd] = k_new[i];
+    vc[(h * max_seq + pos) * D + dd] = v_new[i];
+  }
+}
+
+// Decode attention in position splits (the same softmax, normalised at the
+// end): block (h, j) takes positions [j*ps, min(S, (j+1)*ps)) of query head h
+// (KV head h / nrep), with q pre-scaled and rounded as the reference does,
+// and writes m = max score, l = sum exp(score - m), o[d] = sum exp(score - m)
+// v[s][d] to part[h][j][D + 2].  Each warp keeps kAttnUnroll positions'
+// loads in flight.  Dynamic shared memory: ps scores + 4 warps x D partials.
+constexpr int kAttnWarps = 4;
+constexpr int kAttnUnroll = 4;
+constexpr int kAttnMaxSplit = 8;
+template <int DV>  // features per lane: D = 32 DV
+__global__ void attn_split_kernel(const float* __restrict__ q, const float* __restrict__ kc,
+                                  const float* __restrict__ vc, int64_t nrep, int64_t D,
+                                  int64_t max_seq, int64_t S, int64_t ps, float scale,
+                                  float* __restrict__ part) {
+  extern __shared__ float sc[];
+  __shared__ float sh[32];
+  __shared__ float qs[256];
+  griddep_launch_dependents();
+  griddep_wait();
+  const int64_t h = blockIdx.x, j = blockIdx.y, nsplit = gridDim.y, hkv = h / nrep;
+  const int64_t s0 = j * ps, s1 = min(S, s0 + ps), ns = max((int64_t)0, s1 - s0);
+  const float* K = kc + (hkv * max_seq + s0) * D;
+  const float* V = vc + (hkv * max_seq + s0) * D;
+  float* pp = part + (h * nsplit + j) * (D + 2);
+  for (int64_t dd = threadIdx.x; dd < D; dd += blockDim.x) qs[dd] = __fmul_rn(q[h * D + dd], scale);
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // scores: positions warp, warp + 4, ... in batches of kAttnUnroll per warp
+  float ql[DV];
+#pragma unroll
+  for (int i = 0; i < DV; ++i) ql[i] = qs[lane + 32 * i];
+  for (int64_t b = (int64_t)warp * kAttnUnroll; b < ns; b += kAttnWarps * kAttnUnroll) {
+    // every load of the batch is issued before the products
+    float kv[kAttnUnroll][DV];
+#pragma unroll
+    for (int u = 0; u < kAttnUnroll; ++u)
+#pragma unroll
+      for (int i = 0; i < DV; ++i) kv[u][i] = b + u < ns ? K[(b + u) * D + lane + 32 * i] : 0.f;
+    float a[kAttnUnroll];
+#pragma unroll
+    for (int u = 0; u < kAttnUnroll; ++u) {
+      a[u] = 0.f;
+#pragma unroll
+      for (int i = 0; i < DV; ++i) a[u] = __fadd_rn(a[u], __fmul_rn(ql[i], kv[u][i]));
+    }
+#pragma unroll
+    for (int u = 0; u < kAttnUnroll; ++u) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) a[u] += __shfl_xor_sync(0xffffffffu, a[u], o);
+      if (lane == 0 && b + u < ns) sc[b + u] = a[u];
+    }
+  }
+  __syncthreads();
+  float mx = -INFINITY;
+  for (int64_t s = threadIdx.x; s < ns; s += blockDim.x) mx = fmaxf(mx, sc[s]);
+  mx = block_max(mx, sh);
+  float sum = 0.f;
+  for (int64_t s = threadIdx.x; s < ns; s += blockDim.x) {
+    const float e = expf(__fsub_rn(sc[s], mx));
+    sc[s] = e;
+    sum = __fadd_rn(sum, e);
+  }
+  sum = block_sum(sum, sh);
+  __syncthreads();
+  // P . V with unnormalised weights: warp w takes positions w (mod 4) in
+  // batches, lane the features lane + 32 i; partials summed in warp order
+  float acc[DV];
+#pragma unroll
+  for (int i = 0; i < DV; ++i) acc[i] = 0.f;
+  for (int64_t b = (int64_t)warp * kAttnUnroll; b < ns; b += kAttnWarps * kAttnUnroll) {
+    float vv[kAttnUnroll][DV];
+#pragma unroll
+    for (int u = 0; u < kAttnUnroll; ++u)
+#pragma unroll
+      for (int i = 0; i < DV; ++i) vv[u][i] = b + u < ns ? V[(b + u) * D + lane + 32 * i] : 0.f;
+#pragma unroll
+    for (int u = 0; u < kAttnUnroll; ++u) {
+      if (b + u < ns) {
+        const float e = sc[b + u];
+#pragma unroll
+        for (int i = 0; i < DV; ++i) acc[i] = __fadd_rn(acc[i], __fmul_rn(e, vv[u][i]));
+      }
+    }
+  }
+  float* red = sc + ps;
+#pragma unroll
+  for (int i = 0; i < DV; ++i) red[warp * D + lane + 32 * i] = acc[i];
+  __syncthreads();
+  for (int64_t dd = threadIdx.x; dd < D; dd += blockDim.x) {
+    float a = 0.f;
+    for (int w = 0; w < kAttnWarps; ++w) a = __fadd_rn(a, red[w * D + dd]);
+    pp[dd] = a;
+  }
+  if (threadIdx.x == 0) {
+    pp[D] = mx;
+    pp[D + 1] = sum;
+  }
+}
+
+// out[h][d] = sum_j w_j o_j[d] / sum_j w_j l_j, w_j = exp(m_j - max_j m_j),
+// splits taken in order; one block per head.
+__global__ void attn_combine_kernel(const float* __restrict__ part, int64_t nsplit, int64_t D,
+                                    float* __restrict__ out) {
+  griddep_launch_dependents();
+  griddep_wait();
+  const int64_t h = blockIdx.x;
+  const float* pp = part + h * nsplit * (D + 2);
+  float M = -INFINITY;
+  for (int64_t j = 0; j < nsplit; ++j) M = fmaxf(M, pp[j * (D + 2) + D]);
+  float L = 0.f;
+  for (int64_t j = 0; j < nsplit; ++j) {
+    const float l = pp[j * (D + 2) + D + 1];
+    if (l > 0.f) L = __fadd_rn(L, __fmul_rn(expf(__fsub_rn(pp[j * (D + 2) + D], M)), l));
+  }
+  for (int64_t dd = threadIdx.x; dd < D; dd += blockDim.x) {
+    float a = 0.f;
+    for (int64_t j = 0; j < nsplit; ++j) {
+      const float l = pp[j * (D + 2) + D + 1];
+      if (l > 0.f) a = __fadd_rn(a, __fmul_rn(expf(__fsub_rn(pp[j * (D + 2) + D], M)), pp[j * (D + 2) + dd]));
+    }
+    out[h * D + dd] = __fdiv_rn(a, L);
+  }
+}
+
+// split partials, per device (grown outside stream capture; calls using it
+// are ordered on one stream)
+struct AttnBuf {
+  int device = -1;
+  void* p = nullptr;
+  size_t bytes = 0;
+};
+AttnBuf g_abuf;
+
+int attn_buffer(size_t bytes, cudaStream_t st, float** out) {
+  Context* c = ctx();
+  if (g_abuf.device != c->device || g_abuf.bytes < bytes) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    NIMF_CUDA_TRY(cudaStreamIsCapturing(st, &cs));
+    if (cs != cudaStreamCaptureStatusNone)
+      return set_error(NIMF_ERR_STATE,
+                       "decode attention: its partial buffer must grow, which cannot happen during "
+                       "stream capture; run the same call once before capturing");
+    NIMF_CUDA_TRY(cudaDeviceSynchronize());
+    if (g_abuf.device == c->device) device_free(g_abuf.p);
+    g_abuf = AttnBuf();
+    NIMF_TRY(device_alloc(&g_abuf.p, bytes));
+    g_abuf.device = c->device;
+    g_abuf.bytes = bytes;
+  }
+  *out = (float*)g_abuf.p;
+  return NIMF_OK;
+}
+
+// Launch with programmatic dependent launch allowed, so that a following
+// GEMV can become resident and prefetch its weights while this kernel runs.
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kern)(KArgs...), unsigned grid, unsigned block, size_t smem, cudaStream_t st,
+               Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  NIMF_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ((KArgs)args)...));
+  return NIMF_OK;
+}
+
+unsigned grid_n(int64_t n) {
+  Context* c = ctx();
+  return (unsigned)std::max<int64_t>(1, std::min<int64_t>((int64_t)(c ? c->num_sms : 148) * 8, (n + 255) / 256));
+}
+
+int stream_of(void* stream, cudaStream_t* st) {
+  Context* c;
+  NIMF_TRY(require_ctx(&c));
+  *st = stream ? (cudaStream_t)stream : c->stream;
+  return NIMF_OK;
+}
+
+}  // namespace
+
+void release_attn_buffer() {
+  device_free(g_abuf.p);
+  g_abuf = AttnBuf();
+}
+
+}  // namespace nimf
+
+using namespace nimf;
+
+extern "C" {
+
+int nimf_rmsnorm_dev(const float* x, const float* w, int64_t rows, int64_t cols, float eps,
+                     float* y, void* stream) {
+  cudaStream_t st;
+  NIMF_TRY(stream_of(stream, &st));
+  if (rows < 0 || cols < 0 || rows > INT32_MAX) return set_error(NIMF_ERR_SHAPE, "rmsnorm: rows %lld cols %lld", (long long)rows, (long long)cols);
+  if (rows == 0 || cols == 0) return NIMF_OK;
+  if (!x || !w || !y) return set_error(NIMF_ERR_ARG, "rmsnorm: NULL buffer");
+  NIMF_TRY(launch_pdl(rmsnorm_kernel, (unsigned)rows, 1024, 0, st, x, (const float*)nullptr,
+                      (float*)nullptr, w, cols, eps, y));
+  return NIMF_OK;
+}
+
+int nimf_add_rmsnorm_dev(const float* a, const float* b, const float* w, int64_t rows,
+                         int64_t cols, float eps, float* h, float* y, void* stream) {
+  cudaStream_t st;
+  NIMF_TRY(stream_of(stream, &st));
+  if (rows < 0 || cols < 0 || rows > INT32_MAX) return set_error(NIMF_ERR_SHAPE, "add_rmsnorm: rows %lld cols %lld", (long long)rows, (long long)cols);
+  if (rows == 0 || cols == 0) return NIMF_OK;
+  if (!a || !b || !w || !h || !y) return set_error(NIMF_ERR_ARG, "add_rmsnorm: NULL buffer");
+  NIMF_TRY(launch_pdl(rmsnorm_kernel, (unsigned)rows, 1024, 0, st, a, b, h, w, cols, eps, y));
+  return NIMF_OK;
+}
+
+int nimf_add_dev(const float* a, const float* b, int64_t n, float* out, void* stream) {
+  cudaStream_t st;
+  NIMF_TRY(stream_of(stream, &st));
+  if (n < 0) return set_error(NIMF_ERR_SHAPE, "add: n < 0");
+  if (n == 0) return NIMF_OK;
+  if (!a || !b || !out) return set_error(NIMF_ERR_ARG, "add: NULL buffer");
+  NIMF_TRY(launch_pdl(add_kernel, grid_n(n), 256, 0, st, a, b, n, out));
+  return NIMF_OK;
+}
+
+int nimf_swiglu_dev(const float* gate, const float* up, int64_t n, float* out, void* stream) {
+  cudaStream_t st;
+  NIMF_TRY(stream_of(stream, &st));
+  if (n < 0) return set_error(NIMF_ERR_SHAPE, "swiglu: n < 0");
+  if (n == 0) return NIMF_OK;
+  if (!gate || !up || !out) return set_error(NIMF_ERR_ARG, "swiglu: NULL buffer");
+  NIMF_TRY(launch_pdl(swiglu_kernel, grid_n(n), 256, 0, st, gate, up, n, out));
+  return NIMF_OK;
+}
+
+int nimf_rope_dev(float* data, int64_t B, int64_t T, int64_t H, int64_t D, int64_t pos_offset,
+                  const float* cos_t, const float* sin_t, int64_t max_seq, void* stream) {
+  cudaStream_t st;
+  NIMF_TRY(stream_of(stream, &st));
+  if (B < 0 || T < 0 || H < 0 || D < 0 || (D & 1) || pos_offset < 0)
+    return set_error(NIMF_ERR_SHAPE, "rope: bad shape (D must be even)");
+  if (pos_offset + T > max_seq)
+    return set_error(NIMF_ERR_SHAPE, "rope: positions up to %lld exceed max_seq %lld",
+                     (long long)(pos_offset + T), (long long)max_seq);
+  const int64_t npairs = B * T * H * (D / 2);
+  if (npairs == 0) return NIMF_OK;
+  if (!data || !cos_t || !sin_t) return set_error(NIMF_ERR_ARG, "rope: NULL buffer");
+  NIMF_TRY(launch_pdl(rope_kernel, grid_n(npairs), 256, 0, st, data, T, H, D, npairs, pos_offset,
+                      cos_t, sin_t));
+  return NIMF_OK;
+}
+
+int nimf_attention_decode_dev(const float* q, const float* k_new, const float* v_new,
+                              float* k_cache, float* v_cache, int64_t H, int64_t HKV, int64_t D,
+                              int64_t max_seq, int64_t pos, float scale, float* out, void* stream) {
+  cudaStream_t st;
+  NIMF_TRY(stream_of(stream, &st));
+  if (H <= 0 || HKV <= 0 || H % HKV || D <= 0 || D > 256 || D % 32 || pos < 0 || pos >= max_seq)
+    return set_error(NIMF_ERR_SHAPE, "attention: H %lld HKV %lld D %lld (a multiple of 32, <= 256) pos %lld max_seq %lld",
+                     (long long)H, (long long)HKV, (long long)D, (long long)pos, (long long)max_seq);
+  const int64_t S = pos + 1;
+  if (S > 8 * 40000) return set_error(NIMF_ERR_UNSUPPORTED, "attention: %lld positions exceed the score buffers", (long long)S);
+  if (!q || !k_new || !v_new || !k_cache || !v_cache || !out) return set_error(NIMF_ERR_ARG, "attention: NULL buffer");
+  NIMF_TRY(launch_pdl(kv_append_kernel, grid_n(HKV * D), 256, 0, st, k_new, v_new, k_cache,
+                      v_cache, HKV, D, max_seq, pos));
+  // position splits: about 64 positions per block, at most 8 per head
+  const int64_t nsplit = std::min<int64_t>(kAttnMaxSplit, (S + 63) / 64);
+  const int64_t ps = (S + nsplit - 1) / nsplit;
+  const size_t smem = (size_t)(ps + kAttnWarps * D) * 4;
+  void (*kern)(const float*, const float*, const float*, int64_t, int64_t, int64_t, int64_t,
+               int64_t, float, float*);
+  switch (D / 32) {
+    case 1: kern = attn_split_kernel<1>; break;
+    case 2: kern = attn_split_kernel<2>; break;
+    case 3: kern = attn_split_kernel<3>; break;
+    case 4: kern = attn_split_kernel<4>; break;
+    case 5: kern = attn_split_kernel<5>; break;
+    case 6: kern = attn_split_kernel<6>; break;
+    case 7: kern = attn_split_kernel<7>; break;
+    default: kern = attn_split_kernel<8>; break;
+  }
+  if (smem > 48 * 1024)
+    NIMF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+  float* part = nullptr;
+  NIMF_TRY(attn_buffer((size_t)(H * nsplit * (D + 2)) * 4, st, &part));
+  {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)H, (unsigned)nsplit);
+    cfg.blockDim = dim3(kAttnWarps * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    NIMF_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, q, (const float*)k_cache,
+                                     (const float*)v_cache, H / HKV, D, max_seq, S, ps, scale, part));
+  }
+  NIMF_TRY(launch_pdl(attn_combine_kernel, (unsigned)H, 128, 0, st, (const float*)part, nsplit, D, out));
+  return NIMF_OK;
+}
+
+}  // extern "C"

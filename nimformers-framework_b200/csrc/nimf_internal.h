@@ -197,6 +197,7 @@ int fw_gemm_tc(const FWLayout& L, const float* x, int64_t m, float* y, cudaStrea
 int gather_cols(const float* x, int64_t m, int64_t k, const int32_t* perm, const float** out,
                 cudaStream_t st);
 void release_perm_buffer();
+void release_attn_buffer();  // glue.cu: decode attention's split partials
 
 int fp4_gemv(const FP4Weight& w, const float* x, int64_t m, float* y, cudaStream_t st);
 int fp4_dequant(const FP4Weight& w, float* out, cudaStream_t st);

@@ -609,3 +609,113 @@ void orc_gemv_f64(const float* x, const float* w, int64_t m, int64_t k, int64_t 
       y[i * n + j] = (float)acc;
     }
 }
+
+/* ------------------------------------------------------------------------ */
+/* Decode glue of nim_inference.nim (Llama path).                            */
+
+/* nim_inference.nim:143-200 RMSNorm.forward with rmsNormPrep :114-140:
+ * x2 = x * x, sumSq = beMatmul(x2, ones) (orc_cpu_matmul order), invStd =
+ * 1 / sqrt(sumSq / cols + eps), then (x * invStd) * w as two rounded muls. */
+void orc_rmsnorm(const float* x, const float* w, int64_t rows, int64_t cols, float eps,
+                 float* y) {
+  float* x2 = (float*)malloc((size_t)cols * sizeof(float));
+  float* ones = (float*)malloc((size_t)cols * sizeof(float));
+  for (int64_t c = 0; c < cols; ++c) ones[c] = 1.0f;
+  for (int64_t r = 0; r < rows; ++r) {
+    const float* xr = x + r * cols;
+    for (int64_t c = 0; c < cols; ++c) x2[c] = xr[c] * xr[c];
+    float ss;
+    orc_cpu_matmul(x2, ones, 1, cols, 1, &ss);
+    float inv = 1.0f / sqrtf(ss / (float)cols + eps);
+    for (int64_t c = 0; c < cols; ++c) {
+      float t = xr[c] * inv;
+      y[r * cols + c] = t * w[c];
+    }
+  }
+  free(x2);
+  free(ones);
+}
+
+/* nim_inference.nim:336-356 SwiGLUL gating: sig = 1 / (1 + exp(-g))
+ * (vendor/bybylang/gpubackend.nim:111-114 cpuSigmoid), out = (g * sig) * up. */
+void orc_swiglu(const float* g, const float* u, int64_t n, float* out) {
+  for (int64_t i = 0; i < n; ++i) {
+    float sig = 1.0f / (1.0f + expf(-g[i]));
+    float t = g[i] * sig;
+    out[i] = t * u[i];
+  }
+}
+
+/* nim_inference.nim:261-330 applyRoPEInplace on [B][T][H][D]:
+ * out = x * cosFull + rotHalf * sinFull, rotHalf = concat(-x2, x1), with the
+ * newRoPEL tables cos_t / sin_t [max_seq][D/2] (:246-259). */
+void orc_rope(float* data, int64_t B, int64_t T, int64_t H, int64_t D, int64_t pos_offset,
+              const float* cos_t, const float* sin_t) {
+  int64_t half = D / 2;
+  for (int64_t b = 0; b < B; ++b)
+    for (int64_t t = 0; t < T; ++t) {
+      int64_t pos = pos_offset + t;
+      for (int64_t h = 0; h < H; ++h) {
+        float* d = data + ((b * T + t) * H + h) * D;
+        for (int64_t i = 0; i < half; ++i) {
+          float c = cos_t[pos * half + i], s = sin_t[pos * half + i];
+          float x1 = d[i], x2 = d[i + half];
+          float a1 = x1 * c, b1 = (-x2) * s;
+          float a2 = x2 * c, b2 = x1 * s;
+          d[i] = a1 + b1;
+          d[i + half] = a2 + b2;
+        }
+      }
+    }
+}
+
+/* nim_inference.nim:404-426 appendKV (row pos of each KV head, cache layout
+ * [HKV][max_seq][D]) then the attention core of forwardDecode :624-748: per
+ * KV head, qGroup = q * scale, scores = qGroup . K^T (orc_cpu_matmul),
+ * softmax as vendor/bybylang/gpubackend.nim:236-250 cpuSoftmax, out = P . V. */
+void orc_attention_decode(const float* q, const float* k_new, const float* v_new,
+                          float* k_cache, float* v_cache, int64_t H, int64_t HKV, int64_t D,
+                          int64_t max_seq, int64_t pos, float scale, float* out) {
+  int64_t nrep = H / HKV, S = pos + 1;
+  for (int64_t h = 0; h < HKV; ++h)
+    for (int64_t d = 0; d < D; ++d) {
+      k_cache[(h * max_seq + pos) * D + d] = k_new[h * D + d];
+      v_cache[(h * max_seq + pos) * D + d] = v_new[h * D + d];
+    }
+  float* kt = (float*)malloc((size_t)(D * S) * sizeof(float));
+  float* vb = (float*)malloc((size_t)(S * D) * sizeof(float));
+  float* qg = (float*)malloc((size_t)(nrep * D) * sizeof(float));
+  float* sc = (float*)malloc((size_t)(nrep * S) * sizeof(float));
+  float* og = (float*)malloc((size_t)(nrep * D) * sizeof(float));
+  for (int64_t hk = 0; hk < HKV; ++hk) {
+    for (int64_t s = 0; s < S; ++s)
+      for (int64_t d = 0; d < D; ++d) {
+        kt[d * S + s] = k_cache[(hk * max_seq + s) * D + d];
+        vb[s * D + d] = v_cache[(hk * max_seq + s) * D + d];
+      }
+    for (int64_t r = 0; r < nrep; ++r)
+      for (int64_t d = 0; d < D; ++d) qg[r * D + d] = q[(hk * nrep + r) * D + d] * scale;
+    orc_cpu_matmul(qg, kt, nrep, D, S, sc);
+    for (int64_t r = 0; r < nrep; ++r) {
+      float* row = sc + r * S;
+      float mx = row[0];
+      for (int64_t s = 1; s < S; ++s)
+        if (row[s] > mx) mx = row[s];
+      float sum = 0.0f;
+      for (int64_t s = 0; s < S; ++s) {
+        float e = expf(row[s] - mx);
+        row[s] = e;
+        sum += e;
+      }
+      for (int64_t s = 0; s < S; ++s) row[s] /= sum;
+    }
+    orc_cpu_matmul(sc, vb, nrep, S, D, og);
+    for (int64_t r = 0; r < nrep; ++r)
+      for (int64_t d = 0; d < D; ++d) out[(hk * nrep + r) * D + d] = og[r * D + d];
+  }
+  free(kt);
+  free(vb);
+  free(qg);
+  free(sc);
+  free(og);
+}

@@ -152,6 +152,25 @@ void orc_dequantize_fp4_block16(const uint8_t* packed, const uint8_t* block_scal
 void orc_gemv_f64(const float* x, const float* w, int64_t m, int64_t k, int64_t n,
                   float* y);
 
+/* ------------------------------------------------ nim_inference.nim decode glue */
+
+/* nim_inference.nim:143-200 (+ rmsNormPrep :114-140): y = (x * invStd) * w,
+ * invStd = 1 / sqrt(sum(x*x) / cols + eps), sum in orc_cpu_matmul order. */
+void orc_rmsnorm(const float* x, const float* w, int64_t rows, int64_t cols, float eps,
+                 float* y);
+/* nim_inference.nim:336-356 + vendor/bybylang/gpubackend.nim:111-114:
+ * out = (g * (1 / (1 + exp(-g)))) * u. */
+void orc_swiglu(const float* g, const float* u, int64_t n, float* out);
+/* nim_inference.nim:261-330 applyRoPEInplace (rotate-half) with the caller's
+ * cos / sin tables [max_seq][D/2] (newRoPEL :246-259). */
+void orc_rope(float* data, int64_t B, int64_t T, int64_t H, int64_t D, int64_t pos_offset,
+              const float* cos_t, const float* sin_t);
+/* nim_inference.nim:404-426 appendKV + forwardDecode :624-748 attention core
+ * (softmax as vendor/bybylang/gpubackend.nim:236-250). */
+void orc_attention_decode(const float* q, const float* k_new, const float* v_new,
+                          float* k_cache, float* v_cache, int64_t H, int64_t HKV, int64_t D,
+                          int64_t max_seq, int64_t pos, float scale, float* out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -64,6 +64,11 @@ def lib():
             "orc_quantize_fp4_block16": (None, [_f32p, _i64, _i64, ctypes.c_float, _u8p, _u8p]),
             "orc_dequantize_fp4_block16": (None, [_u8p, _u8p, ctypes.c_float, _i64, _i64, _f32p]),
             "orc_gemv_f64": (None, [_f32p, _f32p, _i64, _i64, _i64, _f32p]),
+            "orc_rmsnorm": (None, [_f32p, _f32p, _i64, _i64, ctypes.c_float, _f32p]),
+            "orc_swiglu": (None, [_f32p, _f32p, _i64, _f32p]),
+            "orc_rope": (None, [_f32p, _i64, _i64, _i64, _i64, _i64, _f32p, _f32p]),
+            "orc_attention_decode": (None, [_f32p, _f32p, _f32p, _f32p, _f32p, _i64, _i64, _i64,
+                                            _i64, _i64, ctypes.c_float, _f32p]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -265,3 +270,36 @@ def gemv_f64(x, w):
     y = np.empty(m * n, np.float32)
     lib().orc_gemv_f64(x.ravel(), w.ravel(), m, k, n, y)
     return y.reshape(m, n)
+
+
+# ------------------------------------------------ nim_inference.nim decode glue
+def rmsnorm(x, w, eps):
+    x = _c(x, np.float32)
+    rows, cols = x.shape
+    y = np.empty(rows * cols, np.float32)
+    lib().orc_rmsnorm(x.ravel(), _c(w, np.float32).ravel(), rows, cols, ctypes.c_float(eps), y)
+    return y.reshape(rows, cols)
+
+
+def swiglu(g, u):
+    g = _c(g, np.float32).ravel()
+    out = np.empty(g.size, np.float32)
+    lib().orc_swiglu(g, _c(u, np.float32).ravel(), g.size, out)
+    return out
+
+
+def rope(data, B, T, H, D, pos_offset, cos_t, sin_t):
+    d = np.array(data, np.float32).ravel()
+    lib().orc_rope(d, B, T, H, D, pos_offset, _c(cos_t, np.float32).ravel(), _c(sin_t, np.float32).ravel())
+    return d
+
+
+def attention_decode(q, k_new, v_new, k_cache, v_cache, H, HKV, D, max_seq, pos, scale):
+    """Returns (out[H*D], k_cache, v_cache) with row pos appended."""
+    kc = np.array(k_cache, np.float32).ravel()
+    vc = np.array(v_cache, np.float32).ravel()
+    out = np.empty(H * D, np.float32)
+    lib().orc_attention_decode(_c(q, np.float32).ravel(), _c(k_new, np.float32).ravel(),
+                               _c(v_new, np.float32).ravel(), kc, vc, H, HKV, D, max_seq, pos,
+                               ctypes.c_float(scale), out)
+    return out, kc, vc

@@ -1,0 +1,128 @@
+"""Device-resident decode glue (RMSNorm, residual add, SwiGLU gating, RoPE,
+decode attention with the KV-cache append) through the C ABI against the CPU
+oracle's restatements of nim_inference.nim.  Element-wise steps whose every
+rounding the reference fixes (residual add, RoPE with the caller's tables, the
+KV-cache append) are bit-exact; steps with reductions (row sums, dot
+products, softmax sums) or exp are held to max|y - y_ref| / max|y_ref| <= 1e-4,
+well inside the path's 1e-3 bar."""
+import ctypes
+
+import numpy as np
+import pytest
+
+import pyoracle as O
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-4   # sequential vs tree fp32 sums of up to 11008 terms differ by ~1e-5
+
+
+def rel_err(y, ref):
+    y, ref = np.asarray(y, np.float64), np.asarray(ref, np.float64)
+    return float(np.max(np.abs(y - ref)) / max(np.max(np.abs(ref)), 1e-30))
+
+
+@pytest.fixture(scope="module")
+def torch_dev(nimf_gpu):
+    import torch
+    return torch
+
+
+def dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+
+
+def p(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def test_rmsnorm_add_swiglu(nimf_gpu, torch_dev):
+    torch = torch_dev
+    L = nimf_gpu.lib()
+    rng = np.random.default_rng(1)
+    for rows, cols in ((1, 4096), (3, 1000), (8, 11008)):
+        x = rng.standard_normal((rows, cols)).astype(np.float32)
+        w = rng.uniform(0.5, 1.5, cols).astype(np.float32)
+        y = torch.empty(rows, cols, device="cuda")
+        dx, dw = dev(torch, x), dev(torch, w)   # held until the kernel has run
+        nimf_gpu.check(L.nimf_rmsnorm_dev(p(dx), p(dw), rows, cols, 1e-6, p(y), None))
+        torch.cuda.synchronize()
+        assert rel_err(y.cpu().numpy(), O.rmsnorm(x, w, 1e-6)) <= TOL
+    # residual add fused with the next RMSNorm: h bit-exact, y as rmsnorm(h)
+    rows, cols = 2, 4096
+    a0 = rng.standard_normal((rows, cols)).astype(np.float32)
+    r0 = rng.standard_normal((rows, cols)).astype(np.float32)
+    w0 = rng.uniform(0.5, 1.5, cols).astype(np.float32)
+    da0, dr0, dw0 = dev(torch, a0), dev(torch, r0), dev(torch, w0)
+    hh = torch.empty(rows, cols, device="cuda")
+    yy = torch.empty(rows, cols, device="cuda")
+    nimf_gpu.check(L.nimf_add_rmsnorm_dev(p(da0), p(dr0), p(dw0), rows, cols, 1e-6, p(hh), p(yy), None))
+    torch.cuda.synchronize()
+    assert np.array_equal(hh.cpu().numpy().view(np.uint32), (a0 + r0).view(np.uint32))
+    assert rel_err(yy.cpu().numpy(), O.rmsnorm(a0 + r0, w0, 1e-6)) <= TOL
+    a = rng.standard_normal(10007).astype(np.float32)
+    b = rng.standard_normal(10007).astype(np.float32)
+    out = torch.empty(10007, device="cuda")
+    da, db = dev(torch, a), dev(torch, b)
+    nimf_gpu.check(L.nimf_add_dev(p(da), p(db), a.size, p(out), None))
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), (a + b).view(np.uint32))
+    g = (rng.standard_normal(11008) * 3).astype(np.float32)
+    u = rng.standard_normal(11008).astype(np.float32)
+    gated = torch.empty(g.size, device="cuda")
+    dg, du = dev(torch, g), dev(torch, u)
+    nimf_gpu.check(L.nimf_swiglu_dev(p(dg), p(du), g.size, p(gated), None))
+    torch.cuda.synchronize()
+    assert rel_err(gated.cpu().numpy(), O.swiglu(g, u)) <= TOL
+
+
+def rope_tables(D, max_seq, theta=10000.0):
+    """newRoPEL (nim_inference.nim:246-259) in float32."""
+    half = D // 2
+    inv = (1.0 / np.power(np.float32(theta), np.arange(half, dtype=np.float32) / np.float32(half))).astype(np.float32)
+    ang = (np.arange(max_seq, dtype=np.float32)[:, None] * inv[None, :]).astype(np.float32)
+    return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+
+def test_rope_bit_exact(nimf_gpu, torch_dev):
+    torch = torch_dev
+    L = nimf_gpu.lib()
+    rng = np.random.default_rng(2)
+    D, max_seq = 128, 640
+    ct, st = rope_tables(D, max_seq)
+    dct, dst = dev(torch, ct), dev(torch, st)
+    for B, T, H, off in ((1, 1, 32, 517), (2, 3, 8, 5), (1, 16, 4, 0)):
+        x = rng.standard_normal((B, T, H, D)).astype(np.float32)
+        d = dev(torch, x)
+        nimf_gpu.check(L.nimf_rope_dev(p(d), B, T, H, D, off, p(dct), p(dst), max_seq, None))
+        torch.cuda.synchronize()
+        ref = O.rope(x, B, T, H, D, off, ct, st)
+        assert np.array_equal(d.cpu().numpy().ravel().view(np.uint32), ref.view(np.uint32))
+    with pytest.raises(nimf_gpu.CatchableError, match="SHAPE"):
+        nimf_gpu.check(L.nimf_rope_dev(p(d), 1, 2, 1, D, max_seq - 1, p(dct), p(dst), max_seq, None))
+
+
+@pytest.mark.parametrize("H,HKV,pos", [(32, 32, 0), (32, 8, 1), (32, 8, 300), (8, 2, 639)])
+def test_attention_decode(nimf_gpu, torch_dev, H, HKV, pos):
+    torch = torch_dev
+    L = nimf_gpu.lib()
+    rng = np.random.default_rng(H + pos)
+    D, max_seq = 128, 640
+    kc = rng.standard_normal(HKV * max_seq * D).astype(np.float32)
+    vc = rng.standard_normal(HKV * max_seq * D).astype(np.float32)
+    q = rng.standard_normal(H * D).astype(np.float32)
+    kn = rng.standard_normal(HKV * D).astype(np.float32)
+    vn = rng.standard_normal(HKV * D).astype(np.float32)
+    scale = np.float32(1.0 / np.sqrt(np.float32(D)))
+    dkc, dvc = dev(torch, kc), dev(torch, vc)
+    dq, dkn, dvn = dev(torch, q), dev(torch, kn), dev(torch, vn)
+    out = torch.empty(H * D, device="cuda")
+    nimf_gpu.check(L.nimf_attention_decode_dev(p(dq), p(dkn), p(dvn), p(dkc), p(dvc), H, HKV, D,
+                                               max_seq, pos, float(scale), p(out), None))
+    torch.cuda.synchronize()
+    ref, rkc, rvc = O.attention_decode(q, kn, vn, kc, vc, H, HKV, D, max_seq, pos, float(scale))
+    assert np.array_equal(dkc.cpu().numpy().view(np.uint32), rkc.view(np.uint32))
+    assert np.array_equal(dvc.cpu().numpy().view(np.uint32), rvc.view(np.uint32))
+    assert rel_err(out.cpu().numpy(), ref) <= TOL
+    with pytest.raises(nimf_gpu.CatchableError, match="SHAPE"):
+        nimf_gpu.check(L.nimf_attention_decode_dev(p(dq), p(dkn), p(dvn), p(dkc), p(dvc), H, HKV,
+                                                   D, max_seq, max_seq, float(scale), p(out), None))
