@@ -917,7 +917,16 @@ def run_ours(args, rank, world, local_rank):
     graph1.reset()
     decode = None
     if args.decode_steps > 0:
-        decode = run_decode_7b(nimf, torch, args.decode_steps, max(3, args.warmup // 4), rank, world)
+        if world == 1:
+            decode = run_decode_7b(nimf, torch, args.decode_steps, max(3, args.warmup // 4))
+        else:
+            # every rank runs the same steps; an error raised on all of them is
+            # reported in the line instead of dropping the GEMV measurement
+            try:
+                decode = run_decode_7b(nimf, torch, args.decode_steps, max(3, args.warmup // 4),
+                                       rank, world)
+            except Exception as e:  # noqa: BLE001
+                decode = {"error": "%s: %s" % (type(e).__name__, e)}
     decode_full = None
     if world == 1 and args.decode_steps > 0:
         decode_full = run_decode_7b_full(nimf, torch, max(5, args.decode_steps // 2), 3)
