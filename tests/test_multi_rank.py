@@ -85,3 +85,54 @@ def test_shard_rows_cover_rows_once():
             assert max(sizes) - min(sizes) <= 16
     with pytest.raises(ValueError):
         nimf.shard_rows(10, 2, 2)
+
+
+def test_7b_projection_shards_are_equal():
+    """The sharded decode measurement all-gathers equal shards: every 7B-shape
+    projection (4096, 11008 and 32000 output channels) splits into whole
+    16-row tiles of equal size at 1, 2, 4 and 8 GPUs."""
+    import nimf
+    for n in (4096, 11008, 32000):
+        for world in (1, 2, 4, 8):
+            sizes = [r1 - r0 for r0, r1 in (nimf.shard_rows(n, world, r) for r in range(world))]
+            assert sizes == [n // world] * world, (n, world, sizes)
+            assert all(s % 16 == 0 for s in sizes)
+
+
+def _gather_layout_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        rng = np.random.default_rng(0)
+        m, n, k = 3, 64, 32
+        ws = [rng.standard_normal((n, k)).astype(np.float32) for _ in range(3)]   # q, k, v
+        x = rng.standard_normal((m, k)).astype(np.float32)
+        r0, r1 = nimf.shard_rows(n, world, rank)
+        local = torch.from_numpy(np.stack([x @ w[r0:r1].T for w in ws]).astype(np.float32))
+        g = torch.empty(world, 3, m, r1 - r0)
+        dist.all_gather_into_tensor(g.view(-1), local.contiguous().view(-1))
+        # the sharded decode step's reassembly of the q output as the next x
+        x_o = g[:, 0].permute(1, 0, 2).reshape(m, n).numpy()
+        # reference: the shards' q outputs side by side, computed the same way
+        ref = np.concatenate([x @ ws[0][a:b].T for a, b in
+                              (nimf.shard_rows(n, world, r) for r in range(world))], axis=1)
+        q.put((rank, bool(np.array_equal(x_o, ref.astype(np.float32)))))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_decode_gather_layout():
+    """The layout the N-sharded decode measurement rebuilds after each
+    projection group's all-gather ([rank][proj][M][N/G] -> [M][N]) equals the
+    unsharded output, with two gloo ranks."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gather_layout_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p_ in procs:
+        p_.start()
+    res = [q.get(timeout=120) for _ in range(2)]
+    for p_ in procs:
+        p_.join(timeout=120)
+    assert all(ok for _, ok in res), res
