@@ -955,8 +955,7 @@ int launch_fast(const Piece* pcs, int npc, const float* x, int64_t ldx, int mc, 
     attr_dev = c->device;
   }
   // Pick direct mode or a k-split count (= cluster size) by the estimated
-  // weight bytes of the busiest CTA (in units of 16 rows x one group); split
-  // mode pays for its cluster reduction with a 25% penalty.
+  // weight bytes of the busiest CTA (in units of 16 rows x one group).
   int best_s = -1, best_gps = 0, best_nclu = 1, best_ns = 0, best_kbg = 0, best_nkb = 1;
   double best_score = 1e30;
   {
@@ -985,7 +984,10 @@ int launch_fast(const Piece* pcs, int npc, const float* x, int64_t ldx, int mc, 
     const SmemLayout L0 = q4g_smem_layout(MODE, KQG, gps, gps, mc, 0, tchunk, false);
     const int ns = ring_stages(L0, KQG, gps, false);
     if (ns == 0 || (size_t)ns * L0.stage < (size_t)tchunk * 512) continue;
-    const double score = 1.25 * tchunk * gps;
+    // split mode pays for its cluster reduction: measured on the 7B decode
+    // stack, a 25% penalty picks the faster mode for up to 4 rows of x, none
+    // for up to 8 (batch 8: 3,255 vs 2,872 tok/s; batch 1 keeps 735)
+    const double score = (MODE == 1 ? 1.25 : 1.0) * tchunk * gps;
     if (score < best_score - 1e-9) {
       best_score = score;
       best_s = ss;
