@@ -54,6 +54,35 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x0, const float* __rest
   griddep_launch_dependents();
   griddep_wait();
   const int64_t off = (int64_t)blockIdx.x * cols;
+  const int64_t step = blockDim.x;
+  if (cols <= 4 * step) {
+    // the row fits in four values per thread: one read of x (and r), the
+    // values stay in registers between the sum and the scaling
+    float v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t c = threadIdx.x + u * step;
+      v[u] = 0.f;
+      if (c < cols) {
+        float a = x0[off + c];
+        if (r) {
+          a = __fadd_rn(a, r[off + c]);
+          h[off + c] = a;
+        }
+        v[u] = a;
+      }
+    }
+    float s = __fadd_rn(__fadd_rn(__fmul_rn(v[0], v[0]), __fmul_rn(v[1], v[1])),
+                        __fadd_rn(__fmul_rn(v[2], v[2]), __fmul_rn(v[3], v[3])));
+    s = block_sum(s, sh);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)cols), eps)));
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t c = threadIdx.x + u * step;
+      if (c < cols) y[off + c] = __fmul_rn(__fmul_rn(v[u], inv), w[c]);
+    }
+    return;
+  }
   if (r) {
     for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) h[off + c] = __fadd_rn(x0[off + c], r[off + c]);
     __syncthreads();  // each thread reads back only what it wrote; the fence orders it for the block
@@ -61,7 +90,6 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x0, const float* __rest
   const float* xr = (r ? h : x0) + off;
   float* yr = y + off;
   float s4[4] = {0.f, 0.f, 0.f, 0.f};
-  const int64_t step = blockDim.x;
   int64_t c = threadIdx.x;
   for (; c + 3 * step < cols; c += 4 * step) {
     const float v0 = xr[c], v1 = xr[c + step], v2 = xr[c + 2 * step], v3 = xr[c + 3 * step];

@@ -39,7 +39,7 @@ def test_rmsnorm_add_swiglu(nimf_gpu, torch_dev):
     torch = torch_dev
     L = nimf_gpu.lib()
     rng = np.random.default_rng(1)
-    for rows, cols in ((1, 4096), (3, 1000), (8, 11008)):
+    for rows, cols in ((1, 4096), (3, 1000), (2, 4097), (8, 11008)):
         x = rng.standard_normal((rows, cols)).astype(np.float32)
         w = rng.uniform(0.5, 1.5, cols).astype(np.float32)
         y = torch.empty(rows, cols, device="cuda")
@@ -47,18 +47,19 @@ def test_rmsnorm_add_swiglu(nimf_gpu, torch_dev):
         nimf_gpu.check(L.nimf_rmsnorm_dev(p(dx), p(dw), rows, cols, 1e-6, p(y), None))
         torch.cuda.synchronize()
         assert rel_err(y.cpu().numpy(), O.rmsnorm(x, w, 1e-6)) <= TOL
-    # residual add fused with the next RMSNorm: h bit-exact, y as rmsnorm(h)
-    rows, cols = 2, 4096
-    a0 = rng.standard_normal((rows, cols)).astype(np.float32)
-    r0 = rng.standard_normal((rows, cols)).astype(np.float32)
-    w0 = rng.uniform(0.5, 1.5, cols).astype(np.float32)
-    da0, dr0, dw0 = dev(torch, a0), dev(torch, r0), dev(torch, w0)
-    hh = torch.empty(rows, cols, device="cuda")
-    yy = torch.empty(rows, cols, device="cuda")
-    nimf_gpu.check(L.nimf_add_rmsnorm_dev(p(da0), p(dr0), p(dw0), rows, cols, 1e-6, p(hh), p(yy), None))
-    torch.cuda.synchronize()
-    assert np.array_equal(hh.cpu().numpy().view(np.uint32), (a0 + r0).view(np.uint32))
-    assert rel_err(yy.cpu().numpy(), O.rmsnorm(a0 + r0, w0, 1e-6)) <= TOL
+    # residual add fused with the next RMSNorm: h bit-exact, y as rmsnorm(h);
+    # rows of up to 4096 values stay in registers, longer rows are re-read
+    for rows, cols in ((2, 4096), (1, 4097), (3, 11008)):
+        a0 = rng.standard_normal((rows, cols)).astype(np.float32)
+        r0 = rng.standard_normal((rows, cols)).astype(np.float32)
+        w0 = rng.uniform(0.5, 1.5, cols).astype(np.float32)
+        da0, dr0, dw0 = dev(torch, a0), dev(torch, r0), dev(torch, w0)
+        hh = torch.empty(rows, cols, device="cuda")
+        yy = torch.empty(rows, cols, device="cuda")
+        nimf_gpu.check(L.nimf_add_rmsnorm_dev(p(da0), p(dr0), p(dw0), rows, cols, 1e-6, p(hh), p(yy), None))
+        torch.cuda.synchronize()
+        assert np.array_equal(hh.cpu().numpy().view(np.uint32), (a0 + r0).view(np.uint32))
+        assert rel_err(yy.cpu().numpy(), O.rmsnorm(a0 + r0, w0, 1e-6)) <= TOL
     a = rng.standard_normal(10007).astype(np.float32)
     b = rng.standard_normal(10007).astype(np.float32)
     out = torch.empty(10007, device="cuda")
