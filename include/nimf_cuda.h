@@ -209,6 +209,14 @@ int nimf_dequant_w(nimf_weight_t w, float* out_host);
 int nimf_rmsnorm_dev(const float* x, const float* w, int64_t rows, int64_t cols, float eps,
                      float* y, void* stream);
 
+/* LayerNorm.forward (nimformer.nim:188-197) = beLayernorm (backend.nim:149-150),
+ * following the CPU path cpuLayernorm (vendor/bybylang/gpubackend.nim:252-266):
+ * mean = sum_c x / cols, var = sum_c (x - mean)^2 / cols,
+ * y[r][c] = ((x[r][c] - mean) * (1 / sqrt(var + eps))) * gamma[c] + beta[c].
+ * x and y may alias. */
+int nimf_layernorm_dev(const float* x, const float* gamma, const float* beta, int64_t rows,
+                       int64_t cols, float eps, float* y, void* stream);
+
 /* beAdd (backend.nim) as the residual connections of TransformerBlockLlama
  * use it (nim_inference.nim:847-875): out = a + b. */
 int nimf_add_dev(const float* a, const float* b, int64_t n, float* out, void* stream);

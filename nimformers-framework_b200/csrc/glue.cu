@@ -2,6 +2,7 @@
 // Llama-style decode step (nim_inference.nim), kept on the device so that the
 // activations never return to the host between the quantised matmuls:
 //   RMSNorm          nim_inference.nim:114-200 (rmsNormPrep + forward)
+//   LayerNorm        nimformer.nim:188-197, CPU path gpubackend.nim:252-266
 //   residual add     beAdd (backend.nim) as used by TransformerBlockLlama
 //   SwiGLU gating    nim_inference.nim:336-356, sigmoid as gpubackend.nim:111-114
 //   RoPE             nim_inference.nim:261-330 (rotate-half, caller's tables)
@@ -103,6 +104,58 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x0, const float* __rest
   s = block_sum(s, sh);
   const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)cols), eps)));
   for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) yr[c] = __fmul_rn(__fmul_rn(xr[c], inv), w[c]);
+}
+
+// LayerNorm, one block per row, two passes over the row as the reference's CPU
+// path: mean = sum x / cols, then var = sum (x - mean)^2 / cols (not
+// E[x^2] - mean^2), y = ((x - mean) * invStd) * gamma + beta.  A row of up to
+// 4 * blockDim values is read once and kept in registers for both passes.
+__global__ void layernorm_kernel(const float* x, const float* __restrict__ gm,
+                                 const float* __restrict__ bt, int64_t cols, float eps,
+                                 float* y) {  // x and y may alias (each thread reads its values before writing them)
+  __shared__ float sh[32];
+  griddep_launch_dependents();
+  griddep_wait();
+  const int64_t off = (int64_t)blockIdx.x * cols;
+  const float* xr = x + off;
+  float* yr = y + off;
+  const int64_t step = blockDim.x;
+  const float fc = (float)cols;
+  if (cols <= 4 * step) {
+    float v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t c = threadIdx.x + u * step;
+      v[u] = c < cols ? xr[c] : 0.f;
+    }
+    float s = __fadd_rn(__fadd_rn(v[0], v[1]), __fadd_rn(v[2], v[3]));
+    const float mean = __fdiv_rn(block_sum(s, sh), fc);
+    float d[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) d[u] = threadIdx.x + u * step < cols ? __fsub_rn(v[u], mean) : 0.f;
+    float q = __fadd_rn(__fadd_rn(__fmul_rn(d[0], d[0]), __fmul_rn(d[1], d[1])),
+                        __fadd_rn(__fmul_rn(d[2], d[2]), __fmul_rn(d[3], d[3])));
+    const float var = __fdiv_rn(block_sum(q, sh), fc);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t c = threadIdx.x + u * step;
+      if (c < cols) yr[c] = __fadd_rn(__fmul_rn(__fmul_rn(d[u], inv), gm[c]), bt[c]);
+    }
+    return;
+  }
+  float s = 0.f;
+  for (int64_t c = threadIdx.x; c < cols; c += step) s = __fadd_rn(s, xr[c]);
+  const float mean = __fdiv_rn(block_sum(s, sh), fc);
+  float q = 0.f;
+  for (int64_t c = threadIdx.x; c < cols; c += step) {
+    const float dv = __fsub_rn(xr[c], mean);
+    q = __fadd_rn(q, __fmul_rn(dv, dv));
+  }
+  const float var = __fdiv_rn(block_sum(q, sh), fc);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+  for (int64_t c = threadIdx.x; c < cols; c += step)
+    yr[c] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xr[c], mean), inv), gm[c]), bt[c]);
 }
 
 __global__ void add_kernel(const float* __restrict__ a, const float* __restrict__ b, int64_t n,
@@ -361,6 +414,17 @@ int nimf_rmsnorm_dev(const float* x, const float* w, int64_t rows, int64_t cols,
   if (!x || !w || !y) return set_error(NIMF_ERR_ARG, "rmsnorm: NULL buffer");
   NIMF_TRY(launch_pdl(rmsnorm_kernel, (unsigned)rows, 1024, 0, st, x, (const float*)nullptr,
                       (float*)nullptr, w, cols, eps, y));
+  return NIMF_OK;
+}
+
+int nimf_layernorm_dev(const float* x, const float* gamma, const float* beta, int64_t rows,
+                       int64_t cols, float eps, float* y, void* stream) {
+  cudaStream_t st;
+  NIMF_TRY(stream_of(stream, &st));
+  if (rows < 0 || cols < 0 || rows > INT32_MAX) return set_error(NIMF_ERR_SHAPE, "layernorm: rows %lld cols %lld", (long long)rows, (long long)cols);
+  if (rows == 0 || cols == 0) return NIMF_OK;
+  if (!x || !gamma || !beta || !y) return set_error(NIMF_ERR_ARG, "layernorm: NULL buffer");
+  NIMF_TRY(launch_pdl(layernorm_kernel, (unsigned)rows, 1024, 0, st, x, gamma, beta, cols, eps, y));
   return NIMF_OK;
 }
 

@@ -636,6 +636,33 @@ void orc_rmsnorm(const float* x, const float* w, int64_t rows, int64_t cols, flo
   free(ones);
 }
 
+/* LayerNorm.forward (nimformer.nim:188-197) through beLayernorm
+ * (backend.nim:149-150) on the CPU path cpuLayernorm
+ * (vendor/bybylang/gpubackend.nim:252-266): per row, mean = (sum x) / cols,
+ * var = (sum (x - mean)^2) / cols, both sums sequential in c; invStd =
+ * 1 / sqrt(var + eps); y = ((x - mean) * invStd) * gamma + beta. */
+void orc_layernorm(const float* x, const float* gamma, const float* beta, int64_t rows,
+                   int64_t cols, float eps, float* y) {
+  for (int64_t r = 0; r < rows; ++r) {
+    const float* xr = x + r * cols;
+    float mean = 0.0f;
+    for (int64_t c = 0; c < cols; ++c) mean += xr[c];
+    mean /= (float)cols;
+    float var = 0.0f;
+    for (int64_t c = 0; c < cols; ++c) {
+      float d = xr[c] - mean;
+      var += d * d;
+    }
+    var /= (float)cols;
+    float inv = 1.0f / sqrtf(var + eps);
+    for (int64_t c = 0; c < cols; ++c) {
+      float t = (xr[c] - mean) * inv;
+      t = t * gamma[c];
+      y[r * cols + c] = t + beta[c];
+    }
+  }
+}
+
 /* nim_inference.nim:336-356 SwiGLUL gating: sig = 1 / (1 + exp(-g))
  * (vendor/bybylang/gpubackend.nim:111-114 cpuSigmoid), out = (g * sig) * up. */
 void orc_swiglu(const float* g, const float* u, int64_t n, float* out) {

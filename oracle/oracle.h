@@ -158,6 +158,11 @@ void orc_gemv_f64(const float* x, const float* w, int64_t m, int64_t k, int64_t 
  * invStd = 1 / sqrt(sum(x*x) / cols + eps), sum in orc_cpu_matmul order. */
 void orc_rmsnorm(const float* x, const float* w, int64_t rows, int64_t cols, float eps,
                  float* y);
+/* nimformer.nim:188-197 LayerNorm.forward, CPU path vendor/bybylang/gpubackend.nim:252-266:
+ * two sequential passes (mean, then variance about the mean);
+ * y = ((x - mean) * invStd) * gamma + beta. */
+void orc_layernorm(const float* x, const float* gamma, const float* beta, int64_t rows,
+                   int64_t cols, float eps, float* y);
 /* nim_inference.nim:336-356 + vendor/bybylang/gpubackend.nim:111-114:
  * out = (g * (1 / (1 + exp(-g)))) * u. */
 void orc_swiglu(const float* g, const float* u, int64_t n, float* out);

@@ -65,6 +65,7 @@ def lib():
             "orc_dequantize_fp4_block16": (None, [_u8p, _u8p, ctypes.c_float, _i64, _i64, _f32p]),
             "orc_gemv_f64": (None, [_f32p, _f32p, _i64, _i64, _i64, _f32p]),
             "orc_rmsnorm": (None, [_f32p, _f32p, _i64, _i64, ctypes.c_float, _f32p]),
+            "orc_layernorm": (None, [_f32p, _f32p, _f32p, _i64, _i64, ctypes.c_float, _f32p]),
             "orc_swiglu": (None, [_f32p, _f32p, _i64, _f32p]),
             "orc_rope": (None, [_f32p, _i64, _i64, _i64, _i64, _i64, _f32p, _f32p]),
             "orc_attention_decode": (None, [_f32p, _f32p, _f32p, _f32p, _f32p, _i64, _i64, _i64,
@@ -278,6 +279,15 @@ def rmsnorm(x, w, eps):
     rows, cols = x.shape
     y = np.empty(rows * cols, np.float32)
     lib().orc_rmsnorm(x.ravel(), _c(w, np.float32).ravel(), rows, cols, ctypes.c_float(eps), y)
+    return y.reshape(rows, cols)
+
+
+def layernorm(x, gamma, beta, eps):
+    x = _c(x, np.float32)
+    rows, cols = x.shape
+    y = np.empty(rows * cols, np.float32)
+    lib().orc_layernorm(x.ravel(), _c(gamma, np.float32).ravel(), _c(beta, np.float32).ravel(),
+                        rows, cols, ctypes.c_float(eps), y)
     return y.reshape(rows, cols)
 
 

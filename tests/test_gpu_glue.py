@@ -1,4 +1,4 @@
-"""Device-resident decode glue (RMSNorm, residual add, SwiGLU gating, RoPE,
+"""Device-resident decode glue (RMSNorm, LayerNorm, residual add, SwiGLU gating, RoPE,
 decode attention with the KV-cache append) through the C ABI against the CPU
 oracle's restatements of nim_inference.nim.  Element-wise steps whose every
 rounding the reference fixes (residual add, RoPE with the caller's tables, the
@@ -74,6 +74,30 @@ def test_rmsnorm_add_swiglu(nimf_gpu, torch_dev):
     nimf_gpu.check(L.nimf_swiglu_dev(p(dg), p(du), g.size, p(gated), None))
     torch.cuda.synchronize()
     assert rel_err(gated.cpu().numpy(), O.swiglu(g, u)) <= TOL
+
+
+def test_layernorm(nimf_gpu, torch_dev):
+    """nimf_layernorm_dev against the oracle's cpuLayernorm restatement, rows
+    with a large mean (two-pass variance), both the register and the re-read
+    path, and in place (y aliasing x)."""
+    torch = torch_dev
+    L = nimf_gpu.lib()
+    rng = np.random.default_rng(4)
+    for rows, cols in ((1, 4096), (3, 1000), (2, 4097), (8, 11008)):
+        x = (rng.standard_normal((rows, cols)) * 2 + 40).astype(np.float32)
+        g = rng.uniform(0.5, 1.5, cols).astype(np.float32)
+        b = rng.standard_normal(cols).astype(np.float32)
+        dx, dg, db = dev(torch, x), dev(torch, g), dev(torch, b)
+        y = torch.empty(rows, cols, device="cuda")
+        nimf_gpu.check(L.nimf_layernorm_dev(p(dx), p(dg), p(db), rows, cols, 1e-5, p(y), None))
+        torch.cuda.synchronize()
+        ref = O.layernorm(x, g, b, 1e-5)
+        assert rel_err(y.cpu().numpy(), ref) <= TOL, (rows, cols)
+        nimf_gpu.check(L.nimf_layernorm_dev(p(dx), p(dg), p(db), rows, cols, 1e-5, p(dx), None))
+        torch.cuda.synchronize()
+        assert np.array_equal(dx.cpu().numpy().view(np.uint32), y.cpu().numpy().view(np.uint32))
+    with pytest.raises(nimf_gpu.CatchableError, match="ARG"):
+        nimf_gpu.check(L.nimf_layernorm_dev(p(dx), None, p(db), 1, 16, 1e-5, p(y), None))
 
 
 def rope_tables(D, max_seq, theta=10000.0):
