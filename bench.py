@@ -368,8 +368,13 @@ def run_decode_7b_full(nimf, torch, steps, warmup, pos=512, max_seq=640, layers=
     KV-cache append + attention over pos + 1 positions (32 heads x 128), o GEMV,
     residual add fused with the next RMSNorm, fused gate/up GEMV, SwiGLU, down
     GEMV, residual add fused with the next layer's (or the final) RMSNorm; then
-    the lm_head GEMV (nim_inference.nim:847-921's order).  One CUDA graph per step; synthetic int4-g128 weights, random
-    norm weights and KV caches (fp32, 32 x 2 x 32 x 640 x 128)."""
+    the lm_head GEMV (nim_inference.nim:847-921's order).  The step starts from
+    a token id on the device (embedding row lookup) and ends with the greedy
+    choice of the next id with the repetition penalty over 64 recent ids
+    (sampleTopP at temperature 0), which the next replay embeds: token in,
+    token out, nothing crosses PCIe.  One CUDA graph per step; synthetic
+    int4-g128 weights, random embedding table, norm weights and KV caches
+    (fp32, 32 x 2 x 32 x 640 x 128)."""
     import ctypes
     import numpy as np
     rng = np.random.default_rng(6)
@@ -404,7 +409,9 @@ def run_decode_7b_full(nimf, torch, steps, warmup, pos=512, max_seq=640, layers=
     cos_t = torch.from_numpy(np.cos(ang).astype(np.float32)).to(dev)
     sin_t = torch.from_numpy(np.sin(ang).astype(np.float32)).to(dev)
     P = lambda t: ctypes.c_void_p(t.data_ptr())
-    x0 = torch.randn(1, D7, device=dev)
+    table = torch.randn(V7, D7, device=dev) * 0.02
+    tok = torch.tensor([1234], dtype=torch.int32, device=dev)
+    recent = torch.from_numpy(rng.integers(0, V7, size=64).astype(np.int32)).to(dev)
     x = torch.empty(1, D7, device=dev)
     h = torch.empty(1, D7, device=dev)
     xn = torch.empty(1, D7, device=dev)
@@ -419,7 +426,7 @@ def run_decode_7b_full(nimf, torch, steps, warmup, pos=512, max_seq=640, layers=
 
     def step(st):
         sp = ctypes.c_void_p(st)
-        x.copy_(x0)   # the same token every replay
+        nimf.check(L.nimf_embedding_lookup_dev(P(table), V7, D7, P(tok), 1, P(x), sp))
         nimf.check(L.nimf_rmsnorm_dev(P(x), P(layers[0][7]), 1, D7, ctypes.c_float(1e-6), P(xn), sp))
         for li, (q, k, v, o, gate, up, down, n1, n2, kc, vc) in enumerate(layers):
             nimf.Weight.matmul_group_dev([q, k, v], xn.data_ptr(), 1,
@@ -442,9 +449,13 @@ def run_decode_7b_full(nimf, torch, steps, warmup, pos=512, max_seq=640, layers=
             nimf.check(L.nimf_add_rmsnorm_dev(P(h), P(dn), P(nxt), 1, D7, ctypes.c_float(1e-6),
                                               P(x), P(xn), sp))
         head.matmul_dev(xn.data_ptr(), 1, logits.data_ptr(), st)
+        nimf.check(L.nimf_greedy_sample_dev(P(logits), 1, V7, P(recent), 64, ctypes.c_float(1.3),
+                                            P(tok), sp))
 
     try:
         ms = graph_ms(torch, step, steps, warmup)
+        next_id = int(tok.item())
+        assert 0 <= next_id < V7
     finally:
         for lw in layers:
             for w in lw[:7]:
@@ -454,9 +465,11 @@ def run_decode_7b_full(nimf, torch, steps, warmup, pos=512, max_seq=640, layers=
     return {"tok_s": 1.0 / (ms * 1e-3), "ms_per_step": ms, "position": pos,
             "weight_bytes_per_step": decode7b_bytes(1), "kv_bytes_per_step": kv_bytes,
             "gb_s": (decode7b_bytes(1) + kv_bytes) / (ms * 1e-3) / 1e9,
-            "launches_per_step": nlayers * 9 + 2,
-            "note": ("batch 1, whole decode step on the device (glue + int4-g128 matmuls), one "
-                     "CUDA graph, KV caches fp32 [32 heads][640][128] per layer, %d timed steps" % steps)}
+            "launches_per_step": nlayers * 9 + 4,
+            "note": ("batch 1, whole decode step on the device, token id in -> greedy token id "
+                     "out (embedding lookup, glue, int4-g128 matmuls, lm_head, repetition-"
+                     "penalised argmax), one CUDA graph, KV caches fp32 [32 heads][640][128] "
+                     "per layer, %d timed steps" % steps)}
 
 
 def prefill7b_flops(tokens):

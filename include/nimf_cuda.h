@@ -248,6 +248,24 @@ int nimf_attention_decode_dev(const float* q, const float* k_new, const float* v
                               float* k_cache, float* v_cache, int64_t H, int64_t HKV, int64_t D,
                               int64_t max_seq, int64_t pos, float scale, float* out, void* stream);
 
+/* Token embedding rows, as cpuEmbeddingLookup (vendor/bybylang/gpubackend.nim:268-278,
+ * beEmbeddingLookup backend.nim:152-153; Embedding.lookupBatch nimformer.nim:401-411):
+ * out[i][0..dim) = table[ids[i]][0..dim) for 0 <= ids[i] < vocab, zeros otherwise.
+ * table [vocab][dim] fp32, ids [n] int32, out [n][dim], all on the device. */
+int nimf_embedding_lookup_dev(const float* table, int64_t vocab, int64_t dim,
+                              const int32_t* ids, int64_t n, float* out, void* stream);
+
+/* The greedy branch of sampleTopP (nim_inference.nim:1019-1036, temperature <= 0),
+ * per row of logits [rows][vocab]: for each entry of the row's recent ids
+ * recent[row][0..n_recent) inside [0, vocab), in order, the logit is divided by
+ * repeat_penalty if it is positive, else multiplied by it (an id listed twice is
+ * adjusted twice); out_ids[row] = the first index of the largest adjusted logit
+ * (a strict-greater scan from index 0: NaNs never win, a NaN at index 0 gives 0).
+ * repeat_penalty 1 skips the adjustment.  vocab <= 262144, n_recent <= 2048;
+ * the logits are not modified.  All buffers on the device. */
+int nimf_greedy_sample_dev(const float* logits, int64_t rows, int64_t vocab, const int32_t* recent,
+                           int64_t n_recent, float repeat_penalty, int32_t* out_ids, void* stream);
+
 /* ------------------------------------------------------------ .nimq state dicts */
 
 /* One tensor record of a NIMQ2 stream (quant.nim:386-409 readQuantTensor).

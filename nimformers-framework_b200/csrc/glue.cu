@@ -8,11 +8,15 @@
 //   RoPE             nim_inference.nim:261-330 (rotate-half, caller's tables)
 //   decode attention nim_inference.nim:624-748 with appendKV :404-426 and
 //                    softmax as gpubackend.nim:236-250
+//   token embedding  cpuEmbeddingLookup, gpubackend.nim:268-278
+//   greedy choice    sampleTopP with temperature <= 0, nim_inference.nim:1019-1036
 // Every product and sum that the reference rounds separately is rounded
 // separately here (__fmul_rn / __fadd_rn, no contraction); reductions (row
 // sums, dot products, softmax sums) run in a tree order instead of the
 // reference's sequential order.
 #include <algorithm>
+#include <climits>
+#include <cstdint>
 
 #include "device_util.cuh"
 #include "nimf_internal.h"
@@ -156,6 +160,132 @@ __global__ void layernorm_kernel(const float* x, const float* __restrict__ gm,
   const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
   for (int64_t c = threadIdx.x; c < cols; c += step)
     yr[c] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xr[c], mean), inv), gm[c]), bt[c]);
+}
+
+// Token embedding rows: out[i][:] = table[ids[i]][:], zeros for an id outside
+// [0, vocab).  One block per id; float4 copies when dim allows.
+__global__ void __launch_bounds__(1024) embedding_kernel(const float* __restrict__ table, int64_t vocab, int64_t dim,
+                                 const int32_t* __restrict__ ids, float* __restrict__ out) {
+  griddep_launch_dependents();
+  griddep_wait();
+  const int64_t id = ids[blockIdx.x];
+  float* o = out + (int64_t)blockIdx.x * dim;
+  const bool ok = id >= 0 && id < vocab;
+  const float* src = table + (ok ? id : 0) * dim;
+  if ((dim & 3) == 0 && ((reinterpret_cast<uintptr_t>(table) | reinterpret_cast<uintptr_t>(out)) & 15) == 0) {
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int64_t j = threadIdx.x; j < dim / 4; j += blockDim.x)
+      reinterpret_cast<float4*>(o)[j] = ok ? reinterpret_cast<const float4*>(src)[j] : z;
+  } else {
+    for (int64_t j = threadIdx.x; j < dim; j += blockDim.x) o[j] = ok ? src[j] : 0.f;
+  }
+}
+
+constexpr int kGreedyMaxRecent = 2048;  // with a 32 KB bitmap: 40 KB of static + dynamic shared memory
+
+// Greedy token choice of one row of logits with the repetition penalty: every
+// occurrence of an id in the row's recent list divides its logit by `penalty`
+// if it is positive at that moment, else multiplies it (so an id listed twice
+// is adjusted twice, in sequence); then the first index of the largest
+// adjusted value wins.  As in a sequential scan with a strict `>` that starts
+// at index 0, NaNs never win, and a NaN at index 0 gives 0.  One block per
+// row; recent ids are marked in a shared bitmap so the scan skips their raw
+// values.
+__global__ void __launch_bounds__(1024) greedy_kernel(const float* __restrict__ logits, int64_t vocab,
+                              const int32_t* __restrict__ recent, int nrec, float penalty,
+                              int32_t* __restrict__ out_ids) {
+  extern __shared__ unsigned gbits[];                 // [ceil(vocab / 32)] bitmap
+  __shared__ int srec[kGreedyMaxRecent];
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  griddep_launch_dependents();
+  griddep_wait();
+  const float* lr = logits + (int64_t)blockIdx.x * vocab;
+  const int32_t* rr = recent + (int64_t)blockIdx.x * nrec;
+  const bool pen = penalty != 1.0f && nrec > 0;
+  const int nwords = (int)((vocab + 31) / 32);
+  if (pen) {
+    for (int i = threadIdx.x; i < nwords; i += blockDim.x) gbits[i] = 0u;
+    for (int r = threadIdx.x; r < nrec; r += blockDim.x) srec[r] = rr[r];
+  }
+  __syncthreads();
+  if (pen)
+    for (int r = threadIdx.x; r < nrec; r += blockDim.x) {
+      const int id = srec[r];
+      if (id >= 0 && id < vocab) atomicOr(&gbits[id >> 5], 1u << (id & 31));
+    }
+  __syncthreads();
+  // the adjusted value of id, applying the penalty once per occurrence
+  auto adjusted = [&](int id) {
+    float v = lr[id];
+    if (!pen) return v;
+    for (int q = 0; q < nrec; ++q)
+      if (srec[q] == id) v = v > 0.f ? __fdiv_rn(v, penalty) : __fmul_rn(v, penalty);
+    return v;
+  };
+  const int kNone = INT_MAX;
+  float bv = 0.f;
+  int bi = kNone;
+  auto consider = [&](float v, int i) {
+    if (v != v) return;  // NaN
+    if (bi == kNone || v > bv || (v == bv && i < bi)) {
+      bv = v;
+      bi = i;
+    }
+  };
+  if (pen)
+    for (int r = threadIdx.x; r < nrec; r += blockDim.x) {
+      const int id = srec[r];
+      if (id < 0 || id >= vocab) continue;
+      bool first = true;
+      for (int q = 0; q < r && first; ++q) first = srec[q] != id;
+      if (first) consider(adjusted(id), id);
+    }
+  // the scan issues kBatch independent loads per thread before comparing them
+  constexpr int kBatch = 16;
+  const int nv = (int)vocab;
+  for (int i0 = threadIdx.x; i0 < nv; i0 += blockDim.x * kBatch) {
+    float v[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int i = i0 + u * (int)blockDim.x;
+      v[u] = i < nv ? lr[i] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int i = i0 + u * (int)blockDim.x;
+      if (i < nv && !(pen && ((gbits[i >> 5] >> (i & 31)) & 1u))) consider(v[u], i);
+    }
+  }
+  auto better = [](float v1, int i1, float v2, int i2) {
+    if (i1 == INT_MAX) return false;
+    if (i2 == INT_MAX) return true;
+    return v1 > v2 || (v1 == v2 && i1 < i2);
+  };
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (better(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    sv[w] = bv;
+    si[w] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 1; i < nw; ++i)
+      if (better(sv[i], si[i], bv, bi)) {
+        bv = sv[i];
+        bi = si[i];
+      }
+    const float v0 = adjusted(0);
+    out_ids[blockIdx.x] = (v0 != v0 || bi == kNone) ? 0 : bi;
+  }
 }
 
 __global__ void add_kernel(const float* __restrict__ a, const float* __restrict__ b, int64_t n,
@@ -524,6 +654,38 @@ int nimf_attention_decode_dev(const float* q, const float* k_new, const float* v
                                      (const float*)v_cache, H / HKV, D, max_seq, S, ps, scale, part));
   }
   NIMF_TRY(launch_pdl(attn_combine_kernel, (unsigned)H, 128, 0, st, (const float*)part, nsplit, D, out));
+  return NIMF_OK;
+}
+
+int nimf_embedding_lookup_dev(const float* table, int64_t vocab, int64_t dim,
+                              const int32_t* ids, int64_t n, float* out, void* stream) {
+  cudaStream_t st;
+  NIMF_TRY(stream_of(stream, &st));
+  if (vocab < 0 || dim < 0 || n < 0 || n > INT32_MAX)
+    return set_error(NIMF_ERR_SHAPE, "embedding_lookup: vocab %lld dim %lld n %lld", (long long)vocab, (long long)dim, (long long)n);
+  if (n == 0 || dim == 0) return NIMF_OK;
+  if (!table || !ids || !out) return set_error(NIMF_ERR_ARG, "embedding_lookup: NULL buffer");
+  const unsigned threads = (unsigned)std::min<int64_t>(1024, ((dim + 3) / 4 + 31) / 32 * 32);
+  NIMF_TRY(launch_pdl(embedding_kernel, (unsigned)n, threads, 0, st, table, vocab, dim, ids, out));
+  return NIMF_OK;
+}
+
+int nimf_greedy_sample_dev(const float* logits, int64_t rows, int64_t vocab, const int32_t* recent,
+                           int64_t n_recent, float repeat_penalty, int32_t* out_ids, void* stream) {
+  cudaStream_t st;
+  NIMF_TRY(stream_of(stream, &st));
+  const int64_t max_vocab = (int64_t)32 * 1024 * 8;  // bitmap within 32 KB of shared memory
+  if (rows < 0 || rows > INT32_MAX || vocab < 1 || vocab > max_vocab || n_recent < 0 ||
+      n_recent > kGreedyMaxRecent)
+    return set_error(NIMF_ERR_SHAPE, "greedy_sample: rows %lld vocab %lld (1..%lld) recent %lld (<= %d)",
+                     (long long)rows, (long long)vocab, (long long)max_vocab, (long long)n_recent,
+                     kGreedyMaxRecent);
+  if (rows == 0) return NIMF_OK;
+  if (!logits || !out_ids || (n_recent > 0 && !recent))
+    return set_error(NIMF_ERR_ARG, "greedy_sample: NULL buffer");
+  const size_t smem = (size_t)((vocab + 31) / 32) * 4;
+  NIMF_TRY(launch_pdl(greedy_kernel, (unsigned)rows, 1024, smem, st, logits, vocab, recent,
+                      (int)n_recent, repeat_penalty, out_ids));
   return NIMF_OK;
 }
 

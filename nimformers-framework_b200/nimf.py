@@ -46,7 +46,7 @@ EXPORTS = [
     "nimf_cf_autoselect", "nimf_apf_cast", "nimf_cf_autoselect_dev_noalloc",
     "nimf_nimq_parse", "nimf_nimq_get", "nimf_nimq_register", "nimf_weight_register_gptq",
     "nimf_rmsnorm_dev", "nimf_layernorm_dev", "nimf_add_rmsnorm_dev", "nimf_add_dev", "nimf_swiglu_dev", "nimf_rope_dev",
-    "nimf_attention_decode_dev",
+    "nimf_attention_decode_dev", "nimf_embedding_lookup_dev", "nimf_greedy_sample_dev",
 ]
 
 
@@ -110,6 +110,8 @@ def lib():
         "nimf_weight_register_gptq": [vp, vp, vp, vp, i64, i64, i64, i64, i64, u64p],
         "nimf_rmsnorm_dev": [vp, vp, i64, i64, ctypes.c_float, vp, vp],
         "nimf_layernorm_dev": [vp, vp, vp, i64, i64, ctypes.c_float, vp, vp],
+        "nimf_embedding_lookup_dev": [vp, i64, i64, vp, i64, vp, vp],
+        "nimf_greedy_sample_dev": [vp, i64, i64, vp, i64, ctypes.c_float, vp, vp],
         "nimf_add_dev": [vp, vp, i64, vp, vp],
         "nimf_add_rmsnorm_dev": [vp, vp, vp, i64, i64, ctypes.c_float, vp, vp, vp],
         "nimf_swiglu_dev": [vp, vp, i64, vp, vp],

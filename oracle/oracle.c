@@ -663,6 +663,42 @@ void orc_layernorm(const float* x, const float* gamma, const float* beta, int64_
   }
 }
 
+/* cpuEmbeddingLookup (vendor/bybylang/gpubackend.nim:268-278): row ids[i] of
+ * table [vocab][dim], zeros for an id outside [0, vocab). */
+void orc_embedding_lookup(const float* table, int64_t vocab, int64_t dim, const int32_t* ids,
+                          int64_t n, float* out) {
+  for (int64_t i = 0; i < n; ++i) {
+    int64_t id = ids[i];
+    for (int64_t j = 0; j < dim; ++j)
+      out[i * dim + j] = (id >= 0 && id < vocab) ? table[id * dim + j] : 0.0f;
+  }
+}
+
+/* sampleTopP (nim_inference.nim:1019-1036) with temperature <= 0, per row:
+ * adjLogits = logits; for id in recentIds (in order, ids in range): divide by
+ * repeatPenalty if adjLogits[id] > 0 else multiply (skipped when the penalty is
+ * 1); best = 0; for i in 1 ..< vocab: if adj[i] > adj[best]: best = i. */
+void orc_greedy_sample(const float* logits, int64_t rows, int64_t vocab, const int32_t* recent,
+                       int64_t n_recent, float penalty, int32_t* out_ids) {
+  float* adj = (float*)malloc((size_t)vocab * sizeof(float));
+  for (int64_t r = 0; r < rows; ++r) {
+    memcpy(adj, logits + r * vocab, (size_t)vocab * sizeof(float));
+    if (penalty != 1.0f)
+      for (int64_t q = 0; q < n_recent; ++q) {
+        int64_t id = recent[r * n_recent + q];
+        if (id >= 0 && id < vocab) {
+          if (adj[id] > 0.0f) adj[id] = adj[id] / penalty;
+          else adj[id] = adj[id] * penalty;
+        }
+      }
+    int64_t best = 0;
+    for (int64_t i = 1; i < vocab; ++i)
+      if (adj[i] > adj[best]) best = i;
+    out_ids[r] = (int32_t)best;
+  }
+  free(adj);
+}
+
 /* nim_inference.nim:336-356 SwiGLUL gating: sig = 1 / (1 + exp(-g))
  * (vendor/bybylang/gpubackend.nim:111-114 cpuSigmoid), out = (g * sig) * up. */
 void orc_swiglu(const float* g, const float* u, int64_t n, float* out) {

@@ -163,6 +163,13 @@ void orc_rmsnorm(const float* x, const float* w, int64_t rows, int64_t cols, flo
  * y = ((x - mean) * invStd) * gamma + beta. */
 void orc_layernorm(const float* x, const float* gamma, const float* beta, int64_t rows,
                    int64_t cols, float eps, float* y);
+/* vendor/bybylang/gpubackend.nim:268-278 cpuEmbeddingLookup (zeros for ids out of range). */
+void orc_embedding_lookup(const float* table, int64_t vocab, int64_t dim, const int32_t* ids,
+                          int64_t n, float* out);
+/* nim_inference.nim:1019-1036 sampleTopP, temperature <= 0 (greedy with the
+ * repetition penalty), one id per row of logits. */
+void orc_greedy_sample(const float* logits, int64_t rows, int64_t vocab, const int32_t* recent,
+                       int64_t n_recent, float penalty, int32_t* out_ids);
 /* nim_inference.nim:336-356 + vendor/bybylang/gpubackend.nim:111-114:
  * out = (g * (1 / (1 + exp(-g)))) * u. */
 void orc_swiglu(const float* g, const float* u, int64_t n, float* out);

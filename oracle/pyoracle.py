@@ -66,6 +66,8 @@ def lib():
             "orc_gemv_f64": (None, [_f32p, _f32p, _i64, _i64, _i64, _f32p]),
             "orc_rmsnorm": (None, [_f32p, _f32p, _i64, _i64, ctypes.c_float, _f32p]),
             "orc_layernorm": (None, [_f32p, _f32p, _f32p, _i64, _i64, ctypes.c_float, _f32p]),
+            "orc_embedding_lookup": (None, [_f32p, _i64, _i64, _i32p, _i64, _f32p]),
+            "orc_greedy_sample": (None, [_f32p, _i64, _i64, _i32p, _i64, ctypes.c_float, _i32p]),
             "orc_swiglu": (None, [_f32p, _f32p, _i64, _f32p]),
             "orc_rope": (None, [_f32p, _i64, _i64, _i64, _i64, _i64, _f32p, _f32p]),
             "orc_attention_decode": (None, [_f32p, _f32p, _f32p, _f32p, _f32p, _i64, _i64, _i64,
@@ -289,6 +291,27 @@ def layernorm(x, gamma, beta, eps):
     lib().orc_layernorm(x.ravel(), _c(gamma, np.float32).ravel(), _c(beta, np.float32).ravel(),
                         rows, cols, ctypes.c_float(eps), y)
     return y.reshape(rows, cols)
+
+
+def embedding_lookup(table, ids):
+    table = _c(table, np.float32)
+    vocab, dim = table.shape
+    ids = _c(ids, np.int32).ravel()
+    out = np.empty(ids.size * dim, np.float32)
+    lib().orc_embedding_lookup(table.ravel(), vocab, dim, ids, ids.size, out)
+    return out.reshape(ids.size, dim)
+
+
+def greedy_sample(logits, recent, penalty):
+    """logits [rows][vocab]; recent [rows][n] int32 (n may be 0)."""
+    logits = _c(logits, np.float32)
+    rows, vocab = logits.shape
+    recent = _c(recent, np.int32).reshape(rows, -1)
+    n = recent.shape[1]
+    out = np.empty(rows, np.int32)
+    rec = recent.ravel() if recent.size else np.zeros(1, np.int32)
+    lib().orc_greedy_sample(logits.ravel(), rows, vocab, rec, n, ctypes.c_float(penalty), out)
+    return out
 
 
 def swiglu(g, u):

@@ -47,3 +47,54 @@ def test_layernorm_two_pass_accuracy():
     m = xd.mean(1, keepdims=True)
     ref = (xd - m) / np.sqrt(((xd - m) ** 2).mean(1, keepdims=True) + 1e-5)
     assert np.max(np.abs(y - ref)) <= 1e-3 * np.max(np.abs(ref))
+
+
+def greedy_loop(logits, recent, penalty):
+    """sampleTopP with temperature <= 0 (nim_inference.nim:1019-1036), in float32."""
+    f = np.float32
+    out = []
+    for r in range(logits.shape[0]):
+        adj = logits[r].copy()
+        if penalty != 1.0:
+            for i in recent[r]:
+                if 0 <= i < adj.size:
+                    adj[i] = f(adj[i] / f(penalty)) if adj[i] > 0 else f(adj[i] * f(penalty))
+        best = 0
+        for i in range(1, adj.size):
+            if adj[i] > adj[best]:
+                best = i
+        out.append(best)
+    return np.array(out, np.int32)
+
+
+def greedy_cases():
+    rng = np.random.default_rng(3)
+    lg = rng.standard_normal((4, 300)).astype(np.float32)
+    rec = rng.integers(-3, 310, size=(4, 20)).astype(np.int32)
+    top = np.argmax(lg, axis=1)
+    rec[:, 0] = top          # the raw winner is penalised
+    rec[:, 1] = top          # twice
+    yield lg, rec, 1.3
+    yield lg, rec, 1.0       # no penalty
+    yield lg, rec[:, :0], 1.3
+    ties = np.zeros((2, 50), np.float32)
+    ties[:, [7, 30]] = 2.0   # first of equal maxima
+    yield ties, np.array([[7], [30]], np.int32), 1.0
+    yield ties, np.array([[7], [30]], np.int32), 1.3
+    neg = -np.abs(lg[:2])    # all negative: the penalty multiplies
+    yield neg, rec[:2], 1.3
+    nan = lg[:2].copy()
+    nan[0, 0] = np.nan       # a NaN at index 0 wins the strict scan
+    nan[1, 5] = np.nan       # elsewhere it never wins
+    yield nan, rec[:2], 1.3
+
+
+def test_greedy_and_embedding_match_reference_loops():
+    for lg, rec, pen in greedy_cases():
+        assert np.array_equal(O.greedy_sample(lg, rec, pen), greedy_loop(lg, rec, pen))
+    rng = np.random.default_rng(4)
+    table = rng.standard_normal((10, 6)).astype(np.float32)
+    ids = np.array([3, -1, 9, 10, 0], np.int32)
+    out = O.embedding_lookup(table, ids)
+    ref = np.stack([table[i] if 0 <= i < 10 else np.zeros(6, np.float32) for i in ids])
+    assert np.array_equal(out, ref)

@@ -151,3 +151,40 @@ def test_attention_decode(nimf_gpu, torch_dev, H, HKV, pos):
     with pytest.raises(nimf_gpu.CatchableError, match="SHAPE"):
         nimf_gpu.check(L.nimf_attention_decode_dev(p(dq), p(dkn), p(dvn), p(dkc), p(dvc), H, HKV,
                                                    D, max_seq, max_seq, float(scale), p(out), None))
+
+
+def test_embedding_and_greedy(nimf_gpu, torch_dev):
+    """nimf_embedding_lookup_dev (zeros for ids out of range) bit-exact, and
+    nimf_greedy_sample_dev giving the oracle's token ids: the penalised
+    winner, a twice-listed id, ties, all-negative rows, NaNs, and 8 rows of
+    the 7B vocabulary with 64 recent ids each."""
+    from test_glue_oracle import greedy_cases
+    torch = torch_dev
+    L = nimf_gpu.lib()
+    rng = np.random.default_rng(6)
+    for vocab, dim in ((1000, 4096), (37, 4098)):
+        table = rng.standard_normal((vocab, dim)).astype(np.float32)
+        ids = np.array([5, -2, vocab - 1, vocab, 0, 5], np.int32)
+        dt = dev(torch, table)
+        di = torch.from_numpy(ids).cuda()
+        out = torch.empty(ids.size, dim, device="cuda")
+        nimf_gpu.check(L.nimf_embedding_lookup_dev(p(dt), vocab, dim, p(di), ids.size, p(out), None))
+        torch.cuda.synchronize()
+        assert np.array_equal(out.cpu().numpy().view(np.uint32),
+                              O.embedding_lookup(table, ids).view(np.uint32))
+    big = rng.standard_normal((8, 32000)).astype(np.float32)
+    brec = rng.integers(0, 32000, size=(8, 64)).astype(np.int32)
+    brec[:, 0] = np.argmax(big, axis=1)
+    cases = list(greedy_cases()) + [(big, brec, 1.3), (big, brec, 1.0)]
+    for lg, rec, pen in cases:
+        rows, vocab = lg.shape
+        dl = dev(torch, lg)
+        dr = torch.from_numpy(np.ascontiguousarray(rec, np.int32).reshape(-1).copy()
+                              if rec.size else np.zeros(1, np.int32)).cuda()
+        ids = torch.full((rows,), -1, dtype=torch.int32, device="cuda")
+        nimf_gpu.check(L.nimf_greedy_sample_dev(p(dl), rows, vocab, p(dr), rec.shape[1], pen, p(ids), None))
+        torch.cuda.synchronize()
+        assert np.array_equal(ids.cpu().numpy(), O.greedy_sample(lg, rec, pen)), (lg.shape, pen)
+        assert np.array_equal(dl.cpu().numpy().view(np.uint32), lg.view(np.uint32))  # logits untouched
+    with pytest.raises(nimf_gpu.CatchableError, match="SHAPE"):
+        nimf_gpu.check(L.nimf_greedy_sample_dev(p(dl), 1, 300000, p(dr), 1, 1.3, p(ids), None))
