@@ -218,7 +218,24 @@ def decode7b_bytes(batch):
     return L7 * per_layer + algo_bytes(V7, D7, batch, GS)
 
 
-def run_decode_7b(nimf, torch, steps, warmup, rank=0, world=1):
+def p2p_group(nimf, world, rank, slot_floats):
+    """A peer-memory all-gather group of the library (CUDA IPC handles
+    exchanged over the process group)."""
+    import ctypes
+    import torch.distributed as dist
+    L = nimf.lib()
+    h = ctypes.create_string_buffer(64)
+    gid = ctypes.c_int64()
+    nimf.check(L.nimf_p2p_create(world, rank, slot_floats, h, ctypes.byref(gid)))
+    handles = [None] * world
+    dist.all_gather_object(handles, h.raw)
+    allh = ctypes.create_string_buffer(b"".join(handles), 64 * world)
+    nimf.check(L.nimf_p2p_connect(gid.value, allh))
+    dist.barrier()
+    return gid.value
+
+
+def run_decode_7b(nimf, torch, steps, warmup, rank=0, world=1, exchange="p2p", batches=(1, 8)):
     """tok/s of the 7B-shape int4 decode matmul path, batch 1 and 8.
 
     Weights are synthetic int4 codes (seeded random bytes) with group scales
@@ -229,9 +246,11 @@ def run_decode_7b(nimf, torch, steps, warmup, rank=0, world=1):
 
     With world > 1 GPUs every projection is N-sharded (rank r holds rows
     nimf.shard_rows(N, world, r) of every weight, 3.7 GB / world per GPU) and
-    each projection group's outputs are all-gathered over NCCL inside the
-    captured step, then laid out as the next projection's x [batch][N].
-    Step time is the max over ranks."""
+    the output slice the next projection reads is all-gathered inside the
+    captured step into that projection's x [batch][N]: exchange "p2p" with the
+    library's peer-memory all-gather (one kernel: peer stores over NVLink, a
+    flag per peer), "nccl" with NCCL all-gathers of each group's outputs
+    followed by a layout copy.  Step time is the max over ranks."""
     import numpy as np
     rng = np.random.default_rng(4)
     dist = None
@@ -262,8 +281,17 @@ def run_decode_7b(nimf, torch, steps, warmup, rank=0, world=1):
     head = reg("head")
     nd, nf, nv = D7 // world, F7 // world, V7 // world   # equal shards at 1/2/4/8 GPUs
     out = {}
+    L = nimf.lib()
+    gid = None
     try:
-        for batch in (1, 8):
+        if world > 1 and exchange == "p2p":
+            gid = p2p_group(nimf, world, rank, max(batches) * max(nd, nf, nv))
+
+        def p2p(src, cols, ld_src, dst, st, batch):
+            nimf.check(L.nimf_p2p_allgather_dev(gid, src.data_ptr(), batch, cols, ld_src,
+                                                dst.data_ptr(), cols * world, st))
+
+        for batch in batches:
             dev = torch.device("cuda")
             x = torch.randn(batch, D7, device=dev)
             qkv = torch.empty(3, batch, nd, device=dev)
@@ -281,6 +309,7 @@ def run_decode_7b(nimf, torch, steps, warmup, rank=0, world=1):
                 x_gu = torch.empty(batch, D7, device=dev)    # full o output
                 x_dn = torch.empty(batch, F7, device=dev)    # full gate output
                 x_l = torch.empty(batch, D7, device=dev)     # full down output
+                x_log = torch.empty(batch, V7, device=dev)   # full logits
             stream = torch.cuda.Stream()
 
             def step(st):
@@ -289,31 +318,45 @@ def run_decode_7b(nimf, torch, steps, warmup, rank=0, world=1):
                     nimf.Weight.matmul_group_dev([q, k, v], h.data_ptr(), batch,
                                                  [qkv[i].data_ptr() for i in range(3)], st)
                     xo = qkv[0]
-                    if world > 1:
+                    if world > 1 and gid is not None:
+                        p2p(qkv[0], nd, nd, x_o, st, batch)
+                        xo = x_o
+                    elif world > 1:
                         dist.all_gather_into_tensor(g_qkv.view(-1), qkv.view(-1))
                         x_o.copy_(g_qkv[:, 0].permute(1, 0, 2).reshape(batch, D7))
                         xo = x_o
                     o.matmul_dev(xo.data_ptr(), batch, att.data_ptr(), st)
                     xg = att
-                    if world > 1:
+                    if world > 1 and gid is not None:
+                        p2p(att, nd, nd, x_gu, st, batch)
+                        xg = x_gu
+                    elif world > 1:
                         dist.all_gather_into_tensor(g_att.view(-1), att.view(-1))
                         x_gu.copy_(g_att.permute(1, 0, 2).reshape(batch, D7))
                         xg = x_gu
                     nimf.Weight.matmul_group_dev([gate, up], xg.data_ptr(), batch,
                                                  [gu[0].data_ptr(), gu[1].data_ptr()], st)
                     xd = gu[0]
-                    if world > 1:
+                    if world > 1 and gid is not None:
+                        p2p(gu[0], nf, nf, x_dn, st, batch)
+                        xd = x_dn
+                    elif world > 1:
                         dist.all_gather_into_tensor(g_gu.view(-1), gu.view(-1))
                         x_dn.copy_(g_gu[:, 0].permute(1, 0, 2).reshape(batch, F7))
                         xd = x_dn
                     down.matmul_dev(xd.data_ptr(), batch, dn.data_ptr(), st)
                     h = dn
-                    if world > 1:
+                    if world > 1 and gid is not None:
+                        p2p(dn, nd, nd, x_l, st, batch)
+                        h = x_l
+                    elif world > 1:
                         dist.all_gather_into_tensor(g_dn.view(-1), dn.view(-1))
                         x_l.copy_(g_dn.permute(1, 0, 2).reshape(batch, D7))
                         h = x_l
                 head.matmul_dev(h.data_ptr(), batch, logits.data_ptr(), st)
-                if world > 1:
+                if world > 1 and gid is not None:
+                    p2p(logits, nv, nv, x_log, st, batch)
+                elif world > 1:
                     dist.all_gather_into_tensor(g_log.view(-1), logits.view(-1))
 
             with torch.cuda.stream(stream):
@@ -333,12 +376,16 @@ def run_decode_7b(nimf, torch, steps, warmup, rank=0, world=1):
                 graph.replay()
             e1.record()
             torch.cuda.synchronize()
+            bad = L.nimf_sync() != 0   # a peer wait that ran out is reported here
             ms = e0.elapsed_time(e1) / steps
             if world > 1:
-                t = torch.tensor([ms], device=dev)
+                # the status travels with the time, so every rank raises together
+                t = torch.tensor([ms, float(bad)], device=dev)
                 dist.all_reduce(t, op=dist.ReduceOp.MAX)
-                ms = float(t.item())
+                ms, bad = float(t[0].item()), t[1].item() > 0
                 dist.barrier()
+            if bad:
+                raise RuntimeError("a device wait of the sharded decode expired on some rank")
             graph.reset()
             del graph
             out["batch%d" % batch] = {
@@ -346,19 +393,26 @@ def run_decode_7b(nimf, torch, steps, warmup, rank=0, world=1):
                 "gb_s": decode7b_bytes(batch) / (ms * 1e-3) / 1e9,
                 "bytes_per_step": decode7b_bytes(batch)}
     finally:
+        if gid is not None:
+            torch.cuda.synchronize()
+            dist.barrier()
+            nimf.check(L.nimf_p2p_destroy(gid))
         for lw in layers:
             for w in lw:
                 w.free()
         head.free()
-    out["launches_per_step"] = 4 * L7 + 1
+    out["launches_per_step"] = 4 * L7 + 1 + ((4 * L7 + 1) if exchange == "p2p" and world > 1 else 0)
     out["n_gpus"] = world
     if world > 1:
         out["all_gathers_per_step"] = 4 * L7 + 1
+        out["exchange"] = exchange
     out["note"] = ("matmul path only (grouped q/k/v and gate/up), one CUDA graph per step, "
                    "synthetic int4-g128 weights, %d timed steps%s" % (
                        steps, "" if world == 1 else
-                       "; N-sharded over %d GPUs, NCCL all-gather after every projection group, "
-                       "step time = max over ranks" % world))
+                       "; N-sharded over %d GPUs, the output slice each next projection reads "
+                       "all-gathered (%s) after every projection group, step time = max over "
+                       "ranks" % (world, "one peer-memory kernel over NVLink" if exchange == "p2p"
+                                  else "NCCL + layout copy")))
     return out
 
 
@@ -938,6 +992,10 @@ def run_ours(args, rank, world, local_rank):
             try:
                 decode = run_decode_7b(nimf, torch, args.decode_steps, max(3, args.warmup // 4),
                                        rank, world)
+                # the same step with NCCL all-gathers, for comparison
+                nccl = run_decode_7b(nimf, torch, args.decode_steps, max(3, args.warmup // 4),
+                                     rank, world, exchange="nccl", batches=(1,))
+                decode["nccl_batch1"] = nccl["batch1"]
             except Exception as e:  # noqa: BLE001
                 decode = {"error": "%s: %s" % (type(e).__name__, e)}
     decode_full = None

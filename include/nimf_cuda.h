@@ -266,6 +266,36 @@ int nimf_embedding_lookup_dev(const float* table, int64_t vocab, int64_t dim,
 int nimf_greedy_sample_dev(const float* logits, int64_t rows, int64_t vocab, const int32_t* recent,
                            int64_t n_recent, float repeat_penalty, int32_t* out_ids, void* stream);
 
+/* ------------------------------------------------- sharded outputs over peer memory */
+/* The reference has no multi-GPU path.  These calls gather N-shard outputs
+ * (rank r computed output columns [r*cols, (r+1)*cols)) into the full x of the
+ * next projection, one process per GPU, with plain peer stores over NVLink
+ * through CUDA IPC and one bounded flag wait per peer, no collective library.
+ *
+ * nimf_p2p_create (each rank, after nimf_init): allocates this rank's shared
+ *   buffer for slices of up to slot_floats floats and writes its 64-byte IPC
+ *   handle to ipc_handle_out; *group receives the group id.  2 <= world <= 8.
+ * nimf_p2p_connect: opens the peers' buffers from the world handles
+ *   (world * 64 bytes, rank order), exchanged by the host (e.g. over the
+ *   process group's object all-gather).  Call on every rank before the first
+ *   all-gather.
+ * nimf_p2p_allgather_dev: dst[i][q*cols + j] = rank q's src[i][j] for every
+ *   rank q, i < rows, j < cols (row strides ld_src, ld_dst in floats;
+ *   rows * cols <= slot_floats).  Every rank must make the same sequence of
+ *   calls on the group (the calls are counted); asynchronous on `stream` and
+ *   capturable in a CUDA graph.  A peer that does not arrive within 2 s makes
+ *   the kernel return with dst incomplete and the next nimf_sync report
+ *   NIMF_ERR_TIMEOUT.
+ * nimf_p2p_destroy: synchronises the device and releases the mappings and
+ *   the buffer (call on every rank after the last all-gather of every rank,
+ *   e.g. after a host barrier). */
+int nimf_p2p_create(int world, int rank, int64_t slot_floats, void* ipc_handle_out,
+                    int64_t* group);
+int nimf_p2p_connect(int64_t group, const void* ipc_handles);
+int nimf_p2p_allgather_dev(int64_t group, const float* src, int64_t rows, int64_t cols,
+                           int64_t ld_src, float* dst, int64_t ld_dst, void* stream);
+int nimf_p2p_destroy(int64_t group);
+
 /* ------------------------------------------------------------ .nimq state dicts */
 
 /* One tensor record of a NIMQ2 stream (quant.nim:386-409 readQuantTensor).

@@ -278,6 +278,7 @@ int nimf_shutdown(void) {
   fw_release_scratch();
   release_perm_buffer();
   release_attn_buffer();
+  release_p2p_groups();
   device_free(g_ctx.stage_in);
   device_free(g_ctx.stage_out);
   if (g_ctx.host_err) cudaFreeHost((void*)g_ctx.host_err);

@@ -47,6 +47,7 @@ EXPORTS = [
     "nimf_nimq_parse", "nimf_nimq_get", "nimf_nimq_register", "nimf_weight_register_gptq",
     "nimf_rmsnorm_dev", "nimf_layernorm_dev", "nimf_add_rmsnorm_dev", "nimf_add_dev", "nimf_swiglu_dev", "nimf_rope_dev",
     "nimf_attention_decode_dev", "nimf_embedding_lookup_dev", "nimf_greedy_sample_dev",
+    "nimf_p2p_create", "nimf_p2p_connect", "nimf_p2p_allgather_dev", "nimf_p2p_destroy",
 ]
 
 
@@ -111,6 +112,10 @@ def lib():
         "nimf_rmsnorm_dev": [vp, vp, i64, i64, ctypes.c_float, vp, vp],
         "nimf_layernorm_dev": [vp, vp, vp, i64, i64, ctypes.c_float, vp, vp],
         "nimf_embedding_lookup_dev": [vp, i64, i64, vp, i64, vp, vp],
+        "nimf_p2p_create": [i32, i32, i64, vp, ctypes.POINTER(i64)],
+        "nimf_p2p_connect": [i64, vp],
+        "nimf_p2p_allgather_dev": [i64, vp, i64, i64, i64, vp, i64, vp],
+        "nimf_p2p_destroy": [i64],
         "nimf_greedy_sample_dev": [vp, i64, i64, vp, i64, ctypes.c_float, vp, vp],
         "nimf_add_dev": [vp, vp, i64, vp, vp],
         "nimf_add_rmsnorm_dev": [vp, vp, vp, i64, i64, ctypes.c_float, vp, vp, vp],
