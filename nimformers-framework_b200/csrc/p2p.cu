@@ -25,7 +25,8 @@
 //
 // The wait is bounded (kWaitNs of %globaltimer): on expiry the block sets the
 // context's error word (reported by nimf_sync as NIMF_ERR_TIMEOUT), leaves its
-// dst columns unwritten and returns.  No TMA and no multicast: plain peer
+// dst columns unwritten and returns; while the word stays set, later waits
+// give up at once, so a missing peer costs one bound, not one per call.  No TMA and no multicast: plain peer
 // stores and local loads only.
 #include <cstdint>
 #include <cstring>
@@ -145,7 +146,8 @@ __global__ void __launch_bounds__(kThreads) p2p_allgather_kernel(const P2PArgs a
       const unsigned* mine = a.flags[a.rank] + b * kChunks + ch;
       const unsigned long long t0 = globaltimer();
       while ((int)(load_acquire_sys(mine) - e) < 0) {
-        if (globaltimer() - t0 > kWaitNs) {
+        // an earlier expired wait (error word still set) fails this one at once
+        if (globaltimer() - t0 > kWaitNs || *(volatile int*)a.err != 0) {
           s_ok = 0;
           atomicExch(a.err, 1);
           break;
