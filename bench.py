@@ -226,12 +226,27 @@ def p2p_group(nimf, world, rank, slot_floats):
     L = nimf.lib()
     h = ctypes.create_string_buffer(64)
     gid = ctypes.c_int64()
-    nimf.check(L.nimf_p2p_create(world, rank, slot_floats, h, ctypes.byref(gid)))
-    handles = [None] * world
-    dist.all_gather_object(handles, h.raw)
-    allh = ctypes.create_string_buffer(b"".join(handles), 64 * world)
-    nimf.check(L.nimf_p2p_connect(gid.value, allh))
-    dist.barrier()
+    err = None
+    try:
+        nimf.check(L.nimf_p2p_create(world, rank, slot_floats, h, ctypes.byref(gid)))
+    except Exception as e:  # noqa: BLE001
+        err = str(e)
+    # every rank learns every rank's outcome, so a failure raises on all of them
+    got = [None] * world
+    dist.all_gather_object(got, (h.raw, err))
+    bad = [(r, e) for r, (_, e) in enumerate(got) if e]
+    if bad:
+        raise RuntimeError("peer-memory group: create failed on %s" % bad)
+    allh = ctypes.create_string_buffer(b"".join(g[0] for g in got), 64 * world)
+    try:
+        nimf.check(L.nimf_p2p_connect(gid.value, allh))
+    except Exception as e:  # noqa: BLE001
+        err = str(e)
+    errs = [None] * world
+    dist.all_gather_object(errs, err)
+    bad = [(r, e) for r, e in enumerate(errs) if e]
+    if bad:
+        raise RuntimeError("peer-memory group: connect failed on %s" % bad)
     return gid.value
 
 
