@@ -73,6 +73,11 @@ int nimf_device_count(int* count);
 /* Blocks until all work on the library stream is done. */
 int nimf_sync(void);
 
+/* Number of device allocations (cudaMalloc) the library has made since it
+ * was loaded, for hosts that check which calls allocate.  No counterpart in
+ * the reference. */
+int nimf_alloc_count(int64_t* count);
+
 /* ------------------------------------------------------------ weights */
 
 /* int4 asymmetric per-group weights exactly as QuantTensor holds them
@@ -171,14 +176,32 @@ int nimf_matmul_w_group(const nimf_weight_t* handles, int count, const float* x,
                         float* const* ys);
 
 /* Drop-in for beMatmulQ4 (backend.nim:93-110 -> gpubackend.nim:655-676):
- * same arguments, HOST arrays, out = float32 [M*N].  The packed weights are
- * cached on the device keyed by (wq pointer, bytes, K, N, group size), valid
- * because Nim weights are immutable after setQuantWeight (nimformer.nim:94-100);
- * nimf_weight_cache_clear() drops the cache. */
+ * same arguments, HOST arrays, out = float32 [M*N].  The reference reads the
+ * arrays afresh on every call; here their device copy is cached, keyed by the
+ * wq, scales and zeros pointers and the shape, and a hit also needs the same
+ * fingerprint of the three arrays' contents (by default over every byte:
+ * about 3 ms for a 4096 x 12288 weight on one host core).  So a weight freed
+ * and replaced by another of the same shape at the same address, or scales /
+ * zeros changed in place, give fresh results.  nimf_weight_cache_clear()
+ * drops the cache. */
 int nimf_matmul_q4(const float* a, const uint8_t* wq, const float* scales,
                    const float* zeros, int64_t m, int64_t k, int64_t n, int64_t group_size,
                    int64_t n_groups_per_row, float* out);
 int nimf_weight_cache_clear(void);
+
+/* How nimf_matmul_q4 checks a cache hit (no reference counterpart):
+ * FULL (default) fingerprints every byte of wq, scales and zeros on each call;
+ * SAMPLED only the first and last 4 KB of each and 64 bytes of every 4 KB in
+ * between (a change elsewhere can go unseen); NONE trusts the pointers and
+ * shape, for hosts whose weights are immutable after setQuantWeight
+ * (nimformer.nim:94-100) and that call nimf_weight_cache_clear() whenever
+ * they free or replace one. */
+#define NIMF_Q4_CACHE_CHECK_FULL 0
+#define NIMF_Q4_CACHE_CHECK_SAMPLED 1
+#define NIMF_Q4_CACHE_CHECK_NONE 2
+int nimf_q4_cache_set_check(int mode);
+/* Number of weights the nimf_matmul_q4 cache holds. */
+int nimf_q4_cache_size(int64_t* entries);
 
 /* Drop-in for beMatmul (backend.nim:87-91 -> cuda_runtime.nim:122-152):
  * C[M][N] = A[M][K] . B[K][N], fp32, HOST arrays.  k2 must equal k. */
@@ -283,9 +306,12 @@ int nimf_greedy_sample_dev(const float* logits, int64_t rows, int64_t vocab, con
  *   rank q, i < rows, j < cols (row strides ld_src, ld_dst in floats;
  *   rows * cols <= slot_floats).  Every rank must make the same sequence of
  *   calls on the group (the calls are counted); asynchronous on `stream` and
- *   capturable in a CUDA graph.  A peer that does not arrive within 2 s makes
- *   the kernel return with dst incomplete and the next nimf_sync report
- *   NIMF_ERR_TIMEOUT.
+ *   capturable in a CUDA graph.  A peer that does not arrive within the wait
+ *   bound (2 s unless nimf_p2p_set_timeout_ms changed it) makes the kernel
+ *   return with dst incomplete and the next nimf_sync report
+ *   NIMF_ERR_TIMEOUT; until then later calls give up at once.
+ * nimf_p2p_set_timeout_ms: the bound of every peer wait of this process, in
+ *   milliseconds (1 .. 600000), for calls launched afterwards.
  * nimf_p2p_destroy: synchronises the device and releases the mappings and
  *   the buffer (call on every rank after the last all-gather of every rank,
  *   e.g. after a host barrier). */
@@ -294,6 +320,7 @@ int nimf_p2p_create(int world, int rank, int64_t slot_floats, void* ipc_handle_o
 int nimf_p2p_connect(int64_t group, const void* ipc_handles);
 int nimf_p2p_allgather_dev(int64_t group, const float* src, int64_t rows, int64_t cols,
                            int64_t ld_src, float* dst, int64_t ld_dst, void* stream);
+int nimf_p2p_set_timeout_ms(int64_t ms);
 int nimf_p2p_destroy(int64_t group);
 
 /* ------------------------------------------------------------ .nimq state dicts */
@@ -378,9 +405,11 @@ int nimf_apf_cast(const float* x, int64_t n, const float* grad, int64_t n_grad,
  * library stream) and the call returns when the chosen format is known.
  * Scratch lives in a fixed 8,200-byte device array inside the library, so it
  * allocates nothing.  The first call on each device looks up that array's
- * address (make it before any stream capture).  Limits: n and n_grad at most
- * 2^31 - 1 (larger gives NIMF_ERR_SHAPE); calls that overlap on the GPU share
- * the array and race, so issue them one at a time. */
+ * address.  The call reads its reductions back to the host and synchronises
+ * `stream`; on a stream that is being captured it returns NIMF_ERR_STATE.
+ * Limits: n and n_grad at most 2^31 - 1 (larger gives NIMF_ERR_SHAPE); calls
+ * that overlap on the GPU share the array and race, so issue them one at a
+ * time. */
 int nimf_cf_autoselect_dev_noalloc(const float* x_dev, int64_t n, const float* grad_dev,
                                    int64_t n_grad, double rel_error_tol, int exp_margin,
                                    int* exponent_bits, int* mantissa_bits, void* stream);

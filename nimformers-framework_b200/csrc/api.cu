@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstring>
 #include <map>
@@ -26,9 +27,65 @@ bool g_ready = false;
 std::mutex g_mu;
 std::unordered_map<nimf_weight_t, std::unique_ptr<Weight>> g_weights;
 nimf_weight_t g_next = 1;
-// beMatmulQ4 host-array cache: (ptr, bytes, k, n, gs, ngr) -> handle
-std::map<std::tuple<uintptr_t, int64_t, int64_t, int64_t, int64_t, int64_t>, nimf_weight_t>
-    g_q4_cache;
+// beMatmulQ4 host-array cache: (wq, scales, zeros pointers, k, n, gs, ngr) ->
+// the registered handle and a fingerprint of the three arrays' contents.  A
+// hit needs the same pointers, shape and fingerprint, so a weight whose
+// address is reused by another of the same shape, or scales / zeros changed in
+// place, are registered afresh.
+using Q4Key = std::tuple<uintptr_t, uintptr_t, uintptr_t, int64_t, int64_t, int64_t, int64_t>;
+struct Q4Entry {
+  nimf_weight_t handle = 0;
+  uint64_t fingerprint = 0;
+};
+std::map<Q4Key, Q4Entry> g_q4_cache;
+int g_q4_check = NIMF_Q4_CACHE_CHECK_FULL;
+
+// 64-bit fingerprint of a byte range: four independent multiply-rotate lanes
+// over 8-byte words (about 10 GB/s on one core), then the tail bytes.
+uint64_t fp_mix(uint64_t h, uint64_t w) {
+  h ^= w * 0x9E3779B97F4A7C15ull;
+  h = (h << 27) | (h >> 37);
+  return h * 0xD6E8FEB86659FD93ull;
+}
+
+uint64_t fingerprint_bytes(const void* p, size_t n, uint64_t seed) {
+  const unsigned char* b = (const unsigned char*)p;
+  uint64_t l0 = seed ^ 0x243F6A8885A308D3ull, l1 = seed ^ 0x13198A2E03707344ull;
+  uint64_t l2 = seed ^ 0xA4093822299F31D0ull, l3 = seed ^ 0x082EFA98EC4E6C89ull;
+  size_t i = 0;
+  for (; i + 32 <= n; i += 32) {
+    uint64_t w[4];
+    std::memcpy(w, b + i, 32);
+    l0 = fp_mix(l0, w[0]);
+    l1 = fp_mix(l1, w[1]);
+    l2 = fp_mix(l2, w[2]);
+    l3 = fp_mix(l3, w[3]);
+  }
+  uint64_t h = fp_mix(fp_mix(fp_mix(fp_mix(0, l0), l1), l2), l3);
+  for (; i < n; ++i) h = fp_mix(h, (uint64_t)b[i] | ((uint64_t)i << 8));
+  return fp_mix(h, (uint64_t)n);
+}
+
+// Sampled fingerprint: the first and last 4 KB and one 64-byte block of every
+// 4 KB in between.
+uint64_t fingerprint_sampled(const void* p, size_t n, uint64_t seed) {
+  const unsigned char* b = (const unsigned char*)p;
+  if (n <= 16384) return fingerprint_bytes(p, n, seed);
+  uint64_t h = fingerprint_bytes(b, 4096, seed);
+  h = fp_mix(h, fingerprint_bytes(b + n - 4096, 4096, seed + 1));
+  for (size_t o = 4096; o + 64 <= n - 4096; o += 4096)
+    h = fp_mix(h, fingerprint_bytes(b + o, 64, o));
+  return fp_mix(h, (uint64_t)n);
+}
+
+uint64_t q4_fingerprint(const uint8_t* wq, size_t wbytes, const float* sc, const float* zp,
+                        size_t sbytes, int mode) {
+  if (mode == NIMF_Q4_CACHE_CHECK_NONE) return 0;
+  auto f = mode == NIMF_Q4_CACHE_CHECK_SAMPLED ? fingerprint_sampled : fingerprint_bytes;
+  uint64_t h = f(wq, wbytes, 1);
+  h = fp_mix(h, f(sc, sbytes, 2));
+  return fp_mix(h, f(zp, sbytes, 3));
+}
 }  // namespace
 
 int set_error(int code, const char* fmt, ...) {
@@ -58,6 +115,8 @@ int require_ctx(Context** out) {
   return NIMF_OK;
 }
 
+std::atomic<int64_t> g_alloc_count{0};
+
 int device_alloc(void** p, size_t bytes) {
   *p = nullptr;
   if (bytes == 0) bytes = 16;
@@ -66,6 +125,7 @@ int device_alloc(void** p, size_t bytes) {
     *p = nullptr;
     return set_error(NIMF_ERR_CUDA, "cudaMalloc(%zu) failed: %s", bytes, cudaGetErrorString(e));
   }
+  g_alloc_count.fetch_add(1, std::memory_order_relaxed);
   return NIMF_OK;
 }
 
@@ -278,6 +338,7 @@ int nimf_shutdown(void) {
   fw_release_scratch();
   release_perm_buffer();
   release_attn_buffer();
+  release_prep_buffers();
   release_p2p_groups();
   device_free(g_ctx.stage_in);
   device_free(g_ctx.stage_out);
@@ -285,6 +346,12 @@ int nimf_shutdown(void) {
   cudaStreamDestroy(g_ctx.stream);
   g_ctx = Context();
   g_ready = false;
+  return NIMF_OK;
+}
+
+int nimf_alloc_count(int64_t* count) {
+  if (!count) return set_error(NIMF_ERR_ARG, "NULL output");
+  *count = g_alloc_count.load(std::memory_order_relaxed);
   return NIMF_OK;
 }
 
@@ -486,7 +553,7 @@ int nimf_weight_free(nimf_weight_t h) {
   free_weight_storage(w);
   g_weights.erase(h);
   for (auto it = g_q4_cache.begin(); it != g_q4_cache.end();) {
-    if (it->second == h) it = g_q4_cache.erase(it);
+    if (it->second.handle == h) it = g_q4_cache.erase(it);
     else ++it;
   }
   return NIMF_OK;
@@ -659,25 +726,49 @@ int nimf_matmul_q4(const float* a, const uint8_t* wq, const float* scales, const
   NIMF_TRY(require_ctx(&c));
   if (m < 0 || k < 0 || n < 0) return set_error(NIMF_ERR_SHAPE, "negative shape");
   if (m == 0 || n == 0) return NIMF_OK;
+  if (!wq || !scales || !zeros) return set_error(NIMF_ERR_ARG, "NULL weight array");
   const int64_t bytes = n * ((k + 1) / 2);
-  auto key = std::make_tuple((uintptr_t)wq, bytes, k, n, group_size, n_groups_per_row);
+  const int64_t sbytes = n * std::max<int64_t>(n_groups_per_row, 0) * (int64_t)sizeof(float);
+  const Q4Key key = std::make_tuple((uintptr_t)wq, (uintptr_t)scales, (uintptr_t)zeros, k, n,
+                                    group_size, n_groups_per_row);
+  const uint64_t fp = q4_fingerprint(wq, (size_t)bytes, scales, zeros, (size_t)sbytes, g_q4_check);
   nimf_weight_t h;
   auto it = g_q4_cache.find(key);
-  if (it != g_q4_cache.end() && lookup(it->second)) {
-    h = it->second;
+  if (it != g_q4_cache.end() && it->second.fingerprint == fp && lookup(it->second.handle)) {
+    h = it->second.handle;
   } else {
+    if (it != g_q4_cache.end()) {
+      // same arrays, other contents: the old device copy is stale
+      const nimf_weight_t old = it->second.handle;
+      g_q4_cache.erase(it);
+      if (lookup(old)) NIMF_TRY(nimf_weight_free(old));
+    }
     NIMF_TRY(nimf_weight_register_q4g(wq, scales, zeros, n, k, group_size, n_groups_per_row, 0, n,
                                       &h));
-    g_q4_cache[key] = h;
+    g_q4_cache[key] = Q4Entry{h, fp};
   }
   return nimf_matmul_w(h, a, m, out);
+}
+
+int nimf_q4_cache_set_check(int mode) {
+  if (mode != NIMF_Q4_CACHE_CHECK_FULL && mode != NIMF_Q4_CACHE_CHECK_SAMPLED &&
+      mode != NIMF_Q4_CACHE_CHECK_NONE)
+    return set_error(NIMF_ERR_ARG, "nimf_q4_cache_set_check: mode %d", mode);
+  g_q4_check = mode;
+  return NIMF_OK;
+}
+
+int nimf_q4_cache_size(int64_t* entries) {
+  if (!entries) return set_error(NIMF_ERR_ARG, "NULL output");
+  *entries = (int64_t)g_q4_cache.size();
+  return NIMF_OK;
 }
 
 int nimf_weight_cache_clear(void) {
   Context* c;
   NIMF_TRY(require_ctx(&c));
   std::vector<nimf_weight_t> hs;
-  for (auto& kv : g_q4_cache) hs.push_back(kv.second);
+  for (auto& kv : g_q4_cache) hs.push_back(kv.second.handle);
   g_q4_cache.clear();
   for (nimf_weight_t h : hs)
     if (lookup(h)) NIMF_TRY(nimf_weight_free(h));

@@ -369,12 +369,15 @@ int cf_dequant(const CFWeight& w, float* out, cudaStream_t st) {
 // ---------------------------------------------------------------------------
 // Allocation-free APF format selection on device buffers.
 //
-// For callers that must not allocate device memory: code running while a
-// stream is being captured into a CUDA graph, or a host that hands the GPU's
-// whole memory to its own allocator and forbids any other cudaMalloc.  The
-// existing nimf_cf_autoselect stages x in buffers the library allocates and
-// keeps its reduction scratch in another allocated buffer; this variant reads
-// the caller's device buffers and keeps its scratch in the fixed array below.
+// For callers that cannot call cudaMalloc: a host that hands the GPU's whole
+// memory to its own allocator (a serving process that reserves it at start-up)
+// and forbids any other allocation, or one that must not add allocations while
+// a step runs.  The existing nimf_cf_autoselect stages x in buffers the
+// library allocates and keeps its reduction scratch in another allocated
+// buffer; this variant reads the caller's device buffers and keeps its scratch
+// in the fixed array below.  It copies its reductions back to the host and
+// synchronises the stream, so a call on a stream that is being captured
+// returns NIMF_ERR_STATE without touching the capture.
 //
 // Scratch: g_noalloc_scratch holds 2 + 2048 32-bit words (8,200 bytes):
 // word 0 / 1 are the min / max of |x| (as float bits), words 2.. a radix
@@ -462,8 +465,17 @@ extern "C" int nimf_cf_autoselect_dev_noalloc(const float* x_dev, int64_t n,
   if (!exponent_bits || !mantissa_bits) return set_error(NIMF_ERR_ARG, "NULL output");
   if ((n > 0 && !x_dev) || (n_grad > 0 && !grad_dev)) return set_error(NIMF_ERR_ARG, "NULL input");
   if (c->device < 0 || c->device >= 64) return set_error(NIMF_ERR_STATE, "device index");
+  cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+  {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    NIMF_CUDA_TRY(cudaStreamIsCapturing(st, &cs));
+    if (cs != cudaStreamCaptureStatusNone)
+      return set_error(NIMF_ERR_STATE,
+                       "nimf_cf_autoselect_dev_noalloc: the stream is being captured; this call "
+                       "reads its reductions back to the host and synchronises the stream");
+  }
   // One-time set-up on this device (the device is current): the array's
-  // device address.  Make the first call before any stream capture.
+  // device address.
   if (!g_noalloc_addr[c->device]) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
@@ -473,7 +485,6 @@ extern "C" int nimf_cf_autoselect_dev_noalloc(const float* x_dev, int64_t n,
     g_noalloc_addr[c->device] = (unsigned*)p;
   }
   unsigned* scratch = g_noalloc_addr[c->device];
-  cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
 
   float mn = 0.f, mx = 0.f;
   bool found = false;

@@ -635,7 +635,28 @@ FwScratch g_fws;
 
 int fw_scratch(size_t part_bytes, size_t cnt_n, cudaStream_t st, float** part, unsigned** cnt) {
   Context* c = ctx();
-  if (g_fws.device != c->device) g_fws = FwScratch();
+  const bool grow = g_fws.device != c->device || g_fws.part_bytes < part_bytes || g_fws.cnt_n < cnt_n;
+  if (grow) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    NIMF_CUDA_TRY(cudaStreamIsCapturing(st, &cs));
+    if (cs != cudaStreamCaptureStatusNone)
+      return set_error(NIMF_ERR_STATE,
+                       "byte-format GEMV: its k-split scratch must grow, which cannot happen "
+                       "during stream capture; run the same call once before capturing");
+  }
+  if (g_fws.device != c->device) {
+    // buffers of another device: free them with that device current
+    if (g_fws.device >= 0 && (g_fws.part || g_fws.cnt)) {
+      int cur = 0;
+      NIMF_CUDA_TRY(cudaGetDevice(&cur));
+      NIMF_CUDA_TRY(cudaSetDevice(g_fws.device));
+      cudaDeviceSynchronize();
+      device_free(g_fws.part);
+      device_free(g_fws.cnt);
+      NIMF_CUDA_TRY(cudaSetDevice(cur));
+    }
+    g_fws = FwScratch();
+  }
   if (g_fws.part_bytes < part_bytes) {
     device_free(g_fws.part);
     g_fws.part = nullptr;

@@ -162,6 +162,7 @@ int q4g_gemm_tc(const Q4GWeight& w, const float* x, int64_t m, float* y, cudaStr
 // Per-device scratch of the tensor-core GEMMs' prepared x (grown outside
 // stream capture; calls using it are ordered on one stream).
 int tc_prep_buffer(size_t bytes, cudaStream_t st, unsigned char** out);
+void release_prep_buffers();
 int q4g_gemm_tc_group(const Q4GWeight* const* ws, int count, const float* x, int64_t m,
                       float* const* ys, cudaStream_t st);
 

@@ -23,7 +23,8 @@
 // does only after its call e kernel, including the reads of stage[par], has
 // completed in stream order.
 //
-// The wait is bounded (kWaitNs of %globaltimer): on expiry the block sets the
+// The wait is bounded (2 s of %globaltimer by default, nimf_p2p_set_timeout_ms
+// changes it): on expiry the block sets the
 // context's error word (reported by nimf_sync as NIMF_ERR_TIMEOUT), leaves its
 // dst columns unwritten and returns; while the word stays set, later waits
 // give up at once, so a missing peer costs one bound, not one per call.  No TMA and no multicast: plain peer
@@ -42,7 +43,8 @@ namespace {
 constexpr int kMaxRanks = 8;
 constexpr int kChunks = 8;      // blocks per peer
 constexpr int kThreads = 256;
-constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s
+// bound of a peer wait, process-wide (nimf_p2p_set_timeout_ms); 2 s by default
+unsigned long long g_wait_ns = 2000000000ull;
 constexpr int64_t kMaxSlot = (int64_t)1 << 28;          // floats per slice
 
 struct P2PArgs {
@@ -50,6 +52,7 @@ struct P2PArgs {
   unsigned* flags[kMaxRanks];   // each rank's flags base
   unsigned* epoch;              // this rank's per-block call counters [kMaxRanks][kChunks]
   int* err;
+  unsigned long long wait_ns;   // bound of the wait for a peer's flag
   int world, rank;
   int64_t slot;                 // floats per stage slot (a multiple of 4)
 };
@@ -147,7 +150,7 @@ __global__ void __launch_bounds__(kThreads) p2p_allgather_kernel(const P2PArgs a
       const unsigned long long t0 = globaltimer();
       while ((int)(load_acquire_sys(mine) - e) < 0) {
         // an earlier expired wait (error word still set) fails this one at once
-        if (globaltimer() - t0 > kWaitNs || *(volatile int*)a.err != 0) {
+        if (globaltimer() - t0 > a.wait_ns || *(volatile int*)a.err != 0) {
           s_ok = 0;
           atomicExch(a.err, 1);
           break;
@@ -276,6 +279,7 @@ int nimf_p2p_allgather_dev(int64_t group, const float* src, int64_t rows, int64_
   }
   a.epoch = g->epoch;
   a.err = c->dev_err;
+  a.wait_ns = g_wait_ns;
   a.world = g->world;
   a.rank = g->rank;
   a.slot = g->slot;
@@ -297,6 +301,13 @@ int nimf_p2p_allgather_dev(int64_t group, const float* src, int64_t rows, int64_
   else
     NIMF_CUDA_TRY(cudaLaunchKernelEx(&cfg, p2p_allgather_kernel<false>, a, src, (int)rows,
                                      (int)cols, ld_src, dst, ld_dst));
+  return NIMF_OK;
+}
+
+int nimf_p2p_set_timeout_ms(int64_t ms) {
+  if (ms < 1 || ms > 600000)
+    return set_error(NIMF_ERR_ARG, "p2p_set_timeout_ms: %lld not in [1, 600000]", (long long)ms);
+  g_wait_ns = (unsigned long long)ms * 1000000ull;
   return NIMF_OK;
 }
 

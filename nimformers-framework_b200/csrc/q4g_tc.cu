@@ -552,12 +552,29 @@ struct PrepBuf {
   void* p = nullptr;
   size_t bytes = 0;
 };
-PrepBuf g_prep[16];
+constexpr int kPrepDevices = 64;
+PrepBuf g_prep[kPrepDevices];
+
+void release_prep_buffers() {
+  int cur = -1;
+  cudaGetDevice(&cur);
+  for (PrepBuf& b : g_prep) {
+    if (b.p) {
+      cudaSetDevice(b.device);
+      cudaDeviceSynchronize();
+      device_free(b.p);
+    }
+    b = PrepBuf();
+  }
+  if (cur >= 0) cudaSetDevice(cur);
+}
 
 int tc_prep_buffer(size_t bytes, cudaStream_t st, unsigned char** out) {
   Context* c = ctx();
   const int dev = c ? c->device : 0;
-  PrepBuf& b = g_prep[dev & 15];
+  if (dev < 0 || dev >= kPrepDevices)
+    return set_error(NIMF_ERR_STATE, "prefill GEMM: device index %d", dev);
+  PrepBuf& b = g_prep[dev];
   if (b.device != dev || b.bytes < bytes) {
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
     NIMF_CUDA_TRY(cudaStreamIsCapturing(st, &cs));

@@ -37,17 +37,20 @@ KIND_F32, KIND_INT8, KIND_INT4_SYM, KIND_INT4_ASYM, KIND_CUSTOM_FLOAT, KIND_FP4 
 # Every symbol include/nimf_cuda.h declares (checked by the ABI test).
 EXPORTS = [
     "nimf_init", "nimf_shutdown", "nimf_last_error", "nimf_device_count", "nimf_sync",
+    "nimf_alloc_count",
     "nimf_weight_register_q4g", "nimf_weight_register_i8", "nimf_weight_register_cf",
     "nimf_weight_register_fp4", "nimf_weight_register_f32", "nimf_weight_free",
     "nimf_weight_info", "nimf_matmul_w", "nimf_matmul_w_dev", "nimf_matmul_w_group_dev",
     "nimf_matmul_w_group", "nimf_matmul_q4",
-    "nimf_weight_cache_clear", "nimf_matmul_f32", "nimf_matmul2_f32", "nimf_dequant_w",
+    "nimf_weight_cache_clear", "nimf_q4_cache_set_check", "nimf_q4_cache_size",
+    "nimf_matmul_f32", "nimf_matmul2_f32", "nimf_dequant_w",
     "nimf_cf_encode", "nimf_cf_decode", "nimf_cf_encode_dev", "nimf_cf_decode_dev",
     "nimf_cf_autoselect", "nimf_apf_cast", "nimf_cf_autoselect_dev_noalloc",
     "nimf_nimq_parse", "nimf_nimq_get", "nimf_nimq_register", "nimf_weight_register_gptq",
     "nimf_rmsnorm_dev", "nimf_layernorm_dev", "nimf_add_rmsnorm_dev", "nimf_add_dev", "nimf_swiglu_dev", "nimf_rope_dev",
     "nimf_attention_decode_dev", "nimf_embedding_lookup_dev", "nimf_greedy_sample_dev",
     "nimf_p2p_create", "nimf_p2p_connect", "nimf_p2p_allgather_dev", "nimf_p2p_destroy",
+    "nimf_p2p_set_timeout_ms",
 ]
 
 
@@ -77,6 +80,7 @@ def lib():
         "nimf_shutdown": [],
         "nimf_device_count": [ctypes.POINTER(ctypes.c_int)],
         "nimf_sync": [],
+        "nimf_alloc_count": [ctypes.POINTER(i64)],
         "nimf_weight_register_q4g": [vp, vp, vp, i64, i64, i64, i64, i64, i64, u64p],
         "nimf_weight_register_i8": [vp, vp, i64, i64, i64, i64, i64, u64p],
         "nimf_weight_register_cf": [vp, i32, i32, vp, i64, i64, i64, i64, u64p],
@@ -91,6 +95,8 @@ def lib():
         "nimf_matmul_w_group": [vp, i32, vp, i64, vp],
         "nimf_matmul_q4": [vp, vp, vp, vp, i64, i64, i64, i64, i64, vp],
         "nimf_weight_cache_clear": [],
+        "nimf_q4_cache_set_check": [i32],
+        "nimf_q4_cache_size": [ctypes.POINTER(i64)],
         "nimf_matmul_f32": [vp, i64, i64, vp, i64, i64, vp],
         "nimf_matmul2_f32": [vp, i64, i64, vp, i64, i64, vp, i64, i64, vp, i64, i64, vp, vp],
         "nimf_dequant_w": [ctypes.c_uint64, vp],
@@ -116,6 +122,7 @@ def lib():
         "nimf_p2p_connect": [i64, vp],
         "nimf_p2p_allgather_dev": [i64, vp, i64, i64, i64, vp, i64, vp],
         "nimf_p2p_destroy": [i64],
+        "nimf_p2p_set_timeout_ms": [i64],
         "nimf_greedy_sample_dev": [vp, i64, i64, vp, i64, ctypes.c_float, vp, vp],
         "nimf_add_dev": [vp, vp, i64, vp, vp],
         "nimf_add_rmsnorm_dev": [vp, vp, vp, i64, i64, ctypes.c_float, vp, vp, vp],
@@ -257,7 +264,9 @@ def beMatmul(ctx, a, M, K, b, K2, N):
 
 def beMatmulQ4(ctx, a, wq, scales, zeros, M, K, N, groupSize, nGroupsPerRow):
     """backend.nim:93-110 (int4 asymmetric per-group weights, host arrays).
-    The packed weight is uploaded once and cached by host address."""
+    The packed weight is uploaded once and cached, keyed by the three arrays'
+    addresses and the shape and checked against a fingerprint of their
+    contents on every call."""
     a = _arr(a, np.float32)
     wq = np.ascontiguousarray(wq, dtype=np.uint8).ravel()
     scales = _arr(scales, np.float32)

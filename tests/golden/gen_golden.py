@@ -1,7 +1,8 @@
 """Generate the golden fixtures under tests/golden/ by running the reference's
 own Python code (export_to_nimq.py of the Nimformer project).
 
-Usage:  python tests/golden/gen_golden.py [--reference /root/reference]
+Usage:  python tests/golden/gen_golden.py --reference <path of the Nimformer source tree>
+        (or set NIMF_REFERENCE to that path)
 
 The reference is imported from its source tree (read-only); nothing is copied
 from it.  Each fixture stores seeded inputs and the reference's outputs:
@@ -86,8 +87,11 @@ def gptq_case(rng, in_features, out_features, group, act_order):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("NIMF_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("NIMF_REFERENCE"),
+                    help="the Nimformer source tree (default: $NIMF_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference or set NIMF_REFERENCE")
     ref = load_reference(args.reference)
 
     for name, w, gs in q4g_cases():

@@ -5,6 +5,7 @@ Bar: dequantised weights bit-exact with quant.nim's LUT formula; GEMV
 outputs within  max|y - y_ref| / max|y_ref| <= 1e-3  (fp32 accumulate) of the
 reference path cpuDequantMatmulQ4Fallback + cpuMatmul (gpubackend.nim:628-653).
 """
+import ctypes
 import glob
 import os
 
@@ -107,6 +108,66 @@ def test_beMatmulQ4_dropin(nimf_gpu):
     ref = O.dequant_matmul_q4(a, p, s, z, m, k, n, gs, ngr).ravel()
     assert rel_err(y1, ref) <= TOL
     nimf_gpu.check(nimf_gpu.lib().nimf_weight_cache_clear())
+
+
+def test_beMatmulQ4_cache_sees_changed_scales(nimf_gpu):
+    """Scales and zeros changed in place behind the same pointers (and the
+    packed bytes too) give fresh results, not the cached device copy."""
+    n, k, gs, m = 64, 512, 128, 2
+    p, s, z, ngr = quantized(n, k, gs, seed=5)
+    a = np.random.default_rng(6).standard_normal(m * k).astype(np.float32)
+    ctx = nimf_gpu.newBackend()
+    L = nimf_gpu.lib()
+    nimf_gpu.check(L.nimf_weight_cache_clear())
+    y1 = nimf_gpu.beMatmulQ4(ctx, a, p, s, z, m, k, n, gs, ngr)
+    s *= np.float32(2.0)                       # in place: same address
+    y2 = nimf_gpu.beMatmulQ4(ctx, a, p, s, z, m, k, n, gs, ngr)
+    ref2 = O.dequant_matmul_q4(a, p, s, z, m, k, n, gs, ngr).ravel()
+    assert rel_err(y2, ref2) <= TOL
+    assert rel_err(y2, 2 * y1) <= 1e-5
+    z[:] = z[::-1]
+    p[: p.size // 2] ^= 0x5A
+    y3 = nimf_gpu.beMatmulQ4(ctx, a, p, s, z, m, k, n, gs, ngr)
+    assert rel_err(y3, O.dequant_matmul_q4(a, p, s, z, m, k, n, gs, ngr).ravel()) <= TOL
+    cnt = ctypes.c_int64()
+    nimf_gpu.check(L.nimf_q4_cache_size(ctypes.byref(cnt)))
+    assert cnt.value == 1                      # the stale copies were dropped
+    nimf_gpu.check(L.nimf_weight_cache_clear())
+
+
+def test_beMatmulQ4_cache_sees_a_new_weight_at_a_reused_address(nimf_gpu):
+    """A weight freed and replaced by another of the same shape in the same
+    host buffers (as a GC'd seq whose memory is reused) is registered afresh,
+    in every fingerprint mode that reads the contents."""
+    n, k, gs, m = 48, 1024, 128, 1
+    L = nimf_gpu.lib()
+    ctx = nimf_gpu.newBackend()
+    a = np.random.default_rng(7).standard_normal(m * k).astype(np.float32)
+    p, s, z, ngr = quantized(n, k, gs, seed=8)
+    p2, s2, z2, _ = quantized(n, k, gs, seed=9)
+    try:
+        for mode in (0, 1):                    # FULL, SAMPLED
+            nimf_gpu.check(L.nimf_q4_cache_set_check(mode))
+            nimf_gpu.check(L.nimf_weight_cache_clear())
+            bp, bs, bz = p.copy(), s.copy(), z.copy()
+            nimf_gpu.beMatmulQ4(ctx, a, bp, bs, bz, m, k, n, gs, ngr)
+            bp[:], bs[:], bz[:] = p2, s2, z2       # the "new" weight, same addresses
+            y = nimf_gpu.beMatmulQ4(ctx, a, bp, bs, bz, m, k, n, gs, ngr)
+            assert rel_err(y, O.dequant_matmul_q4(a, p2, s2, z2, m, k, n, gs, ngr).ravel()) <= TOL
+        # NONE trusts the pointers: the caller clears the cache on replacement
+        nimf_gpu.check(L.nimf_q4_cache_set_check(2))
+        nimf_gpu.check(L.nimf_weight_cache_clear())
+        bp, bs, bz = p.copy(), s.copy(), z.copy()
+        y0 = nimf_gpu.beMatmulQ4(ctx, a, bp, bs, bz, m, k, n, gs, ngr)
+        bs *= np.float32(3.0)
+        assert np.array_equal(nimf_gpu.beMatmulQ4(ctx, a, bp, bs, bz, m, k, n, gs, ngr), y0)
+        nimf_gpu.check(L.nimf_weight_cache_clear())
+        y = nimf_gpu.beMatmulQ4(ctx, a, bp, bs, bz, m, k, n, gs, ngr)
+        assert rel_err(y, 3 * y0) <= 1e-5
+        assert L.nimf_q4_cache_set_check(7) == -1
+    finally:
+        nimf_gpu.check(L.nimf_q4_cache_set_check(0))
+        nimf_gpu.check(L.nimf_weight_cache_clear())
 
 
 def test_row_shards_concatenate_to_full(nimf_gpu):

@@ -65,18 +65,53 @@ def test_noalloc_autoselect_matches_allocating_entry(nimf_gpu):
         assert second == want, name
 
 
-def test_noalloc_leaves_device_memory_unchanged(nimf_gpu):
+def _alloc_count(nimf):
+    n = ctypes.c_int64()
+    nimf.check(nimf.lib().nimf_alloc_count(ctypes.byref(n)))
+    return n.value
+
+
+def test_noalloc_makes_no_device_allocation(nimf_gpu):
+    """The library's own allocation counter and torch's allocator both stay
+    put across calls (device-wide free memory is not compared: other
+    processes on the GPU move it)."""
     import torch
     x = torch.randn(1 << 20, device="cuda")
     g = torch.randn(1 << 16, device="cuda") * 1e-5
     stream = torch.cuda.current_stream().cuda_stream
     args = (x.data_ptr(), x.numel(), g.data_ptr(), g.numel(), stream)
-    first = _noalloc_select(nimf_gpu, *args)     # first call on the device does its set-up
-    free0 = torch.cuda.mem_get_info()[0]
+    n0 = _alloc_count(nimf_gpu)
+    t0 = torch.cuda.memory_allocated()
+    first = _noalloc_select(nimf_gpu, *args)     # the first call on the device does its set-up
     for _ in range(3):
         assert _noalloc_select(nimf_gpu, *args) == first
-    assert torch.cuda.mem_get_info()[0] == free0
+    assert _alloc_count(nimf_gpu) == n0
+    assert torch.cuda.memory_allocated() == t0
     assert first == _alloc_select(nimf_gpu, x.cpu().numpy(), g.cpu().numpy())
+
+
+def test_noalloc_refuses_a_capturing_stream(nimf_gpu):
+    """It reads its reductions back to the host and synchronises, so on a
+    stream that is being captured it answers NIMF_ERR_STATE and leaves the
+    capture intact."""
+    import torch
+    x = torch.randn(4096, device="cuda")
+    side = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    e, m = ctypes.c_int(-1), ctypes.c_int(-1)
+    with torch.cuda.stream(side):
+        graph.capture_begin()
+        try:
+            x.mul_(1.0)
+            rc = nimf_gpu.lib().nimf_cf_autoselect_dev_noalloc(
+                ctypes.c_void_p(x.data_ptr()), x.numel(), None, 0, 1e-3, 1,
+                ctypes.byref(e), ctypes.byref(m), ctypes.c_void_p(side.cuda_stream))
+        finally:
+            graph.capture_end()
+    assert rc == -7 and b"captured" in nimf_gpu.lib().nimf_last_error()
+    assert (e.value, m.value) == (-1, -1)
+    graph.replay()                               # the capture is still valid
+    torch.cuda.synchronize()
 
 
 def test_noalloc_rejects_oversize_and_bad_arguments(nimf_gpu):
