@@ -289,6 +289,71 @@ int nimf_embedding_lookup_dev(const float* table, int64_t vocab, int64_t dim,
 int nimf_greedy_sample_dev(const float* logits, int64_t rows, int64_t vocab, const int32_t* recent,
                            int64_t n_recent, float repeat_penalty, int32_t* out_ids, void* stream);
 
+/* ------------------------------------------------------------ whole decode step */
+/* One decode token of a Llama-style stack with int4 group-128 weights as ONE
+ * persistent, cooperative launch: LlamaModelL.forwardStep(ids = [token],
+ * isPrefill = false) (nim_inference.nim:887-921) -- embedding lookup, per
+ * layer RMSNorm, q/k/v, RoPE, KV append and attention (forwardDecode
+ * :624-748), o, residual add + RMSNorm, gate/up, SwiGLU, down, residual add --
+ * then the final RMSNorm and the lm_head, followed by the greedy branch of
+ * sampleTopP (:1019-1036) when a next-token buffer is given.  The results
+ * equal the one-launch-per-op path of the glue entry points above up to the
+ * order of the reductions (x is quantised into two 8-bit digits per element
+ * with one scale per stage, as in the GEMV).
+ *
+ * Every pointer in the descriptors is a device pointer borrowed by the plan
+ * (it must stay valid until nimf_decode_destroy); every weight is a handle of
+ * an int4 asymmetric weight with group size 128 registered without an
+ * act-order permutation: wq [d_model x d_model], wk / wv [n_kv_heads*head_dim
+ * x d_model], wo [d_model x d_model], wgate / wup [ffn x d_model], wdown
+ * [d_model x ffn], lm_head [vocab x d_model] (rows = output features, as
+ * quant.nim).  Caches are [n_kv_heads][max_seq][head_dim] fp32 and rope
+ * tables [max_seq][head_dim/2] (newRoPEL).  Limits: d_model and ffn multiples
+ * of 128 up to 14336, head_dim 64 or 128, n_heads * head_dim = d_model,
+ * n_heads <= 64 and a multiple of n_kv_heads, at most 256 recent ids. */
+typedef struct nimf_decode_layer_desc {
+  nimf_weight_t wq, wk, wv, wo, wgate, wup, wdown;
+  const float* attn_norm; /* [d_model] RMSNorm weight before attention */
+  const float* ffn_norm;  /* [d_model] RMSNorm weight before the FFN   */
+  float* k_cache;         /* [n_kv_heads][max_seq][head_dim]            */
+  float* v_cache;
+} nimf_decode_layer_desc;
+
+typedef struct nimf_decode_desc {
+  int64_t n_layers, d_model, n_heads, n_kv_heads, head_dim, ffn_dim, vocab, max_seq;
+  int64_t n_recent_max;   /* recent ids a step may pass (<= 256) */
+  float norm_eps;
+  const float* embedding; /* [vocab][d_model] */
+  const float* final_norm;
+  nimf_weight_t lm_head;
+  const float* rope_cos;  /* [max_seq][head_dim/2] */
+  const float* rope_sin;
+  const nimf_decode_layer_desc* layers; /* host array of n_layers (copied) */
+} nimf_decode_desc;
+
+/* Builds the step's stage table and its device scratch (a few hundred KB). */
+int nimf_decode_create(const nimf_decode_desc* desc, int64_t* plan);
+/* Enqueues one step on `stream` (NULL: the library stream); asynchronous.
+ * token_dev [1] int32: the input token (out-of-range ids embed as zeros);
+ * pos_dev [1] int32: its position (the KV row appended; 0 <= pos < max_seq,
+ * else the step reports NIMF_ERR_TIMEOUT-class device error 4 through
+ * nimf_sync and appends nothing), incremented by the step when advance_pos is
+ * non-zero; logits_dev [vocab] fp32 receives the logits; next_token_dev
+ * (nullable, may equal token_dev) receives the greedy choice over the logits
+ * with repeat_penalty applied once per occurrence of an id in
+ * recent_dev[0..n_recent).  Both token and position are read on the device,
+ * so a CUDA graph of this call can be replayed token after token.  A grid
+ * barrier that waits longer than the bound (nimf_decode_set_timeout_ms, 2 s by
+ * default) gives up, and nimf_sync reports NIMF_ERR_TIMEOUT. */
+int nimf_decode_step_dev(int64_t plan, int32_t* token_dev, int32_t* next_token_dev,
+                         int32_t* pos_dev, int advance_pos, const int32_t* recent_dev,
+                         int64_t n_recent, float repeat_penalty, float* logits_dev, void* stream);
+/* Grid size (CTAs), number of stages and attention position splits of a plan. */
+int nimf_decode_info(int64_t plan, int64_t* grid, int64_t* stages, int64_t* attn_splits);
+/* Bound of the step's grid-barrier waits, milliseconds (1 .. 600000). */
+int nimf_decode_set_timeout_ms(int64_t ms);
+int nimf_decode_destroy(int64_t plan);
+
 /* ------------------------------------------------- sharded outputs over peer memory */
 /* The reference has no multi-GPU path.  These calls gather N-shard outputs
  * (rank r computed output columns [r*cols, (r+1)*cols)) into the full x of the

@@ -339,6 +339,7 @@ int nimf_shutdown(void) {
   release_perm_buffer();
   release_attn_buffer();
   release_prep_buffers();
+  release_decode_plans();
   release_p2p_groups();
   device_free(g_ctx.stage_in);
   device_free(g_ctx.stage_out);

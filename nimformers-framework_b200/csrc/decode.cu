@@ -1,0 +1,1175 @@
+// decode.cu -- one whole decode step of a Llama-style stack with int4
+// group-128 weights (LlamaModelL.forwardStep with isPrefill = false,
+// nim_inference.nim:887-921, followed by the temperature <= 0 branch of
+// sampleTopP, :1019-1036) as ONE persistent launch.
+//
+// Why one launch: a decode step at batch 1 is 129 weight-streaming GEMVs
+// (3.7 GB at the 7B shape) separated by small glue steps.  Launched one by one,
+// every GEMV pays a ramp (an empty weight ring at launch), a drain (the
+// slowest CTA) and the launch gap, about 6 us each against 4 us of streaming
+// for a 28 MB projection.  Here the producer warp of every CTA streams the
+// weights of the whole step back to back: the weights do not depend on the
+// activations, so the ring keeps filling with the next projection's weights
+// while the grid waits for the previous projection's outputs.
+//
+// Grid: one CTA per SM (cooperative launch, so every CTA is resident), 18
+// warps: a producer (bulk copies of the packed weights into a 4-stage
+// mbarrier ring of 36 KB stages), 16 consumer warps and a merge warp, as in
+// the standalone GEMV (q4g.cu).  The step is a table of stages:
+//   per layer  S1 q/k/v GEMV     x = RMSNorm(h + down_prev) (layer 0: the
+//                                embedding row), the sum kept as the residual
+//              S2 attention      (head, position split) units: RoPE on q and
+//                                the new k, KV append, scores, softmax
+//                                partials (max, sum, unnormalised P.V)
+//              S3 o GEMV         x = the split partials combined
+//              S4 gate/up GEMV   x = RMSNorm(residual + o), sum kept
+//              S5 down GEMV      x = SwiGLU(gate, up)
+//   then       lm_head GEMV      x = RMSNorm(residual + down) with the final
+//                                norm; the merge warps keep the repetition-
+//                                penalised argmax of their rows, and CTA 0
+//                                picks the next token from the CTA results.
+// Stage s may start (its consumers compute x) only when every CTA has
+// finished stage s-1: a grid barrier on a per-stage arrival counter, waited
+// on by one consumer thread with ld.acquire and a %globaltimer bound.  Every
+// x is computed redundantly by every CTA from the previous stage's outputs
+// (read through L2 with ld.global.cg, since they were written in this launch),
+// quantised into two signed 8-bit digits per element with one scale per row
+// (max|x| / 127), and multiplied on the s8 tensor cores against the nibbles,
+// as in q4g.cu: per group sc s (A - zp D) with A the exact MMA sum, D the exact
+// digit sum.  The glue arithmetic follows glue.cu (same roundings).
+//
+// Every wait is bounded: mbarrier waits as in the GEMV, grid barriers by the
+// plan's wait bound; an expired wait sets the context's host-mapped error word
+// (nimf_sync then reports NIMF_ERR_TIMEOUT) and a device-side abort flag that
+// makes later waits of the plan give up at once.  No TMA multicast, no
+// cluster: plain bulk copies into this CTA's shared memory.
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <vector>
+
+#include "device_util.cuh"
+#include "nimf_internal.h"
+
+namespace nimf {
+
+namespace {
+
+constexpr int kCons = 16;                        // consumer warps
+constexpr int kConsThreads = kCons * 32;         // 512
+constexpr int kThreads = (kCons + 2) * 32;       // + producer + merge warp
+constexpr int kKQG = 2;                          // 64-k quads per group of 128
+constexpr int kGS = 128;
+constexpr int kChunkQ = 8;                       // quads per consumer chunk (512 k)
+constexpr int kCG = kChunkQ / kKQG;              // groups per chunk
+constexpr int kKbg = 32;                         // groups per ring stage (4096 k)
+constexpr int kNcs = kKbg / kCG;                 // chunks per ring stage
+constexpr int kStageW = kKbg * kKQG * 512;       // weight bytes of a ring stage
+constexpr int kStageBytes = kStageW + kKbg * 128;  // + the scale/zero float4s
+constexpr int kNS = 4;                           // ring stages
+constexpr int kIssuers = 4;                      // producer lanes (lane l issues stages q = l mod 4)
+constexpr int kMaxK = 14336;                     // largest K of a stage
+constexpr int kMaxGroups = kMaxK / kGS;
+constexpr int kNV = (kMaxK / 4 + kConsThreads - 1) / kConsThreads;  // float4 of x per thread
+constexpr int kMaxHeads = 64;
+constexpr int kMaxSplit = 8;
+constexpr int kMaxProb = 3;
+constexpr int kMaxRecent = 256;
+constexpr int kMaxPs = 4096;                     // positions of one attention unit
+constexpr int kMaxHeadDim = 256;
+constexpr int kBarCons = 1;                      // named barrier of the consumer warps
+// ring slot q % kNS always serves the same 8 consumer warps and producer lane
+static_assert(kNS % kIssuers == 0 && (kNS * kNcs) % kCons == 0, "ring period");
+
+// ---- shared memory
+constexpr int kOffBar = 0;                        // full, empty, merged, pfull [kNS] uint64
+constexpr int kOffRed = 128;                      // float[32] reduction scratch
+constexpr int kOffZpad = 256;                     // 32 zero bytes
+constexpr int kOffMisc = 288;                     // xmax, counters
+constexpr int kOffComb = 384;                     // combine weights [kMaxHeads][kMaxSplit]
+constexpr int kOffCombML = kOffComb + kMaxHeads * kMaxSplit * 4;   // [kMaxHeads][2]
+constexpr int kOffRecent = kOffCombML + kMaxHeads * 2 * 4;         // int[kMaxRecent]
+constexpr int kOffMark = kOffRecent + kMaxRecent * 4;              // uint32[128]: recent rows of this CTA
+constexpr int kOffRing = 4608;
+constexpr int kOffXs = kOffRing + kNS * kStageBytes;
+constexpr int kXsBytes = kMaxK / 32 * 64;         // [k32][2 digits][4 lanes][2 words]
+constexpr int kOffSdi = kOffXs + kXsBytes;
+constexpr int kSdiBytes = kMaxGroups * 16 * 4;
+constexpr int kOffPart = kOffSdi + kSdiBytes;
+constexpr int kPartBytes = kNS * kNcs * 128 * 4;
+constexpr int kSmemBytes = kOffPart + kPartBytes;
+// attention scratch reuses xs + sdi (the digits are dead during attention)
+constexpr int kAttnBytes = (3 * kMaxHeadDim + kMaxPs) * 4 + kCons * kMaxHeadDim * 4;
+static_assert(kAttnBytes <= kXsBytes + kSdiBytes, "attention scratch");
+static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+static_assert(kOffRing >= kOffMark + 128 * 4, "head layout");
+
+enum { ST_GEMV = 0, ST_ATTN = 1 };
+enum { PRO_EMB_RMS = 0, PRO_ADD_RMS = 1, PRO_COMBINE = 2, PRO_SWIGLU = 3 };
+
+struct DecStage {
+  int kind, pro;
+  int k, groups, nkb, n_rt, nprob, greedy;
+  int rt_prefix[kMaxProb + 1];
+  int rows[kMaxProb];
+  const uint4* frag[kMaxProb];
+  const float4* sz[kMaxProb];
+  float* y[kMaxProb];       // nullptr: the launch's logits buffer
+  const float* a;           // prologue inputs
+  const float* b;
+  const float* w;           // norm weight
+  float* res_out;           // residual written by CTA 0
+  float* kc;                // attention: this layer's caches
+  float* vc;
+};
+
+struct DecArgs {
+  const DecStage* stages;
+  int nstages;
+  int D, H, HKV, HD, max_seq, nsplit, vocab;
+  float eps, scale, penalty;
+  const float* emb;         // [vocab][D]
+  const float* cos_t;       // [max_seq][HD/2]
+  const float* sin_t;
+  const float* q;           // S1 outputs, read by S2
+  const float* k;
+  const float* v;
+  float* part_o;            // [H][nsplit][HD]
+  float* part_ml;           // [H][nsplit][2]
+  float* logits;            // [vocab]
+  const int* tok_in;
+  int* tok_out;             // nullptr: no token choice
+  int* pos;
+  int advance_pos;
+  const int* recent;
+  int n_recent;
+  int* cand;                // [grid][4] per-CTA argmax (value bits, index, NaN-at-0, valid)
+  unsigned* ctl;            // [0] launches, [1] abort, [2 + s] arrivals at stage s
+  int* err;                 // host-mapped error word
+  unsigned long long wait_ns;
+};
+
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ float4 ldcg4(const float* p) {
+  return __ldcg(reinterpret_cast<const float4*>(p));
+}
+
+// Waits until *p >= target (wrap-safe); false if the bound ran out or the plan
+// was aborted by an earlier expiry.
+__device__ bool wait_count(const DecArgs& a, const unsigned* p, unsigned target) {
+  const unsigned long long t0 = gtimer();
+  for (unsigned it = 0;; ++it) {
+    if ((int)(ld_acquire(p) - target) >= 0) {
+      __threadfence();
+      return true;
+    }
+    if ((it & 63u) == 63u) {
+      if (*(volatile unsigned*)(a.ctl + 1) != 0u) return false;
+      if (gtimer() - t0 > a.wait_ns) {
+        atomicExch(a.ctl + 1, 1u);
+        if (a.err) atomicExch(a.err, 3);
+        return false;
+      }
+    }
+    __nanosleep(20);
+  }
+}
+
+// Bounded mbarrier wait of the ring (HINT as mbar_wait_t): gives up when the
+// plan's wait bound runs out or an earlier wait of the launch gave up, so one
+// failure cannot chain into many full-length waits.
+template <int HINT>
+__device__ bool dwait(const DecArgs& a, uint64_t* m, uint32_t parity) {
+  unsigned long long t0 = 0;
+  for (uint32_t i = 0;; ++i) {
+    if (HINT > 0) {
+      if (mbar_try_wait_sleep(m, parity, (uint32_t)HINT)) return true;
+    } else {
+      if (mbar_test_wait(m, parity)) return true;
+      __nanosleep((unsigned)(-HINT));
+    }
+    if ((i & 255u) == 255u) {
+      if (*(volatile unsigned*)(a.ctl + 1) != 0u) return false;
+      const unsigned long long t = gtimer();
+      if (t0 == 0) {
+        t0 = t;
+      } else if (t - t0 > a.wait_ns) {
+        atomicExch(a.ctl + 1, 1u);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void arrive(const DecArgs& a, int s) {
+  __threadfence();
+  atomicAdd(a.ctl + 2 + s, 1u);
+}
+
+__device__ __forceinline__ void row_split(int n_rt, int cid, int G, int* rt0, int* nrt) {
+  const int base = n_rt / G, rem = n_rt % G;
+  *rt0 = cid * base + min(cid, rem);
+  *nrt = base + (cid < rem ? 1 : 0);
+}
+
+__device__ __forceinline__ int prob_of(const DecStage& st, int grt) {
+  int p = 0;
+  while (p + 1 < st.nprob && grt >= st.rt_prefix[p + 1]) ++p;
+  return p;
+}
+
+// consumer-wide reductions (512 threads, named barrier 1)
+__device__ __forceinline__ float cons_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  named_barrier(kBarCons, kConsThreads);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  named_barrier(kBarCons, kConsThreads);
+  float t = 0.f;
+#pragma unroll
+  for (int i = 0; i < kCons; ++i) t += red[i];
+  return t;
+}
+__device__ __forceinline__ float cons_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  named_barrier(kBarCons, kConsThreads);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  named_barrier(kBarCons, kConsThreads);
+  float t = red[0];
+#pragma unroll
+  for (int i = 1; i < kCons; ++i) t = fmaxf(t, red[i]);
+  return t;
+}
+
+// ------------------------------------------------------------ x prologue
+// Computes x of a GEMV stage (K values, float4 f = tid + 512 j), writes the
+// residual (CTA 0), then the digits into xs, the group digit sums into sdi and
+// max|x| into *xmax.
+__device__ void prologue(const DecArgs& a, const DecStage& st, int cid, int tok, unsigned char* smem) {
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  float* red = reinterpret_cast<float*>(smem + kOffRed);
+  float* xmaxp = reinterpret_cast<float*>(smem + kOffMisc);
+  int* sdi = reinterpret_cast<int*>(smem + kOffSdi);
+  uint32_t* xw = reinterpret_cast<uint32_t*>(smem + kOffXs);
+  const int K = st.k;
+  const int f4 = K >> 2;
+  for (int i = tid; i < st.groups * 16; i += kConsThreads) sdi[i] = 0;
+  float4 v[kNV];
+  if (st.pro == PRO_COMBINE) {
+    // per head: M = max_j m_j, L = sum_j [l_j > 0] e^(m_j - M) l_j, weights
+    // e^(m_j - M) (attn_combine_kernel's arithmetic, splits in order)
+    float* cw = reinterpret_cast<float*>(smem + kOffComb);
+    float* cml = reinterpret_cast<float*>(smem + kOffCombML);
+    const int ns = a.nsplit;
+    for (int h = tid >> 5; h < a.H; h += kCons) {
+      const float* ml = a.part_ml + (size_t)h * ns * 2;
+      if (lane == 0) {
+        float M = -INFINITY;
+        for (int j = 0; j < ns; ++j) M = fmaxf(M, __ldcg(ml + 2 * j));
+        float L = 0.f;
+        for (int j = 0; j < ns; ++j) {
+          const float l = __ldcg(ml + 2 * j + 1);
+          const float e = expf(__fsub_rn(__ldcg(ml + 2 * j), M));
+          cw[h * kMaxSplit + j] = l > 0.f ? e : 0.f;
+          if (l > 0.f) L = __fadd_rn(L, __fmul_rn(e, l));
+        }
+        for (int j = ns; j < kMaxSplit; ++j) cw[h * kMaxSplit + j] = 0.f;
+        cml[2 * h] = L;
+        // splits with l_j = 0 take no part (flag in the sign of a second copy)
+        int mask = 0;
+        for (int j = 0; j < ns; ++j) mask |= (__ldcg(ml + 2 * j + 1) > 0.f) << j;
+        cml[2 * h + 1] = __int_as_float(mask);
+      }
+    }
+    named_barrier(kBarCons, kConsThreads);
+#pragma unroll
+    for (int j = 0; j < kNV; ++j) {
+      const int f = tid + j * kConsThreads;
+      float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (f < f4) {
+        const int e0 = 4 * f;
+        const int h = e0 / a.HD, d = e0 - h * a.HD;
+        const int mask = __float_as_int(cml[2 * h + 1]);
+        float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+        for (int s = 0; s < ns; ++s) {
+          if (!((mask >> s) & 1)) continue;
+          const float wgt = cw[h * kMaxSplit + s];
+          const float4 o = ldcg4(a.part_o + ((size_t)h * ns + s) * a.HD + d);
+          o0 = __fadd_rn(o0, __fmul_rn(wgt, o.x));
+          o1 = __fadd_rn(o1, __fmul_rn(wgt, o.y));
+          o2 = __fadd_rn(o2, __fmul_rn(wgt, o.z));
+          o3 = __fadd_rn(o3, __fmul_rn(wgt, o.w));
+        }
+        const float L = cml[2 * h];
+        r = make_float4(__fdiv_rn(o0, L), __fdiv_rn(o1, L), __fdiv_rn(o2, L), __fdiv_rn(o3, L));
+      }
+      v[j] = r;
+    }
+  } else if (st.pro == PRO_SWIGLU) {
+#pragma unroll
+    for (int j = 0; j < kNV; ++j) {
+      const int f = tid + j * kConsThreads;
+      float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (f < f4) {
+        const float4 g = ldcg4(st.a + 4 * f), u = ldcg4(st.b + 4 * f);
+        const float gv[4] = {g.x, g.y, g.z, g.w}, uv[4] = {u.x, u.y, u.z, u.w};
+        float o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gv[e])));
+          o[e] = __fmul_rn(__fmul_rn(gv[e], sig), uv[e]);
+        }
+        r = make_float4(o[0], o[1], o[2], o[3]);
+      }
+      v[j] = r;
+    }
+  } else {
+    // RMSNorm of (embedding row) or (a + b); the sum is the residual stream
+    const bool emb = st.pro == PRO_EMB_RMS;
+    const float* erow = a.emb + (size_t)tok * K;
+    const bool tok_ok = tok >= 0 && tok < a.vocab;
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < kNV; ++j) {
+      const int f = tid + j * kConsThreads;
+      float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (f < f4) {
+        if (emb) {
+          if (tok_ok) r = __ldg(reinterpret_cast<const float4*>(erow) + f);
+        } else {
+          const float4 x0 = ldcg4(st.a + 4 * f), x1 = ldcg4(st.b + 4 * f);
+          r = make_float4(__fadd_rn(x0.x, x1.x), __fadd_rn(x0.y, x1.y), __fadd_rn(x0.z, x1.z),
+                          __fadd_rn(x0.w, x1.w));
+        }
+        if (cid == 0 && st.res_out) {
+          reinterpret_cast<float4*>(st.res_out)[f] = r;
+          __threadfence();
+        }
+        ss = __fadd_rn(ss, __fadd_rn(__fadd_rn(__fmul_rn(r.x, r.x), __fmul_rn(r.y, r.y)),
+                                     __fadd_rn(__fmul_rn(r.z, r.z), __fmul_rn(r.w, r.w))));
+      }
+      v[j] = r;
+    }
+    ss = cons_sum(ss, red);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
+#pragma unroll
+    for (int j = 0; j < kNV; ++j) {
+      const int f = tid + j * kConsThreads;
+      if (f < f4) {
+        const float4 w = __ldg(reinterpret_cast<const float4*>(st.w) + f);
+        v[j] = make_float4(__fmul_rn(__fmul_rn(v[j].x, inv), w.x), __fmul_rn(__fmul_rn(v[j].y, inv), w.y),
+                           __fmul_rn(__fmul_rn(v[j].z, inv), w.z), __fmul_rn(__fmul_rn(v[j].w, inv), w.w));
+      }
+    }
+  }
+  // max |x|, then the digits (as q4g_gemv_kernel, M = 1)
+  float mx = 0.f;
+#pragma unroll
+  for (int j = 0; j < kNV; ++j)
+    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
+  mx = cons_max(mx, red);
+  if (tid == 0) *xmaxp = mx;
+  const float inv = mx > 0.f ? 127.0f / mx : 0.f;
+#pragma unroll
+  for (int j = 0; j < kNV; ++j) {
+    const int f = tid + j * kConsThreads;
+    const float xv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+    uint32_t w0 = 0, w1 = 0;
+    int s0 = 0, s1 = 0;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const float q = xv[b] * inv;
+      const int d0 = max(-127, min(127, __float2int_rn(q)));
+      const int d1 = max(-127, min(127, __float2int_rn((q - (float)d0) * 256.0f)));
+      w0 |= (uint32_t)(d0 & 0xFF) << (8 * b);
+      w1 |= (uint32_t)(d1 & 0xFF) << (8 * b);
+      s0 += d0;
+      s1 += d1;
+    }
+    if (f < f4) {
+      const int kt32 = f >> 3, jj = f & 7;
+      const int half = jj >> 2, tt = jj & 3;
+      xw[(((size_t)kt32 * 2 + 0) * 4 + tt) * 2 + half] = w0;
+      xw[(((size_t)kt32 * 2 + 1) * 4 + tt) * 2 + half] = w1;
+    }
+    // a warp's 32 float4 are one group of 128 k (512 | 32 | f4 boundaries)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+      s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+    }
+    if (lane == 0 && f < f4) {
+      const int grp = f >> 5;
+      sdi[grp * 16] += s0;       // one writer per group
+      sdi[grp * 16 + 8] += s1;
+    }
+  }
+  named_barrier(kBarCons, kConsThreads);
+}
+
+// ------------------------------------------------------------ attention unit
+// Query head h, positions [s0, s1) of split j (attn_split_kernel's arithmetic,
+// with 16 warps): RoPE (rotate-half) on q and the new k, q scaled, KV append
+// of row pos, scores, max, exp-sum, unnormalised P.V.
+template <int DV>
+__device__ void attn_unit(const DecArgs& a, const DecStage& st, int h, int j, int pos,
+                          unsigned char* smem) {
+  constexpr int HD = 32 * DV;
+  constexpr int half = HD / 2;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  float* red = reinterpret_cast<float*>(smem + kOffRed);
+  float* qs = reinterpret_cast<float*>(smem + kOffXs);
+  float* kn = qs + kMaxHeadDim;
+  float* vn = kn + kMaxHeadDim;
+  float* sc = vn + kMaxHeadDim;
+  float* ared = sc + kMaxPs;
+  const int nrep = a.H / a.HKV, hkv = h / nrep;
+  const int S = pos + 1;
+  const int ps = (S + a.nsplit - 1) / a.nsplit;
+  const int s0 = j * ps, s1 = min(S, s0 + ps), ns = max(0, s1 - s0);
+  const bool has_new = ns > 0 && s1 == S;
+  const float* cs = a.cos_t + (size_t)pos * half;
+  const float* sn = a.sin_t + (size_t)pos * half;
+  if (tid < half) {
+    const float c = __ldg(cs + tid), s = __ldg(sn + tid);
+    const float x1 = __ldcg(a.q + (size_t)h * HD + tid), x2 = __ldcg(a.q + (size_t)h * HD + tid + half);
+    qs[tid] = __fmul_rn(__fadd_rn(__fmul_rn(x1, c), __fmul_rn(-x2, s)), a.scale);
+    qs[tid + half] = __fmul_rn(__fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s)), a.scale);
+  } else if (tid >= 128 && tid < 128 + half && has_new) {
+    const int i = tid - 128;
+    const float c = __ldg(cs + i), s = __ldg(sn + i);
+    const float x1 = __ldcg(a.k + (size_t)hkv * HD + i), x2 = __ldcg(a.k + (size_t)hkv * HD + i + half);
+    kn[i] = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(-x2, s));
+    kn[i + half] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+  } else if (tid >= 256 && tid < 256 + HD && has_new) {
+    vn[tid - 256] = __ldcg(a.v + (size_t)hkv * HD + tid - 256);
+  }
+  named_barrier(kBarCons, kConsThreads);
+  if (has_new && h % nrep == 0) {
+    // appendKV: this unit is the only writer of row pos of KV head hkv
+    const size_t row = ((size_t)hkv * a.max_seq + pos) * HD;
+    if (tid < HD) st.kc[row + tid] = kn[tid];
+    else if (tid >= 256 && tid < 256 + HD) st.vc[row + tid - 256] = vn[tid - 256];
+  }
+  const float* K = st.kc + ((size_t)hkv * a.max_seq + s0) * HD;
+  const float* V = st.vc + ((size_t)hkv * a.max_seq + s0) * HD;
+  float ql[DV];
+#pragma unroll
+  for (int i = 0; i < DV; ++i) ql[i] = qs[lane + 32 * i];
+  constexpr int U = 4;
+  for (int b = warp * U; b < ns; b += kCons * U) {
+    float kv[U][DV];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int p = b + u;
+      const bool isnew = s0 + p == pos;
+#pragma unroll
+      for (int i = 0; i < DV; ++i)
+        kv[u][i] = p < ns ? (isnew ? kn[lane + 32 * i] : __ldg(K + (size_t)p * HD + lane + 32 * i)) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      float acc = 0.f;
+#pragma unroll
+      for (int i = 0; i < DV; ++i) acc = __fadd_rn(acc, __fmul_rn(ql[i], kv[u][i]));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (lane == 0 && b + u < ns) sc[b + u] = acc;
+    }
+  }
+  named_barrier(kBarCons, kConsThreads);
+  float mx = -INFINITY;
+  for (int s = tid; s < ns; s += kConsThreads) mx = fmaxf(mx, sc[s]);
+  mx = cons_max(mx, red);
+  float sum = 0.f;
+  for (int s = tid; s < ns; s += kConsThreads) {
+    const float e = expf(__fsub_rn(sc[s], mx));
+    sc[s] = e;
+    sum = __fadd_rn(sum, e);
+  }
+  sum = cons_sum(sum, red);   // its barriers also publish sc
+  float acc[DV];
+#pragma unroll
+  for (int i = 0; i < DV; ++i) acc[i] = 0.f;
+  for (int b = warp * U; b < ns; b += kCons * U) {
+    float vv[U][DV];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int p = b + u;
+      const bool isnew = s0 + p == pos;
+#pragma unroll
+      for (int i = 0; i < DV; ++i)
+        vv[u][i] = p < ns ? (isnew ? vn[lane + 32 * i] : __ldg(V + (size_t)p * HD + lane + 32 * i)) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (b + u < ns) {
+        const float e = sc[b + u];
+#pragma unroll
+        for (int i = 0; i < DV; ++i) acc[i] = __fadd_rn(acc[i], __fmul_rn(e, vv[u][i]));
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < DV; ++i) ared[warp * HD + lane + 32 * i] = acc[i];
+  named_barrier(kBarCons, kConsThreads);
+  float* po = a.part_o + ((size_t)h * a.nsplit + j) * HD;
+  for (int d = tid; d < HD; d += kConsThreads) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < kCons; ++w) t = __fadd_rn(t, ared[w * HD + d]);
+    po[d] = t;
+  }
+  if (tid == 0) {
+    a.part_ml[((size_t)h * a.nsplit + j) * 2] = mx;
+    a.part_ml[((size_t)h * a.nsplit + j) * 2 + 1] = sum;
+  }
+  __threadfence();                        // partials and KV row visible before the arrival
+  named_barrier(kBarCons, kConsThreads);  // scratch reused by the next unit
+}
+
+// ------------------------------------------------------------ the kernel
+__global__ void __maxnreg__(112) decode_step_kernel(const DecArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int cid = blockIdx.x, G = gridDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* empty = full + kNS;
+  uint64_t* merged = empty + kNS;
+  uint64_t* pfull = merged + kNS;
+  unsigned char* ring = smem + kOffRing;
+  float* part = reinterpret_cast<float*>(smem + kOffPart);
+  int* rec = reinterpret_cast<int*>(smem + kOffRecent);
+  const unsigned epoch = __ldcg(a.ctl);          // launches completed before this one
+  const unsigned target = (epoch + 1u) * (unsigned)G;
+  const int pos = *(volatile const int*)a.pos;
+  const int tok = *(volatile const int*)a.tok_in;
+  const int nst = a.nstages;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kNS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kNcs);
+      mbar_init(&merged[s], 1);
+      mbar_init(&pfull[s], kNcs);
+    }
+    mbar_fence_init();
+  }
+  if (threadIdx.x < 8) reinterpret_cast<unsigned*>(smem + kOffZpad)[threadIdx.x] = 0u;
+  for (int i = threadIdx.x; i < a.n_recent; i += blockDim.x) rec[i] = __ldg(a.recent + i);
+  __syncthreads();
+
+  if (warp == kCons) {
+    // ---------------- producer: the weights of every GEMV stage, in order
+    if (lane < kIssuers) {
+      bool ok = true;
+      int q0 = 0, issued_last = -1;
+      for (int s = 0; s < nst && ok; ++s) {
+        const DecStage& st = a.stages[s];
+        if (__ldg(&st.kind) != ST_GEMV) continue;
+        int rt0, nrt;
+        row_split(__ldg(&st.n_rt), cid, G, &rt0, &nrt);
+        const int nkb = __ldg(&st.nkb), groups = __ldg(&st.groups);
+        const int nstg = nrt * nkb;
+        const int first = ((lane - q0) % kIssuers + kIssuers) % kIssuers;
+        for (int i = first; i < nstg; i += kIssuers) {
+          const int qq = q0 + i;
+          const int slot = qq % kNS;
+          if (qq >= kNS && !dwait<-32>(a, &empty[slot], ((qq / kNS) - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          const int rti = i / nkb, kb = i - rti * nkb;
+          const int grt = rt0 + rti;
+          const int p = prob_of(st, grt);
+          const int rt = grt - __ldg(&st.rt_prefix[p]);
+          const int ngk = min(kKbg, groups - kb * kKbg);
+          const uint32_t wb = (uint32_t)ngk * kKQG * 512u, zb = (uint32_t)ngk * 128u;
+          unsigned char* dst = ring + (size_t)slot * kStageBytes;
+          const uint4* fr = reinterpret_cast<const uint4*>(__ldg(reinterpret_cast<const unsigned long long*>(&st.frag[p])));
+          const float4* sz = reinterpret_cast<const float4*>(__ldg(reinterpret_cast<const unsigned long long*>(&st.sz[p])));
+          mbar_arrive_expect_tx(&full[slot], wb + zb);
+          bulk_g2s(dst, fr + ((size_t)rt * groups * kKQG + (size_t)kb * kKbg * kKQG) * 32, wb, &full[slot]);
+          bulk_g2s(dst + kStageW, sz + ((size_t)rt * groups + (size_t)kb * kKbg) * 8, zb, &full[slot]);
+          issued_last = qq;
+        }
+        q0 += nstg;
+      }
+      if (ok) {
+        for (int q = issued_last; q >= 0 && q > issued_last - kNS; q -= kIssuers)
+          if (!dwait<-32>(a, &full[q % kNS], (q / kNS) & 1)) ok = false;
+      }
+      if (!ok && a.err) atomicExch(a.err, 1);
+    }
+    __syncwarp();
+  } else if (warp == kCons + 1) {
+    // ---------------- merge warp: chunk partials -> y, stage arrivals, argmax
+    uint32_t* mark = reinterpret_cast<uint32_t*>(smem + kOffMark);
+    int q0 = 0;
+    for (int s = 0; s < nst; ++s) {
+      const DecStage& st = a.stages[s];
+      if (st.kind != ST_GEMV) continue;
+      int rt0, nrt;
+      row_split(st.n_rt, cid, G, &rt0, &nrt);
+      const int nkb = st.nkb;
+      const int nstg = nrt * nkb;
+      const bool greedy = st.greedy && a.tok_out != nullptr;
+      if (greedy) {
+        // rows of this CTA that the recent list names get the ordered penalty
+        for (int i = lane; i < 128; i += 32) mark[i] = 0u;
+        __syncwarp();
+        for (int i = lane; i < a.n_recent; i += 32) {
+          const int r = rec[i] - rt0 * 16;
+          if (r >= 0 && r < nrt * 16 && r < 4096) atomicOr(&mark[r >> 5], 1u << (r & 31));
+        }
+        __syncwarp();
+      }
+      float bestv = -INFINITY;
+      int besti = -1, nan0 = 0;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int i = 0; i < nstg; ++i) {
+        const int qq = q0 + i;
+        const int slot = qq % kNS;
+        const int kb = i % nkb;
+        if (!dwait<1000>(a, &pfull[slot], (qq / kNS) & 1)) {
+          if (lane == 0 && a.err) atomicExch(a.err, 1);
+          break;
+        }
+        const float* rd = part + (size_t)slot * kNcs * 128;
+        if (kb == 0) v = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int c2 = 0; c2 < kNcs; ++c2) {
+          const float4 e4 = reinterpret_cast<const float4*>(rd + c2 * 128)[lane];
+          v.x += e4.x;
+          v.y += e4.y;
+          v.z += e4.z;
+          v.w += e4.w;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&merged[slot]);
+        if (kb != nkb - 1) continue;
+        // columns 4..7 hold the second digit's part of x row 0
+        const float yv = v.x + __shfl_xor_sync(0xffffffffu, v.x, 1);
+        const int grt = rt0 + i / nkb;
+        const int p = prob_of(st, grt);
+        const int r = (grt - st.rt_prefix[p]) * 16 + (lane >> 1);
+        if ((lane & 1) == 0 && r < st.rows[p]) {
+          float* yp = st.y[p] ? st.y[p] : a.logits;
+          yp[r] = yv;
+          if (greedy) {
+            float adj = yv;
+            const int lr = r - rt0 * 16;
+            if (lr >= 4096 || ((mark[lr >> 5] >> (lr & 31)) & 1u)) {
+              for (int t = 0; t < a.n_recent; ++t)
+                if (rec[t] == r) adj = adj > 0.0f ? __fdiv_rn(adj, a.penalty) : __fmul_rn(adj, a.penalty);
+            }
+            if (r == 0 && adj != adj) nan0 = 1;
+            if (adj == adj && (besti < 0 || adj > bestv)) {
+              bestv = adj;
+              besti = r;
+            }
+          }
+        }
+      }
+      q0 += nstg;
+      if (greedy) {
+        // warp argmax: larger value, then lower index (rows rise with lanes and tiles)
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, bestv, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, besti, o);
+          if (oi >= 0 && (besti < 0 || ov > bestv || (ov == bestv && oi < besti))) {
+            bestv = ov;
+            besti = oi;
+          }
+        }
+        nan0 = __any_sync(0xffffffffu, nan0);
+        if (lane == 0) {
+          int* cd = a.cand + (size_t)cid * 4;
+          cd[0] = __float_as_int(bestv);
+          cd[1] = besti;
+          cd[2] = nan0;
+        }
+      }
+      __threadfence();   // this lane's y (and argmax) visible before the arrival
+      __syncwarp();
+      if (lane == 0) arrive(a, s);
+    }
+  } else {
+    // ---------------- consumers
+    const int g = lane >> 2, t = lane & 3;
+    const float* xmaxp = reinterpret_cast<const float*>(smem + kOffMisc);
+    const int* sdi = reinterpret_cast<const int*>(smem + kOffSdi);
+    const bool bvalid = (g & 3) == 0;               // x row 0: columns 0 (d0) and 4 (d1)
+    const int ccol = g < 4 ? 0 : 1;
+    const uint2* zpad = reinterpret_cast<const uint2*>(smem + kOffZpad);
+    const uint2* xs2 = bvalid ? reinterpret_cast<const uint2*>(smem + kOffXs) + ccol * 4 + t : zpad;
+    const int xstride = bvalid ? 8 : 0;
+    const int sd_off = t < 2 ? 2 * t : 2 * t + 4;
+    int q0 = 0;
+    for (int s = 0; s < nst; ++s) {
+      const DecStage& st = a.stages[s];
+      if (st.kind == ST_ATTN) {
+        // wait for q/k/v of every CTA, then this CTA's (head, split) units
+        if (threadIdx.x == 0 && s > 0) wait_count(a, a.ctl + 2 + (s - 1), target);
+        named_barrier(kBarCons, kConsThreads);
+        const int units = a.H * a.nsplit;
+        if (pos >= 0 && pos < a.max_seq) {
+          for (int u = cid; u < units; u += G) {
+            const int h = u / a.nsplit, j = u - h * a.nsplit;
+            if (a.HD == 128) attn_unit<4>(a, st, h, j, pos, smem);
+            else attn_unit<2>(a, st, h, j, pos, smem);
+          }
+        } else if (cid == 0 && threadIdx.x == 0 && a.err) {
+          atomicExch(a.err, 4);   // position outside the KV cache: nothing is read or appended
+        }
+        named_barrier(kBarCons, kConsThreads);
+        if (threadIdx.x == 0) arrive(a, s);
+        continue;
+      }
+      int rt0, nrt;
+      row_split(st.n_rt, cid, G, &rt0, &nrt);
+      const int nkb = st.nkb;
+      const int nstg = nrt * nkb;
+      if (threadIdx.x == 0 && s > 0) wait_count(a, a.ctl + 2 + (s - 1), target);
+      named_barrier(kBarCons, kConsThreads);  // also: every warp is done with the last x
+      prologue(a, st, cid, tok, smem);
+      const float sm = *xmaxp / 127.0f;
+      const float dsc = t < 2 ? sm : sm * (1.0f / 256.0f);
+      const int groups = st.groups;
+      const int ubeg = q0 * kNcs, uend = (q0 + nstg) * kNcs;
+      const int u0 = ubeg + ((warp - ubeg) % kCons + kCons) % kCons;
+      for (int u = u0; u < uend; u += kCons) {
+        const int qq = u / kNcs, c = u - qq * kNcs;
+        const int i = qq - q0;
+        const int slot = qq % kNS;
+        const int kb = i % nkb;
+        const int ngk = min(kKbg, groups - kb * kKbg);
+        const int cg0 = c * kCG, ncg = max(0, min(kCG, ngk - cg0));
+        const int gb = kb * kKbg + cg0;  // first group of the chunk
+        float tot[4] = {0.f, 0.f, 0.f, 0.f};
+        if (!dwait<1000>(a, &full[slot], (qq / kNS) & 1)) {
+          if (lane == 0 && a.err) atomicExch(a.err, 1);
+        } else {
+          const unsigned char* stg = ring + (size_t)slot * kStageBytes;
+          const uint4* wq = reinterpret_cast<const uint4*>(stg + (size_t)c * kChunkQ * 512) + lane;
+          const float4* szp = reinterpret_cast<const float4*>(stg + kStageW + (size_t)cg0 * 128) + g;
+          uint4 wr[kChunkQ];
+          float4 sr[kCG];
+#pragma unroll
+          for (int gl = 0; gl < kCG; ++gl) {
+            if (gl < ncg) {
+#pragma unroll
+              for (int qq2 = 0; qq2 < kKQG; ++qq2) wr[gl * kKQG + qq2] = wq[(gl * kKQG + qq2) * 32];
+              sr[gl] = szp[gl * 8];
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[slot]);
+          int acc[kCG][4];
+#pragma unroll
+          for (int gl = 0; gl < kCG; ++gl)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[gl][e] = 0;
+#pragma unroll
+          for (int gl = 0; gl < kCG; ++gl) {
+            if (gl < ncg) {
+#pragma unroll
+              for (int qq2 = 0; qq2 < kKQG; ++qq2) {
+                const int ql = gl * kKQG + qq2;
+                const uint4 w = wr[ql];
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                  const uint32_t wa = hh == 0 ? w.x : w.z, wb = hh == 0 ? w.y : w.w;
+                  const uint32_t a0 = wa & 0x0F0F0F0Fu, a1 = (wa >> 4) & 0x0F0F0F0Fu;
+                  const uint32_t a2 = wb & 0x0F0F0F0Fu, a3 = (wb >> 4) & 0x0F0F0F0Fu;
+                  const int kt32 = (gb * kKQG + ql) * 2 + hh;
+                  const uint2 bfr = xs2[(size_t)kt32 * xstride];
+                  mma_s8_16832(acc[gl], a0, a1, a2, a3, bfr.x, bfr.y);
+                }
+              }
+            }
+          }
+#pragma unroll
+          for (int gl = 0; gl < kCG; ++gl) {
+            if (gl < ncg) {
+              const float4 sp = sr[gl];
+              const float d0 = (float)sdi[(gb + gl) * 16 + sd_off];
+              tot[0] = fmaf(sp.x * dsc, fmaf(-sp.y, d0, (float)acc[gl][0]), tot[0]);
+              tot[2] = fmaf(sp.z * dsc, fmaf(-sp.w, d0, (float)acc[gl][2]), tot[2]);
+            }
+          }
+        }
+        // hand the chunk's partial to the merge warp (slot reused: wait until
+        // the merge warp has read the previous round)
+        float* rd = part + (size_t)slot * kNcs * 128;
+        if (qq >= kNS && !dwait<1000>(a, &merged[slot], ((qq / kNS) - 1) & 1)) {
+          if (lane == 0 && a.err) atomicExch(a.err, 1);
+          continue;
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int r = g + ((e & 2) ? 8 : 0);
+          const int mm = 2 * t + (e & 1);
+          rd[(size_t)c * 128 + r * 8 + mm] = tot[e];
+        }
+        __threadfence_block();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&pfull[slot]);
+      }
+      q0 += nstg;
+    }
+    // CTA 0 picks the next token from the per-CTA argmax results
+    if (cid == 0 && a.tok_out != nullptr && threadIdx.x == 0) {
+      bool ok = wait_count(a, a.ctl + 2 + (nst - 1), target);
+      float bv = -INFINITY;
+      int bi = -1, n0 = 0;
+      for (int c2 = 0; c2 < G && ok; ++c2) {
+        const int* cd = a.cand + (size_t)c2 * 4;
+        const float cv = __int_as_float(__ldcg(cd));
+        const int ci = __ldcg(cd + 1);
+        n0 |= __ldcg(cd + 2);
+        if (ci >= 0 && (bi < 0 || cv > bv || (cv == bv && ci < bi))) {
+          bv = cv;
+          bi = ci;
+        }
+      }
+      *a.tok_out = (n0 || bi < 0) ? 0 : bi;
+    }
+    if (cid == 0 && threadIdx.x == 0 && a.advance_pos) {
+      wait_count(a, a.ctl + 2 + (nst - 1), target);
+      *a.pos = pos + 1;
+    }
+  }
+  __syncthreads();
+  // the last CTA to finish the step counts the launch
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned old = atomicAdd(a.ctl + 2 + nst, 1u);
+    if (old == target - 1u) atomicAdd(a.ctl, 1u);
+  }
+}
+
+// ------------------------------------------------------------ host side
+struct DecodePlan {
+  int device = -1;
+  int grid = 0;
+  std::vector<DecStage> stages;
+  DecStage* d_stages = nullptr;
+  void* scratch = nullptr;
+  DecArgs base = {};
+  int64_t vocab = 0;
+};
+
+std::vector<DecodePlan*> g_plans;
+unsigned long long g_dec_wait_ns = 2000000000ull;
+
+DecodePlan* find_plan(int64_t id) {
+  if (id < 1 || id > (int64_t)g_plans.size()) return nullptr;
+  return g_plans[(size_t)id - 1];
+}
+
+int q4_of(nimf_weight_t h, int64_t k, int64_t rows, const char* what, const Q4GWeight** out) {
+  Weight* w = lookup(h);
+  if (!w) return set_error(NIMF_ERR_STATE, "decode plan: %s: unknown weight handle", what);
+  if (w->kind != NIMF_KIND_INT4_ASYM || !w->q4.fast || w->q4.gs != kGS)
+    return set_error(NIMF_ERR_UNSUPPORTED,
+                     "decode plan: %s must be an int4 asymmetric weight with group size 128", what);
+  if (w->kperm) return set_error(NIMF_ERR_UNSUPPORTED, "decode plan: %s has an act-order permutation", what);
+  if (w->q4.k != k || w->q4.rows != rows)
+    return set_error(NIMF_ERR_SHAPE, "decode plan: %s is [%lld x %lld], expected [%lld x %lld]", what,
+                     (long long)w->q4.rows, (long long)w->q4.k, (long long)rows, (long long)k);
+  *out = &w->q4;
+  return NIMF_OK;
+}
+
+DecStage gemv_stage(int pro, const Q4GWeight* const* ws, float* const* ys, int n, int64_t k) {
+  DecStage s = {};
+  s.kind = ST_GEMV;
+  s.pro = pro;
+  s.k = (int)k;
+  s.groups = (int)(k / kGS);
+  s.nkb = (s.groups + kKbg - 1) / kKbg;
+  s.nprob = n;
+  s.rt_prefix[0] = 0;
+  for (int i = 0; i < n; ++i) {
+    s.frag[i] = (const uint4*)ws[i]->frag;
+    s.sz[i] = (const float4*)ws[i]->sz;
+    s.y[i] = ys[i];
+    s.rows[i] = (int)ws[i]->rows;
+    s.rt_prefix[i + 1] = s.rt_prefix[i] + (int)ws[i]->n_rt;
+  }
+  s.n_rt = s.rt_prefix[n];
+  return s;
+}
+
+}  // namespace
+
+void release_decode_plans() {
+  for (DecodePlan*& p : g_plans) {
+    if (!p) continue;
+    device_free(p->d_stages);
+    device_free(p->scratch);
+    delete p;
+    p = nullptr;
+  }
+  g_plans.clear();
+}
+
+}  // namespace nimf
+
+using namespace nimf;
+
+extern "C" {
+
+int nimf_decode_create(const nimf_decode_desc* d, int64_t* plan_out) {
+  Context* c;
+  NIMF_TRY(require_ctx(&c));
+  if (!d || !plan_out || !d->layers) return set_error(NIMF_ERR_ARG, "decode_create: NULL argument");
+  const int64_t L = d->n_layers, D = d->d_model, H = d->n_heads, HKV = d->n_kv_heads,
+                HD = d->head_dim, F = d->ffn_dim, V = d->vocab, MS = d->max_seq;
+  if (L < 1 || D < kGS || D % kGS || F % kGS || D > kMaxK || F > kMaxK || V < 1 || H < 1 ||
+      H > kMaxHeads || HKV < 1 || H % HKV || (HD != 64 && HD != 128) || H * HD != D || MS < 1)
+    return set_error(NIMF_ERR_SHAPE,
+                     "decode_create: unsupported shape (layers %lld, d_model %lld, heads %lld/%lld, "
+                     "head_dim %lld, ffn %lld, vocab %lld, max_seq %lld); needs d_model and ffn "
+                     "multiples of 128 up to %d, head_dim 64 or 128, heads x head_dim = d_model",
+                     (long long)L, (long long)D, (long long)H, (long long)HKV, (long long)HD,
+                     (long long)F, (long long)V, (long long)MS, kMaxK);
+  if (d->n_recent_max < 0 || d->n_recent_max > kMaxRecent)
+    return set_error(NIMF_ERR_SHAPE, "decode_create: n_recent_max %lld not in [0, %d]",
+                     (long long)d->n_recent_max, kMaxRecent);
+  if (!d->embedding || !d->final_norm || !d->rope_cos || !d->rope_sin)
+    return set_error(NIMF_ERR_ARG, "decode_create: NULL model array");
+  const int64_t KVD = HKV * HD;
+  // grid: one CTA per SM, at most the row tiles of the smallest GEMV stage
+  // (so every CTA takes part in every stage)
+  // (n_rt of q/k/v, o, gate/up, down and lm_head)
+  int64_t min_rt = std::min<int64_t>((D + 15) / 16 + 2 * ((KVD + 15) / 16), (D + 15) / 16);
+  min_rt = std::min<int64_t>(min_rt, 2 * ((F + 15) / 16));
+  min_rt = std::min<int64_t>(min_rt, (V + 15) / 16);
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(c->num_sms, min_rt));
+  int nsplit = std::max(1, std::min(kMaxSplit, grid / (int)H));
+  while (nsplit < kMaxSplit && (MS + nsplit - 1) / nsplit > kMaxPs) ++nsplit;
+  if ((MS + nsplit - 1) / nsplit > kMaxPs)
+    return set_error(NIMF_ERR_SHAPE, "decode_create: max_seq %lld too long", (long long)MS);
+
+  DecodePlan* P = new DecodePlan();
+  P->device = c->device;
+  P->grid = grid;
+  P->vocab = V;
+  // scratch: q, k, v, attention partials, o out, gate, up, down out, two
+  // residual rows, per-CTA argmax, control words
+  const int nst = (int)(5 * L + 1);
+  size_t off = 0;
+  auto take = [&](size_t bytes) { size_t o = off; off += (bytes + 255) / 256 * 256; return o; };
+  const size_t o_q = take(D * 4), o_k = take(KVD * 4), o_v = take(KVD * 4);
+  const size_t o_po = take((size_t)H * nsplit * HD * 4), o_pml = take((size_t)H * nsplit * 2 * 4);
+  const size_t o_ao = take(D * 4), o_g = take(F * 4), o_u = take(F * 4), o_dn = take(D * 4);
+  const size_t o_xr = take(D * 4), o_hr = take(D * 4);
+  const size_t o_cand = take((size_t)grid * 4 * 4);
+  const size_t o_ctl = take((size_t)(nst + 3) * 4);
+  int rc = device_alloc(&P->scratch, off);
+  if (rc != NIMF_OK) {
+    delete P;
+    return rc;
+  }
+  char* sb = (char*)P->scratch;
+  float *bq = (float*)(sb + o_q), *bk = (float*)(sb + o_k), *bv = (float*)(sb + o_v);
+  float *bao = (float*)(sb + o_ao), *bg = (float*)(sb + o_g), *bu = (float*)(sb + o_u);
+  float *bdn = (float*)(sb + o_dn), *bxr = (float*)(sb + o_xr), *bhr = (float*)(sb + o_hr);
+  auto fail = [&](int code) {
+    device_free(P->scratch);
+    delete P;
+    return code;
+  };
+  for (int64_t l = 0; l < L; ++l) {
+    const nimf_decode_layer_desc& ld = d->layers[l];
+    const Q4GWeight *wq, *wk, *wv, *wo, *wg, *wu, *wd;
+    int r;
+    if ((r = q4_of(ld.wq, D, D, "wq", &wq)) || (r = q4_of(ld.wk, D, KVD, "wk", &wk)) ||
+        (r = q4_of(ld.wv, D, KVD, "wv", &wv)) || (r = q4_of(ld.wo, D, D, "wo", &wo)) ||
+        (r = q4_of(ld.wgate, D, F, "wgate", &wg)) || (r = q4_of(ld.wup, D, F, "wup", &wu)) ||
+        (r = q4_of(ld.wdown, F, D, "wdown", &wd)))
+      return fail(r);
+    if (!ld.attn_norm || !ld.ffn_norm || !ld.k_cache || !ld.v_cache)
+      return fail(set_error(NIMF_ERR_ARG, "decode_create: layer %lld has a NULL array", (long long)l));
+    {
+      const Q4GWeight* ws[3] = {wq, wk, wv};
+      float* ys[3] = {bq, bk, bv};
+      DecStage s = gemv_stage(l == 0 ? PRO_EMB_RMS : PRO_ADD_RMS, ws, ys, 3, D);
+      s.a = bhr;
+      s.b = bdn;
+      s.w = ld.attn_norm;
+      s.res_out = bxr;
+      P->stages.push_back(s);
+    }
+    {
+      DecStage s = {};
+      s.kind = ST_ATTN;
+      s.kc = ld.k_cache;
+      s.vc = ld.v_cache;
+      P->stages.push_back(s);
+    }
+    {
+      const Q4GWeight* ws[1] = {wo};
+      float* ys[1] = {bao};
+      P->stages.push_back(gemv_stage(PRO_COMBINE, ws, ys, 1, D));
+    }
+    {
+      const Q4GWeight* ws[2] = {wg, wu};
+      float* ys[2] = {bg, bu};
+      DecStage s = gemv_stage(PRO_ADD_RMS, ws, ys, 2, D);
+      s.a = bxr;
+      s.b = bao;
+      s.w = ld.ffn_norm;
+      s.res_out = bhr;
+      P->stages.push_back(s);
+    }
+    {
+      const Q4GWeight* ws[1] = {wd};
+      float* ys[1] = {bdn};
+      DecStage s = gemv_stage(PRO_SWIGLU, ws, ys, 1, F);
+      s.a = bg;
+      s.b = bu;
+      P->stages.push_back(s);
+    }
+  }
+  {
+    const Q4GWeight* wh;
+    int r = q4_of(d->lm_head, D, V, "lm_head", &wh);
+    if (r) return fail(r);
+    float* ys[1] = {nullptr};  // the launch's logits buffer
+    DecStage s = gemv_stage(PRO_ADD_RMS, &wh, ys, 1, D);
+    s.a = bhr;
+    s.b = bdn;
+    s.w = d->final_norm;
+    s.res_out = bxr;
+    s.greedy = 1;
+    P->stages.push_back(s);
+  }
+  int rc2 = device_alloc((void**)&P->d_stages, P->stages.size() * sizeof(DecStage));
+  if (rc2) return fail(rc2);
+  cudaError_t e = cudaMemcpy(P->d_stages, P->stages.data(), P->stages.size() * sizeof(DecStage),
+                             cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemset(sb + o_ctl, 0, (size_t)(nst + 3) * 4);
+  if (e == cudaSuccess) e = cudaMemset(P->scratch, 0, off);
+  if (e != cudaSuccess) {
+    device_free(P->d_stages);
+    return fail(set_error(NIMF_ERR_CUDA, "decode_create: %s", cudaGetErrorString(e)));
+  }
+  DecArgs& A = P->base;
+  A.stages = P->d_stages;
+  A.nstages = (int)P->stages.size();
+  A.D = (int)D;
+  A.H = (int)H;
+  A.HKV = (int)HKV;
+  A.HD = (int)HD;
+  A.max_seq = (int)MS;
+  A.nsplit = nsplit;
+  A.vocab = (int)V;
+  A.eps = d->norm_eps;
+  A.scale = 1.0f / sqrtf((float)HD);
+  A.emb = d->embedding;
+  A.cos_t = d->rope_cos;
+  A.sin_t = d->rope_sin;
+  A.q = bq;
+  A.k = bk;
+  A.v = bv;
+  A.part_o = (float*)(sb + o_po);
+  A.part_ml = (float*)(sb + o_pml);
+  A.cand = (int*)(sb + o_cand);
+  A.ctl = (unsigned*)(sb + o_ctl);
+  NIMF_CUDA_TRY(cudaFuncSetAttribute(decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemBytes));
+  int per_sm = 0;
+  NIMF_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_step_kernel, kThreads,
+                                                              kSmemBytes));
+  if (per_sm < 1) {
+    device_free(P->d_stages);
+    return fail(set_error(NIMF_ERR_UNSUPPORTED, "decode_create: the step kernel does not fit an SM"));
+  }
+  g_plans.push_back(P);
+  *plan_out = (int64_t)g_plans.size();
+  return NIMF_OK;
+}
+
+int nimf_decode_step_dev(int64_t plan, int32_t* token_dev, int32_t* next_token_dev,
+                         int32_t* pos_dev, int advance_pos, const int32_t* recent_dev,
+                         int64_t n_recent, float penalty, float* logits_dev, void* stream) {
+  Context* c;
+  NIMF_TRY(require_ctx(&c));
+  DecodePlan* P = find_plan(plan);
+  if (!P) return set_error(NIMF_ERR_STATE, "decode_step: unknown plan %lld", (long long)plan);
+  if (P->device != c->device)
+    return set_error(NIMF_ERR_STATE, "decode_step: plan of device %d used on %d", P->device, c->device);
+  if (!token_dev || !pos_dev || !logits_dev)
+    return set_error(NIMF_ERR_ARG, "decode_step: NULL token, position or logits buffer");
+  if (n_recent < 0 || n_recent > kMaxRecent || (n_recent > 0 && !recent_dev))
+    return set_error(NIMF_ERR_SHAPE, "decode_step: %lld recent ids (at most %d)", (long long)n_recent,
+                     kMaxRecent);
+  DecArgs A = P->base;
+  A.logits = logits_dev;
+  A.tok_in = token_dev;
+  A.tok_out = next_token_dev;
+  A.pos = pos_dev;
+  A.advance_pos = advance_pos ? 1 : 0;
+  A.recent = recent_dev;
+  A.n_recent = (int)n_recent;
+  A.penalty = penalty;
+  A.err = c->dev_err;
+  A.wait_ns = g_dec_wait_ns;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)P->grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream ? (cudaStream_t)stream : c->stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeCooperative;
+  at[0].val.cooperative = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  NIMF_CUDA_TRY(cudaLaunchKernelEx(&cfg, decode_step_kernel, A));
+  return NIMF_OK;
+}
+
+int nimf_decode_info(int64_t plan, int64_t* grid, int64_t* stages, int64_t* attn_splits) {
+  DecodePlan* P = find_plan(plan);
+  if (!P) return set_error(NIMF_ERR_STATE, "decode_info: unknown plan %lld", (long long)plan);
+  if (grid) *grid = P->grid;
+  if (stages) *stages = (int64_t)P->stages.size();
+  if (attn_splits) *attn_splits = P->base.nsplit;
+  return NIMF_OK;
+}
+
+int nimf_decode_set_timeout_ms(int64_t ms) {
+  if (ms < 1 || ms > 600000)
+    return set_error(NIMF_ERR_ARG, "decode_set_timeout_ms: %lld not in [1, 600000]", (long long)ms);
+  g_dec_wait_ns = (unsigned long long)ms * 1000000ull;
+  return NIMF_OK;
+}
+
+int nimf_decode_destroy(int64_t plan) {
+  DecodePlan* P = find_plan(plan);
+  if (!P) return set_error(NIMF_ERR_STATE, "decode_destroy: unknown plan %lld", (long long)plan);
+  cudaDeviceSynchronize();
+  device_free(P->d_stages);
+  device_free(P->scratch);
+  delete P;
+  g_plans[(size_t)plan - 1] = nullptr;
+  return NIMF_OK;
+}
+
+}  // extern "C"

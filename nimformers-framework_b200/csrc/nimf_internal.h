@@ -199,6 +199,7 @@ int gather_cols(const float* x, int64_t m, int64_t k, const int32_t* perm, const
                 cudaStream_t st);
 void release_perm_buffer();
 void release_attn_buffer();  // glue.cu: decode attention's split partials
+void release_decode_plans(); // decode.cu: whole-step plans
 void release_p2p_groups();   // p2p.cu: IPC buffers and peer mappings of the all-gather groups
 
 int fp4_gemv(const FP4Weight& w, const float* x, int64_t m, float* y, cudaStream_t st);

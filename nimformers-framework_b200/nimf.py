@@ -51,6 +51,8 @@ EXPORTS = [
     "nimf_attention_decode_dev", "nimf_embedding_lookup_dev", "nimf_greedy_sample_dev",
     "nimf_p2p_create", "nimf_p2p_connect", "nimf_p2p_allgather_dev", "nimf_p2p_destroy",
     "nimf_p2p_set_timeout_ms",
+    "nimf_decode_create", "nimf_decode_step_dev", "nimf_decode_info", "nimf_decode_set_timeout_ms",
+    "nimf_decode_destroy",
 ]
 
 
@@ -123,6 +125,11 @@ def lib():
         "nimf_p2p_allgather_dev": [i64, vp, i64, i64, i64, vp, i64, vp],
         "nimf_p2p_destroy": [i64],
         "nimf_p2p_set_timeout_ms": [i64],
+        "nimf_decode_create": [ctypes.POINTER(DecodeDesc), ctypes.POINTER(i64)],
+        "nimf_decode_step_dev": [i64, vp, vp, vp, i32, vp, i64, ctypes.c_float, vp, vp],
+        "nimf_decode_info": [i64, ctypes.POINTER(i64), ctypes.POINTER(i64), ctypes.POINTER(i64)],
+        "nimf_decode_set_timeout_ms": [i64],
+        "nimf_decode_destroy": [i64],
         "nimf_greedy_sample_dev": [vp, i64, i64, vp, i64, ctypes.c_float, vp, vp],
         "nimf_add_dev": [vp, vp, i64, vp, vp],
         "nimf_add_rmsnorm_dev": [vp, vp, vp, i64, i64, ctypes.c_float, vp, vp, vp],
@@ -139,6 +146,70 @@ def lib():
     L.nimf_last_error.restype = ctypes.c_char_p
     _lib = L
     return L
+
+
+class DecodeLayerDesc(ctypes.Structure):
+    """nimf_decode_layer_desc: one layer's weights (handles), norms and caches."""
+    _fields_ = [("wq", ctypes.c_uint64), ("wk", ctypes.c_uint64), ("wv", ctypes.c_uint64),
+                ("wo", ctypes.c_uint64), ("wgate", ctypes.c_uint64), ("wup", ctypes.c_uint64),
+                ("wdown", ctypes.c_uint64), ("attn_norm", ctypes.c_void_p),
+                ("ffn_norm", ctypes.c_void_p), ("k_cache", ctypes.c_void_p),
+                ("v_cache", ctypes.c_void_p)]
+
+
+class DecodeDesc(ctypes.Structure):
+    """nimf_decode_desc: the stack's shape and its model-wide arrays."""
+    _fields_ = [("n_layers", ctypes.c_int64), ("d_model", ctypes.c_int64),
+                ("n_heads", ctypes.c_int64), ("n_kv_heads", ctypes.c_int64),
+                ("head_dim", ctypes.c_int64), ("ffn_dim", ctypes.c_int64),
+                ("vocab", ctypes.c_int64), ("max_seq", ctypes.c_int64),
+                ("n_recent_max", ctypes.c_int64), ("norm_eps", ctypes.c_float),
+                ("embedding", ctypes.c_void_p), ("final_norm", ctypes.c_void_p),
+                ("lm_head", ctypes.c_uint64), ("rope_cos", ctypes.c_void_p),
+                ("rope_sin", ctypes.c_void_p), ("layers", ctypes.POINTER(DecodeLayerDesc))]
+
+
+class DecodePlan:
+    """One whole decode step of a Llama-style int4-g128 stack as one launch
+    (LlamaModelL.forwardStep with isPrefill = false, nim_inference.nim:887-921,
+    plus the greedy branch of sampleTopP).  `layers` is a list of dicts with
+    the keys of DecodeLayerDesc (weights as Weight objects or handles, arrays
+    as device pointers); the other arrays are device pointers too."""
+
+    def __init__(self, *, layers, embedding, final_norm, lm_head, rope_cos, rope_sin, d_model,
+                 n_heads, n_kv_heads, head_dim, ffn_dim, vocab, max_seq, norm_eps=1e-6,
+                 n_recent_max=64):
+        h = lambda w: w.handle if isinstance(w, Weight) else int(w)
+        arr = (DecodeLayerDesc * len(layers))()
+        for i, l in enumerate(layers):
+            arr[i] = DecodeLayerDesc(h(l["wq"]), h(l["wk"]), h(l["wv"]), h(l["wo"]),
+                                     h(l["wgate"]), h(l["wup"]), h(l["wdown"]),
+                                     l["attn_norm"], l["ffn_norm"], l["k_cache"], l["v_cache"])
+        d = DecodeDesc(len(layers), d_model, n_heads, n_kv_heads, head_dim, ffn_dim, vocab, max_seq,
+                       n_recent_max, norm_eps, embedding, final_norm, h(lm_head), rope_cos, rope_sin,
+                       arr)
+        pid = ctypes.c_int64()
+        check(lib().nimf_decode_create(ctypes.byref(d), ctypes.byref(pid)))
+        self.plan = pid.value
+
+    def step(self, token, next_token, pos, logits, recent=None, n_recent=0, penalty=1.0,
+             advance_pos=False, stream=None):
+        """Device pointers (ints); asynchronous on `stream`."""
+        vp = ctypes.c_void_p
+        check(lib().nimf_decode_step_dev(self.plan, vp(token), vp(next_token) if next_token else None,
+                                         vp(pos), 1 if advance_pos else 0,
+                                         vp(recent) if recent else None, n_recent,
+                                         ctypes.c_float(penalty), vp(logits), vp(stream or 0)))
+
+    def info(self):
+        g, s, a = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
+        check(lib().nimf_decode_info(self.plan, ctypes.byref(g), ctypes.byref(s), ctypes.byref(a)))
+        return {"grid": g.value, "stages": s.value, "attn_splits": a.value}
+
+    def destroy(self):
+        if self.plan:
+            check(lib().nimf_decode_destroy(self.plan))
+            self.plan = 0
 
 
 class NimqTensor(ctypes.Structure):

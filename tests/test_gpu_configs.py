@@ -292,3 +292,92 @@ def test_decode_step_7b_two_layers_against_oracle(nimf_gpu, step7b):
         kc, vc, wk, wv = (a.reshape(H, MAX_SEQ, HD) for a in (kc, vc, wk, wv))
         assert np.array_equal(kc[:, :POS], wk[:, :POS]) and np.array_equal(vc[:, :POS], wv[:, :POS])
         assert rel_err(kc[:, POS], wk[:, POS]) <= TOL and rel_err(vc[:, POS], wv[:, POS]) <= TOL
+
+
+def gpu_step_persistent(nimf, s, runs=2):
+    """The same step as ONE launch (nimf_decode_step_dev), `runs` times at the
+    same position; returns the logits, token and caches of every run and the
+    position after a final run with advance_pos."""
+    import torch
+    dev = torch.device("cuda")
+    T = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    ws, plan = [], None
+    try:
+        layers, keep = [], []
+        for li in range(2):
+            hw = {nm: nimf.Weight.q4g(*s["lw"][nm], *s["shapes"][nm], 128) for nm in s["lw"]}
+            ws += list(hw.values())
+            an, fn = T(s["norms"][2 * li]), T(s["norms"][1 + 2 * li])
+            kc, vc = T(s["kc"][li]), T(s["vc"][li])
+            keep += [an, fn, kc, vc]
+            layers.append({"wq": hw["q"], "wk": hw["k"], "wv": hw["v"], "wo": hw["o"],
+                           "wgate": hw["gate"], "wup": hw["up"], "wdown": hw["down"],
+                           "attn_norm": an.data_ptr(), "ffn_norm": fn.data_ptr(),
+                           "k_cache": kc.data_ptr(), "v_cache": vc.data_ptr()})
+        head = nimf.Weight.q4g(*s["head"], V, D, 128)
+        ws.append(head)
+        table, fin = T(s["table"]), T(s["norms"][4])
+        cos_t, sin_t = T(s["cos"]), T(s["sin"])
+        plan = nimf.DecodePlan(layers=layers, embedding=table.data_ptr(), final_norm=fin.data_ptr(),
+                               lm_head=head, rope_cos=cos_t.data_ptr(), rope_sin=sin_t.data_ptr(),
+                               d_model=D, n_heads=H, n_kv_heads=H, head_dim=HD, ffn_dim=F, vocab=V,
+                               max_seq=MAX_SEQ, norm_eps=EPS)
+        info = plan.info()
+        assert info["stages"] == 5 * 2 + 1 and info["grid"] >= 1
+        recent = T(s["recent"])
+        tok_in = T(s["tok"])
+        nxt = torch.full((1,), -1, dtype=torch.int32, device=dev)
+        pos = torch.tensor([POS], dtype=torch.int32, device=dev)
+        logits = torch.empty(V, device=dev)
+        out = []
+        for _ in range(runs):
+            plan.step(tok_in.data_ptr(), nxt.data_ptr(), pos.data_ptr(), logits.data_ptr(),
+                      recent.data_ptr(), 64, PENALTY)
+            torch.cuda.synchronize()
+            nimf.check(nimf.lib().nimf_sync())
+            out.append((logits.cpu().numpy().copy(), int(nxt.item()),
+                        [(keep[4 * li + 2].cpu().numpy(), keep[4 * li + 3].cpu().numpy())
+                         for li in range(2)]))
+        plan.step(tok_in.data_ptr(), None, pos.data_ptr(), logits.data_ptr(), advance_pos=True)
+        torch.cuda.synchronize()
+        nimf.check(nimf.lib().nimf_sync())
+        return out, int(pos.item())
+    finally:
+        if plan is not None:
+            plan.destroy()
+        for w in ws:
+            w.free()
+
+
+def test_decode_step_one_launch_against_oracle(nimf_gpu, step7b):
+    """The whole step as one persistent launch: logits within 1e-3 of the
+    oracle's composition, the same greedy id (unless a near tie), the KV rows
+    appended, and repeated launches at one position bit-identical."""
+    want_logits, want_tok, want_kv = oracle_step(step7b)
+    runs, pos_after = gpu_step_persistent(nimf_gpu, step7b)
+    logits, tok, kv = runs[0]
+    assert rel_err(logits, want_logits) <= TOL
+    adj = penalised(want_logits, step7b["recent"])
+    top2 = np.sort(adj)[-2:]
+    if top2[1] - top2[0] > TOL * np.max(np.abs(want_logits)):
+        assert tok == want_tok
+    else:
+        assert adj[tok] >= top2[1] - TOL * np.max(np.abs(want_logits))
+    for (kc, vc), (wk, wv) in zip(kv, want_kv):
+        kc, vc, wk, wv = (a.reshape(H, MAX_SEQ, HD) for a in (kc, vc, wk, wv))
+        assert np.array_equal(kc[:, :POS], wk[:, :POS]) and np.array_equal(vc[:, :POS], wv[:, :POS])
+        assert rel_err(kc[:, POS], wk[:, POS]) <= TOL and rel_err(vc[:, POS], wv[:, POS]) <= TOL
+    for l2, t2, _ in runs[1:]:
+        assert np.array_equal(l2.view(np.uint32), logits.view(np.uint32)) and t2 == tok
+    assert pos_after == POS + 1
+
+
+def test_decode_step_one_launch_matches_per_op_path(nimf_gpu, step7b):
+    """The one-launch step against the one-launch-per-op path on the GPU: the
+    same arithmetic up to reduction order and x's per-stage digit scale."""
+    logits1, tok1, _ = gpu_step(nimf_gpu, step7b)
+    runs, _ = gpu_step_persistent(nimf_gpu, step7b, runs=1)
+    logits2, tok2, _ = runs[0]
+    assert rel_err(logits2, logits1) <= TOL
+    adj = penalised(logits1, step7b["recent"])
+    assert adj[tok2] >= np.max(adj) - TOL * np.max(np.abs(logits1))
