@@ -111,7 +111,8 @@ def workload_config(world, copies):
             "group_size": GS, "weight_copies": copies,
             "l2": "inputs larger than L2: %d rotating weight copies, %.0f MB per GPU"
                   % (copies, copies * algo_bytes(N_PER_GPU, K, M, GS) / 1e6),
-            "parallelism": ("N-shard x%d + NCCL all-gather" % world) if world > 1 else "single GPU"}
+            "parallelism": ("N-shard x%d, output all-gather fused into the GEMV launch"
+                            % world) if world > 1 else "single GPU"}
 
 
 def cpu_reference_gemv_rate(p, s, z, x, seconds, rows=None):
@@ -591,6 +592,129 @@ def run_decode_7b_full(nimf, torch, steps, warmup, pos=512, max_seq=640, layers=
     return res
 
 
+def lib_comm_init(nimf, rank, world):
+    """The library's own NCCL communicator (nimf_comm_init); rank 0's unique
+    id travels over the process group."""
+    import ctypes
+    import torch.distributed as dist
+    L = nimf.lib()
+    w, r = ctypes.c_int(), ctypes.c_int()
+    nimf.check(L.nimf_comm_info(ctypes.byref(w), ctypes.byref(r)))
+    if w.value == world and world > 1:
+        return                      # already initialised
+    uid = ctypes.create_string_buffer(128)
+    if rank == 0:
+        nimf.check(L.nimf_comm_unique_id(uid))
+    box = [uid.raw]
+    dist.broadcast_object_list(box, src=0)
+    nimf.check(L.nimf_comm_init(world, rank, ctypes.create_string_buffer(box[0], 128)))
+
+
+def run_decode_7b_sharded(nimf, torch, steps, warmup, rank, world, pos=512, max_seq=640,
+                          layers=L7):
+    """tok/s of the whole 7B-shape batch-1 decode step N-sharded over `world`
+    GPUs as one launch per GPU (nimf_decode_create_sharded): rank r holds
+    nimf.shard_rows rows of every projection and lm_head (3.7 GB / world) and
+    the KV caches of heads [r*32/world, (r+1)*32/world); inside the launch
+    every stage's outputs go to every GPU over NVLink with plain peer stores
+    and cross-GPU arrival counters.  Token id in -> greedy token id out, as
+    run_decode_7b_full; step time = max over ranks of CUDA-event time."""
+    import torch.distributed as dist
+    import numpy as np
+    rng = np.random.default_rng(6)
+    H, HD = 32, 128
+    hl = H // world
+
+    def make(n, k):
+        ngr = k // GS
+        p = rng.integers(0, 256, size=n * (k // 2), dtype=np.uint8)
+        sc = rng.uniform(0.002, 0.004, size=n * ngr).astype(np.float32)
+        zp = rng.uniform(6.0, 9.0, size=n * ngr).astype(np.float32)
+        return p, sc, zp
+
+    hq, hg, hd, hh = make(D7, D7), make(F7, D7), make(D7, F7), make(V7, D7)
+    dev = torch.device("cuda")
+    rows = lambda n: nimf.shard_rows(n, world, rank)
+    lws, keep, ws = [], [], []
+    plan = None
+    try:
+        for _ in range(layers):
+            q, k, v, o = [nimf.Weight.q4g(*hq, D7, D7, GS, rows=rows(D7)) for _ in range(4)]
+            gate, up = [nimf.Weight.q4g(*hg, F7, D7, GS, rows=rows(F7)) for _ in range(2)]
+            down = nimf.Weight.q4g(*hd, D7, F7, GS, rows=rows(D7))
+            ws += [q, k, v, o, gate, up, down]
+            n1 = torch.rand(D7, device=dev) + 0.5
+            n2 = torch.rand(D7, device=dev) + 0.5
+            kc = torch.randn(hl * max_seq * HD, device=dev)
+            vc = torch.randn(hl * max_seq * HD, device=dev)
+            keep += [n1, n2, kc, vc]
+            lws.append({"wq": q, "wk": k, "wv": v, "wo": o, "wgate": gate, "wup": up, "wdown": down,
+                        "attn_norm": n1.data_ptr(), "ffn_norm": n2.data_ptr(),
+                        "k_cache": kc.data_ptr(), "v_cache": vc.data_ptr()})
+        head = nimf.Weight.q4g(*hh, V7, D7, GS, rows=rows(V7))
+        ws.append(head)
+        nf = torch.rand(D7, device=dev) + 0.5
+        half = HD // 2
+        inv = 1.0 / np.power(np.float32(10000.0), np.arange(half, dtype=np.float32) / np.float32(half))
+        ang = np.arange(max_seq, dtype=np.float32)[:, None] * inv[None, :].astype(np.float32)
+        cos_t = torch.from_numpy(np.cos(ang).astype(np.float32)).to(dev)
+        sin_t = torch.from_numpy(np.sin(ang).astype(np.float32)).to(dev)
+        table = torch.randn(V7, D7, device=dev) * 0.02
+        recent = torch.from_numpy(np.random.default_rng(7).integers(0, V7, size=64)
+                                  .astype(np.int32)).to(dev)
+        keep += [nf, cos_t, sin_t, table, recent]
+        plan = nimf.DecodePlan(layers=lws, embedding=table.data_ptr(), final_norm=nf.data_ptr(),
+                               lm_head=head, rope_cos=cos_t.data_ptr(), rope_sin=sin_t.data_ptr(),
+                               d_model=D7, n_heads=H, n_kv_heads=H, head_dim=HD, ffn_dim=F7,
+                               vocab=V7, max_seq=max_seq, norm_eps=1e-6, sharded=True)
+        pos_d = torch.tensor([pos], dtype=torch.int32, device=dev)
+        tok = torch.tensor([1234], dtype=torch.int32, device=dev)
+        logits = torch.empty(V7, device=dev)
+        sp = torch.cuda.Stream()
+
+        def one():
+            plan.step(tok.data_ptr(), tok.data_ptr(), pos_d.data_ptr(), logits.data_ptr(),
+                      recent.data_ptr(), 64, 1.3, stream=sp.cuda_stream)
+
+        for _ in range(warmup):
+            one()
+        torch.cuda.synchronize()
+        bad = nimf.lib().nimf_sync() != 0
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(sp):
+            e0.record()
+            for _ in range(steps):
+                one()
+            e1.record()
+        torch.cuda.synchronize()
+        bad = bad or nimf.lib().nimf_sync() != 0
+        ms = e0.elapsed_time(e1) / steps
+        toks = [None] * world
+        dist.all_gather_object(toks, int(tok.item()))
+        t = torch.tensor([ms, float(bad)], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, bad = float(t[0].item()), t[1].item() > 0
+        if bad:
+            raise RuntimeError("a grid-barrier wait of the sharded decode step expired on some rank")
+        info = plan.info()
+    finally:
+        if plan is not None:
+            plan.destroy()
+        for w in ws:
+            w.free()
+    kv_bytes = layers * 2 * H * (pos + 1) * HD * 4
+    return {"one_launch": {"tok_s": 1.0 / (ms * 1e-3), "ms_per_step": ms,
+                           "gb_s": (decode7b_bytes(1) + kv_bytes) / (ms * 1e-3) / 1e9,
+                           "launches_per_step": 1, "plan": info,
+                           "same_token_on_every_rank": len(set(toks)) == 1},
+            "tok_s": 1.0 / (ms * 1e-3), "ms_per_step": ms, "position": pos, "n_gpus": world,
+            "note": ("batch 1, whole decode step as one launch per GPU, N-sharded over %d GPUs "
+                     "(projections by output rows, attention by heads), stage outputs exchanged "
+                     "inside the launch over NVLink peer stores; %d timed steps, max over ranks"
+                     % (world, steps))}
+
+
 def prefill7b_flops(tokens):
     """Multiply-add FLOPs of one 7B layer's projections for `tokens` rows."""
     return 2 * tokens * (4 * D7 * D7 + 3 * F7 * D7)
@@ -909,7 +1033,9 @@ def compact_7b(decode, decode_full, prefill, formats):
                 d[k + "_gb_s"] = r(v.get("gb_s"))
         out["decode_7b"] = d
     if decode_full:
-        d = {}
+        d = {"n_gpus": decode_full.get("n_gpus", 1)}
+        if "error" in decode_full:
+            d["error"] = decode_full["error"][:200]
         for k, v in decode_full.items():
             if isinstance(v, dict) and "tok_s" in v:
                 d[k + "_tok_s"] = r(v["tok_s"])
@@ -945,11 +1071,31 @@ def run_ours(args, rank, world, local_rank):
 
     stream = torch.cuda.Stream()
     y_ptrs = [ys[r].data_ptr() for r in range(R)]
+    import ctypes
+    gid = None
+    if world > 1:
+        # the library's own communicator and a gather buffer shared by every
+        # rank: the GEMV's merge warps store each output into every GPU
+        lib_comm_init(nimf, rank, world)
+        gid_c, base = ctypes.c_int64(), ctypes.c_void_p()
+        nimf.check(nimf.lib().nimf_gather_create(R * M * n_total * 4, ctypes.byref(gid_c),
+                                                 ctypes.byref(base)))
+        gid = gid_c.value
+        g_ptrs = (ctypes.c_void_p * R)(*[base.value + r * M * n_total * 4 for r in range(R)])
+        g_handles = (ctypes.c_uint64 * R)(*[w.handle for w in weights])
 
     def step(st):
-        nimf.Weight.matmul_group_dev(weights, x.data_ptr(), M, y_ptrs, st.cuda_stream)
         if world > 1:
-            dist.all_gather_into_tensor(gathered.view(-1), ys.view(-1))
+            # one launch: GEMVs of the 14 shards with the all-gather fused in
+            nimf.check(nimf.lib().nimf_matmul_w_group_gather_dev(
+                gid, g_handles, R, ctypes.c_void_p(x.data_ptr()), M, g_ptrs,
+                ctypes.c_void_p(st.cuda_stream)))
+        else:
+            nimf.Weight.matmul_group_dev(weights, x.data_ptr(), M, y_ptrs, st.cuda_stream)
+
+    def step_nccl(st):
+        nimf.Weight.matmul_group_dev(weights, x.data_ptr(), M, y_ptrs, st.cuda_stream)
+        dist.all_gather_into_tensor(gathered.view(-1), ys.view(-1))
 
     def step_single(st):
         for r in range(R):
@@ -968,6 +1114,14 @@ def run_ours(args, rank, world, local_rank):
     graph1 = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph1, stream=stream):
         step_single(stream)
+    graph_nccl = None
+    if world > 1:
+        with torch.cuda.stream(stream):
+            step_nccl(stream)
+        torch.cuda.synchronize()
+        graph_nccl = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph_nccl, stream=stream):
+            step_nccl(stream)
     torch.cuda.synchronize()
 
     # correctness spot check of one output against a host computation
@@ -1028,6 +1182,29 @@ def run_ours(args, rank, world, local_rank):
     single = {"value": bytes_step / (ms1 / args.steps * 1e-3) / 1e9, "unit": "GB/s",
               "us_per_gemv": ms1 * 1e3 / (args.steps * R),
               "note": "one launch per GEMV, PDL-chained in a CUDA graph"}
+    nccl_cmp = None
+    if world > 1:
+        # the same step with the grouped GEMV followed by an NCCL all-gather
+        for _ in range(args.warmup):
+            graph_nccl.replay()
+        torch.cuda.synchronize()
+        dist.barrier()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for _ in range(args.steps):
+            graph_nccl.replay()
+        e2.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([s2.elapsed_time(e2)], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms2 = float(t.item()) / args.steps
+        nccl_cmp = {"value": bytes_step / (ms2 * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms2,
+                    "note": "grouped GEMV launch, then an NCCL all_gather_into_tensor of the "
+                            "14 output slices"}
+        bad = torch.tensor([float(nimf.lib().nimf_sync() != 0)], device="cuda")
+        dist.all_reduce(bad, op=dist.ReduceOp.MAX)
+        if bad.item() > 0:
+            raise RuntimeError("bench: a gathering GEMV's arrival wait expired on some rank")
 
     # kernel-level roofline: the grouped GEMV launch (one per step)
     pk, how = peaks()
@@ -1080,6 +1257,11 @@ def run_ours(args, rank, world, local_rank):
 
     graph.reset()
     graph1.reset()
+    if graph_nccl is not None:
+        graph_nccl.reset()
+    if gid is not None:
+        torch.cuda.synchronize()
+        nimf.check(nimf.lib().nimf_gather_destroy(gid))
     decode = None
     if args.decode_steps > 0:
         if world == 1:
@@ -1099,6 +1281,13 @@ def run_ours(args, rank, world, local_rank):
     decode_full = None
     if world == 1 and args.decode_steps > 0:
         decode_full = run_decode_7b_full(nimf, torch, max(5, args.decode_steps // 2), 3)
+    elif args.decode_steps > 0:
+        try:
+            lib_comm_init(nimf, rank, world)
+            decode_full = run_decode_7b_sharded(nimf, torch, max(5, args.decode_steps // 2), 3,
+                                                rank, world)
+        except Exception as e:  # noqa: BLE001
+            decode_full = {"error": "%s: %s" % (type(e).__name__, e)}
     prefill = None
     if world == 1 and args.prefill_steps > 0:
         prefill = run_prefill_7b(nimf, torch, args.prefill_steps, 3)
@@ -1126,6 +1315,10 @@ def run_ours(args, rank, world, local_rank):
             line["cpu_baseline"] = cpu
         line["pct_of_hbm_peak"] = value / world / pk["hbm_gbs"]
         line["single_launch_gb_s"] = single["value"]
+        if nccl_cmp is not None:
+            line["nccl_allgather_gb_s"] = nccl_cmp["value"]
+            line["exchange"] = ("all-gather fused into the GEMV: merge warps store every output "
+                                "into every GPU over NVLink, one arrival per rank per launch")
         line.update(compact_7b(decode, decode_full, prefill, formats))
         print(json.dumps(line), flush=True)
     for wt in weights:

@@ -333,6 +333,22 @@ typedef struct nimf_decode_desc {
 
 /* Builds the step's stage table and its device scratch (a few hundred KB). */
 int nimf_decode_create(const nimf_decode_desc* desc, int64_t* plan);
+/* The same step N-sharded over the communicator's GPUs (nimf_comm_init; no
+ * counterpart in the reference, which has no multi-GPU path).  Collective:
+ * every rank calls it with its own descriptor.  Every weight handle holds
+ * this rank's nimf_shard_range rows of the full weight; the caches hold this
+ * rank's KV heads, [n_kv_heads / world][max_seq][head_dim] (KV heads
+ * [rank * n_kv_heads / world, ...) and the query heads that read them);
+ * n_heads and n_kv_heads must be multiples of world.  Each step computes
+ * this rank's rows of every projection and its heads' attention and stores
+ * them into every rank's plan scratch over NVLink (plain peer stores through
+ * CUDA IPC, no multicast); a stage starts once every rank's last CTA has
+ * raised its arrival on every rank (bounded waits, as the one-GPU step).
+ * logits_dev receives this rank's lm_head rows at their positions of the
+ * full [vocab] vector; next_token_dev receives the same greedy choice on
+ * every rank.  Every rank must make the same sequence of step calls;
+ * nimf_decode_destroy of a sharded plan is collective too. */
+int nimf_decode_create_sharded(const nimf_decode_desc* desc, int64_t* plan);
 /* Enqueues one step on `stream` (NULL: the library stream); asynchronous.
  * token_dev [1] int32: the input token (out-of-range ids embed as zeros);
  * pos_dev [1] int32: its position (the KV row appended; 0 <= pos < max_seq,
@@ -387,6 +403,70 @@ int nimf_p2p_allgather_dev(int64_t group, const float* src, int64_t rows, int64_
                            int64_t ld_src, float* dst, int64_t ld_dst, void* stream);
 int nimf_p2p_set_timeout_ms(int64_t ms);
 int nimf_p2p_destroy(int64_t group);
+/* nimf_p2p_connect_comm: nimf_p2p_connect with the handles exchanged over the
+ * library's communicator (nimf_comm_init) instead of by the host.  Collective:
+ * every rank of the group calls it once, after nimf_p2p_create. */
+int nimf_p2p_connect_comm(int64_t group);
+
+/* ------------------------------------------------- communicator (NCCL) */
+/* north_star's N-sharded weights with an NCCL all-gather of the output
+ * slices, inside the library so that a host binding only this header gets
+ * the sharded path.  The reference has no multi-GPU path (its CUDA device is
+ * fixed at 0, vendor/bybylang/backends/cuda/cuda_driver.nim:183); these calls
+ * replace nothing of it.  One process per GPU.  NCCL is opened at run time
+ * (libnccl.so.2); without it these calls return NIMF_ERR_UNSUPPORTED.
+ *
+ * nimf_comm_unique_id: rank 0 writes 128 bytes that every rank must receive
+ *   out of band (a file, a pipe, the launcher's environment).
+ * nimf_comm_init: after nimf_init, on every rank, with the same id; world
+ *   1 .. 8.  Collective (blocks until every rank has joined).
+ * nimf_comm_info: world and rank (1 and 0 without a communicator).
+ * nimf_comm_allgather_dev: dst[q * bytes .. (q + 1) * bytes) = rank q's src,
+ *   asynchronous on `stream` (NULL: the library stream).
+ * nimf_comm_barrier: blocks until every rank has called it.
+ * nimf_comm_destroy: synchronises and releases the communicator.
+ * nimf_shard_range: rows [*row_begin, *row_end) of an n-row weight that rank
+ *   `rank` of `world` holds -- whole 16-row tiles, sizes within one tile.
+ *   Register each rank's shard with exactly this range (row = output channel,
+ *   nimformer.nim:90).
+ * nimf_matmul_w_allgather_dev: y[m][N] = x[m][K] . W^T on every rank, where
+ *   this rank's handle holds its nimf_shard_range rows of the N-row weight:
+ *   the shard's matmul, an NCCL all-gather of the slices and (unless m == 1
+ *   and the shards are equal) a layout pass.  Collective; asynchronous on
+ *   `stream`.  A call that must grow its gather buffers refuses a capturing
+ *   stream (NIMF_ERR_STATE): run it once before capture. */
+int nimf_comm_unique_id(void* id_out);
+int nimf_comm_init(int world, int rank, const void* id);
+int nimf_comm_info(int* world, int* rank);
+int nimf_comm_allgather_dev(const void* src, int64_t bytes, void* dst, void* stream);
+int nimf_comm_barrier(void);
+int nimf_comm_destroy(void);
+int nimf_shard_range(int64_t n, int world, int rank, int64_t* row_begin, int64_t* row_end);
+int nimf_matmul_w_allgather_dev(nimf_weight_t w, const float* x_dev, int64_t m, float* y_dev,
+                                void* stream);
+/* The all-gather fused into the int4 GEMV (no separate collective):
+ * nimf_gather_create (collective) allocates a buffer of `bytes` on every rank,
+ * shared by CUDA IPC, and returns its local address; outputs of
+ * nimf_matmul_w_group_gather_dev must lie inside it.  That call runs the
+ * grouped GEMV of up to 16 int4 group weights (shards per nimf_shard_range,
+ * the same K, 1 .. 8 rows of x) whose merge warps store every finished output
+ * value into the same place of every rank's buffer with plain peer stores
+ * over NVLink (no multicast); y_devs[i] is where weight i's full output
+ * [m][N_i] starts.  The launch's last CTA raises an arrival on every rank and
+ * waits (bounded: nimf_gather_set_timeout_ms, 2 s by default; expiry is
+ * reported by nimf_sync as NIMF_ERR_TIMEOUT) for every rank's arrival, so
+ * when the call completes in stream order the gathered outputs are in place.
+ * Every rank must make the same sequence of calls on a group, and an output
+ * must not be overwritten by a call while another rank may still read the
+ * previous call's values there (a chain of dependent projections, as in
+ * decode, satisfies this; alternate buffers otherwise).  nimf_gather_destroy
+ * is collective. */
+int nimf_gather_create(int64_t bytes, int64_t* group, void** buffer_dev);
+int nimf_matmul_w_group_gather_dev(int64_t group, const nimf_weight_t* handles, int count,
+                                   const float* x_dev, int64_t m, float* const* y_devs,
+                                   void* stream);
+int nimf_gather_set_timeout_ms(int64_t ms);
+int nimf_gather_destroy(int64_t group);
 
 /* ------------------------------------------------------------ .nimq state dicts */
 

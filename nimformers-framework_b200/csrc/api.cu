@@ -277,6 +277,10 @@ static int matmul_dev(Weight* w, const float* x, int64_t m, float* y, cudaStream
   return set_error(NIMF_ERR_UNSUPPORTED, "weight kind %d has no matmul path", w->kind);
 }
 
+int weight_matmul_dev(Weight* w, const float* x, int64_t m, float* y, cudaStream_t st) {
+  return matmul_dev(w, x, m, y, st);
+}
+
 }  // namespace nimf
 
 using namespace nimf;
@@ -341,6 +345,8 @@ int nimf_shutdown(void) {
   release_prep_buffers();
   release_decode_plans();
   release_p2p_groups();
+  release_comm();
+  release_f32_scratch();
   device_free(g_ctx.stage_in);
   device_free(g_ctx.stage_out);
   if (g_ctx.host_err) cudaFreeHost((void*)g_ctx.host_err);
@@ -384,6 +390,8 @@ int nimf_weight_register_q4g(const uint8_t* wq, const float* scales, const float
   const int64_t bpr = (k + 1) / 2;
   const int64_t rows = row_end - row_begin;
   auto w = std::make_unique<Weight>();
+  w->row_begin = row_begin;
+  w->n_full = n;
   w->kind = NIMF_KIND_INT4_ASYM;
   TempBuffers tmp;
   void *dq = nullptr, *ds = nullptr, *dz = nullptr;
@@ -415,6 +423,8 @@ int nimf_weight_register_i8(const int8_t* q, const float* scales, int64_t n_scal
   if (!scales || ((n * k > 0) && !q)) return set_error(NIMF_ERR_ARG, "NULL weight array");
   const int64_t rows = row_end - row_begin;
   auto w = std::make_unique<Weight>();
+  w->row_begin = row_begin;
+  w->n_full = n;
   w->kind = NIMF_KIND_INT8;
   I8Weight& d = w->i8;
   d.rows = rows;
@@ -454,6 +464,8 @@ int nimf_weight_register_cf(const uint8_t* data, int e, int m, const float* row_
   const int item = (1 + e + m + 7) / 8;
   const int64_t rows = row_end - row_begin;
   auto w = std::make_unique<Weight>();
+  w->row_begin = row_begin;
+  w->n_full = n;
   w->kind = NIMF_KIND_CUSTOM_FLOAT;
   CFWeight& d = w->cf;
   d.rows = rows;
@@ -501,6 +513,8 @@ int nimf_weight_register_fp4(const uint8_t* packed, const uint8_t* block_scales,
   const int64_t rows = row_end - row_begin;
   const int64_t bpr = (k + 1) / 2, nb = (k + 15) / 16;
   auto w = std::make_unique<Weight>();
+  w->row_begin = row_begin;
+  w->n_full = n;
   w->kind = NIMF_KIND_FP4_E2M1;
   FP4Weight& d = w->fp4;
   d.rows = rows;

@@ -75,12 +75,13 @@ constexpr int kNV = (kMaxK / 4 + kConsThreads - 1) / kConsThreads;  // float4 of
 constexpr int kMaxHeads = 64;
 constexpr int kMaxSplit = 8;
 constexpr int kMaxProb = 3;
+constexpr int kMaxRanks = kCommMaxRanks;         // GPUs of a sharded plan
 constexpr int kMaxRecent = 256;
 constexpr int kMaxPs = 4096;                     // positions of one attention unit
 constexpr int kMaxHeadDim = 256;
 constexpr int kBarCons = 1;                      // named barrier of the consumer warps
 // ring slot q % kNS always serves the same 8 consumer warps and producer lane
-static_assert(kNS % kIssuers == 0 && (kNS * kNcs) % kCons == 0, "ring period");
+static_assert(kNS == kIssuers && (kNS * kNcs) % kCons == 0, "ring period: producer lane l owns slot l");
 
 // ---- shared memory
 constexpr int kOffBar = 0;                        // full, empty, merged, pfull [kNS] uint64
@@ -113,6 +114,7 @@ struct DecStage {
   int k, groups, nkb, n_rt, nprob, greedy;
   int rt_prefix[kMaxProb + 1];
   int rows[kMaxProb];
+  int row0[kMaxProb];       // first output row of this rank's shard (0 unsharded)
   const uint4* frag[kMaxProb];
   const float4* sz[kMaxProb];
   float* y[kMaxProb];       // nullptr: the launch's logits buffer
@@ -148,7 +150,28 @@ struct DecArgs {
   unsigned* ctl;            // [0] launches, [1] abort, [2 + s] arrivals at stage s
   int* err;                 // host-mapped error word
   unsigned long long wait_ns;
+  // sharded plans (world > 1): every stage output, attention partial and
+  // argmax candidate is stored into every rank's scratch (rank q's copy of a
+  // local scratch address p is p + peer_off[q] bytes, through CUDA IPC), and
+  // the last CTA of a rank to finish stage s adds 1 to gctl[s] of every rank.
+  int world, rank;
+  int h0, hk0, hloc;        // first query / KV head and query heads of this rank
+  long long peer_off[kMaxRanks];
+  unsigned* gctl;
 };
+
+template <typename T>
+__device__ __forceinline__ T* at_rank(const DecArgs& a, T* p, int q) {
+  return reinterpret_cast<T*>(reinterpret_cast<char*>(p) + a.peer_off[q]);
+}
+__device__ __forceinline__ void red_release_sys(unsigned* p, unsigned v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 
 __device__ __forceinline__ unsigned long long gtimer() {
   unsigned long long t;
@@ -166,10 +189,11 @@ __device__ __forceinline__ float4 ldcg4(const float* p) {
 
 // Waits until *p >= target (wrap-safe); false if the bound ran out or the plan
 // was aborted by an earlier expiry.
+template <bool SYS = false>
 __device__ bool wait_count(const DecArgs& a, const unsigned* p, unsigned target) {
   const unsigned long long t0 = gtimer();
   for (unsigned it = 0;; ++it) {
-    if ((int)(ld_acquire(p) - target) >= 0) {
+    if ((int)((SYS ? ld_acquire_sys(p) : ld_acquire(p)) - target) >= 0) {
       __threadfence();
       return true;
     }
@@ -211,9 +235,30 @@ __device__ bool dwait(const DecArgs& a, uint64_t* m, uint32_t parity) {
   }
 }
 
-__device__ __forceinline__ void arrive(const DecArgs& a, int s) {
+// Arrival of this CTA at the end of stage s.  One GPU: a count per CTA on the
+// stage counter.  Sharded: the CTA's stores to the ranks' scratch were fenced
+// at system scope by the threads that made them; the rank's last CTA at
+// stage s (its local count reaches `target`) then adds 1 to gctl[s] of every
+// rank.
+__device__ __forceinline__ void arrive(const DecArgs& a, int s, unsigned target) {
   __threadfence();
-  atomicAdd(a.ctl + 2 + s, 1u);
+  if (a.world == 1) {
+    atomicAdd(a.ctl + 2 + s, 1u);
+    return;
+  }
+  const unsigned old = atomicAdd(a.ctl + 2 + s, 1u);
+  if (old == target - 1u) {
+    __threadfence_system();
+    for (int q = 0; q < a.world; ++q) red_release_sys(at_rank(a, a.gctl + s, q), 1u);
+  }
+}
+
+// The grid barrier before stage s + 1: every CTA of every rank has finished
+// stage s.
+__device__ __forceinline__ bool stage_wait(const DecArgs& a, int s, unsigned target,
+                                           unsigned gtarget) {
+  if (a.world == 1) return wait_count(a, a.ctl + 2 + s, target);
+  return wait_count<true>(a, a.gctl + s, gtarget);
 }
 
 __device__ __forceinline__ void row_split(int n_rt, int cid, int G, int* rt0, int* nrt) {
@@ -435,7 +480,7 @@ __device__ void attn_unit(const DecArgs& a, const DecStage& st, int h, int j, in
   float* vn = kn + kMaxHeadDim;
   float* sc = vn + kMaxHeadDim;
   float* ared = sc + kMaxPs;
-  const int nrep = a.H / a.HKV, hkv = h / nrep;
+  const int nrep = a.H / a.HKV, hkv = h / nrep, hkl = hkv - a.hk0;
   const int S = pos + 1;
   const int ps = (S + a.nsplit - 1) / a.nsplit;
   const int s0 = j * ps, s1 = min(S, s0 + ps), ns = max(0, s1 - s0);
@@ -459,12 +504,12 @@ __device__ void attn_unit(const DecArgs& a, const DecStage& st, int h, int j, in
   named_barrier(kBarCons, kConsThreads);
   if (has_new && h % nrep == 0) {
     // appendKV: this unit is the only writer of row pos of KV head hkv
-    const size_t row = ((size_t)hkv * a.max_seq + pos) * HD;
+    const size_t row = ((size_t)hkl * a.max_seq + pos) * HD;
     if (tid < HD) st.kc[row + tid] = kn[tid];
     else if (tid >= 256 && tid < 256 + HD) st.vc[row + tid - 256] = vn[tid - 256];
   }
-  const float* K = st.kc + ((size_t)hkv * a.max_seq + s0) * HD;
-  const float* V = st.vc + ((size_t)hkv * a.max_seq + s0) * HD;
+  const float* K = st.kc + ((size_t)hkl * a.max_seq + s0) * HD;
+  const float* V = st.vc + ((size_t)hkl * a.max_seq + s0) * HD;
   float ql[DV];
 #pragma unroll
   for (int i = 0; i < DV; ++i) ql[i] = qs[lane + 32 * i];
@@ -526,22 +571,34 @@ __device__ void attn_unit(const DecArgs& a, const DecStage& st, int h, int j, in
   for (int i = 0; i < DV; ++i) ared[warp * HD + lane + 32 * i] = acc[i];
   named_barrier(kBarCons, kConsThreads);
   float* po = a.part_o + ((size_t)h * a.nsplit + j) * HD;
+  float* pml = a.part_ml + ((size_t)h * a.nsplit + j) * 2;
   for (int d = tid; d < HD; d += kConsThreads) {
     float t = 0.f;
 #pragma unroll
     for (int w = 0; w < kCons; ++w) t = __fadd_rn(t, ared[w * HD + d]);
-    po[d] = t;
+    if (a.world == 1) po[d] = t;
+    else
+      for (int q = 0; q < a.world; ++q) at_rank(a, po, q)[d] = t;
   }
   if (tid == 0) {
-    a.part_ml[((size_t)h * a.nsplit + j) * 2] = mx;
-    a.part_ml[((size_t)h * a.nsplit + j) * 2 + 1] = sum;
+    if (a.world == 1) {
+      pml[0] = mx;
+      pml[1] = sum;
+    } else {
+      for (int q = 0; q < a.world; ++q) {
+        at_rank(a, pml, q)[0] = mx;
+        at_rank(a, pml, q)[1] = sum;
+      }
+    }
   }
-  __threadfence();                        // partials and KV row visible before the arrival
+  // partials and KV row visible before the arrival
+  if (a.world == 1) __threadfence();
+  else __threadfence_system();
   named_barrier(kBarCons, kConsThreads);  // scratch reused by the next unit
 }
 
 // ------------------------------------------------------------ the kernel
-__global__ void __maxnreg__(112) decode_step_kernel(const DecArgs a) {
+__global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int cid = blockIdx.x, G = gridDim.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -554,6 +611,7 @@ __global__ void __maxnreg__(112) decode_step_kernel(const DecArgs a) {
   int* rec = reinterpret_cast<int*>(smem + kOffRecent);
   const unsigned epoch = __ldcg(a.ctl);          // launches completed before this one
   const unsigned target = (epoch + 1u) * (unsigned)G;
+  const unsigned gtarget = (epoch + 1u) * (unsigned)a.world;
   const int pos = *(volatile const int*)a.pos;
   const int tok = *(volatile const int*)a.tok_in;
   const int nst = a.nstages;
@@ -607,10 +665,12 @@ __global__ void __maxnreg__(112) decode_step_kernel(const DecArgs a) {
         }
         q0 += nstg;
       }
-      if (ok) {
-        for (int q = issued_last; q >= 0 && q > issued_last - kNS; q -= kIssuers)
-          if (!dwait<-32>(a, &full[q % kNS], (q / kNS) & 1)) ok = false;
-      }
+      // Drain: lane l issues only into slot l (kNS == kIssuers), and it waits
+      // for `empty` before reusing it, so at most its last copy can still be in
+      // flight.  Wait for it even after an abort (with the launch-independent
+      // bound of mbar_wait), so the CTA never exits with a bulk copy landing
+      // in its shared memory.
+      if (issued_last >= 0 && !mbar_wait(&full[issued_last % kNS], (issued_last / kNS) & 1)) ok = false;
       if (!ok && a.err) atomicExch(a.err, 1);
     }
     __syncwarp();
@@ -631,7 +691,7 @@ __global__ void __maxnreg__(112) decode_step_kernel(const DecArgs a) {
         for (int i = lane; i < 128; i += 32) mark[i] = 0u;
         __syncwarp();
         for (int i = lane; i < a.n_recent; i += 32) {
-          const int r = rec[i] - rt0 * 16;
+          const int r = rec[i] - (st.row0[0] + rt0 * 16);
           if (r >= 0 && r < nrt * 16 && r < 4096) atomicOr(&mark[r >> 5], 1u << (r & 31));
         }
         __syncwarp();
@@ -667,18 +727,23 @@ __global__ void __maxnreg__(112) decode_step_kernel(const DecArgs a) {
         const int r = (grt - st.rt_prefix[p]) * 16 + (lane >> 1);
         if ((lane & 1) == 0 && r < st.rows[p]) {
           float* yp = st.y[p] ? st.y[p] : a.logits;
-          yp[r] = yv;
+          const int gr = st.row0[p] + r;   // output row of the full weight
+          if (a.world == 1 || !st.y[p]) {
+            yp[gr] = yv;                   // (logits: this rank's rows, locally)
+          } else {
+            for (int q2 = 0; q2 < a.world; ++q2) at_rank(a, yp, q2)[gr] = yv;
+          }
           if (greedy) {
             float adj = yv;
             const int lr = r - rt0 * 16;
             if (lr >= 4096 || ((mark[lr >> 5] >> (lr & 31)) & 1u)) {
               for (int t = 0; t < a.n_recent; ++t)
-                if (rec[t] == r) adj = adj > 0.0f ? __fdiv_rn(adj, a.penalty) : __fmul_rn(adj, a.penalty);
+                if (rec[t] == gr) adj = adj > 0.0f ? __fdiv_rn(adj, a.penalty) : __fmul_rn(adj, a.penalty);
             }
-            if (r == 0 && adj != adj) nan0 = 1;
+            if (gr == 0 && adj != adj) nan0 = 1;
             if (adj == adj && (besti < 0 || adj > bestv)) {
               bestv = adj;
-              besti = r;
+              besti = gr;
             }
           }
         }
@@ -697,15 +762,20 @@ __global__ void __maxnreg__(112) decode_step_kernel(const DecArgs a) {
         }
         nan0 = __any_sync(0xffffffffu, nan0);
         if (lane == 0) {
-          int* cd = a.cand + (size_t)cid * 4;
-          cd[0] = __float_as_int(bestv);
-          cd[1] = besti;
-          cd[2] = nan0;
+          int* cd = a.cand + ((size_t)a.rank * G + cid) * 4;
+          for (int q2 = 0; q2 < a.world; ++q2) {
+            int* cq = a.world == 1 ? cd : at_rank(a, cd, q2);
+            cq[0] = __float_as_int(bestv);
+            cq[1] = besti;
+            cq[2] = nan0;
+          }
         }
       }
-      __threadfence();   // this lane's y (and argmax) visible before the arrival
+      // this lane's y (and argmax) visible before the arrival
+      if (a.world == 1) __threadfence();
+      else __threadfence_system();
       __syncwarp();
-      if (lane == 0) arrive(a, s);
+      if (lane == 0) arrive(a, s, target);
     }
   } else {
     // ---------------- consumers
@@ -723,12 +793,12 @@ __global__ void __maxnreg__(112) decode_step_kernel(const DecArgs a) {
       const DecStage& st = a.stages[s];
       if (st.kind == ST_ATTN) {
         // wait for q/k/v of every CTA, then this CTA's (head, split) units
-        if (threadIdx.x == 0 && s > 0) wait_count(a, a.ctl + 2 + (s - 1), target);
+        if (threadIdx.x == 0 && s > 0) stage_wait(a, s - 1, target, gtarget);
         named_barrier(kBarCons, kConsThreads);
-        const int units = a.H * a.nsplit;
+        const int units = a.hloc * a.nsplit;   // this rank's heads
         if (pos >= 0 && pos < a.max_seq) {
           for (int u = cid; u < units; u += G) {
-            const int h = u / a.nsplit, j = u - h * a.nsplit;
+            const int h = a.h0 + u / a.nsplit, j = u - (h - a.h0) * a.nsplit;
             if (a.HD == 128) attn_unit<4>(a, st, h, j, pos, smem);
             else attn_unit<2>(a, st, h, j, pos, smem);
           }
@@ -736,14 +806,14 @@ __global__ void __maxnreg__(112) decode_step_kernel(const DecArgs a) {
           atomicExch(a.err, 4);   // position outside the KV cache: nothing is read or appended
         }
         named_barrier(kBarCons, kConsThreads);
-        if (threadIdx.x == 0) arrive(a, s);
+        if (threadIdx.x == 0) arrive(a, s, target);
         continue;
       }
       int rt0, nrt;
       row_split(st.n_rt, cid, G, &rt0, &nrt);
       const int nkb = st.nkb;
       const int nstg = nrt * nkb;
-      if (threadIdx.x == 0 && s > 0) wait_count(a, a.ctl + 2 + (s - 1), target);
+      if (threadIdx.x == 0 && s > 0) stage_wait(a, s - 1, target, gtarget);
       named_barrier(kBarCons, kConsThreads);  // also: every warp is done with the last x
       prologue(a, st, cid, tok, smem);
       const float sm = *xmaxp / 127.0f;
@@ -833,10 +903,10 @@ __global__ void __maxnreg__(112) decode_step_kernel(const DecArgs a) {
     }
     // CTA 0 picks the next token from the per-CTA argmax results
     if (cid == 0 && a.tok_out != nullptr && threadIdx.x == 0) {
-      bool ok = wait_count(a, a.ctl + 2 + (nst - 1), target);
+      bool ok = stage_wait(a, nst - 1, target, gtarget);
       float bv = -INFINITY;
       int bi = -1, n0 = 0;
-      for (int c2 = 0; c2 < G && ok; ++c2) {
+      for (int c2 = 0; c2 < G * a.world && ok; ++c2) {   // every rank's CTAs, in rank order
         const int* cd = a.cand + (size_t)c2 * 4;
         const float cv = __int_as_float(__ldcg(cd));
         const int ci = __ldcg(cd + 1);
@@ -849,7 +919,7 @@ __global__ void __maxnreg__(112) decode_step_kernel(const DecArgs a) {
       *a.tok_out = (n0 || bi < 0) ? 0 : bi;
     }
     if (cid == 0 && threadIdx.x == 0 && a.advance_pos) {
-      wait_count(a, a.ctl + 2 + (nst - 1), target);
+      stage_wait(a, nst - 1, target, gtarget);
       *a.pos = pos + 1;
     }
   }
@@ -866,9 +936,11 @@ __global__ void __maxnreg__(112) decode_step_kernel(const DecArgs a) {
 struct DecodePlan {
   int device = -1;
   int grid = 0;
+  int world = 1, rank = 0;
   std::vector<DecStage> stages;
   DecStage* d_stages = nullptr;
   void* scratch = nullptr;
+  void* peers[kMaxRanks] = {};   // sharded: every rank's scratch as mapped here
   DecArgs base = {};
   int64_t vocab = 0;
 };
@@ -881,21 +953,33 @@ DecodePlan* find_plan(int64_t id) {
   return g_plans[(size_t)id - 1];
 }
 
-int q4_of(nimf_weight_t h, int64_t k, int64_t rows, const char* what, const Q4GWeight** out) {
+// The int4-g128 weight behind handle h, which must hold rows [r0, r1) of an
+// n-row, k-column weight (the whole weight on one GPU, this rank's
+// shard_range rows on a sharded plan).
+int q4_of(nimf_weight_t h, int64_t k, int64_t n, int world, int rank, const char* what,
+          const Q4GWeight** out, int* row0) {
   Weight* w = lookup(h);
   if (!w) return set_error(NIMF_ERR_STATE, "decode plan: %s: unknown weight handle", what);
   if (w->kind != NIMF_KIND_INT4_ASYM || !w->q4.fast || w->q4.gs != kGS)
     return set_error(NIMF_ERR_UNSUPPORTED,
                      "decode plan: %s must be an int4 asymmetric weight with group size 128", what);
   if (w->kperm) return set_error(NIMF_ERR_UNSUPPORTED, "decode plan: %s has an act-order permutation", what);
-  if (w->q4.k != k || w->q4.rows != rows)
-    return set_error(NIMF_ERR_SHAPE, "decode plan: %s is [%lld x %lld], expected [%lld x %lld]", what,
-                     (long long)w->q4.rows, (long long)w->q4.k, (long long)rows, (long long)k);
+  int64_t r0 = 0, r1 = n;
+  if (world > 1) shard_range(n, world, rank, &r0, &r1);
+  const int64_t nf = w->n_full > 0 ? w->n_full : w->q4.rows;
+  if (w->q4.k != k || w->q4.rows != r1 - r0 || w->row_begin != r0 || nf != n)
+    return set_error(NIMF_ERR_SHAPE,
+                     "decode plan: %s holds rows [%lld, %lld) of [%lld x %lld], expected rows "
+                     "[%lld, %lld) of [%lld x %lld]", what, (long long)w->row_begin,
+                     (long long)(w->row_begin + w->q4.rows), (long long)nf, (long long)w->q4.k,
+                     (long long)r0, (long long)r1, (long long)n, (long long)k);
   *out = &w->q4;
+  *row0 = (int)r0;
   return NIMF_OK;
 }
 
-DecStage gemv_stage(int pro, const Q4GWeight* const* ws, float* const* ys, int n, int64_t k) {
+DecStage gemv_stage(int pro, const Q4GWeight* const* ws, const int* row0, float* const* ys, int n,
+                    int64_t k) {
   DecStage s = {};
   s.kind = ST_GEMV;
   s.pro = pro;
@@ -909,167 +993,226 @@ DecStage gemv_stage(int pro, const Q4GWeight* const* ws, float* const* ys, int n
     s.sz[i] = (const float4*)ws[i]->sz;
     s.y[i] = ys[i];
     s.rows[i] = (int)ws[i]->rows;
+    s.row0[i] = row0[i];
     s.rt_prefix[i + 1] = s.rt_prefix[i] + (int)ws[i]->n_rt;
   }
   s.n_rt = s.rt_prefix[n];
   return s;
 }
 
-}  // namespace
-
-void release_decode_plans() {
-  for (DecodePlan*& p : g_plans) {
-    if (!p) continue;
-    device_free(p->d_stages);
-    device_free(p->scratch);
-    delete p;
-    p = nullptr;
-  }
-  g_plans.clear();
+void free_plan(DecodePlan* P) {
+  if (!P) return;
+  if (P->world > 1) comm_unshare_buffer(P->peers, P->world, P->rank);
+  device_free(P->d_stages);
+  device_free(P->scratch);
+  delete P;
 }
 
-}  // namespace nimf
-
-using namespace nimf;
-
-extern "C" {
-
-int nimf_decode_create(const nimf_decode_desc* d, int64_t* plan_out) {
+// Validates the descriptor and builds the stage table and scratch.  A sharded
+// plan (world > 1) also exchanges the scratch's IPC handle with every rank;
+// before that exchange the ranks agree on whether all of them validated, so a
+// rank whose arguments are wrong makes every rank fail instead of leaving the
+// others waiting in the exchange.
+int create_plan(const nimf_decode_desc* d, int world, int rank, int64_t* plan_out) {
   Context* c;
   NIMF_TRY(require_ctx(&c));
-  if (!d || !plan_out || !d->layers) return set_error(NIMF_ERR_ARG, "decode_create: NULL argument");
-  const int64_t L = d->n_layers, D = d->d_model, H = d->n_heads, HKV = d->n_kv_heads,
-                HD = d->head_dim, F = d->ffn_dim, V = d->vocab, MS = d->max_seq;
-  if (L < 1 || D < kGS || D % kGS || F % kGS || D > kMaxK || F > kMaxK || V < 1 || H < 1 ||
-      H > kMaxHeads || HKV < 1 || H % HKV || (HD != 64 && HD != 128) || H * HD != D || MS < 1)
-    return set_error(NIMF_ERR_SHAPE,
+  DecodePlan* P = nullptr;
+  int rc = NIMF_OK;
+  int64_t L = 0, D = 0, H = 0, HKV = 0, HD = 0, F = 0, V = 0, MS = 0, KVD = 0;
+  int grid = 0, nsplit = 1;
+  size_t off = 0, o_q = 0, o_k = 0, o_v = 0, o_po = 0, o_pml = 0, o_ao = 0, o_g = 0, o_u = 0,
+         o_dn = 0, o_xr = 0, o_hr = 0, o_cand = 0, o_ctl = 0, o_gctl = 0;
+  int nst = 0;
+  auto take = [&](size_t bytes) { size_t o = off; off += (bytes + 255) / 256 * 256; return o; };
+  // ---- validation (no collective before the agreement below)
+  do {
+    if (!d || !plan_out || !d->layers) {
+      rc = set_error(NIMF_ERR_ARG, "decode_create: NULL argument");
+      break;
+    }
+    L = d->n_layers, D = d->d_model, H = d->n_heads, HKV = d->n_kv_heads, HD = d->head_dim,
+    F = d->ffn_dim, V = d->vocab, MS = d->max_seq;
+    if (L < 1 || D < kGS || D % kGS || F % kGS || D > kMaxK || F > kMaxK || V < 1 || H < 1 ||
+        H > kMaxHeads || HKV < 1 || H % HKV || (HD != 64 && HD != 128) || H * HD != D || MS < 1) {
+      rc = set_error(NIMF_ERR_SHAPE,
                      "decode_create: unsupported shape (layers %lld, d_model %lld, heads %lld/%lld, "
                      "head_dim %lld, ffn %lld, vocab %lld, max_seq %lld); needs d_model and ffn "
                      "multiples of 128 up to %d, head_dim 64 or 128, heads x head_dim = d_model",
                      (long long)L, (long long)D, (long long)H, (long long)HKV, (long long)HD,
                      (long long)F, (long long)V, (long long)MS, kMaxK);
-  if (d->n_recent_max < 0 || d->n_recent_max > kMaxRecent)
-    return set_error(NIMF_ERR_SHAPE, "decode_create: n_recent_max %lld not in [0, %d]",
+      break;
+    }
+    if (world > 1 && (HKV % world || H % world)) {
+      rc = set_error(NIMF_ERR_SHAPE,
+                     "decode_create_sharded: %lld query and %lld KV heads do not split over %d GPUs",
+                     (long long)H, (long long)HKV, world);
+      break;
+    }
+    if (d->n_recent_max < 0 || d->n_recent_max > kMaxRecent) {
+      rc = set_error(NIMF_ERR_SHAPE, "decode_create: n_recent_max %lld not in [0, %d]",
                      (long long)d->n_recent_max, kMaxRecent);
-  if (!d->embedding || !d->final_norm || !d->rope_cos || !d->rope_sin)
-    return set_error(NIMF_ERR_ARG, "decode_create: NULL model array");
-  const int64_t KVD = HKV * HD;
-  // grid: one CTA per SM, at most the row tiles of the smallest GEMV stage
-  // (so every CTA takes part in every stage)
-  // (n_rt of q/k/v, o, gate/up, down and lm_head)
-  int64_t min_rt = std::min<int64_t>((D + 15) / 16 + 2 * ((KVD + 15) / 16), (D + 15) / 16);
-  min_rt = std::min<int64_t>(min_rt, 2 * ((F + 15) / 16));
-  min_rt = std::min<int64_t>(min_rt, (V + 15) / 16);
-  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(c->num_sms, min_rt));
-  int nsplit = std::max(1, std::min(kMaxSplit, grid / (int)H));
-  while (nsplit < kMaxSplit && (MS + nsplit - 1) / nsplit > kMaxPs) ++nsplit;
-  if ((MS + nsplit - 1) / nsplit > kMaxPs)
-    return set_error(NIMF_ERR_SHAPE, "decode_create: max_seq %lld too long", (long long)MS);
-
-  DecodePlan* P = new DecodePlan();
-  P->device = c->device;
-  P->grid = grid;
-  P->vocab = V;
-  // scratch: q, k, v, attention partials, o out, gate, up, down out, two
-  // residual rows, per-CTA argmax, control words
-  const int nst = (int)(5 * L + 1);
-  size_t off = 0;
-  auto take = [&](size_t bytes) { size_t o = off; off += (bytes + 255) / 256 * 256; return o; };
-  const size_t o_q = take(D * 4), o_k = take(KVD * 4), o_v = take(KVD * 4);
-  const size_t o_po = take((size_t)H * nsplit * HD * 4), o_pml = take((size_t)H * nsplit * 2 * 4);
-  const size_t o_ao = take(D * 4), o_g = take(F * 4), o_u = take(F * 4), o_dn = take(D * 4);
-  const size_t o_xr = take(D * 4), o_hr = take(D * 4);
-  const size_t o_cand = take((size_t)grid * 4 * 4);
-  const size_t o_ctl = take((size_t)(nst + 3) * 4);
-  int rc = device_alloc(&P->scratch, off);
+      break;
+    }
+    if (!d->embedding || !d->final_norm || !d->rope_cos || !d->rope_sin) {
+      rc = set_error(NIMF_ERR_ARG, "decode_create: NULL model array");
+      break;
+    }
+    KVD = HKV * HD;
+    // One GPU: one CTA per SM, at most the row tiles of the smallest GEMV
+    // stage (n_rt of q/k/v, o, gate/up, down and lm_head).  A sharded plan
+    // takes every SM (a rank's shards can be a few tiles; CTAs without rows in
+    // a stage still take part in its barrier).  The attention split count is
+    // the one-GPU plan's, so a sharded step computes the same numbers.
+    int64_t min_rt = std::min<int64_t>((D + 15) / 16 + 2 * ((KVD + 15) / 16), (D + 15) / 16);
+    min_rt = std::min<int64_t>(min_rt, 2 * ((F + 15) / 16));
+    min_rt = std::min<int64_t>(min_rt, (V + 15) / 16);
+    const int grid1 = (int)std::max<int64_t>(1, std::min<int64_t>(c->num_sms, min_rt));
+    grid = world > 1 ? c->num_sms : grid1;
+    nsplit = std::max(1, std::min(kMaxSplit, grid1 / (int)H));
+    while (nsplit < kMaxSplit && (MS + nsplit - 1) / nsplit > kMaxPs) ++nsplit;
+    if ((MS + nsplit - 1) / nsplit > kMaxPs) {
+      rc = set_error(NIMF_ERR_SHAPE, "decode_create: max_seq %lld too long", (long long)MS);
+      break;
+    }
+  } while (0);
+  if (rc == NIMF_OK) {
+    P = new DecodePlan();
+    P->device = c->device;
+    P->grid = grid;
+    P->vocab = V;
+    P->world = world;
+    P->rank = rank;
+    // scratch: q, k, v, attention partials, o out, gate, up, down out, two
+    // residual rows, per-CTA argmax of every rank, control words
+    nst = (int)(5 * L + 1);
+    o_q = take(D * 4), o_k = take(KVD * 4), o_v = take(KVD * 4);
+    o_po = take((size_t)H * nsplit * HD * 4), o_pml = take((size_t)H * nsplit * 2 * 4);
+    o_ao = take(D * 4), o_g = take(F * 4), o_u = take(F * 4), o_dn = take(D * 4);
+    o_xr = take(D * 4), o_hr = take(D * 4);
+    o_cand = take((size_t)world * grid * 4 * 4);
+    o_ctl = take((size_t)(nst + 3) * 4);
+    o_gctl = take((size_t)(nst + 1) * 4);
+    rc = device_alloc(&P->scratch, off);
+  }
+  if (rc == NIMF_OK) {
+    char* sb = (char*)P->scratch;
+    float *bq = (float*)(sb + o_q), *bk = (float*)(sb + o_k), *bv = (float*)(sb + o_v);
+    float *bao = (float*)(sb + o_ao), *bg = (float*)(sb + o_g), *bu = (float*)(sb + o_u);
+    float *bdn = (float*)(sb + o_dn), *bxr = (float*)(sb + o_xr), *bhr = (float*)(sb + o_hr);
+    for (int64_t l = 0; l < L && rc == NIMF_OK; ++l) {
+      const nimf_decode_layer_desc& ld = d->layers[l];
+      const Q4GWeight *wq, *wk, *wv, *wo, *wg, *wu, *wd;
+      int r0q, r0k, r0v, r0o, r0g, r0u, r0d;
+      if ((rc = q4_of(ld.wq, D, D, world, rank, "wq", &wq, &r0q)) ||
+          (rc = q4_of(ld.wk, D, KVD, world, rank, "wk", &wk, &r0k)) ||
+          (rc = q4_of(ld.wv, D, KVD, world, rank, "wv", &wv, &r0v)) ||
+          (rc = q4_of(ld.wo, D, D, world, rank, "wo", &wo, &r0o)) ||
+          (rc = q4_of(ld.wgate, D, F, world, rank, "wgate", &wg, &r0g)) ||
+          (rc = q4_of(ld.wup, D, F, world, rank, "wup", &wu, &r0u)) ||
+          (rc = q4_of(ld.wdown, F, D, world, rank, "wdown", &wd, &r0d)))
+        break;
+      if (!ld.attn_norm || !ld.ffn_norm || !ld.k_cache || !ld.v_cache) {
+        rc = set_error(NIMF_ERR_ARG, "decode_create: layer %lld has a NULL array", (long long)l);
+        break;
+      }
+      {
+        const Q4GWeight* ws[3] = {wq, wk, wv};
+        const int r0s[3] = {r0q, r0k, r0v};
+        float* ys[3] = {bq, bk, bv};
+        DecStage s = gemv_stage(l == 0 ? PRO_EMB_RMS : PRO_ADD_RMS, ws, r0s, ys, 3, D);
+        s.a = bhr;
+        s.b = bdn;
+        s.w = ld.attn_norm;
+        s.res_out = bxr;
+        P->stages.push_back(s);
+      }
+      {
+        DecStage s = {};
+        s.kind = ST_ATTN;
+        s.kc = ld.k_cache;
+        s.vc = ld.v_cache;
+        P->stages.push_back(s);
+      }
+      {
+        const Q4GWeight* ws[1] = {wo};
+        const int r0s[1] = {r0o};
+        float* ys[1] = {bao};
+        P->stages.push_back(gemv_stage(PRO_COMBINE, ws, r0s, ys, 1, D));
+      }
+      {
+        const Q4GWeight* ws[2] = {wg, wu};
+        const int r0s[2] = {r0g, r0u};
+        float* ys[2] = {bg, bu};
+        DecStage s = gemv_stage(PRO_ADD_RMS, ws, r0s, ys, 2, D);
+        s.a = bxr;
+        s.b = bao;
+        s.w = ld.ffn_norm;
+        s.res_out = bhr;
+        P->stages.push_back(s);
+      }
+      {
+        const Q4GWeight* ws[1] = {wd};
+        const int r0s[1] = {r0d};
+        float* ys[1] = {bdn};
+        DecStage s = gemv_stage(PRO_SWIGLU, ws, r0s, ys, 1, F);
+        s.a = bg;
+        s.b = bu;
+        P->stages.push_back(s);
+      }
+    }
+    if (rc == NIMF_OK) {
+      const Q4GWeight* wh;
+      int r0h;
+      rc = q4_of(d->lm_head, D, V, world, rank, "lm_head", &wh, &r0h);
+      if (rc == NIMF_OK) {
+        float* ys[1] = {nullptr};  // the launch's logits buffer
+        DecStage s = gemv_stage(PRO_ADD_RMS, &wh, &r0h, ys, 1, D);
+        s.a = bhr;
+        s.b = bdn;
+        s.w = d->final_norm;
+        s.res_out = bxr;
+        s.greedy = 1;
+        P->stages.push_back(s);
+      }
+    }
+    if (rc == NIMF_OK) rc = device_alloc((void**)&P->d_stages, P->stages.size() * sizeof(DecStage));
+    if (rc == NIMF_OK) {
+      cudaError_t e = cudaMemcpy(P->d_stages, P->stages.data(), P->stages.size() * sizeof(DecStage),
+                                 cudaMemcpyHostToDevice);
+      if (e == cudaSuccess) e = cudaMemset(P->scratch, 0, off);
+      if (e == cudaSuccess) e = cudaDeviceSynchronize();
+      if (e != cudaSuccess) rc = set_error(NIMF_ERR_CUDA, "decode_create: %s", cudaGetErrorString(e));
+    }
+    if (rc == NIMF_OK) {
+      cudaError_t e = cudaFuncSetAttribute(decode_step_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+      int per_sm = 0;
+      if (e == cudaSuccess)
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_step_kernel, kThreads,
+                                                          kSmemBytes);
+      if (e != cudaSuccess) rc = set_error(NIMF_ERR_CUDA, "decode_create: %s", cudaGetErrorString(e));
+      else if (per_sm < 1)
+        rc = set_error(NIMF_ERR_UNSUPPORTED, "decode_create: the step kernel does not fit an SM");
+    }
+  }
+  if (world > 1) {
+    // every rank learns whether all of them got this far, then (all did)
+    // shares its scratch with the others
+    int ok_all = 0;
+    const int rc_agree = comm_agree(rc == NIMF_OK, &ok_all);
+    if (rc == NIMF_OK && rc_agree != NIMF_OK) rc = rc_agree;
+    if (rc == NIMF_OK && !ok_all)
+      rc = set_error(NIMF_ERR_STATE, "decode_create_sharded: another rank failed to build its plan");
+    if (rc == NIMF_OK) rc = comm_share_buffer(P->scratch, P->peers);
+  }
   if (rc != NIMF_OK) {
-    delete P;
+    if (P) {
+      P->world = 1;  // nothing was opened
+      free_plan(P);
+    }
     return rc;
   }
   char* sb = (char*)P->scratch;
-  float *bq = (float*)(sb + o_q), *bk = (float*)(sb + o_k), *bv = (float*)(sb + o_v);
-  float *bao = (float*)(sb + o_ao), *bg = (float*)(sb + o_g), *bu = (float*)(sb + o_u);
-  float *bdn = (float*)(sb + o_dn), *bxr = (float*)(sb + o_xr), *bhr = (float*)(sb + o_hr);
-  auto fail = [&](int code) {
-    device_free(P->scratch);
-    delete P;
-    return code;
-  };
-  for (int64_t l = 0; l < L; ++l) {
-    const nimf_decode_layer_desc& ld = d->layers[l];
-    const Q4GWeight *wq, *wk, *wv, *wo, *wg, *wu, *wd;
-    int r;
-    if ((r = q4_of(ld.wq, D, D, "wq", &wq)) || (r = q4_of(ld.wk, D, KVD, "wk", &wk)) ||
-        (r = q4_of(ld.wv, D, KVD, "wv", &wv)) || (r = q4_of(ld.wo, D, D, "wo", &wo)) ||
-        (r = q4_of(ld.wgate, D, F, "wgate", &wg)) || (r = q4_of(ld.wup, D, F, "wup", &wu)) ||
-        (r = q4_of(ld.wdown, F, D, "wdown", &wd)))
-      return fail(r);
-    if (!ld.attn_norm || !ld.ffn_norm || !ld.k_cache || !ld.v_cache)
-      return fail(set_error(NIMF_ERR_ARG, "decode_create: layer %lld has a NULL array", (long long)l));
-    {
-      const Q4GWeight* ws[3] = {wq, wk, wv};
-      float* ys[3] = {bq, bk, bv};
-      DecStage s = gemv_stage(l == 0 ? PRO_EMB_RMS : PRO_ADD_RMS, ws, ys, 3, D);
-      s.a = bhr;
-      s.b = bdn;
-      s.w = ld.attn_norm;
-      s.res_out = bxr;
-      P->stages.push_back(s);
-    }
-    {
-      DecStage s = {};
-      s.kind = ST_ATTN;
-      s.kc = ld.k_cache;
-      s.vc = ld.v_cache;
-      P->stages.push_back(s);
-    }
-    {
-      const Q4GWeight* ws[1] = {wo};
-      float* ys[1] = {bao};
-      P->stages.push_back(gemv_stage(PRO_COMBINE, ws, ys, 1, D));
-    }
-    {
-      const Q4GWeight* ws[2] = {wg, wu};
-      float* ys[2] = {bg, bu};
-      DecStage s = gemv_stage(PRO_ADD_RMS, ws, ys, 2, D);
-      s.a = bxr;
-      s.b = bao;
-      s.w = ld.ffn_norm;
-      s.res_out = bhr;
-      P->stages.push_back(s);
-    }
-    {
-      const Q4GWeight* ws[1] = {wd};
-      float* ys[1] = {bdn};
-      DecStage s = gemv_stage(PRO_SWIGLU, ws, ys, 1, F);
-      s.a = bg;
-      s.b = bu;
-      P->stages.push_back(s);
-    }
-  }
-  {
-    const Q4GWeight* wh;
-    int r = q4_of(d->lm_head, D, V, "lm_head", &wh);
-    if (r) return fail(r);
-    float* ys[1] = {nullptr};  // the launch's logits buffer
-    DecStage s = gemv_stage(PRO_ADD_RMS, &wh, ys, 1, D);
-    s.a = bhr;
-    s.b = bdn;
-    s.w = d->final_norm;
-    s.res_out = bxr;
-    s.greedy = 1;
-    P->stages.push_back(s);
-  }
-  int rc2 = device_alloc((void**)&P->d_stages, P->stages.size() * sizeof(DecStage));
-  if (rc2) return fail(rc2);
-  cudaError_t e = cudaMemcpy(P->d_stages, P->stages.data(), P->stages.size() * sizeof(DecStage),
-                             cudaMemcpyHostToDevice);
-  if (e == cudaSuccess) e = cudaMemset(sb + o_ctl, 0, (size_t)(nst + 3) * 4);
-  if (e == cudaSuccess) e = cudaMemset(P->scratch, 0, off);
-  if (e != cudaSuccess) {
-    device_free(P->d_stages);
-    return fail(set_error(NIMF_ERR_CUDA, "decode_create: %s", cudaGetErrorString(e)));
-  }
   DecArgs& A = P->base;
   A.stages = P->d_stages;
   A.nstages = (int)P->stages.size();
@@ -1085,25 +1228,52 @@ int nimf_decode_create(const nimf_decode_desc* d, int64_t* plan_out) {
   A.emb = d->embedding;
   A.cos_t = d->rope_cos;
   A.sin_t = d->rope_sin;
-  A.q = bq;
-  A.k = bk;
-  A.v = bv;
+  A.q = (float*)(sb + o_q);
+  A.k = (float*)(sb + o_k);
+  A.v = (float*)(sb + o_v);
   A.part_o = (float*)(sb + o_po);
   A.part_ml = (float*)(sb + o_pml);
   A.cand = (int*)(sb + o_cand);
   A.ctl = (unsigned*)(sb + o_ctl);
-  NIMF_CUDA_TRY(cudaFuncSetAttribute(decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     kSmemBytes));
-  int per_sm = 0;
-  NIMF_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_step_kernel, kThreads,
-                                                              kSmemBytes));
-  if (per_sm < 1) {
-    device_free(P->d_stages);
-    return fail(set_error(NIMF_ERR_UNSUPPORTED, "decode_create: the step kernel does not fit an SM"));
-  }
+  A.gctl = (unsigned*)(sb + o_gctl);
+  A.world = world;
+  A.rank = rank;
+  A.hloc = (int)(H / world);
+  A.h0 = (int)(rank * (H / world));
+  A.hk0 = (int)(rank * (HKV / world));
+  for (int q = 0; q < kMaxRanks; ++q)
+    A.peer_off[q] = (q < world && P->peers[q]) ? (long long)((char*)P->peers[q] - sb) : 0;
   g_plans.push_back(P);
   *plan_out = (int64_t)g_plans.size();
   return NIMF_OK;
+}
+
+}  // namespace
+
+void release_decode_plans() {
+  for (DecodePlan*& p : g_plans) {
+    free_plan(p);
+    p = nullptr;
+  }
+  g_plans.clear();
+}
+
+}  // namespace nimf
+
+using namespace nimf;
+
+extern "C" {
+
+int nimf_decode_create(const nimf_decode_desc* d, int64_t* plan_out) {
+  return create_plan(d, 1, 0, plan_out);
+}
+
+int nimf_decode_create_sharded(const nimf_decode_desc* d, int64_t* plan_out) {
+  Context* c;
+  NIMF_TRY(require_ctx(&c));
+  int world = 1, rank = 0;
+  NIMF_TRY(comm_world(&world, &rank));
+  return create_plan(d, world, rank, plan_out);
 }
 
 int nimf_decode_step_dev(int64_t plan, int32_t* token_dev, int32_t* next_token_dev,
@@ -1165,11 +1335,12 @@ int nimf_decode_destroy(int64_t plan) {
   DecodePlan* P = find_plan(plan);
   if (!P) return set_error(NIMF_ERR_STATE, "decode_destroy: unknown plan %lld", (long long)plan);
   cudaDeviceSynchronize();
-  device_free(P->d_stages);
-  device_free(P->scratch);
-  delete P;
+  // a sharded plan's scratch receives the peers' stores: no rank releases it
+  // before every rank has finished its last step
+  const int rc = P->world > 1 ? comm_barrier() : NIMF_OK;
+  free_plan(P);
   g_plans[(size_t)plan - 1] = nullptr;
-  return NIMF_OK;
+  return rc;
 }
 
 }  // extern "C"

@@ -173,6 +173,11 @@ int nimf_weight_register_gptq(const int32_t* qweight, const int32_t* qzeros,
   nimf_weight_t h;
   NIMF_TRY(nimf_weight_register_q4g(wq.data(), sc.data(), zp.data(), rows, K, gs, n_groups, 0,
                                     rows, &h));
+  {
+    Weight* w = lookup(h);
+    w->row_begin = row_begin;
+    w->n_full = N;
+  }
   if (!identity) {
     Weight* w = lookup(h);
     void* d = nullptr;

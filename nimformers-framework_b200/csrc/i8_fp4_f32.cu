@@ -1,12 +1,9 @@
-// i8_fp4_f32.cu -- the int8 (quant.nim:51-67), FP4 E2M1 block-16 (no
-// reference counterpart) and raw fp32 (beMatmul, gpubackend.nim:584-604)
-// weight paths.
+// i8_fp4_f32.cu -- the int8 (quant.nim:51-67) and FP4 E2M1 block-16 (no
+// reference counterpart) warp-per-row kernels, and the fp32 weight transpose
+// (beMatmul's b, gpubackend.nim:584-604).  The fp32 matmul itself is f32.cu.
 //
 // int8 and FP4 GEMVs here are warp-per-row kernels that dequantise each weight
-// with the reference's rounding and accumulate in fp32; raw fp32 GEMMs go to
-// cuBLAS SGEMM (pure fp32 math, the same library call the reference makes in
-// cuda_runtime.nim:147-150, minus its per-call host copies of the weight).
-#include <cublas_v2.h>
+// with the reference's rounding and accumulate in fp32.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -143,8 +140,6 @@ __global__ void transpose_kernel(const float* __restrict__ in, int64_t rows, int
   }
 }
 
-cublasHandle_t g_blas = nullptr;
-int g_blas_dev = -1;
 
 }  // namespace
 
@@ -189,31 +184,6 @@ int f32_transpose(const float* b_kn, int64_t k, int64_t n, float* w_nk, cudaStre
   dim3 grid((unsigned)((n + 31) / 32), (unsigned)((k + 31) / 32));
   transpose_kernel<<<grid, dim3(32, 8), 0, st>>>(b_kn, k, n, w_nk);
   NIMF_CUDA_TRY(cudaGetLastError());
-  return NIMF_OK;
-}
-
-// C[m][n] = A[m][k] . B[k][n] (row-major), as cuda_runtime.nim:147-150 issues it.
-int f32_gemm(const float* a, int64_t m, int64_t k, const float* b_kn, int64_t n, float* c,
-             cudaStream_t st) {
-  Context* cx = ctx();
-  if (!g_blas || g_blas_dev != cx->device) {
-    if (cublasCreate(&g_blas) != CUBLAS_STATUS_SUCCESS)
-      return set_error(NIMF_ERR_CUDA, "cublasCreate failed");
-    cublasSetMathMode(g_blas, CUBLAS_PEDANTIC_MATH);
-    g_blas_dev = cx->device;
-  }
-  if (m == 0 || n == 0) return NIMF_OK;
-  if (k == 0) {
-    NIMF_CUDA_TRY(cudaMemsetAsync(c, 0, (size_t)(m * n) * 4, st));
-    return NIMF_OK;
-  }
-  if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX)
-    return set_error(NIMF_ERR_UNSUPPORTED, "fp32 GEMM dimension exceeds int32");
-  cublasSetStream(g_blas, st);
-  const float alpha = 1.0f, beta = 0.0f;
-  cublasStatus_t s = cublasSgemm(g_blas, CUBLAS_OP_N, CUBLAS_OP_N, (int)n, (int)m, (int)k, &alpha,
-                                 b_kn, (int)n, a, (int)k, &beta, c, (int)n);
-  if (s != CUBLAS_STATUS_SUCCESS) return set_error(NIMF_ERR_CUDA, "cublasSgemm failed (%d)", (int)s);
   return NIMF_OK;
 }
 

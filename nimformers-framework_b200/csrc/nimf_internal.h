@@ -108,6 +108,8 @@ struct Weight {
   // (device int32 [K]; x is gathered through it before each matmul)
   void* kperm = nullptr;
   std::vector<int32_t> kperm_host;
+  // N-shard registration: rows [row_begin, row_begin + rows()) of n_full
+  int64_t row_begin = 0, n_full = 0;
   int64_t rows() const;
   int64_t k() const;
 };
@@ -155,6 +157,19 @@ int q4g_gemv(const Q4GWeight& w, const float* x, int64_t m, float* y, cudaStream
 int q4g_gemv_group(const Q4GWeight* const* ws, int count, const float* x, int64_t m,
                    float* const* ys, cudaStream_t st);
 int q4g_dequant(const Q4GWeight& w, float* out, cudaStream_t st);
+// The grouped GEMV with its outputs also stored into every rank's buffer
+// (the fused all-gather of N-shard outputs, comm.cu): ys[i] is where this
+// rank's first row goes in the local full output (row stride ldys[i]).
+constexpr int kCommMaxRanks = 8;  // GPUs of one node the multi-GPU paths address
+struct GatherSpec {
+  int world = 1;
+  long long peer_off[kCommMaxRanks] = {};  // byte offset from a local output address to rank q's copy
+  unsigned* ctl = nullptr;     // the group's control words (local)
+  unsigned long long wait_ns = 0;
+};
+int q4g_gemv_group_gather(const Q4GWeight* const* ws, int count, const float* x, int64_t m,
+                          float* const* ys, const int64_t* ldys, const GatherSpec& g,
+                          cudaStream_t st);
 // Prefill GEMM on tcgen05 (x with many rows); q4g_tc_supported tells whether
 // the weight's group size has a tensor-core kernel.
 bool q4g_tc_supported(const Q4GWeight& w);
@@ -205,6 +220,27 @@ void release_p2p_groups();   // p2p.cu: IPC buffers and peer mappings of the all
 int fp4_gemv(const FP4Weight& w, const float* x, int64_t m, float* y, cudaStream_t st);
 int fp4_dequant(const FP4Weight& w, float* out, cudaStream_t st);
 
+// Runs a registered weight's matmul on device buffers (any kind).
+int weight_matmul_dev(Weight* w, const float* x, int64_t m, float* y, cudaStream_t st);
+
+// ----------------------------------------------------------------- multi-GPU
+// Rows [*r0, *r1) of an n-row weight held by `rank` of `world`: whole 16-row
+// tiles, sizes within one tile (the host mirror's shard_rows).
+void shard_range(int64_t n, int world, int rank, int64_t* r0, int64_t* r1);
+// world 1 / rank 0 without a communicator.
+int comm_world(int* world, int* rank);
+// Shares a cudaMalloc'd buffer with every rank (CUDA IPC handles exchanged
+// over the communicator); peers[q] is rank q's buffer as mapped here
+// (peers[rank] = local).  Collective: every rank calls it in the same order.
+int comm_share_buffer(void* local, void** peers);
+void comm_unshare_buffer(void** peers, int world, int rank);
+int comm_allgather_bytes(const void* src, size_t bytes, void* dst_host);
+int comm_barrier();
+// *all_ok = 1 when every rank passed ok != 0 (collective)
+int comm_agree(int ok, int* all_ok);
+void release_comm();
+
+void release_f32_scratch();     // f32.cu: split-K partials of the fp32 GEMV
 int f32_gemm(const float* a, int64_t m, int64_t k, const float* w_nk, int64_t n, float* c,
              cudaStream_t st);
 int f32_transpose(const float* b_kn, int64_t k, int64_t n, float* w_nk, cudaStream_t st);

@@ -259,6 +259,22 @@ int nimf_p2p_connect(int64_t group, const void* ipc_handles) {
   return NIMF_OK;
 }
 
+int nimf_p2p_connect_comm(int64_t group) {
+  P2PGroup* g = find_group(group);
+  if (!g) return set_error(NIMF_ERR_STATE, "p2p_connect_comm: unknown group %lld", (long long)group);
+  int world = 1, rank = 0;
+  NIMF_TRY(comm_world(&world, &rank));
+  if (world != g->world || rank != g->rank)
+    return set_error(NIMF_ERR_STATE,
+                     "p2p_connect_comm: group is rank %d of %d, the communicator rank %d of %d",
+                     g->rank, g->world, rank, world);
+  cudaIpcMemHandle_t mine;
+  NIMF_CUDA_TRY(cudaIpcGetMemHandle(&mine, g->base));
+  std::vector<cudaIpcMemHandle_t> all((size_t)world);
+  NIMF_TRY(comm_allgather_bytes(&mine, sizeof(mine), all.data()));
+  return nimf_p2p_connect(group, all.data());
+}
+
 int nimf_p2p_allgather_dev(int64_t group, const float* src, int64_t rows, int64_t cols,
                            int64_t ld_src, float* dst, int64_t ld_dst, void* stream) {
   Context* c;

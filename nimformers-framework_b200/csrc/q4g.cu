@@ -190,7 +190,62 @@ struct GemvArgs {
   int tchunk;          // max row tiles per cluster (sizes the partial-y buffers)
   int ns;              // stages in the weight ring (a multiple of kCons)
   int vec4;            // x rows 16-byte aligned
+  // Fused all-gather of N-shard outputs (world > 1): every y value is also
+  // stored at the same offset of each rank's output buffer (rank q's copy of
+  // a local address p is p + peer_off[q] bytes, through CUDA IPC); the last
+  // CTA to finish raises one arrival on every rank and waits (bounded) until
+  // every rank's arrival for this launch is in, so the launch completes with
+  // the gathered outputs in place on this rank.
+  int world;
+  long long peer_off[kCommMaxRanks];
+  unsigned* gctl;      // local control words: [0] launches, [1] CTAs done, [2] rank arrivals
+  unsigned long long wait_ns;
 };
+
+__device__ __forceinline__ void gather_store(const GemvArgs& a, float* p, float v) {
+  if (a.world <= 1) {
+    *p = v;
+    return;
+  }
+  for (int q = 0; q < a.world; ++q)
+    *reinterpret_cast<float*>(reinterpret_cast<char*>(p) + a.peer_off[q]) = v;
+}
+
+// End of a gathering launch, called by every CTA after a __syncthreads that
+// follows its last y stores (each storing thread fenced them at system scope).
+__device__ void gather_finish(const GemvArgs& a) {
+  if (threadIdx.x != 0) return;
+  unsigned* done = a.gctl + 1;
+  if (atomicAdd(done, 1u) != gridDim.x - 1) return;
+  // the last CTA of this rank's launch: nothing else of the launch touches
+  // the control words now, and the next launch on this stream starts after
+  // this one completes
+  *done = 0u;
+  const unsigned epoch = *(volatile unsigned*)a.gctl;
+  __threadfence_system();
+  for (int q = 0; q < a.world; ++q) {
+    unsigned* arr = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(a.gctl + 2) + a.peer_off[q]);
+    asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(arr) : "memory");
+  }
+  const unsigned target = (epoch + 1u) * (unsigned)a.world;
+  unsigned long long t0, t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (unsigned it = 0;; ++it) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a.gctl + 2) : "memory");
+    if ((int)(v - target) >= 0) break;
+    if ((it & 63u) == 63u) {
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (t - t0 > a.wait_ns) {
+        if (a.err) atomicExch(a.err, 5);
+        break;
+      }
+    }
+    __nanosleep(64);
+  }
+  *(volatile unsigned*)a.gctl = epoch + 1u;
+  __threadfence();
+}
 
 // A stage holds one k-block of a row tile's slice of this CTA's k-split
 // (packed weights, then the scale/zero pairs of its groups), moved by two bulk
@@ -425,12 +480,13 @@ q4g_gemv_kernel(const GemvArgs a) {
         if ((MODE == 2 || (lane & 1) == 0) && rbase + r < trows[pp]) {
           float* yp = ty[pp] + rbase + r;
           const int64_t ld = tldy[pp];
-          if (m0 < a.m) yp[(size_t)m0 * ld] = o.x;
-          if (m0 + 1 < a.m) yp[(size_t)(m0 + 1) * ld] = o.y;
-          if (m0 + 2 < a.m) yp[(size_t)(m0 + 2) * ld] = o.z;
-          if (m0 + 3 < a.m) yp[(size_t)(m0 + 3) * ld] = o.w;
+          if (m0 < a.m) gather_store(a, yp + (size_t)m0 * ld, o.x);
+          if (m0 + 1 < a.m) gather_store(a, yp + (size_t)(m0 + 1) * ld, o.y);
+          if (m0 + 2 < a.m) gather_store(a, yp + (size_t)(m0 + 2) * ld, o.z);
+          if (m0 + 3 < a.m) gather_store(a, yp + (size_t)(m0 + 3) * ld, o.w);
         }
       }
+      if (a.world > 1) __threadfence_system();
     }
   } else {
     // ---------------- consumers: quantise x of the k-split into two s8 digits
@@ -712,6 +768,7 @@ q4g_gemv_kernel(const GemvArgs a) {
   }
   if (direct) {
     __syncthreads();  // the producer's drain completes before the CTA exits
+    if (a.world > 1) gather_finish(a);
     return;
   }
   // sum the chunks of each row tile locally (chunk order) into the now idle
@@ -734,9 +791,11 @@ q4g_gemv_kernel(const GemvArgs a) {
     if (mm >= a.m || row >= trows[p]) continue;
     float s = 0.0f;
     for (int r = 0; r < nsplit; ++r) s += cluster.map_shared_rank(sums, r)[e];
-    ty[p][(size_t)mm * tldy[p] + row] = s;
+    gather_store(a, ty[p] + (size_t)mm * tldy[p] + row, s);
   }
+  if (a.world > 1) __threadfence_system();
   cluster.sync();
+  if (a.world > 1) gather_finish(a);
 }
 
 // Any group size (including <= 0, one group per row), any K: one warp per
@@ -920,7 +979,7 @@ struct Piece {
 // Launches the GEMV over the given pieces (same K, group size and x).
 template <int MODE, int KQG>
 int launch_fast(const Piece* pcs, int npc, const float* x, int64_t ldx, int mc, int num_sms,
-                cudaStream_t st) {
+                cudaStream_t st, const GatherSpec* gsp) {
   Context* c = ctx();
   const Q4GWeight& w0 = *pcs[0].w;
   const int groups = (int)w0.groups;
@@ -1032,6 +1091,10 @@ int launch_fast(const Piece* pcs, int npc, const float* x, int64_t ldx, int mc, 
   a.tchunk = tchunk;
   a.ns = ns;
   a.vec4 = ((reinterpret_cast<uintptr_t>(x) & 15) == 0) && (ldx % 4 == 0);
+  a.world = gsp ? gsp->world : 1;
+  for (int q = 0; q < kCommMaxRanks; ++q) a.peer_off[q] = gsp ? gsp->peer_off[q] : 0;
+  a.gctl = gsp ? gsp->ctl : nullptr;
+  a.wait_ns = gsp ? gsp->wait_ns : 0;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(n_clusters * s), 1, 1);
@@ -1055,7 +1118,8 @@ int launch_fast(const Piece* pcs, int npc, const float* x, int64_t ldx, int mc, 
 // kMaxProblems pieces and a bounded number of row tiles per cluster.
 template <int MODE, int KQG>
 int launch_rows(const Q4GWeight* const* ws, float* const* ys, int count, const float* x,
-                int64_t ldx, int mc, int64_t m0, int num_sms, cudaStream_t st) {
+                int64_t ldx, int mc, int64_t m0, int num_sms, cudaStream_t st,
+                const GatherSpec* gsp = nullptr, const int64_t* ldys = nullptr) {
   // Direct mode (no k-split) streams any number of row tiles; split mode keeps
   // at most kMaxTilesPerCluster partial row tiles per cluster in shared memory.
   int kbg, nkb, nsd;
@@ -1063,6 +1127,10 @@ int launch_rows(const Q4GWeight* const* ws, float* const* ys, int count, const f
   const int64_t cap = direct_fits ? ((int64_t)1 << 40)
                                   : (int64_t)kMaxTilesPerCluster *
                                         std::max(1, num_sms * kCtasPerSm / kMaxSplits);
+  if (gsp && (!direct_fits || count > kMaxProblems))
+    return set_error(NIMF_ERR_UNSUPPORTED,
+                     "gathering GEMV: %d weights of K=%lld at %d rows of x need more than one launch",
+                     count, (long long)ws[0]->k, mc);
   Piece pcs[kMaxProblems];
   int npc = 0;
   int64_t in_launch = 0;
@@ -1073,29 +1141,30 @@ int launch_rows(const Q4GWeight* const* ws, float* const* ys, int count, const f
       pcs[npc].w = &w;
       pcs[npc].rt_begin = r0;
       pcs[npc].n_rt = (int)n;
-      pcs[npc].y = ys[i] + m0 * w.rows;
-      pcs[npc].ldy = w.rows;
+      pcs[npc].y = ys[i] + m0 * (ldys ? ldys[i] : w.rows);
+      pcs[npc].ldy = ldys ? ldys[i] : w.rows;
       ++npc;
       in_launch += n;
       r0 += n;
       if (npc == kMaxProblems || in_launch == cap) {
-        NIMF_TRY((launch_fast<MODE, KQG>(pcs, npc, x, ldx, mc, num_sms, st)));
+        NIMF_TRY((launch_fast<MODE, KQG>(pcs, npc, x, ldx, mc, num_sms, st, gsp)));
         npc = 0;
         in_launch = 0;
       }
     }
   }
-  if (npc > 0) NIMF_TRY((launch_fast<MODE, KQG>(pcs, npc, x, ldx, mc, num_sms, st)));
+  if (npc > 0) NIMF_TRY((launch_fast<MODE, KQG>(pcs, npc, x, ldx, mc, num_sms, st, gsp)));
   return NIMF_OK;
 }
 
 template <int MODE>
 int launch_mode(const Q4GWeight* const* ws, float* const* ys, int count, const float* x,
-                int64_t ldx, int mc, int64_t m0, int num_sms, cudaStream_t st) {
+                int64_t ldx, int mc, int64_t m0, int num_sms, cudaStream_t st,
+                const GatherSpec* gsp = nullptr, const int64_t* ldys = nullptr) {
   switch (ws[0]->gs) {
-    case 64: return launch_rows<MODE, 1>(ws, ys, count, x, ldx, mc, m0, num_sms, st);
-    case 128: return launch_rows<MODE, 2>(ws, ys, count, x, ldx, mc, m0, num_sms, st);
-    case 256: return launch_rows<MODE, 4>(ws, ys, count, x, ldx, mc, m0, num_sms, st);
+    case 64: return launch_rows<MODE, 1>(ws, ys, count, x, ldx, mc, m0, num_sms, st, gsp, ldys);
+    case 128: return launch_rows<MODE, 2>(ws, ys, count, x, ldx, mc, m0, num_sms, st, gsp, ldys);
+    case 256: return launch_rows<MODE, 4>(ws, ys, count, x, ldx, mc, m0, num_sms, st, gsp, ldys);
   }
   return set_error(NIMF_ERR_UNSUPPORTED, "q4g fast path: group size %lld", (long long)ws[0]->gs);
 }
@@ -1169,6 +1238,22 @@ int q4g_gemv_group(const Q4GWeight* const* ws, int count, const float* x, int64_
     }
   }
   return NIMF_OK;
+}
+
+int q4g_gemv_group_gather(const Q4GWeight* const* ws, int count, const float* x, int64_t m,
+                          float* const* ys, const int64_t* ldys, const GatherSpec& g,
+                          cudaStream_t st) {
+  Context* c = ctx();
+  const int num_sms = c ? c->num_sms : 148;
+  if (m <= 0 || m > 8 || count <= 0)
+    return set_error(NIMF_ERR_UNSUPPORTED, "gathering GEMV: %lld rows of x (1 .. 8)", (long long)m);
+  const Q4GWeight& w0 = *ws[0];
+  for (int i = 0; i < count; ++i)
+    if (ws[i]->k != w0.k || ws[i]->gs != w0.gs || !ws[i]->fast || ws[i]->k == 0)
+      return set_error(NIMF_ERR_UNSUPPORTED,
+                       "gathering GEMV: weights must share K > 0 and a group size of 64, 128 or 256");
+  if (m <= 4) return launch_mode<1>(ws, ys, count, x, w0.k, (int)m, 0, num_sms, st, &g, ldys);
+  return launch_mode<2>(ws, ys, count, x, w0.k, (int)m, 0, num_sms, st, &g, ldys);
 }
 
 int q4g_gemv(const Q4GWeight& w, const float* x, int64_t m, float* y, cudaStream_t st) {

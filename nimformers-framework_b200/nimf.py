@@ -53,6 +53,11 @@ EXPORTS = [
     "nimf_p2p_set_timeout_ms",
     "nimf_decode_create", "nimf_decode_step_dev", "nimf_decode_info", "nimf_decode_set_timeout_ms",
     "nimf_decode_destroy",
+    "nimf_p2p_connect_comm", "nimf_comm_unique_id", "nimf_comm_init", "nimf_comm_info",
+    "nimf_comm_allgather_dev", "nimf_comm_barrier", "nimf_comm_destroy", "nimf_shard_range",
+    "nimf_matmul_w_allgather_dev", "nimf_decode_create_sharded",
+    "nimf_gather_create", "nimf_matmul_w_group_gather_dev", "nimf_gather_set_timeout_ms",
+    "nimf_gather_destroy",
 ]
 
 
@@ -126,10 +131,24 @@ def lib():
         "nimf_p2p_destroy": [i64],
         "nimf_p2p_set_timeout_ms": [i64],
         "nimf_decode_create": [ctypes.POINTER(DecodeDesc), ctypes.POINTER(i64)],
+        "nimf_decode_create_sharded": [ctypes.POINTER(DecodeDesc), ctypes.POINTER(i64)],
         "nimf_decode_step_dev": [i64, vp, vp, vp, i32, vp, i64, ctypes.c_float, vp, vp],
         "nimf_decode_info": [i64, ctypes.POINTER(i64), ctypes.POINTER(i64), ctypes.POINTER(i64)],
         "nimf_decode_set_timeout_ms": [i64],
         "nimf_decode_destroy": [i64],
+        "nimf_p2p_connect_comm": [i64],
+        "nimf_comm_unique_id": [vp],
+        "nimf_comm_init": [i32, i32, vp],
+        "nimf_comm_info": [ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)],
+        "nimf_comm_allgather_dev": [vp, i64, vp, vp],
+        "nimf_comm_barrier": [],
+        "nimf_comm_destroy": [],
+        "nimf_shard_range": [i64, i32, i32, ctypes.POINTER(i64), ctypes.POINTER(i64)],
+        "nimf_matmul_w_allgather_dev": [ctypes.c_uint64, vp, i64, vp, vp],
+        "nimf_gather_create": [i64, ctypes.POINTER(i64), ctypes.POINTER(vp)],
+        "nimf_matmul_w_group_gather_dev": [i64, vp, i32, vp, i64, vp, vp],
+        "nimf_gather_set_timeout_ms": [i64],
+        "nimf_gather_destroy": [i64],
         "nimf_greedy_sample_dev": [vp, i64, i64, vp, i64, ctypes.c_float, vp, vp],
         "nimf_add_dev": [vp, vp, i64, vp, vp],
         "nimf_add_rmsnorm_dev": [vp, vp, vp, i64, i64, ctypes.c_float, vp, vp, vp],
@@ -174,11 +193,16 @@ class DecodePlan:
     (LlamaModelL.forwardStep with isPrefill = false, nim_inference.nim:887-921,
     plus the greedy branch of sampleTopP).  `layers` is a list of dicts with
     the keys of DecodeLayerDesc (weights as Weight objects or handles, arrays
-    as device pointers); the other arrays are device pointers too."""
+    as device pointers); the other arrays are device pointers too.
+
+    sharded=True builds the plan over the library communicator's GPUs
+    (nimf_decode_create_sharded, collective): every weight is this rank's
+    nimf.shard_rows rows, the caches hold this rank's n_kv_heads / world KV
+    heads, and the step's outputs travel between the GPUs inside the launch."""
 
     def __init__(self, *, layers, embedding, final_norm, lm_head, rope_cos, rope_sin, d_model,
                  n_heads, n_kv_heads, head_dim, ffn_dim, vocab, max_seq, norm_eps=1e-6,
-                 n_recent_max=64):
+                 n_recent_max=64, sharded=False):
         h = lambda w: w.handle if isinstance(w, Weight) else int(w)
         arr = (DecodeLayerDesc * len(layers))()
         for i, l in enumerate(layers):
@@ -189,7 +213,8 @@ class DecodePlan:
                        n_recent_max, norm_eps, embedding, final_norm, h(lm_head), rope_cos, rope_sin,
                        arr)
         pid = ctypes.c_int64()
-        check(lib().nimf_decode_create(ctypes.byref(d), ctypes.byref(pid)))
+        create = lib().nimf_decode_create_sharded if sharded else lib().nimf_decode_create
+        check(create(ctypes.byref(d), ctypes.byref(pid)))
         self.plan = pid.value
 
     def step(self, token, next_token, pos, logits, recent=None, n_recent=0, penalty=1.0,

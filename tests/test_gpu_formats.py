@@ -183,3 +183,22 @@ def test_beMatmul_and_beMatmul2(nimf_gpu):
     assert np.array_equal(h.dequant(), np.ascontiguousarray(b.T))
     assert rel_err(h.matmul(a, 5), O.cpu_matmul(a, b, 5, 300, 70)) <= TOL
     h.free()
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 1024, 1024), (3, 4096, 1000), (8, 300, 70), (9, 257, 131),
+                                   (130, 512, 384), (256, 1024, 640), (1, 7, 5), (17, 3, 2)])
+def test_beMatmul_hand_written_kernels(nimf_gpu, m, k, n):
+    """beMatmul's fp32 kernels (f32.cu: the GEMV for M <= 8 with its split-K
+    reduction, the tiled GEMM above), vector and ragged shapes, against the
+    reference's cpuMatmul order and against float64; repeat calls are
+    bit-identical (fixed summation order)."""
+    ctx = nimf_gpu.newBackend()
+    rng = np.random.default_rng(m * 1000 + n)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = rng.standard_normal((k, n)).astype(np.float32)
+    a[0, : min(k, 5)] = 0.0          # cpuMatmul skips zero a values
+    y = np.asarray(nimf_gpu.beMatmul(ctx, a, m, k, b, k, n), dtype=np.float32)
+    assert rel_err(y, O.cpu_matmul(a, b, m, k, n).ravel()) <= TOL
+    assert rel_err(y, (a.astype(np.float64) @ b.astype(np.float64)).ravel()) <= 1e-5
+    y2 = np.asarray(nimf_gpu.beMatmul(ctx, a, m, k, b, k, n), dtype=np.float32)
+    assert np.array_equal(y.view(np.uint32), y2.view(np.uint32))

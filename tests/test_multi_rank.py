@@ -136,3 +136,17 @@ def test_sharded_decode_gather_layout():
     for p_ in procs:
         p_.join(timeout=120)
     assert all(ok for _, ok in res), res
+
+
+def test_library_shard_range_matches_host_rule():
+    """nimf_shard_range (the library's rule, used by the sharded matmul and the
+    sharded decode plan to locate every rank's rows) equals nimf.shard_rows."""
+    import ctypes
+    L = nimf.lib()
+    a, b = ctypes.c_int64(), ctypes.c_int64()
+    for n in (0, 1, 15, 16, 17, 4096, 11008, 12288, 28672, 32000, 32001):
+        for world in range(1, 9):
+            for rank in range(world):
+                nimf.check(L.nimf_shard_range(n, world, rank, ctypes.byref(a), ctypes.byref(b)))
+                assert (a.value, b.value) == nimf.shard_rows(n, world, rank), (n, world, rank)
+    assert L.nimf_shard_range(16, 2, 2, ctypes.byref(a), ctypes.byref(b)) == -1   # NIMF_ERR_ARG
