@@ -715,6 +715,213 @@ def run_decode_7b_sharded(nimf, torch, steps, warmup, rank, world, pos=512, max_
                      % (world, steps))}
 
 
+def run_generate_7b(nimf, torch, batch=1, prompt=512, new_tokens=128, layers=L7, max_seq=640):
+    """The 7B-shape stack's whole generation (LlamaModelL.generate,
+    nim_inference.nim:1064-1140) for `batch` independent sequences: each
+    prompt of `prompt` random token ids goes through forwardPrefill
+    (:574-620) -- per layer RMSNorm, the q/k/v, o, gate/up and down
+    projections as tcgen05 GEMMs over all batch x prompt rows, RoPE, the
+    causal prompt attention with appendKV (per sequence), SwiGLU and the
+    residual adds -- then the final norm, lm_head on each sequence's last row
+    and the greedy first tokens; then `new_tokens` greedy decode steps over
+    the caches the prefill filled (token out -> token in, positions advanced
+    on the device).  Batch 1 decodes with the one-launch plan; batch > 1 with
+    one captured step of the per-op path (grouped GEMVs over the batch rows,
+    nimf_attention_decode_batch_dev at device positions), replayed per token.
+    Synthetic int4-g128 weights; CUDA events around each phase."""
+    import ctypes
+    import numpy as np
+    rng = np.random.default_rng(8)
+    L = nimf.lib()
+    H, HD, B = 32, 128, batch
+
+    def make(n, k):
+        ngr = k // GS
+        p = rng.integers(0, 256, size=n * (k // 2), dtype=np.uint8)
+        sc = rng.uniform(0.002, 0.004, size=n * ngr).astype(np.float32)
+        zp = rng.uniform(6.0, 9.0, size=n * ngr).astype(np.float32)
+        return p, sc, zp
+
+    hq, hg, hd, hh = make(D7, D7), make(F7, D7), make(D7, F7), make(V7, D7)
+    dev = torch.device("cuda")
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+    kvs = B * H * max_seq * HD       # one layer's K (or V) cache, all sequences
+    lw, ws = [], []
+    plan, graph = None, None
+    try:
+        for _ in range(layers):
+            q, k, v, o = [nimf.Weight.q4g(*hq, D7, D7, GS) for _ in range(4)]
+            gate, up = [nimf.Weight.q4g(*hg, F7, D7, GS) for _ in range(2)]
+            down = nimf.Weight.q4g(*hd, D7, F7, GS)
+            ws += [q, k, v, o, gate, up, down]
+            n1 = torch.rand(D7, device=dev) + 0.5
+            n2 = torch.rand(D7, device=dev) + 0.5
+            kc = torch.zeros(kvs, device=dev)
+            vc = torch.zeros(kvs, device=dev)
+            lw.append((q, k, v, o, gate, up, down, n1, n2, kc, vc))
+        head = nimf.Weight.q4g(*hh, V7, D7, GS)
+        ws.append(head)
+        nf = torch.rand(D7, device=dev) + 0.5
+        half = HD // 2
+        inv = 1.0 / np.power(np.float32(10000.0), np.arange(half, dtype=np.float32) / np.float32(half))
+        ang = np.arange(max_seq, dtype=np.float32)[:, None] * inv[None, :].astype(np.float32)
+        cos_t = torch.from_numpy(np.cos(ang).astype(np.float32)).to(dev)
+        sin_t = torch.from_numpy(np.sin(ang).astype(np.float32)).to(dev)
+        table = torch.randn(V7, D7, device=dev) * 0.02
+        ids = torch.from_numpy(rng.integers(0, V7, size=B * prompt).astype(np.int32)).to(dev)
+        T, R = prompt, B * prompt            # tokens per sequence, prefill rows
+        x = torch.empty(R, D7, device=dev)
+        h = torch.empty(R, D7, device=dev)
+        xn = torch.empty(R, D7, device=dev)
+        qkv = [torch.empty(R, D7, device=dev) for _ in range(3)]
+        att = torch.empty(R, D7, device=dev)
+        ao = torch.empty(R, D7, device=dev)
+        gu = [torch.empty(R, F7, device=dev) for _ in range(2)]
+        act = torch.empty(R, F7, device=dev)
+        dn = torch.empty(R, D7, device=dev)
+        last = torch.empty(B, D7, device=dev)
+        logits = torch.empty(B, V7, device=dev)
+        tok = torch.zeros(B, dtype=torch.int32, device=dev)
+        recent = torch.zeros(B, 64, dtype=torch.int32, device=dev)
+        scale = float(np.float32(1.0) / np.sqrt(np.float32(HD)))
+        eps = ctypes.c_float(1e-6)
+        seq_kv = H * max_seq * HD * 4        # bytes of one sequence's cache in a layer
+
+        def prefill(st):
+            sp = ctypes.c_void_p(st)
+            nimf.check(L.nimf_embedding_lookup_dev(P(table), V7, D7, P(ids), R, P(x), sp))
+            nimf.check(L.nimf_rmsnorm_dev(P(x), P(lw[0][7]), R, D7, eps, P(xn), sp))
+            for li, (q, k, v, o, gate, up, down, n1, n2, kc, vc) in enumerate(lw):
+                nimf.Weight.matmul_group_dev([q, k, v], xn.data_ptr(), R,
+                                             [t.data_ptr() for t in qkv], st)
+                nimf.check(L.nimf_rope_dev(P(qkv[0]), B, T, H, HD, 0, P(cos_t), P(sin_t), max_seq, sp))
+                nimf.check(L.nimf_rope_dev(P(qkv[1]), B, T, H, HD, 0, P(cos_t), P(sin_t), max_seq, sp))
+                for b in range(B):
+                    off = b * T * D7 * 4
+                    nimf.check(L.nimf_attention_prefill_dev(
+                        ctypes.c_void_p(qkv[0].data_ptr() + off), ctypes.c_void_p(qkv[1].data_ptr() + off),
+                        ctypes.c_void_p(qkv[2].data_ptr() + off), ctypes.c_void_p(kc.data_ptr() + b * seq_kv),
+                        ctypes.c_void_p(vc.data_ptr() + b * seq_kv), T, H, H, HD, max_seq, 0,
+                        ctypes.c_float(scale), ctypes.c_void_p(att.data_ptr() + off), sp))
+                o.matmul_dev(att.data_ptr(), R, ao.data_ptr(), st)
+                nimf.check(L.nimf_add_rmsnorm_dev(P(x), P(ao), P(n2), R, D7, eps, P(h), P(xn), sp))
+                nimf.Weight.matmul_group_dev([gate, up], xn.data_ptr(), R,
+                                             [gu[0].data_ptr(), gu[1].data_ptr()], st)
+                nimf.check(L.nimf_swiglu_dev(P(gu[0]), P(gu[1]), R * F7, P(act), sp))
+                down.matmul_dev(act.data_ptr(), R, dn.data_ptr(), st)
+                nxt = lw[li + 1][7] if li + 1 < len(lw) else nf
+                nimf.check(L.nimf_add_rmsnorm_dev(P(h), P(dn), P(nxt), R, D7, eps, P(x), P(xn), sp))
+            # lm_head and the greedy choice on each sequence's last prompt row
+            last.copy_(xn.view(B, T, D7)[:, T - 1])
+            head.matmul_dev(last.data_ptr(), B, logits.data_ptr(), st)
+            nimf.check(L.nimf_greedy_sample_dev(P(logits), B, V7, P(recent), 0, ctypes.c_float(1.0),
+                                                P(tok), sp))
+
+        pos = torch.zeros(B, dtype=torch.int32, device=dev)
+        st = torch.cuda.Stream()
+        out_ids = torch.zeros(new_tokens, B, dtype=torch.int32, device=dev)
+        if B == 1:
+            lds = [{"wq": q, "wk": k, "wv": v, "wo": o, "wgate": gate, "wup": up, "wdown": down,
+                    "attn_norm": n1.data_ptr(), "ffn_norm": n2.data_ptr(),
+                    "k_cache": kc.data_ptr(), "v_cache": vc.data_ptr()}
+                   for (q, k, v, o, gate, up, down, n1, n2, kc, vc) in lw]
+            plan = nimf.DecodePlan(layers=lds, embedding=table.data_ptr(), final_norm=nf.data_ptr(),
+                                   lm_head=head, rope_cos=cos_t.data_ptr(), rope_sin=sin_t.data_ptr(),
+                                   d_model=D7, n_heads=H, n_kv_heads=H, head_dim=HD, ffn_dim=F7,
+                                   vocab=V7, max_seq=max_seq, norm_eps=1e-6)
+
+            def decode_step(sv):
+                plan.step(tok.data_ptr(), tok.data_ptr(), pos.data_ptr(), logits.data_ptr(),
+                          None, 0, 1.0, advance_pos=True, stream=sv)
+        else:
+            xd = torch.empty(B, D7, device=dev)
+            hd_ = torch.empty(B, D7, device=dev)
+            xnd = torch.empty(B, D7, device=dev)
+            qd = [torch.empty(B, D7, device=dev) for _ in range(3)]
+            attd = torch.empty(B, D7, device=dev)
+            aod = torch.empty(B, D7, device=dev)
+            gud = [torch.empty(B, F7, device=dev) for _ in range(2)]
+            actd = torch.empty(B, F7, device=dev)
+            dnd = torch.empty(B, D7, device=dev)
+
+            def step_ops(sv):
+                sp = ctypes.c_void_p(sv)
+                nimf.check(L.nimf_embedding_lookup_dev(P(table), V7, D7, P(tok), B, P(xd), sp))
+                nimf.check(L.nimf_rmsnorm_dev(P(xd), P(lw[0][7]), B, D7, eps, P(xnd), sp))
+                for li, (q, k, v, o, gate, up, down, n1, n2, kc, vc) in enumerate(lw):
+                    nimf.Weight.matmul_group_dev([q, k, v], xnd.data_ptr(), B,
+                                                 [t.data_ptr() for t in qd], sv)
+                    nimf.check(L.nimf_attention_decode_batch_dev(
+                        P(qd[0]), P(qd[1]), P(qd[2]), P(kc), P(vc), B, H, H, HD, max_seq, P(pos),
+                        P(cos_t), P(sin_t), ctypes.c_float(scale), 1 if li + 1 == len(lw) else 0,
+                        P(attd), sp))
+                    o.matmul_dev(attd.data_ptr(), B, aod.data_ptr(), sv)
+                    nimf.check(L.nimf_add_rmsnorm_dev(P(xd), P(aod), P(n2), B, D7, eps, P(hd_), P(xnd), sp))
+                    nimf.Weight.matmul_group_dev([gate, up], xnd.data_ptr(), B,
+                                                 [gud[0].data_ptr(), gud[1].data_ptr()], sv)
+                    nimf.check(L.nimf_swiglu_dev(P(gud[0]), P(gud[1]), B * F7, P(actd), sp))
+                    down.matmul_dev(actd.data_ptr(), B, dnd.data_ptr(), sv)
+                    nxt = lw[li + 1][7] if li + 1 < len(lw) else nf
+                    nimf.check(L.nimf_add_rmsnorm_dev(P(hd_), P(dnd), P(nxt), B, D7, eps, P(xd),
+                                                      P(xnd), sp))
+                head.matmul_dev(xnd.data_ptr(), B, logits.data_ptr(), sv)
+                nimf.check(L.nimf_greedy_sample_dev(P(logits), B, V7, P(recent), 0, ctypes.c_float(1.0),
+                                                    P(tok), sp))
+
+            # capture one step (the first replay set-up runs eagerly once)
+            with torch.cuda.stream(st):
+                pos.fill_(prompt)
+                step_ops(st.cuda_stream)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=st):
+                step_ops(st.cuda_stream)
+
+            def decode_step(sv):
+                graph.replay()
+
+        def run():
+            with torch.cuda.stream(st):
+                pos.fill_(prompt)
+                e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+                e0.record()
+                prefill(st.cuda_stream)
+                e1.record()
+                for i in range(new_tokens):
+                    decode_step(st.cuda_stream)
+                    out_ids[i].copy_(tok)
+                e2.record()
+            torch.cuda.synchronize()
+            nimf.check(L.nimf_sync())
+            return e0.elapsed_time(e1), e1.elapsed_time(e2)
+
+        run()                            # warm-up (first tcgen05 calls set up their buffers)
+        pre_ms, dec_ms = run()
+        assert pos.cpu().numpy().tolist() == [prompt + new_tokens] * B
+        ids_out = out_ids.cpu().numpy()
+        assert ((ids_out >= 0) & (ids_out < V7)).all()
+    finally:
+        if graph is not None:
+            graph.reset()
+        if plan is not None:
+            plan.destroy()
+        for w in ws:
+            w.free()
+    pre_flops = layers * prefill7b_flops(B * prompt)
+    return {"batch": B, "prompt_tokens": prompt, "new_tokens": new_tokens,
+            "prefill_ms": pre_ms, "prefill_tok_s": B * prompt / (pre_ms * 1e-3),
+            "prefill_tflop_s": pre_flops / (pre_ms * 1e-3) / 1e12,
+            "decode_ms": dec_ms, "decode_tok_s": B * new_tokens / (dec_ms * 1e-3),
+            "generate_ms": pre_ms + dec_ms,
+            "generate_tok_s": B * new_tokens / ((pre_ms + dec_ms) * 1e-3),
+            "note": ("%d sequence(s): prefill of %d prompt tokens each through 32 layers (tcgen05 "
+                     "GEMMs, causal prompt attention, glue) + lm_head on the last rows; decode: %d "
+                     "greedy steps (%s), token chained on the device; prefill_tflop_s counts the "
+                     "projections only" % (B, prompt, new_tokens,
+                                           "one-launch plan" if B == 1 else
+                                           "one captured per-op step per token"))}
+
+
 def prefill7b_flops(tokens):
     """Multiply-add FLOPs of one 7B layer's projections for `tokens` rows."""
     return 2 * tokens * (4 * D7 * D7 + 3 * F7 * D7)
@@ -1291,6 +1498,14 @@ def run_ours(args, rank, world, local_rank):
     prefill = None
     if world == 1 and args.prefill_steps > 0:
         prefill = run_prefill_7b(nimf, torch, args.prefill_steps, 3)
+    generate = None
+    if world == 1 and args.decode_steps > 0:
+        generate = {}
+        for gb in (1, 8):
+            try:
+                generate["batch%d" % gb] = run_generate_7b(nimf, torch, batch=gb)
+            except Exception as e:  # noqa: BLE001
+                generate["batch%d" % gb] = {"error": "%s: %s" % (type(e).__name__, e)}
     formats = None
     if world == 1 and args.format_steps > 0:
         formats = run_formats(nimf, torch, args.format_steps)
@@ -1299,7 +1514,8 @@ def run_ours(args, rank, world, local_rank):
         # ends with compact 7B summaries, so a record that keeps only the end
         # of the output still holds them
         detail = {"decode_7b": decode, "decode_7b_full_step": decode_full,
-                  "prefill_7b": prefill, "formats": formats, "single_launch": single}
+                  "prefill_7b": prefill, "generate_7b": generate, "formats": formats,
+                  "single_launch": single}
         for key, val in detail.items():
             if val is not None:
                 print("# %s %s" % (key, json.dumps(val)), flush=True)
@@ -1320,6 +1536,12 @@ def run_ours(args, rank, world, local_rank):
             line["exchange"] = ("all-gather fused into the GEMV: merge warps store every output "
                                 "into every GPU over NVLink, one arrival per rank per launch")
         line.update(compact_7b(decode, decode_full, prefill, formats))
+        if generate:
+            line["generate_7b"] = {
+                bk: ({"error": g["error"][:200]} if "error" in g else
+                     {k: round(g[k], 2) for k in ("prefill_ms", "prefill_tok_s", "decode_tok_s",
+                                                   "generate_tok_s")})
+                for bk, g in generate.items()}
         print(json.dumps(line), flush=True)
     for wt in weights:
         wt.free()

@@ -271,6 +271,36 @@ int nimf_attention_decode_dev(const float* q, const float* k_new, const float* v
                               float* k_cache, float* v_cache, int64_t H, int64_t HKV, int64_t D,
                               int64_t max_seq, int64_t pos, float scale, float* out, void* stream);
 
+/* The attention of forwardPrefill (nim_inference.nim:574-620) for T prompt
+ * tokens at positions pos0 .. pos0 + T - 1 (pos0 = 0: the whole prompt; > 0:
+ * a later chunk): appendKV (:404-426) of k_new / v_new [T][HKV][D] into rows
+ * pos0 .. of the caches [HKV][max_seq][D], then for each token t and query
+ * head h the causal softmax attention of cpuAttentionFused
+ * (vendor/bybylang/gpubackend.nim:171-201) over cache rows 0 .. pos0 + t of
+ * KV head h / (H / HKV): score = (q . k) * scale.  q and out are [T][H][D]
+ * (the projections' rows).  D a multiple of 32, at most 256;
+ * pos0 + T <= max_seq. */
+int nimf_attention_prefill_dev(const float* q, const float* k_new, const float* v_new,
+                               float* k_cache, float* v_cache, int64_t T, int64_t H, int64_t HKV,
+                               int64_t D, int64_t max_seq, int64_t pos0, float scale, float* out,
+                               void* stream);
+
+/* One decode token for each of B sequences at positions read on the device,
+ * so a captured batch step can be replayed token after token (the batch form
+ * of nimf_rope_dev + nimf_attention_decode_dev; forwardDecode,
+ * nim_inference.nim:624-748, per sequence).  q [B][H][D], k_new / v_new
+ * [B][HKV][D], caches [B][HKV][max_seq][D], pos_dev [B] int32 (each
+ * sequence's position; outside [0, max_seq) the sequence appends nothing, its
+ * output is undefined and nimf_sync reports NIMF_ERR_TIMEOUT-class error 4).
+ * With cos_t / sin_t (nullable together) q and k_new are first rotated in
+ * place at pos[b] (applyRoPEInplace, :261-330).  advance_pos != 0 adds 1 to
+ * every pos[b] after the call's last use of it.  out [B][H][D]. */
+int nimf_attention_decode_batch_dev(float* q, float* k_new, const float* v_new, float* k_cache,
+                                    float* v_cache, int64_t B, int64_t H, int64_t HKV, int64_t D,
+                                    int64_t max_seq, int32_t* pos_dev, const float* cos_t,
+                                    const float* sin_t, float scale, int advance_pos, float* out,
+                                    void* stream);
+
 /* Token embedding rows, as cpuEmbeddingLookup (vendor/bybylang/gpubackend.nim:268-278,
  * beEmbeddingLookup backend.nim:152-153; Embedding.lookupBatch nimformer.nim:401-411):
  * out[i][0..dim) = table[ids[i]][0..dim) for 0 <= ids[i] < vocab, zeros otherwise.
@@ -409,7 +439,7 @@ int nimf_p2p_destroy(int64_t group);
 int nimf_p2p_connect_comm(int64_t group);
 
 /* ------------------------------------------------- communicator (NCCL) */
-/* north_star's N-sharded weights with an NCCL all-gather of the output
+/* N-sharded weights (row = output channel) with an NCCL all-gather of the output
  * slices, inside the library so that a host binding only this header gets
  * the sharded path.  The reference has no multi-GPU path (its CUDA device is
  * fixed at 0, vendor/bybylang/backends/cuda/cuda_driver.nim:183); these calls

@@ -325,6 +325,34 @@ __global__ void rope_kernel(float* __restrict__ d, int64_t T, int64_t H, int64_t
   }
 }
 
+// RoPE of one token per sequence at the sequence's device position:
+// data [B][H][D] in place (rotate-half, as rope_kernel)
+__global__ void rope_batch_kernel(float* __restrict__ d, int64_t B, int64_t H, int64_t D,
+                                  const int32_t* __restrict__ pos, int64_t max_seq,
+                                  const float* __restrict__ cos_t, const float* __restrict__ sin_t) {
+  griddep_launch_dependents();
+  griddep_wait();
+  const int64_t half = D / 2, npairs = B * H * half;
+  for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < npairs;
+       p += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = p % half, bh = p / half, b = bh / H;
+    const int64_t ps = pos[b];
+    if (ps < 0 || ps >= max_seq) continue;
+    const int64_t base = bh * D;
+    const float c = cos_t[ps * half + i], s = sin_t[ps * half + i];
+    const float x1 = d[base + i], x2 = d[base + i + half];
+    d[base + i] = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(-x2, s));
+    d[base + i + half] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+  }
+}
+
+// pos[b] += 1 for every sequence (after the step's last reader)
+__global__ void advance_pos_kernel(int32_t* pos, int64_t B) {
+  griddep_launch_dependents();
+  griddep_wait();
+  for (int64_t b = threadIdx.x; b < B; b += blockDim.x) pos[b] += 1;
+}
+
 // appendKV: row pos of every KV head; one thread per element
 __global__ void kv_append_kernel(const float* __restrict__ k_new, const float* __restrict__ v_new,
                                  float* __restrict__ kc, float* __restrict__ vc, int64_t HKV,
@@ -338,6 +366,94 @@ __global__ void kv_append_kernel(const float* __restrict__ k_new, const float* _
   }
 }
 
+// appendKV of T prompt rows: k_new / v_new [T][HKV][D] -> rows pos0 + t
+__global__ void kv_append_rows_kernel(const float* __restrict__ k_new, const float* __restrict__ v_new,
+                                      float* __restrict__ kc, float* __restrict__ vc, int64_t T,
+                                      int64_t HKV, int64_t D, int64_t max_seq, int64_t pos0) {
+  griddep_launch_dependents();
+  griddep_wait();
+  const int64_t total = T * HKV * D;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / (HKV * D), r = i - t * HKV * D;
+    const int64_t h = r / D, dd = r - h * D;
+    kc[(h * max_seq + pos0 + t) * D + dd] = k_new[i];
+    vc[(h * max_seq + pos0 + t) * D + dd] = v_new[i];
+  }
+}
+
+// Causal prompt attention (forwardPrefill, nim_inference.nim:574-620, through
+// cpuAttentionFused, vendor/bybylang/gpubackend.nim:171-201): one warp per
+// (query token t, query head h), over cache rows 0 .. pos0 + t of KV head
+// h / nrep.  score = (q . k) * scale; the softmax runs online over batches of
+// kPrefUnroll rows (running max, rescaled exp-sum and P.V), normalised at the
+// end -- the reference's two passes up to rounding.  Lane l holds features
+// l + 32 i.  The 8 warps of a block take 8 consecutive tokens of one head, so
+// they read the same K / V rows through L1.
+constexpr int kPrefWarps = 8;
+constexpr int kPrefUnroll = 4;   // cache rows per online-softmax batch
+template <int DV>
+__global__ void __launch_bounds__(kPrefWarps * 32)
+attn_prefill_kernel(const float* __restrict__ q, const float* __restrict__ kc,
+                    const float* __restrict__ vc, int64_t T, int64_t H, int64_t nrep,
+                    int64_t max_seq, int64_t pos0, float scale, float* __restrict__ out) {
+  constexpr int D = 32 * DV;
+  griddep_launch_dependents();
+  griddep_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * kPrefWarps + warp;
+  const int64_t h = blockIdx.y;
+  if (t >= T) return;
+  const float* K = kc + (h / nrep) * max_seq * D;
+  const float* V = vc + (h / nrep) * max_seq * D;
+  float qv[DV], acc[DV];
+#pragma unroll
+  for (int i = 0; i < DV; ++i) {
+    qv[i] = q[(t * H + h) * D + lane + 32 * i];
+    acc[i] = 0.f;
+  }
+  const int64_t S = pos0 + t + 1;
+  float m = -INFINITY, l = 0.f;
+  for (int64_t j0 = 0; j0 < S; j0 += kPrefUnroll) {
+    float kv[kPrefUnroll][DV];
+#pragma unroll
+    for (int u = 0; u < kPrefUnroll; ++u)
+#pragma unroll
+      for (int i = 0; i < DV; ++i)
+        kv[u][i] = j0 + u < S ? __ldg(K + (j0 + u) * D + lane + 32 * i) : 0.f;
+    float sc[kPrefUnroll];
+#pragma unroll
+    for (int u = 0; u < kPrefUnroll; ++u) {
+      float dot = 0.f;
+#pragma unroll
+      for (int i = 0; i < DV; ++i) dot = fmaf(qv[i], kv[u][i], dot);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+      sc[u] = j0 + u < S ? dot * scale : -INFINITY;
+    }
+    float mn = m;
+#pragma unroll
+    for (int u = 0; u < kPrefUnroll; ++u) mn = fmaxf(mn, sc[u]);
+    const float corr = expf(m - mn);   // m = -inf at the start: 0
+    l *= corr;
+#pragma unroll
+    for (int i = 0; i < DV; ++i) acc[i] *= corr;
+#pragma unroll
+    for (int u = 0; u < kPrefUnroll; ++u) {
+      if (j0 + u < S) {
+        const float e = expf(sc[u] - mn);
+        l += e;
+#pragma unroll
+        for (int i = 0; i < DV; ++i) acc[i] = fmaf(e, __ldg(V + (j0 + u) * D + lane + 32 * i), acc[i]);
+      }
+    }
+    m = mn;
+  }
+  const float inv = 1.0f / l;
+#pragma unroll
+  for (int i = 0; i < DV; ++i) out[(t * H + h) * D + lane + 32 * i] = acc[i] * inv;
+}
+
 // Decode attention in position splits (the same softmax, normalised at the
 // end): block (h, j) takes positions [j*ps, min(S, (j+1)*ps)) of query head h
 // (KV head h / nrep), with q pre-scaled and rounded as the reference does,
@@ -347,22 +463,18 @@ __global__ void kv_append_kernel(const float* __restrict__ k_new, const float* _
 constexpr int kAttnWarps = 4;
 constexpr int kAttnUnroll = 4;
 constexpr int kAttnMaxSplit = 8;
+// The split's work for query head q_h (D values) over cache rows [s0, s1)
+// of K / V (the KV head's rows from 0); writes D partials, m and l to pp.
 template <int DV>  // features per lane: D = 32 DV
-__global__ void attn_split_kernel(const float* __restrict__ q, const float* __restrict__ kc,
-                                  const float* __restrict__ vc, int64_t nrep, int64_t D,
-                                  int64_t max_seq, int64_t S, int64_t ps, float scale,
-                                  float* __restrict__ part) {
-  extern __shared__ float sc[];
-  __shared__ float sh[32];
-  __shared__ float qs[256];
-  griddep_launch_dependents();
-  griddep_wait();
-  const int64_t h = blockIdx.x, j = blockIdx.y, nsplit = gridDim.y, hkv = h / nrep;
-  const int64_t s0 = j * ps, s1 = min(S, s0 + ps), ns = max((int64_t)0, s1 - s0);
-  const float* K = kc + (hkv * max_seq + s0) * D;
-  const float* V = vc + (hkv * max_seq + s0) * D;
-  float* pp = part + (h * nsplit + j) * (D + 2);
-  for (int64_t dd = threadIdx.x; dd < D; dd += blockDim.x) qs[dd] = __fmul_rn(q[h * D + dd], scale);
+__device__ __forceinline__ void attn_split_body(const float* __restrict__ q_h,
+                                                const float* __restrict__ Kh,
+                                                const float* __restrict__ Vh, int64_t D,
+                                                int64_t s0, int64_t s1, float scale, float* pp,
+                                                float* sc, float* sh, float* qs, int64_t ps) {
+  const int64_t ns = max((int64_t)0, s1 - s0);
+  const float* K = Kh + s0 * D;
+  const float* V = Vh + s0 * D;
+  for (int64_t dd = threadIdx.x; dd < D; dd += blockDim.x) qs[dd] = __fmul_rn(q_h[dd], scale);
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // scores: positions warp, warp + 4, ... in batches of kAttnUnroll per warp
@@ -434,6 +546,71 @@ __global__ void attn_split_kernel(const float* __restrict__ q, const float* __re
   if (threadIdx.x == 0) {
     pp[D] = mx;
     pp[D + 1] = sum;
+  }
+}
+
+template <int DV>  // features per lane: D = 32 DV
+__global__ void attn_split_kernel(const float* __restrict__ q, const float* __restrict__ kc,
+                                  const float* __restrict__ vc, int64_t nrep, int64_t D,
+                                  int64_t max_seq, int64_t S, int64_t ps, float scale,
+                                  float* __restrict__ part) {
+  extern __shared__ float sc[];
+  __shared__ float sh[32];
+  __shared__ float qs[256];
+  griddep_launch_dependents();
+  griddep_wait();
+  const int64_t h = blockIdx.x, j = blockIdx.y, nsplit = gridDim.y, hkv = h / nrep;
+  const int64_t s0 = j * ps, s1 = min(S, s0 + ps);
+  attn_split_body<DV>(q + h * D, kc + hkv * max_seq * D, vc + hkv * max_seq * D, D, s0, s1, scale,
+                      part + (h * nsplit + j) * (D + 2), sc, sh, qs, ps);
+}
+
+// The same for B sequences at once, each at its own position read on the
+// device (so a captured step can be replayed token after token): block
+// (h, j, b) works on sequence b (q [B][H][D], caches [B][HKV][max_seq][D]);
+// the split length is ceil(S_b / nsplit) for S_b = pos[b] + 1, with shared
+// memory sized for S = max_seq.  A position outside [0, max_seq) leaves the
+// split empty (its partial has l = 0) and sets the error word.
+template <int DV>
+__global__ void attn_split_batch_kernel(const float* __restrict__ q, const float* __restrict__ kc,
+                                        const float* __restrict__ vc, const int32_t* __restrict__ pos,
+                                        int64_t H, int64_t nrep, int64_t D, int64_t max_seq,
+                                        int64_t ps_max, float scale, float* __restrict__ part,
+                                        int* err) {
+  extern __shared__ float sc[];
+  __shared__ float sh[32];
+  __shared__ float qs[256];
+  griddep_launch_dependents();
+  griddep_wait();
+  const int64_t h = blockIdx.x, j = blockIdx.y, nsplit = gridDim.y, b = blockIdx.z;
+  const int64_t p = pos[b];
+  const bool ok = p >= 0 && p < max_seq;
+  if (!ok && h == 0 && j == 0 && threadIdx.x == 0 && err) atomicExch(err, 4);
+  const int64_t S = ok ? p + 1 : 0;
+  const int64_t ps = (S + nsplit - 1) / nsplit;
+  const int64_t s0 = min(S, j * ps), s1 = min(S, s0 + ps);
+  const int64_t HKV = H / nrep, hkv = h / nrep;
+  const float* Kh = kc + ((b * HKV + hkv) * max_seq) * D;
+  const float* Vh = vc + ((b * HKV + hkv) * max_seq) * D;
+  attn_split_body<DV>(q + (b * H + h) * D, Kh, Vh, D, s0, s1, scale,
+                      part + ((b * H + h) * nsplit + j) * (D + 2), sc, sh, qs, ps_max);
+}
+
+// appendKV for B sequences at their device positions: row pos[b] of
+// sequence b's caches; one thread per element
+__global__ void kv_append_batch_kernel(const float* __restrict__ k_new, const float* __restrict__ v_new,
+                                       float* __restrict__ kc, float* __restrict__ vc,
+                                       const int32_t* __restrict__ pos, int64_t B, int64_t HKV,
+                                       int64_t D, int64_t max_seq) {
+  griddep_launch_dependents();
+  griddep_wait();
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < B * HKV * D;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = i / (HKV * D), r = i - b * HKV * D, h = r / D, dd = r - h * D;
+    const int64_t p = pos[b];
+    if (p < 0 || p >= max_seq) continue;
+    kc[((b * HKV + h) * max_seq + p) * D + dd] = k_new[i];
+    vc[((b * HKV + h) * max_seq + p) * D + dd] = v_new[i];
   }
 }
 
@@ -654,6 +831,117 @@ int nimf_attention_decode_dev(const float* q, const float* k_new, const float* v
                                      (const float*)v_cache, H / HKV, D, max_seq, S, ps, scale, part));
   }
   NIMF_TRY(launch_pdl(attn_combine_kernel, (unsigned)H, 128, 0, st, (const float*)part, nsplit, D, out));
+  return NIMF_OK;
+}
+
+int nimf_attention_prefill_dev(const float* q, const float* k_new, const float* v_new,
+                               float* k_cache, float* v_cache, int64_t T, int64_t H, int64_t HKV,
+                               int64_t D, int64_t max_seq, int64_t pos0, float scale, float* out,
+                               void* stream) {
+  cudaStream_t st;
+  NIMF_TRY(stream_of(stream, &st));
+  if (T < 0 || H <= 0 || HKV <= 0 || H % HKV || D <= 0 || D > 256 || D % 32 || pos0 < 0 ||
+      pos0 + T > max_seq || H > 65535)
+    return set_error(NIMF_ERR_SHAPE,
+                     "prefill attention: T %lld H %lld HKV %lld D %lld (a multiple of 32, <= 256) "
+                     "pos0 %lld max_seq %lld",
+                     (long long)T, (long long)H, (long long)HKV, (long long)D, (long long)pos0,
+                     (long long)max_seq);
+  if (T == 0) return NIMF_OK;
+  if (!q || !k_new || !v_new || !k_cache || !v_cache || !out)
+    return set_error(NIMF_ERR_ARG, "prefill attention: NULL buffer");
+  NIMF_TRY(launch_pdl(kv_append_rows_kernel, grid_n(T * HKV * D), 256, 0, st, k_new, v_new,
+                      k_cache, v_cache, T, HKV, D, max_seq, pos0));
+  void (*kern)(const float*, const float*, const float*, int64_t, int64_t, int64_t, int64_t,
+               int64_t, float, float*);
+  switch (D / 32) {
+    case 1: kern = attn_prefill_kernel<1>; break;
+    case 2: kern = attn_prefill_kernel<2>; break;
+    case 3: kern = attn_prefill_kernel<3>; break;
+    case 4: kern = attn_prefill_kernel<4>; break;
+    case 5: kern = attn_prefill_kernel<5>; break;
+    case 6: kern = attn_prefill_kernel<6>; break;
+    case 7: kern = attn_prefill_kernel<7>; break;
+    default: kern = attn_prefill_kernel<8>; break;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((T + kPrefWarps - 1) / kPrefWarps), (unsigned)H);
+  cfg.blockDim = dim3(kPrefWarps * 32);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  NIMF_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, q, (const float*)k_cache, (const float*)v_cache, T,
+                                   H, H / HKV, max_seq, pos0, scale, out));
+  return NIMF_OK;
+}
+
+int nimf_attention_decode_batch_dev(float* q, float* k_new, const float* v_new, float* k_cache,
+                                    float* v_cache, int64_t B, int64_t H, int64_t HKV, int64_t D,
+                                    int64_t max_seq, int32_t* pos_dev, const float* cos_t,
+                                    const float* sin_t, float scale, int advance_pos, float* out,
+                                    void* stream) {
+  cudaStream_t st;
+  NIMF_TRY(stream_of(stream, &st));
+  Context* c = ctx();
+  if (B < 0 || H <= 0 || HKV <= 0 || H % HKV || D <= 0 || D > 256 || D % 32 || max_seq < 1 ||
+      max_seq > 8 * 40000 || B * H > 65535 * 8)
+    return set_error(NIMF_ERR_SHAPE,
+                     "batch attention: B %lld H %lld HKV %lld D %lld (a multiple of 32, <= 256) "
+                     "max_seq %lld",
+                     (long long)B, (long long)H, (long long)HKV, (long long)D, (long long)max_seq);
+  if (B == 0) return NIMF_OK;
+  if (!q || !k_new || !v_new || !k_cache || !v_cache || !out || !pos_dev || (!cos_t != !sin_t))
+    return set_error(NIMF_ERR_ARG, "batch attention: NULL buffer");
+  if (cos_t) {
+    NIMF_TRY(launch_pdl(rope_batch_kernel, grid_n(B * H * D / 2), 256, 0, st, q, B, H, D,
+                        (const int32_t*)pos_dev, max_seq, cos_t, sin_t));
+    NIMF_TRY(launch_pdl(rope_batch_kernel, grid_n(B * HKV * D / 2), 256, 0, st, k_new, B, HKV, D,
+                        (const int32_t*)pos_dev, max_seq, cos_t, sin_t));
+  }
+  NIMF_TRY(launch_pdl(kv_append_batch_kernel, grid_n(B * HKV * D), 256, 0, st,
+                      (const float*)k_new, v_new, k_cache, v_cache, (const int32_t*)pos_dev, B,
+                      HKV, D, max_seq));
+  // splits fixed by max_seq (the positions are only known on the device)
+  const int64_t nsplit = std::min<int64_t>(kAttnMaxSplit, (max_seq + 63) / 64);
+  const int64_t ps_max = (max_seq + nsplit - 1) / nsplit;
+  const size_t smem = (size_t)(ps_max + kAttnWarps * D) * 4;
+  void (*kern)(const float*, const float*, const float*, const int32_t*, int64_t, int64_t, int64_t,
+               int64_t, int64_t, float, float*, int*);
+  switch (D / 32) {
+    case 1: kern = attn_split_batch_kernel<1>; break;
+    case 2: kern = attn_split_batch_kernel<2>; break;
+    case 3: kern = attn_split_batch_kernel<3>; break;
+    case 4: kern = attn_split_batch_kernel<4>; break;
+    case 5: kern = attn_split_batch_kernel<5>; break;
+    case 6: kern = attn_split_batch_kernel<6>; break;
+    case 7: kern = attn_split_batch_kernel<7>; break;
+    default: kern = attn_split_batch_kernel<8>; break;
+  }
+  if (smem > 48 * 1024)
+    NIMF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+  float* part = nullptr;
+  NIMF_TRY(attn_buffer((size_t)(B * H * nsplit * (D + 2)) * 4, st, &part));
+  {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)H, (unsigned)nsplit, (unsigned)B);
+    cfg.blockDim = dim3(kAttnWarps * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    NIMF_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, (const float*)q, (const float*)k_cache,
+                                     (const float*)v_cache, (const int32_t*)pos_dev, H, H / HKV, D,
+                                     max_seq, ps_max, scale, part, c ? c->dev_err : nullptr));
+  }
+  NIMF_TRY(launch_pdl(attn_combine_kernel, (unsigned)(B * H), 128, 0, st, (const float*)part,
+                      nsplit, D, out));
+  if (advance_pos) NIMF_TRY(launch_pdl(advance_pos_kernel, 1, 32, 0, st, pos_dev, B));
   return NIMF_OK;
 }
 

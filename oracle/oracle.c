@@ -782,3 +782,53 @@ void orc_attention_decode(const float* q, const float* k_new, const float* v_new
   free(sc);
   free(og);
 }
+
+/* nim_inference.nim:574-620 forwardPrefill's attention core, generalised to a
+ * chunk of T prompt tokens at positions pos0 .. pos0 + T - 1: appendKV
+ * (:404-426) of the T new K / V rows [T][HKV][D] into the caches
+ * [HKV][max_seq][D], then for each query head h (KV head h / (H / HKV), the
+ * repeat_kv expansion of :596-606) and query t, the causal softmax attention
+ * of vendor/bybylang/gpubackend.nim:171-201 cpuAttentionFused over cache rows
+ * 0 .. pos0 + t: score = (q . k) * scale with the dot summed over d in order,
+ * max, exp(score - max) summed in order, p = e / sum, out = sum_j p_j v_j in
+ * order.  q and out are [T][H][D] (the projections' row layout). */
+void orc_attention_prefill(const float* q, const float* k_new, const float* v_new,
+                           float* k_cache, float* v_cache, int64_t T, int64_t H, int64_t HKV,
+                           int64_t D, int64_t max_seq, int64_t pos0, float scale, float* out) {
+  int64_t nrep = H / HKV;
+  for (int64_t t = 0; t < T; ++t)
+    for (int64_t h = 0; h < HKV; ++h)
+      for (int64_t d = 0; d < D; ++d) {
+        k_cache[(h * max_seq + pos0 + t) * D + d] = k_new[(t * HKV + h) * D + d];
+        v_cache[(h * max_seq + pos0 + t) * D + d] = v_new[(t * HKV + h) * D + d];
+      }
+  float* sc = (float*)malloc((size_t)(pos0 + T) * sizeof(float));
+  for (int64_t h = 0; h < H; ++h) {
+    const int64_t hk = h / nrep;
+    const float* K = k_cache + hk * max_seq * D;
+    const float* V = v_cache + hk * max_seq * D;
+    for (int64_t t = 0; t < T; ++t) {
+      const float* qr = q + (t * H + h) * D;
+      const int64_t S = pos0 + t + 1;
+      float mx = -1e30f;
+      for (int64_t j = 0; j < S; ++j) {
+        float dot = 0.0f;
+        for (int64_t d = 0; d < D; ++d) dot += qr[d] * K[j * D + d];
+        sc[j] = dot * scale;
+        if (sc[j] > mx) mx = sc[j];
+      }
+      float sum = 0.0f;
+      for (int64_t j = 0; j < S; ++j) {
+        sc[j] = expf(sc[j] - mx);
+        sum += sc[j];
+      }
+      for (int64_t j = 0; j < S; ++j) sc[j] /= sum;
+      for (int64_t d = 0; d < D; ++d) {
+        float acc = 0.0f;
+        for (int64_t j = 0; j < S; ++j) acc += sc[j] * V[j * D + d];
+        out[(t * H + h) * D + d] = acc;
+      }
+    }
+  }
+  free(sc);
+}

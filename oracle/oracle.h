@@ -183,6 +183,14 @@ void orc_attention_decode(const float* q, const float* k_new, const float* v_new
                           float* k_cache, float* v_cache, int64_t H, int64_t HKV, int64_t D,
                           int64_t max_seq, int64_t pos, float scale, float* out);
 
+/* forwardPrefill's attention (nim_inference.nim:574-620) for T prompt tokens at
+ * positions pos0 ..: appendKV, then causal cpuAttentionFused
+ * (vendor/bybylang/gpubackend.nim:171-201) per query head; q, out [T][H][D],
+ * k_new / v_new [T][HKV][D], caches [HKV][max_seq][D]. */
+void orc_attention_prefill(const float* q, const float* k_new, const float* v_new,
+                           float* k_cache, float* v_cache, int64_t T, int64_t H, int64_t HKV,
+                           int64_t D, int64_t max_seq, int64_t pos0, float scale, float* out);
+
 #ifdef __cplusplus
 }
 #endif

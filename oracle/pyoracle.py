@@ -72,6 +72,8 @@ def lib():
             "orc_rope": (None, [_f32p, _i64, _i64, _i64, _i64, _i64, _f32p, _f32p]),
             "orc_attention_decode": (None, [_f32p, _f32p, _f32p, _f32p, _f32p, _i64, _i64, _i64,
                                             _i64, _i64, ctypes.c_float, _f32p]),
+            "orc_attention_prefill": (None, [_f32p, _f32p, _f32p, _f32p, _f32p, _i64, _i64, _i64,
+                                             _i64, _i64, _i64, ctypes.c_float, _f32p]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -325,6 +327,17 @@ def rope(data, B, T, H, D, pos_offset, cos_t, sin_t):
     d = np.array(data, np.float32).ravel()
     lib().orc_rope(d, B, T, H, D, pos_offset, _c(cos_t, np.float32).ravel(), _c(sin_t, np.float32).ravel())
     return d
+
+
+def attention_prefill(q, k_new, v_new, k_cache, v_cache, T, H, HKV, D, max_seq, pos0, scale):
+    """Returns (out[T*H*D], k_cache, v_cache) with rows pos0 .. pos0+T-1 appended."""
+    kc = np.array(k_cache, np.float32).ravel()
+    vc = np.array(v_cache, np.float32).ravel()
+    out = np.empty(T * H * D, np.float32)
+    lib().orc_attention_prefill(_c(q, np.float32).ravel(), _c(k_new, np.float32).ravel(),
+                                _c(v_new, np.float32).ravel(), kc, vc, T, H, HKV, D, max_seq, pos0,
+                                ctypes.c_float(scale), out)
+    return out, kc, vc
 
 
 def attention_decode(q, k_new, v_new, k_cache, v_cache, H, HKV, D, max_seq, pos, scale):

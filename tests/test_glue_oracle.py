@@ -98,3 +98,31 @@ def test_greedy_and_embedding_match_reference_loops():
     out = O.embedding_lookup(table, ids)
     ref = np.stack([table[i] if 0 <= i < 10 else np.zeros(6, np.float32) for i in ids])
     assert np.array_equal(out, ref)
+
+
+def test_prefill_attention_oracle_against_float64():
+    """orc_attention_prefill (cpuAttentionFused, causal, with appendKV) within
+    float32 rounding of a float64 evaluation, GQA and a chunk at pos0 > 0; the
+    appended rows are the new K / V rows and earlier rows are untouched."""
+    rng = np.random.default_rng(3)
+    H, HKV, D, MS, T, pos0 = 6, 3, 64, 40, 11, 7
+    kc = rng.standard_normal(HKV * MS * D).astype(np.float32)
+    vc = rng.standard_normal(HKV * MS * D).astype(np.float32)
+    q = rng.standard_normal(T * H * D).astype(np.float32)
+    kn = rng.standard_normal(T * HKV * D).astype(np.float32)
+    vn = rng.standard_normal(T * HKV * D).astype(np.float32)
+    out, kc2, vc2 = O.attention_prefill(q, kn, vn, kc, vc, T, H, HKV, D, MS, pos0, 0.125)
+    K, V = kc2.reshape(HKV, MS, D), vc2.reshape(HKV, MS, D)
+    assert np.array_equal(K[:, :pos0], kc.reshape(HKV, MS, D)[:, :pos0])
+    assert np.array_equal(K[:, pos0:pos0 + T], kn.reshape(T, HKV, D).transpose(1, 0, 2))
+    assert np.array_equal(V[:, pos0:pos0 + T], vn.reshape(T, HKV, D).transpose(1, 0, 2))
+    Q = q.reshape(T, H, D).astype(np.float64)
+    ref = np.zeros((T, H, D))
+    for h in range(H):
+        for t in range(T):
+            S = pos0 + t + 1
+            sc = (K[h // 2, :S].astype(np.float64) @ Q[t, h]) * 0.125
+            pr = np.exp(sc - sc.max())
+            pr /= pr.sum()
+            ref[t, h] = pr @ V[h // 2, :S].astype(np.float64)
+    assert np.max(np.abs(out.reshape(T, H, D) - ref)) <= 1e-5 * np.max(np.abs(ref))

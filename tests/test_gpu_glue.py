@@ -153,6 +153,91 @@ def test_attention_decode(nimf_gpu, torch_dev, H, HKV, pos):
                                                    D, max_seq, max_seq, float(scale), p(out), None))
 
 
+@pytest.mark.parametrize("T,H,HKV,D,pos0", [(37, 4, 2, 64, 0), (16, 8, 8, 128, 20), (1, 4, 1, 32, 9),
+                                            (512, 32, 32, 128, 0), (40, 6, 3, 256, 100)])
+def test_attention_prefill(nimf_gpu, torch_dev, T, H, HKV, D, pos0):
+    """nimf_attention_prefill_dev: the appended cache rows bit-exact (earlier
+    rows untouched) and the causal attention within 1e-4 of max|out| of the
+    oracle's cpuAttentionFused restatement, including GQA, a later chunk
+    (pos0 > 0), one token, head_dim 256 and the 7B prompt (512 x 32 x 128)."""
+    torch = torch_dev
+    L = nimf_gpu.lib()
+    rng = np.random.default_rng(T * 7 + H)
+    max_seq = pos0 + T + 3
+    kc = rng.standard_normal(HKV * max_seq * D).astype(np.float32)
+    vc = rng.standard_normal(HKV * max_seq * D).astype(np.float32)
+    q = rng.standard_normal(T * H * D).astype(np.float32)
+    kn = rng.standard_normal(T * HKV * D).astype(np.float32)
+    vn = rng.standard_normal(T * HKV * D).astype(np.float32)
+    scale = float(np.float32(1.0 / np.sqrt(np.float32(D))))
+    dkc, dvc = dev(torch, kc), dev(torch, vc)
+    dq, dkn, dvn = dev(torch, q), dev(torch, kn), dev(torch, vn)
+    out = torch.empty(T * H * D, device="cuda")
+    nimf_gpu.check(L.nimf_attention_prefill_dev(p(dq), p(dkn), p(dvn), p(dkc), p(dvc), T, H, HKV, D,
+                                                max_seq, pos0, scale, p(out), None))
+    torch.cuda.synchronize()
+    ref, rkc, rvc = O.attention_prefill(q, kn, vn, kc, vc, T, H, HKV, D, max_seq, pos0, scale)
+    assert np.array_equal(dkc.cpu().numpy().view(np.uint32), rkc.view(np.uint32))
+    assert np.array_equal(dvc.cpu().numpy().view(np.uint32), rvc.view(np.uint32))
+    assert rel_err(out.cpu().numpy(), ref) <= TOL
+    with pytest.raises(nimf_gpu.CatchableError, match="SHAPE"):
+        nimf_gpu.check(L.nimf_attention_prefill_dev(p(dq), p(dkn), p(dvn), p(dkc), p(dvc), T, H, HKV,
+                                                    D, max_seq, max_seq - T + 1, scale, p(out), None))
+
+
+def test_attention_decode_batch_device_positions(nimf_gpu, torch_dev):
+    """nimf_attention_decode_batch_dev: three sequences at different positions
+    read on the device, RoPE applied in place to q and k_new (bit-exact with
+    the oracle's applyRoPEInplace), each sequence's cache row appended
+    bit-exactly and its attention within 1e-4 of the oracle's forwardDecode
+    core; advance_pos moves every position by one; a position past max_seq
+    appends nothing and is reported by nimf_sync."""
+    torch = torch_dev
+    L = nimf_gpu.lib()
+    rng = np.random.default_rng(17)
+    B, H, HKV, D, MS = 3, 8, 4, 128, 64
+    pos = np.array([5, 17, 0], np.int32)
+    kc = rng.standard_normal((B, HKV * MS * D)).astype(np.float32)
+    vc = rng.standard_normal((B, HKV * MS * D)).astype(np.float32)
+    q = rng.standard_normal((B, H * D)).astype(np.float32)
+    kn = rng.standard_normal((B, HKV * D)).astype(np.float32)
+    vn = rng.standard_normal((B, HKV * D)).astype(np.float32)
+    half = D // 2
+    inv = 1.0 / np.power(np.float32(10000.0), np.arange(half, dtype=np.float32) / np.float32(half))
+    ang = np.arange(MS, dtype=np.float32)[:, None] * inv[None, :].astype(np.float32)
+    cos_t, sin_t = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    scale = float(np.float32(1.0 / np.sqrt(np.float32(D))))
+    dq, dkn, dvn = dev(torch, q), dev(torch, kn), dev(torch, vn)
+    dkc, dvc = dev(torch, kc), dev(torch, vc)
+    dcos, dsin = dev(torch, cos_t), dev(torch, sin_t)
+    dpos = torch.from_numpy(pos).cuda()
+    out = torch.empty(B, H * D, device="cuda")
+    nimf_gpu.check(L.nimf_attention_decode_batch_dev(p(dq), p(dkn), p(dvn), p(dkc), p(dvc), B, H, HKV,
+                                                     D, MS, p(dpos), p(dcos), p(dsin), scale, 1,
+                                                     p(out), None))
+    torch.cuda.synchronize()
+    nimf_gpu.check(L.nimf_sync())
+    assert dpos.cpu().numpy().tolist() == (pos + 1).tolist()
+    for b in range(B):
+        qr = O.rope(q[b], 1, 1, H, D, int(pos[b]), cos_t, sin_t)
+        kr = O.rope(kn[b], 1, 1, HKV, D, int(pos[b]), cos_t, sin_t)
+        assert np.array_equal(dq[b].cpu().numpy().view(np.uint32), qr.view(np.uint32))
+        assert np.array_equal(dkn[b].cpu().numpy().view(np.uint32), kr.view(np.uint32))
+        ref, rkc, rvc = O.attention_decode(qr, kr, vn[b], kc[b], vc[b], H, HKV, D, MS, int(pos[b]),
+                                           scale)
+        assert np.array_equal(dkc[b].cpu().numpy().view(np.uint32), rkc.view(np.uint32))
+        assert np.array_equal(dvc[b].cpu().numpy().view(np.uint32), rvc.view(np.uint32))
+        assert rel_err(out[b].cpu().numpy(), ref) <= TOL
+    # a position outside the cache: nothing appended, reported as an expired-wait class error
+    bad = torch.tensor([MS, 3, 4], dtype=torch.int32, device="cuda")
+    before = dkc[0].clone()
+    nimf_gpu.check(L.nimf_attention_decode_batch_dev(p(dq), p(dkn), p(dvn), p(dkc), p(dvc), B, H, HKV,
+                                                     D, MS, p(bad), None, None, scale, 0, p(out), None))
+    torch.cuda.synchronize()
+    assert L.nimf_sync() == -5
+    assert torch.equal(before, dkc[0])
+
+
 def test_embedding_and_greedy(nimf_gpu, torch_dev):
     """nimf_embedding_lookup_dev (zeros for ids out of range) bit-exact, and
     nimf_greedy_sample_dev giving the oracle's token ids: the penalised
