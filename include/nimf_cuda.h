@@ -361,7 +361,10 @@ typedef struct nimf_decode_desc {
   const nimf_decode_layer_desc* layers; /* host array of n_layers (copied) */
 } nimf_decode_desc;
 
-/* Builds the step's stage table and its device scratch (a few hundred KB). */
+/* Builds the step's stage table and its device scratch (a few hundred KB).
+ * The environment variable NIMF_DECODE_L2_AHEAD (0 .. 16, default 2), read
+ * here, sets how many of its items each weight-streaming lane prefetches into
+ * L2 ahead of its shared-memory ring (0: none). */
 int nimf_decode_create(const nimf_decode_desc* desc, int64_t* plan);
 /* The same step N-sharded over the communicator's GPUs (nimf_comm_init; no
  * counterpart in the reference, which has no multi-GPU path).  Collective:

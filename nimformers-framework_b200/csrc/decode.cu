@@ -46,6 +46,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -158,6 +159,7 @@ struct DecArgs {
   int h0, hk0, hloc;        // first query / KV head and query heads of this rank
   long long peer_off[kMaxRanks];
   unsigned* gctl;
+  int l2_ahead;             // producer items (per lane) prefetched into L2 ahead of the ring
 };
 
 template <typename T>
@@ -271,6 +273,68 @@ __device__ __forceinline__ int prob_of(const DecStage& st, int grt) {
   int p = 0;
   while (p + 1 < st.nprob && grt >= st.rt_prefix[p + 1]) ++p;
   return p;
+}
+
+// Global sources and sizes of item i (row tile i / nkb, k-block i % nkb) of
+// GEMV stage st for the CTA whose row tiles start at rt0.
+struct ItemSrc {
+  const uint4* w;
+  const float4* z;
+  uint32_t wb, zb;
+};
+__device__ __forceinline__ ItemSrc item_src(const DecStage& st, int rt0, int i) {
+  const int nkb = __ldg(&st.nkb), groups = __ldg(&st.groups);
+  const int rti = i / nkb, kb = i - rti * nkb;
+  const int grt = rt0 + rti;
+  const int p = prob_of(st, grt);
+  const int rt = grt - __ldg(&st.rt_prefix[p]);
+  const int ngk = min(kKbg, groups - kb * kKbg);
+  const uint4* fr = reinterpret_cast<const uint4*>(__ldg(reinterpret_cast<const unsigned long long*>(&st.frag[p])));
+  const float4* sz = reinterpret_cast<const float4*>(__ldg(reinterpret_cast<const unsigned long long*>(&st.sz[p])));
+  ItemSrc r;
+  r.w = fr + ((size_t)rt * groups * kKQG + (size_t)kb * kKbg * kKQG) * 32;
+  r.z = sz + ((size_t)rt * groups + (size_t)kb * kKbg) * 8;
+  r.wb = (uint32_t)ngk * kKQG * 512u;
+  r.zb = (uint32_t)ngk * 128u;
+  return r;
+}
+
+// A producer lane's position in its item sequence (global items q = lane
+// mod kIssuers over every GEMV stage of the step, in order), used to look
+// ahead for L2 prefetches.
+struct LaneCursor {
+  int s, q0, nstg, rt0, i;
+  bool valid;
+};
+// Moves to GEMV stage s or the next one after it, starting at global item
+// q0; the lane's first item there is `want` (a global index >= q0).
+__device__ void cursor_seek(const DecArgs& a, LaneCursor& c, int s, int q0, int want, int cid, int G) {
+  for (; s < a.nstages; ++s) {
+    const DecStage& st = a.stages[s];
+    if (__ldg(&st.kind) != ST_GEMV) continue;
+    int nrt;
+    row_split(__ldg(&st.n_rt), cid, G, &c.rt0, &nrt);
+    const int nstg = nrt * __ldg(&st.nkb);
+    if (want < q0 + nstg) {
+      c.s = s;
+      c.q0 = q0;
+      c.nstg = nstg;
+      c.i = want - q0;
+      c.valid = true;
+      return;
+    }
+    q0 += nstg;
+  }
+  c.valid = false;
+}
+__device__ __forceinline__ void cursor_next(const DecArgs& a, LaneCursor& c, int cid, int G) {
+  if (!c.valid) return;
+  const int want = c.q0 + c.i + kIssuers;
+  if (want < c.q0 + c.nstg) {
+    c.i = want - c.q0;
+    return;
+  }
+  cursor_seek(a, c, c.s + 1, c.q0 + c.nstg, want, cid, G);
 }
 
 // consumer-wide reductions (512 threads, named barrier 1)
@@ -634,33 +698,38 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecArgs 
     if (lane < kIssuers) {
       bool ok = true;
       int q0 = 0, issued_last = -1;
+      // L2 look-ahead: while the ring is full (consumers at a grid barrier),
+      // DRAM keeps streaming the weights of this lane's item l2_ahead places
+      // further on into L2, so the later bulk copy reads L2
+      LaneCursor ahead;
+      cursor_seek(a, ahead, 0, 0, lane, cid, G);
+      for (int j = 0; j < a.l2_ahead && ahead.valid; ++j) cursor_next(a, ahead, cid, G);
+      if (a.l2_ahead <= 0) ahead.valid = false;
       for (int s = 0; s < nst && ok; ++s) {
         const DecStage& st = a.stages[s];
         if (__ldg(&st.kind) != ST_GEMV) continue;
         int rt0, nrt;
         row_split(__ldg(&st.n_rt), cid, G, &rt0, &nrt);
-        const int nkb = __ldg(&st.nkb), groups = __ldg(&st.groups);
-        const int nstg = nrt * nkb;
+        const int nstg = nrt * __ldg(&st.nkb);
         const int first = ((lane - q0) % kIssuers + kIssuers) % kIssuers;
         for (int i = first; i < nstg; i += kIssuers) {
           const int qq = q0 + i;
           const int slot = qq % kNS;
+          if (ahead.valid) {
+            const ItemSrc pf = item_src(a.stages[ahead.s], ahead.rt0, ahead.i);
+            bulk_prefetch_l2(pf.w, pf.wb);
+            bulk_prefetch_l2(pf.z, pf.zb);
+            cursor_next(a, ahead, cid, G);
+          }
           if (qq >= kNS && !dwait<-32>(a, &empty[slot], ((qq / kNS) - 1) & 1)) {
             ok = false;
             break;
           }
-          const int rti = i / nkb, kb = i - rti * nkb;
-          const int grt = rt0 + rti;
-          const int p = prob_of(st, grt);
-          const int rt = grt - __ldg(&st.rt_prefix[p]);
-          const int ngk = min(kKbg, groups - kb * kKbg);
-          const uint32_t wb = (uint32_t)ngk * kKQG * 512u, zb = (uint32_t)ngk * 128u;
+          const ItemSrc src = item_src(st, rt0, i);
           unsigned char* dst = ring + (size_t)slot * kStageBytes;
-          const uint4* fr = reinterpret_cast<const uint4*>(__ldg(reinterpret_cast<const unsigned long long*>(&st.frag[p])));
-          const float4* sz = reinterpret_cast<const float4*>(__ldg(reinterpret_cast<const unsigned long long*>(&st.sz[p])));
-          mbar_arrive_expect_tx(&full[slot], wb + zb);
-          bulk_g2s(dst, fr + ((size_t)rt * groups * kKQG + (size_t)kb * kKbg * kKQG) * 32, wb, &full[slot]);
-          bulk_g2s(dst + kStageW, sz + ((size_t)rt * groups + (size_t)kb * kKbg) * 8, zb, &full[slot]);
+          mbar_arrive_expect_tx(&full[slot], src.wb + src.zb);
+          bulk_g2s(dst, src.w, src.wb, &full[slot]);
+          bulk_g2s(dst + kStageW, src.z, src.zb, &full[slot]);
           issued_last = qq;
         }
         q0 += nstg;
@@ -1238,6 +1307,10 @@ int create_plan(const nimf_decode_desc* d, int world, int rank, int64_t* plan_ou
   A.gctl = (unsigned*)(sb + o_gctl);
   A.world = world;
   A.rank = rank;
+  // L2 look-ahead of the producer lanes, in items of up to 36 KB per lane
+  // (NIMF_DECODE_L2_AHEAD, 0 .. 16; default 2: 8 ring stages ahead per SM)
+  A.l2_ahead = 2;
+  if (const char* ev = getenv("NIMF_DECODE_L2_AHEAD")) A.l2_ahead = std::max(0, std::min(16, atoi(ev)));
   A.hloc = (int)(H / world);
   A.h0 = (int)(rank * (H / world));
   A.hk0 = (int)(rank * (HKV / world));
