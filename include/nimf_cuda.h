@@ -220,6 +220,19 @@ int nimf_matmul2_f32(const float* a1, int64_t m1, int64_t k1, const float* b1, i
  * quant.nim:162), so a bit-exact comparison with dequantizeTensor is possible. */
 int nimf_dequant_w(nimf_weight_t w, float* out_host);
 
+/* Which tensor-core GEMM serves int4 group weights at more than 16 rows of x
+ * (prefill).  No reference counterpart (the reference dequantises on the host,
+ * gpubackend.nim:628-653).  AUTO (default): the fp16-tile GEMM, where each
+ * weight is dequantised into fp16 tiles ((nibble - zp) * scale times a
+ * per-weight power of two) and one fp32 accumulator runs over K, for weights
+ * whose values fit fp16 tiles, else the exact-nibble GEMM; EXACT: always the
+ * exact-nibble GEMM (nibbles exact in fp16, an fp32 epilogue per group).
+ * Both keep max|y - y_ref| / max|y_ref| within 1e-3; the exact form is about
+ * 2e-4, the fp16 tiles about 3e-4 at K = 4096. */
+#define NIMF_Q4_PREFILL_AUTO 0
+#define NIMF_Q4_PREFILL_EXACT 1
+int nimf_q4_prefill_mode(int mode);
+
 /* ------------------------------------------------------------ decode glue */
 /* The steps between the linears of a Llama-style decode step
  * (nim_inference.nim), on DEVICE buffers and asynchronous on `stream`, so the

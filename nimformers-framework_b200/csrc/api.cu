@@ -765,6 +765,13 @@ int nimf_matmul_q4(const float* a, const uint8_t* wq, const float* scales, const
   return nimf_matmul_w(h, a, m, out);
 }
 
+int nimf_q4_prefill_mode(int mode) {
+  if (mode != NIMF_Q4_PREFILL_AUTO && mode != NIMF_Q4_PREFILL_EXACT)
+    return set_error(NIMF_ERR_ARG, "q4_prefill_mode: %d is not AUTO (0) or EXACT (1)", mode);
+  g_q4_prefill_mode = mode;
+  return NIMF_OK;
+}
+
 int nimf_q4_cache_set_check(int mode) {
   if (mode != NIMF_Q4_CACHE_CHECK_FULL && mode != NIMF_Q4_CACHE_CHECK_SAMPLED &&
       mode != NIMF_Q4_CACHE_CHECK_NONE)

@@ -45,6 +45,8 @@ struct Q4GWeight {
   int64_t rows = 0, k = 0, gs = 0, ngr = 0;
   bool fast = false;
   bool tc_zp_ok = false;  // every zero point finite with |zp| < 60000 (tensor-core GEMM)
+  bool tc16_ok = false;   // (n - zp) * sc * 2^tc16_exp fits fp16 tiles (fp16-tile GEMM)
+  int tc16_exp = 0;
   int64_t n_rt = 0, kq_total = 0, groups = 0;
   void* frag = nullptr;   // uint4*
   void* sz = nullptr;     // float4*
@@ -180,6 +182,13 @@ int tc_prep_buffer(size_t bytes, cudaStream_t st, unsigned char** out);
 void release_prep_buffers();
 int q4g_gemm_tc_group(const Q4GWeight* const* ws, int count, const float* x, int64_t m,
                       float* const* ys, cudaStream_t st);
+// Prefill GEMM with the weights dequantised into fp16 tiles and one
+// accumulator over K (q4g_tc16.cu); used when every weight qualifies and the
+// mode (nimf_q4_prefill_mode) allows it.
+bool q4g_tc16_supported(const Q4GWeight& w);
+int q4g_gemm_tc16_group(const Q4GWeight* const* ws, int count, const float* x, int64_t m,
+                        float* const* ys, cudaStream_t st);
+extern int g_q4_prefill_mode;   // NIMF_Q4_PREFILL_*
 
 int i8_gemv(const I8Weight& w, const float* x, int64_t m, float* y, cudaStream_t st);
 int i8_dequant(const I8Weight& w, float* out, cudaStream_t st);

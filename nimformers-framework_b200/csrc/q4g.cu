@@ -29,6 +29,8 @@
 #include <cooperative_groups.h>
 
 #include <algorithm>
+#include <cmath>
+#include <cstring>
 
 #include "device_util.cuh"
 #include "nimf_internal.h"
@@ -118,12 +120,23 @@ __global__ void q4g_repack_sz(const float* __restrict__ sc, const float* __restr
 
 // *bad = 1 if a zero point is not finite or |zp| >= 60000 (the tensor-core
 // GEMM carries zp + 64 as two fp16 parts).
-__global__ void q4g_zp_range(const float* __restrict__ zp, int64_t ngr, int64_t rows,
-                             int* __restrict__ bad) {
+// Registration checks of the tensor-core paths, over every (row, group):
+// st[0] = 1 if a zero point is not finite or |zp| >= 60000 (the exact-nibble
+// GEMM splits 64 + zp into two fp16 parts); st[1] = the largest dequantised
+// magnitude sc * max(|zp|, |15 - zp|) and st[2] = the smallest non-zero |sc|,
+// as float bits (non-negative floats order like their bits), for the
+// fp16-tile GEMM's range check.
+__global__ void q4g_zp_range(const float* __restrict__ sc, const float* __restrict__ zp,
+                             int64_t ngr, int64_t rows, unsigned* __restrict__ st) {
   const int64_t n = rows * ngr;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x)
-    if (!(fabsf(zp[i]) < 60000.0f)) *bad = 1;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float z = zp[i], a = fabsf(sc[i]);
+    if (!(fabsf(z) < 60000.0f)) st[0] = 1u;
+    const float m = a * fmaxf(fabsf(z), fabsf(15.0f - z));
+    atomicMax(&st[1], m == m ? __float_as_uint(m) : 0x7F800000u);   // NaN counts as inf
+    if (a > 0.0f) atomicMin(&st[2], a == a ? __float_as_uint(a) : 0x7F800000u);
+  }
 }
 
 // out[r][c] = (float(nib) - zp) * sc with the reference's two roundings
@@ -866,21 +879,36 @@ int q4g_build(Weight* wt, const uint8_t* wq_dev, const float* sc_dev, const floa
                                                       (float4*)w.sz);
     NIMF_CUDA_TRY(cudaGetLastError());
     w.tc_zp_ok = false;
+    w.tc16_ok = false;
     if (rows * ngr > 0) {
-      int* bad = nullptr;
-      NIMF_TRY(device_alloc((void**)&bad, sizeof(int)));
-      int hb = 0;
-      cudaError_t e = cudaMemsetAsync(bad, 0, sizeof(int), st);
+      unsigned* stats = nullptr;
+      NIMF_TRY(device_alloc((void**)&stats, 3 * sizeof(unsigned)));
+      unsigned hs[3] = {0u, 0u, 0x7F800000u};
+      cudaError_t e = cudaMemcpyAsync(stats, hs, sizeof(hs), cudaMemcpyHostToDevice, st);
       if (e == cudaSuccess) {
         const int64_t n = rows * ngr;
-        q4g_zp_range<<<(unsigned)std::min<int64_t>((n + 255) / 256, 1024), 256, 0, st>>>(zps, ngr, rows, bad);
+        q4g_zp_range<<<(unsigned)std::min<int64_t>((n + 255) / 256, 1024), 256, 0, st>>>(scs, zps, ngr, rows, stats);
         e = cudaGetLastError();
       }
-      if (e == cudaSuccess) e = cudaMemcpyAsync(&hb, bad, sizeof(int), cudaMemcpyDeviceToHost, st);
+      if (e == cudaSuccess) e = cudaMemcpyAsync(hs, stats, sizeof(hs), cudaMemcpyDeviceToHost, st);
       if (e == cudaSuccess) e = cudaStreamSynchronize(st);
-      device_free(bad);
+      device_free(stats);
       NIMF_CUDA_TRY(e);
-      w.tc_zp_ok = hb == 0;
+      w.tc_zp_ok = hs[0] == 0u;
+      // fp16 tiles of (n - zp) * sc * 2^e: e puts the largest magnitude in
+      // [2^13, 2^14); the smallest group scale must then stay >= 2^-10 so a
+      // unit step of the nibbles keeps fp16's relative precision
+      float wmax, smin;
+      std::memcpy(&wmax, &hs[1], 4);
+      std::memcpy(&smin, &hs[2], 4);
+      if (std::isfinite(wmax)) {
+        int ex = 0;
+        if (wmax > 0.f) std::frexp(wmax, &ex);   // wmax = f 2^ex, f in [0.5, 1)
+        const int e2 = wmax > 0.f ? 14 - ex : 0;
+        w.tc16_exp = e2;
+        w.tc16_ok = e2 > -100 && e2 < 100 &&
+                    (!(smin < 3e38f) || std::ldexp((double)smin, e2) >= std::ldexp(1.0, -10));
+      }
     }
   } else {
     const size_t nb = (size_t)(rows * bpr);
@@ -1173,6 +1201,7 @@ int launch_mode(const Q4GWeight* const* ws, float* const* ys, int count, const f
 
 // Rows of x above which the tensor-core GEMM replaces the GEMV.
 constexpr int64_t kTcMinRows = 16;
+int g_q4_prefill_mode = NIMF_Q4_PREFILL_AUTO;
 
 int q4g_gemv_group(const Q4GWeight* const* ws, int count, const float* x, int64_t m,
                    float* const* ys, cudaStream_t st) {
@@ -1199,21 +1228,29 @@ int q4g_gemv_group(const Q4GWeight* const* ws, int count, const float* x, int64_
       if (gs0 == 0) gs0 = ws[i]->gs;
       tc = tc && q4g_tc_supported(*ws[i]) && ws[i]->gs == gs0;
     }
-    if (tc) {
+    // the fp16-tile GEMM when every weight fits fp16 tiles (and the mode
+    // allows it), else the exact-nibble GEMM
+    bool t16 = g_q4_prefill_mode != NIMF_Q4_PREFILL_EXACT;
+    for (int i = 0; i < count && t16; ++i)
+      if (ws[i]->rows > 0) t16 = q4g_tc16_supported(*ws[i]) && ws[i]->gs == gs0;
+    if (t16 || tc) {
       // weights with rows share one x preparation and one launch per 4
       const Q4GWeight* tw[64];
       float* ty[64];
       int n = 0;
+      auto run = [&](int cnt) {
+        return t16 ? q4g_gemm_tc16_group(tw, cnt, x, m, ty, st) : q4g_gemm_tc_group(tw, cnt, x, m, ty, st);
+      };
       for (int i = 0; i < count; ++i) {
         if (ws[i]->rows <= 0) continue;
         tw[n] = ws[i];
         ty[n] = ys[i];
         if (++n == 64) {
-          NIMF_TRY(q4g_gemm_tc_group(tw, n, x, m, ty, st));
+          NIMF_TRY(run(n));
           n = 0;
         }
       }
-      if (n > 0) NIMF_TRY(q4g_gemm_tc_group(tw, n, x, m, ty, st));
+      if (n > 0) NIMF_TRY(run(n));
       return NIMF_OK;
     }
   }

@@ -15,6 +15,15 @@ pytestmark = pytest.mark.gpu
 TOL = 1e-3
 
 
+@pytest.fixture(autouse=True, params=[0, 1], ids=["fp16_tiles", "exact_nibbles"])
+def prefill_mode(request, nimf_gpu):
+    """Every test runs on both int4 GEMMs: AUTO (the fp16-tile GEMM for weights
+    that fit fp16 tiles) and EXACT (the exact-nibble GEMM)."""
+    nimf_gpu.check(nimf_gpu.lib().nimf_q4_prefill_mode(request.param))
+    yield request.param
+    nimf_gpu.check(nimf_gpu.lib().nimf_q4_prefill_mode(0))
+
+
 def rel_err(y, ref):
     y, ref = np.asarray(y, np.float64), np.asarray(ref, np.float64)
     return float(np.max(np.abs(y - ref)) / max(np.max(np.abs(ref)), 1e-30))
@@ -118,8 +127,10 @@ def test_prefill_mixed_group_sizes_in_one_call(nimf_gpu):
 
 
 def test_prefill_zero_points_outside_fp16_split(nimf_gpu):
-    """A weight whose zero points do not fit the split-fp16 zero-point step
-    (|zp| >= 60000) is computed on the CUDA-core path, still to the bar."""
+    """A weight whose zero points do not fit the exact GEMM's split-fp16
+    zero-point step (|zp| >= 60000) is computed by the fp16-tile GEMM (its
+    values fit fp16 tiles) or, in EXACT mode, on the CUDA-core path; both to
+    the bar."""
     n, k, gs, m = 64, 256, 128, 40
     rng = np.random.default_rng(12)
     p = rng.integers(0, 256, size=n * k // 2, dtype=np.uint8)
@@ -132,3 +143,56 @@ def test_prefill_zero_points_outside_fp16_split(nimf_gpu):
     w.free()
     ref = O.dequant_matmul_q4(x, p, s, z, m, k, n, gs, 2)
     assert rel_err(y, ref) <= TOL
+
+
+@pytest.mark.parametrize("scale", [1e-6, 3e-3, 40.0])
+def test_prefill_weight_scales_across_fp16_range(nimf_gpu, scale):
+    """Weights far from N(0, 0.02): tiny scales (the fp16 tiles take a
+    per-weight power of two) and large ones; within 1e-3 of float64 on every
+    path (weights whose groups span too wide a scale range use the exact
+    GEMM)."""
+    n, k, gs, m = 256, 1024, 128, 300
+    rng = np.random.default_rng(31)
+    w = (rng.standard_normal((n, k)) * scale).astype(np.float32)
+    p, s, z = O.quantize_int4_asym_per_group(w, gs)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    h = nimf_gpu.Weight.q4g(p, s, z, n, k, gs)
+    y = h.matmul(x, m)
+    h.free()
+    wd = O.dequantize_int4_asym(p, s, z, n, k, gs).astype(np.float64)
+    assert rel_err(y, x.astype(np.float64) @ wd.T) <= TOL
+
+
+def test_prefill_groups_with_scales_2e30_apart(nimf_gpu):
+    """One weight whose group scales differ by 2^30 (one group of each row
+    scaled down): too wide for fp16 tiles, so AUTO falls back to the exact
+    GEMM; still within 1e-3."""
+    n, k, gs, m = 64, 512, 128, 40
+    rng = np.random.default_rng(32)
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    w[:, :128] *= 2.0 ** -30
+    p, s, z = O.quantize_int4_asym_per_group(w, gs)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    h = nimf_gpu.Weight.q4g(p, s, z, n, k, gs)
+    y = h.matmul(x, m)
+    h.free()
+    wd = O.dequantize_int4_asym(p, s, z, n, k, gs).astype(np.float64)
+    assert rel_err(y, x.astype(np.float64) @ wd.T) <= TOL
+
+
+def test_prefill_batch8_prompt_rows(nimf_gpu):
+    """4096 rows of x (eight 512-token prompts) through a grouped gate/up pair:
+    16 x tiles of 256 rows on the fp16-tile GEMM."""
+    k, gs, m = 4096, 128, 4096
+    ws, ref = [], []
+    x = np.random.default_rng(33).standard_normal((m, k)).astype(np.float32)
+    for i, n in enumerate((1024, 512)):
+        p, s, z, _ = quantized(n, k, gs, seed=40 + i)
+        ws.append(nimf_gpu.Weight.q4g(p, s, z, n, k, gs))
+        ref.append(O.dequantize_int4_asym(p, s, z, n, k, gs).astype(np.float64))
+    ys = nimf_gpu.Weight.matmul_group(ws, x, m)
+    for w in ws:
+        w.free()
+    xd = x.astype(np.float64)
+    for y, wd in zip(ys, ref):
+        assert rel_err(y, xd @ wd.T) <= TOL
