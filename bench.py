@@ -992,37 +992,50 @@ def run_prefill_7b(nimf, torch, steps, warmup, tokens=512, copies=4):
                                              [gu[0].data_ptr(), gu[1].data_ptr()], st)
                 down.matmul_dev(gu[0].data_ptr(), tokens, dn.data_ptr(), st)
 
-        with torch.cuda.stream(stream):
-            step(stream.cuda_stream)
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            step(stream.cuda_stream)
-        for _ in range(warmup):
-            graph.replay()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(steps):
-            graph.replay()
-        e1.record()
-        torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / steps
-        graph.reset()
+        L = nimf.lib()
+        ms_mode = {}
+        for mode in (1, 0):      # the exact-nibble GEMM, then the default (fp16 tiles)
+            nimf.check(L.nimf_q4_prefill_mode(mode))
+            ms_mode[mode] = graph_ms(torch, step, steps, warmup)
+        # each projection alone (default GEMM), one layer copy per replay in turn
+        (q, k, v, o, gate, up, down) = layers[0]
+        proj = {
+            "qkv": (lambda st: nimf.Weight.matmul_group_dev([q, k, v], x.data_ptr(), tokens,
+                                                            [qkv[i].data_ptr() for i in range(3)], st),
+                    2 * tokens * 3 * D7 * D7),
+            "o": (lambda st: o.matmul_dev(qkv[0].data_ptr(), tokens, att.data_ptr(), st),
+                  2 * tokens * D7 * D7),
+            "gate_up": (lambda st: nimf.Weight.matmul_group_dev([gate, up], att.data_ptr(), tokens,
+                                                                [gu[0].data_ptr(), gu[1].data_ptr()], st),
+                        2 * tokens * 2 * F7 * D7),
+            "down": (lambda st: down.matmul_dev(gu[0].data_ptr(), tokens, dn.data_ptr(), st),
+                     2 * tokens * F7 * D7),
+        }
+        per_proj = {}
+        for nm, (fn, fl) in proj.items():
+            pms = graph_ms(torch, fn, steps, warmup)
+            per_proj[nm] = {"us": pms * 1e3, "tflop_s": fl / (pms * 1e-3) / 1e12}
     finally:
+        nimf.check(nimf.lib().nimf_q4_prefill_mode(0))
         for lw in layers:
             for w in lw:
                 w.free()
+    ms = ms_mode[0]
     per_layer = ms / copies
     tflops = prefill7b_flops(tokens) / (per_layer * 1e-3) / 1e12
+    tflops_exact = prefill7b_flops(tokens) / (ms_mode[1] / copies * 1e-3) / 1e12
     pk, kind = peaks()
     peak = float(pk.get("bf16_tflops", 1590.0)) if kind == "measured" else 1590.0
     return {"tokens": tokens, "ms_per_layer": per_layer, "tflop_s": tflops,
             "frac_of_bf16_peak": tflops / peak, "bf16_peak_tflop_s": peak,
             "peak_source": kind,
+            "exact_nibble_gemm_tflop_s": tflops_exact,
+            "per_projection": per_proj,
             "matmul_tok_s_32_layers": tokens / (32 * per_layer * 1e-3),
             "launches_per_layer": 4 * 3,
-            "note": ("x prepared once per call (row scale + fp16 tiles) then one tcgen05 GEMM "
+            "note": ("default GEMM: int4 dequantised into fp16 tiles, one accumulator over K; "
+                     "exact_nibble_gemm: nibbles exact in fp16 with an fp32 epilogue per group; "
+                     "x prepared once per call (row scale + fp16 tiles) then one tcgen05 GEMM "
                      "launch per call; %d layer copies per step, %d timed steps" % (copies, steps))}
 
 
@@ -1250,6 +1263,7 @@ def compact_7b(decode, decode_full, prefill, formats):
         out["formats_tflop_s"] = {k: r(v.get("tflop_s")) for k, v in f3.items() if k.endswith("_m512")}
     if prefill:
         out["prefill_7b"] = {"tflop_s": r(prefill.get("tflop_s")),
+                             "exact_nibble_tflop_s": r(prefill.get("exact_nibble_gemm_tflop_s")),
                              "ms_per_layer": r(prefill.get("ms_per_layer"), 4),
                              "tokens": prefill.get("tokens")}
     if decode:
