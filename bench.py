@@ -1252,39 +1252,46 @@ def run_ncu_case(name):
     print("ncu case %s done" % name)
 
 
-def compact_7b(decode, decode_full, prefill, formats):
+def compact_7b(decode, decode_full, prefill, formats, generate=None):
     """Short summaries of the 7B-shape and format measurements for the end of
-    the JSON line (the full objects are printed on comment lines)."""
-    r = lambda v, d=1: None if v is None else round(float(v), d)
+    the JSON line (the full objects are printed on comment lines first).  A
+    record that keeps only the last ~1,500 characters of the output still
+    holds these, the most important last: formats, prefill, the matmul-only
+    decode, the whole decode step, the generation."""
+    r = lambda v, d=0: None if v is None else (round(float(v)) if d == 0 else round(float(v), d))
     out = {}
     if formats:
         f3 = formats.get("config3_k8192_n28672", {})
-        out["formats_gb_s"] = {k: r(v.get("gb_s")) for k, v in f3.items() if k.endswith(("_m1", "_m8"))}
-        out["formats_tflop_s"] = {k: r(v.get("tflop_s")) for k, v in f3.items() if k.endswith("_m512")}
+        out["fmt_gb_s"] = {k.replace("_rowscale", "").replace("_block16", ""): r(v.get("gb_s"))
+                           for k, v in f3.items() if k.endswith(("_m1", "_m8"))}
+        out["fmt_tflop_s"] = {k.replace("_rowscale", "").replace("_block16", ""): r(v.get("tflop_s"))
+                              for k, v in f3.items() if k.endswith("_m512")}
     if prefill:
         out["prefill_7b"] = {"tflop_s": r(prefill.get("tflop_s")),
-                             "exact_nibble_tflop_s": r(prefill.get("exact_nibble_gemm_tflop_s")),
-                             "ms_per_layer": r(prefill.get("ms_per_layer"), 4),
-                             "tokens": prefill.get("tokens")}
+                             "exact_tflop_s": r(prefill.get("exact_nibble_gemm_tflop_s")),
+                             "ms_layer": r(prefill.get("ms_per_layer"), 3)}
     if decode:
-        d = {"n_gpus": decode.get("n_gpus")}
+        d = {}
         if "error" in decode:
-            d["error"] = decode["error"][:200]
+            d["error"] = decode["error"][:160]
         for k, v in decode.items():
             if isinstance(v, dict) and "tok_s" in v:
-                d[k + "_tok_s"] = r(v["tok_s"])
-                d[k + "_gb_s"] = r(v.get("gb_s"))
-        out["decode_7b"] = d
+                d[k] = r(v["tok_s"])
+        out["decode_7b_matmul_tok_s"] = d
     if decode_full:
-        d = {"n_gpus": decode_full.get("n_gpus", 1)}
+        d = {}
         if "error" in decode_full:
-            d["error"] = decode_full["error"][:200]
+            d["error"] = decode_full["error"][:160]
         for k, v in decode_full.items():
             if isinstance(v, dict) and "tok_s" in v:
-                d[k + "_tok_s"] = r(v["tok_s"])
-            elif k in ("tok_s", "ms_per_step", "position"):
-                d[k] = r(v, 3)
-        out["decode_7b_full_step"] = d
+                d[k] = r(v["tok_s"])
+        out["decode_7b_step_tok_s"] = d
+    if generate:
+        out["generate_7b"] = {
+            bk: ({"error": g["error"][:160]} if "error" in g else
+                 {"prefill_ms": r(g["prefill_ms"], 1), "decode_tok_s": r(g["decode_tok_s"]),
+                  "generate_tok_s": r(g["generate_tok_s"])})
+            for bk, g in generate.items()}
     return out
 
 
@@ -1571,13 +1578,7 @@ def run_ours(args, rank, world, local_rank):
             line["nccl_allgather_gb_s"] = nccl_cmp["value"]
             line["exchange"] = ("all-gather fused into the GEMV: merge warps store every output "
                                 "into every GPU over NVLink, one arrival per rank per launch")
-        line.update(compact_7b(decode, decode_full, prefill, formats))
-        if generate:
-            line["generate_7b"] = {
-                bk: ({"error": g["error"][:200]} if "error" in g else
-                     {k: round(g[k], 2) for k in ("prefill_ms", "prefill_tok_s", "decode_tok_s",
-                                                   "generate_tok_s")})
-                for bk, g in generate.items()}
+        line.update(compact_7b(decode, decode_full, prefill, formats, generate))
         print(json.dumps(line), flush=True)
     for wt in weights:
         wt.free()
