@@ -1217,6 +1217,8 @@ def run_ncu_case(name):
     per case, so `-s` / `-c` select the final round.
       decode_step: the whole-step 7B decode of run_decode_7b_full with 2 layers
           (graph replays: 2 warm-up, 2 timed);
+      prefill: run_prefill_7b with one layer copy (both int4 GEMMs, each
+          projection alone);
       fw: an FP4 E2M1 block-16 weight and a one-byte CustomFloat(4,3) weight
           with per-row scales, both 28672 x 8192 (random codes), at M = 1 and 1
           (GEMV), 16 (GEMV), 17 and 128 (tcgen05 GEMM) and 512."""
@@ -1226,6 +1228,15 @@ def run_ncu_case(name):
     if name == "decode_step":
         nimf.init(0)
         run_decode_7b_full(nimf, torch, 2, 2, layers=2)
+        print("ncu case %s done" % name)
+        return
+    if name == "prefill":
+        # one 7B layer's q/k/v, o, gate/up and down at 512 prompt rows: 3 warm-up
+        # rounds and one final round on the fp16-tile GEMM (12 launches per
+        # round: a row scale, an x preparation and a GEMM per call), then the
+        # same on the exact-nibble GEMM
+        nimf.init(0)
+        run_prefill_7b(nimf, torch, 1, 3, copies=1)
         print("ncu case %s done" % name)
         return
     if name != "fw":
@@ -1599,7 +1610,7 @@ def main():
     ap.add_argument("--format-steps", type=int, default=40,
                     help="timed steps of the FP4/fp8/APF/int8 measurements (0: skip)")
     ap.add_argument("--ncu-case", default=None,
-                    help="run one small fixed workload for an ncu capture and exit (fw)")
+                    help="run one small fixed workload for an ncu capture and exit (fw, decode_step, prefill)")
     args = ap.parse_args()
     if args.ncu_case:
         run_ncu_case(args.ncu_case)
