@@ -1,9 +1,8 @@
 """The library's communicator paths on one GPU (a communicator of one rank):
-the shard rule, nimf_matmul_w_allgather_dev (which is then the plain GEMV),
-the gather group with the fused-gather GEMV (its outputs land in the group's
-buffer; the arrival exchange is skipped for one rank), the sharded decode
-plan (identical to the one-GPU plan), and the argument checks.  The 2-GPU
-behaviour is in test_sharded_multi_gpu.py."""
+nimf_matmul_w_allgather_dev (which is then the plain GEMV), the gather group
+with the fused-gather GEMV (its outputs land in the group's buffer; the
+arrival exchange is skipped for one rank), and the argument checks.  The
+2-GPU behaviour is in test_sharded_multi_gpu.py."""
 import ctypes
 
 import numpy as np
@@ -62,7 +61,7 @@ def test_gather_group_one_rank(comm1):
     rng = np.random.default_rng(4)
     k = 1024
     ns = [512, 1000]
-    ws, ref = [], []
+    ws = []
     for n in ns:
         w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
         p, s, z = O.quantize_int4_asym_per_group(w, 128)
