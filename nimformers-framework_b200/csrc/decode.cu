@@ -160,7 +160,20 @@ struct DecArgs {
   long long peer_off[kMaxRanks];
   unsigned* gctl;
   int l2_ahead;             // producer items (per lane) prefetched into L2 ahead of the ring
+  // optional stage timeline of CTA tl_cta (%globaltimer ns), [stage][3]:
+  // consumers past the stage's grid barrier, prologue done, merge warp's
+  // arrival (attention stages: units done); nullptr: not recorded
+  unsigned long long* timeline;
+  int tl_cta;
 };
+
+__device__ __forceinline__ void tl_mark(const DecArgs& a, int s, int what) {
+  if (a.timeline != nullptr && (int)blockIdx.x == a.tl_cta) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    a.timeline[(size_t)s * 3 + what] = t;
+  }
+}
 
 template <typename T>
 __device__ __forceinline__ T* at_rank(const DecArgs& a, T* p, int q) {
@@ -844,7 +857,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecArgs 
       if (a.world == 1) __threadfence();
       else __threadfence_system();
       __syncwarp();
-      if (lane == 0) arrive(a, s, target);
+      if (lane == 0) {
+        tl_mark(a, s, 2);
+        arrive(a, s, target);
+      }
     }
   } else {
     // ---------------- consumers
@@ -864,6 +880,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecArgs 
         // wait for q/k/v of every CTA, then this CTA's (head, split) units
         if (threadIdx.x == 0 && s > 0) stage_wait(a, s - 1, target, gtarget);
         named_barrier(kBarCons, kConsThreads);
+        if (threadIdx.x == 0) tl_mark(a, s, 0);
         const int units = a.hloc * a.nsplit;   // this rank's heads
         if (pos >= 0 && pos < a.max_seq) {
           for (int u = cid; u < units; u += G) {
@@ -875,7 +892,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecArgs 
           atomicExch(a.err, 4);   // position outside the KV cache: nothing is read or appended
         }
         named_barrier(kBarCons, kConsThreads);
-        if (threadIdx.x == 0) arrive(a, s, target);
+        if (threadIdx.x == 0) {
+          tl_mark(a, s, 2);
+          arrive(a, s, target);
+        }
         continue;
       }
       int rt0, nrt;
@@ -884,7 +904,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecArgs 
       const int nstg = nrt * nkb;
       if (threadIdx.x == 0 && s > 0) stage_wait(a, s - 1, target, gtarget);
       named_barrier(kBarCons, kConsThreads);  // also: every warp is done with the last x
+      if (threadIdx.x == 0) tl_mark(a, s, 0);
       prologue(a, st, cid, tok, smem);
+      if (threadIdx.x == 0) tl_mark(a, s, 1);
       const float sm = *xmaxp / 127.0f;
       const float dsc = t < 2 ? sm : sm * (1.0f / 256.0f);
       const int groups = st.groups;
@@ -1012,6 +1034,8 @@ struct DecodePlan {
   void* peers[kMaxRanks] = {};   // sharded: every rank's scratch as mapped here
   DecArgs base = {};
   int64_t vocab = 0;
+  unsigned long long* timeline = nullptr;   // caller's buffer (not owned)
+  int tl_cta = 0;
 };
 
 std::vector<DecodePlan*> g_plans;
@@ -1307,6 +1331,7 @@ int create_plan(const nimf_decode_desc* d, int world, int rank, int64_t* plan_ou
   A.gctl = (unsigned*)(sb + o_gctl);
   A.world = world;
   A.rank = rank;
+  A.timeline = nullptr;
   // L2 look-ahead of the producer lanes, in items of up to 36 KB per lane
   // (NIMF_DECODE_L2_AHEAD, 0 .. 16; default 2: 8 ring stages ahead per SM)
   A.l2_ahead = 2;
@@ -1385,6 +1410,17 @@ int nimf_decode_step_dev(int64_t plan, int32_t* token_dev, int32_t* next_token_d
   cfg.attrs = at;
   cfg.numAttrs = 1;
   NIMF_CUDA_TRY(cudaLaunchKernelEx(&cfg, decode_step_kernel, A));
+  return NIMF_OK;
+}
+
+int nimf_decode_timeline(int64_t plan, uint64_t* timeline_dev, int64_t n, int cta) {
+  DecodePlan* P = find_plan(plan);
+  if (!P) return set_error(NIMF_ERR_STATE, "decode_timeline: unknown plan %lld", (long long)plan);
+  if (timeline_dev && (n < 3 * (int64_t)P->stages.size() || cta < 0 || cta >= P->grid))
+    return set_error(NIMF_ERR_SHAPE, "decode_timeline: %lld entries for %zu stages, CTA %d of %d",
+                     (long long)n, P->stages.size(), cta, P->grid);
+  P->base.timeline = (unsigned long long*)timeline_dev;
+  P->base.tl_cta = cta;
   return NIMF_OK;
 }
 

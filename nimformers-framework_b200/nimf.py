@@ -58,7 +58,7 @@ EXPORTS = [
     "nimf_matmul_w_allgather_dev", "nimf_decode_create_sharded",
     "nimf_gather_create", "nimf_matmul_w_group_gather_dev", "nimf_gather_set_timeout_ms",
     "nimf_gather_destroy", "nimf_attention_prefill_dev", "nimf_attention_decode_batch_dev",
-    "nimf_q4_prefill_mode",
+    "nimf_q4_prefill_mode", "nimf_decode_timeline",
 ]
 
 
@@ -151,6 +151,7 @@ def lib():
         "nimf_gather_set_timeout_ms": [i64],
         "nimf_gather_destroy": [i64],
         "nimf_q4_prefill_mode": [i32],
+        "nimf_decode_timeline": [i64, vp, i64, i32],
         "nimf_attention_prefill_dev": [vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i64,
                                        ctypes.c_float, vp, vp],
         "nimf_attention_decode_batch_dev": [vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, vp, vp,
