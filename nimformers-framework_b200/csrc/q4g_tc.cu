@@ -309,9 +309,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int sh0 = hi ? 0 : 4, sh1 = hi ? 8 : 4;  // bytes 0, 2: left; bytes 1, 3: right
     const int rt = min(rt0 + rl, W.n_rt - 1);
     const float4* szp = W.sz + (size_t)rt * a.groups * 8 + g8;
+    float4 zn = uset < G ? __ldg(szp + (size_t)uset * 8) : make_float4(0.f, 0.f, 0.f, 0.f);
     for (int g = uset; g < G; g += 2) {
       const int s = g % NS, ab = g % NA;
-      const float4 zz = __ldg(szp + (size_t)g * 8);
+      const float4 zz = zn;
+      if (g + 2 < G) zn = __ldg(szp + (size_t)(g + 2) * 8);
       int ok = 1;
       if (lane == 0)
         ok = (!stop() && mbar_wait_t<kTcWait>(&sfull[s], (g / NS) & 1) &&
@@ -336,20 +338,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           u[j] = make_uint4(0u, 0u, 0u, 0u);
           if (rl < nrt) u[j] = wsrc[(rl * KQG + qq) * 32 + g8 * 4 + ((j + rot) & 3)];
         }
-        // back to fragment order: u[t] <- u[(t - rot) & 3]
-        if (NIMF_TC_ROTATE && (rot & 1)) {
-          const uint4 t3 = u[3];
-          u[3] = u[2];
-          u[2] = u[1];
-          u[1] = u[0];
-          u[0] = t3;
-        }
-        if (NIMF_TC_ROTATE && (rot & 2)) {
-          const uint4 t0 = u[0], t1 = u[1];
-          u[0] = u[2];
-          u[1] = u[3];
-          u[2] = t0;
-          u[3] = t1;
+        // back to fragment order, u[t] <- u[(t - rot) & 3], with selects
+        // (per-lane branches here stall the warps on branch resolution)
+        if (NIMF_TC_ROTATE) {
+          const bool r1 = (rot & 1) != 0, r2 = (rot & 2) != 0;
+          auto sel = [](bool c, const uint4& x, const uint4& y) {
+            return make_uint4(c ? x.x : y.x, c ? x.y : y.y, c ? x.z : y.z, c ? x.w : y.w);
+          };
+          const uint4 v0 = sel(r1, u[3], u[0]), v1 = sel(r1, u[0], u[1]);
+          const uint4 v2 = sel(r1, u[1], u[2]), v3 = sel(r1, u[2], u[3]);
+          u[0] = sel(r2, v2, v0);
+          u[1] = sel(r2, v3, v1);
+          u[2] = sel(r2, v0, v2);
+          u[3] = sel(r2, v1, v3);
         }
         uint32_t col[32];
 #pragma unroll
@@ -393,9 +394,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
     for (int i = 0; i < 64; ++i) acc[i] = 0.f;
     griddep_wait();
+    // scales one group ahead (their global load off the critical path)
+    float4 zn = G > 0 ? __ldg(szp) : make_float4(0.f, 0.f, 0.f, 0.f);
     for (int g = 0; g < G; ++g) {
       const int b = g & 1;
-      const float4 zz = __ldg(szp + (size_t)g * 8);
+      const float4 zz = zn;
+      if (g + 1 < G) zn = __ldg(szp + (size_t)(g + 1) * 8);
       const float sc = (r16 >> 3) ? zz.z : zz.x;
       int ok = 1;
       if (lane == 0) ok = (!stop() && mbar_wait_t<kTcWait>(&tfull[b], (g >> 1) & 1)) ? 1 : 0;

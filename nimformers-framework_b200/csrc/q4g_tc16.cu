@@ -135,10 +135,29 @@ struct T6Maps {
   CUtensorMap m[kT6MaxW];
 };
 
-// fp16 pair of one fragment byte pair: nibble n (bits 0..3 of byte b of m)
-// as the float 2^23 + n by a byte permute, then exact n, then the fma
-__device__ __forceinline__ float nib_f(uint32_t m, uint32_t sel) {
-  return __uint_as_float(__byte_perm(m, 0x4B000000u, sel)) - 8388608.0f;
+// Two nibbles of m (bits 0..3 of bytes b0 and b1) -> the fp16 pair
+// {lo: fp16(fma(n0, sc, nzs)), hi: fp16(fma(n1, sc, nzs))}: byte permutes make
+// the floats 2^23 + n, one packed subtraction gives n exactly, one packed fma
+// the dequantised values, one conversion packs them (5 instructions a pair).
+__device__ __forceinline__ uint32_t nib2_h2(uint32_t m, uint32_t sel0, uint32_t sel1,
+                                            unsigned long long sc2, unsigned long long nzs2) {
+  const uint32_t f0 = __byte_perm(m, 0x4B000000u, sel0);
+  const uint32_t f1 = __byte_perm(m, 0x4B000000u, sel1);
+  unsigned long long v;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "r"(f0), "r"(f1));
+  asm("add.rn.f32x2 %0, %0, %1;" : "+l"(v) : "l"(0xCB000000CB000000ull));   // - 2^23 each
+  asm("fma.rn.f32x2 %0, %0, %1, %2;" : "+l"(v) : "l"(sc2), "l"(nzs2));
+  uint32_t lo, hi, h;
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(v));
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "r"(hi), "r"(lo));
+  return h;
+}
+__device__ __forceinline__ unsigned long long f32x2_splat(float v) {
+  const uint32_t b = __float_as_uint(v);
+  return ((unsigned long long)b << 32) | b;
+}
+__device__ __forceinline__ uint4 sel4(bool c, const uint4& a, const uint4& b) {
+  return make_uint4(c ? a.x : b.x, c ? a.y : b.y, c ? a.z : b.z, c ? a.w : b.w);
 }
 
 template <int KQG, int NR>
@@ -278,11 +297,17 @@ __global__ void __launch_bounds__(kT6Threads, 1)
     const bool hi = (r & 8) != 0;
     const int rt = min(rt0 + rl, W.n_rt - 1);
     const float4* szp = W.sz + (size_t)rt * a.groups * 8 + g8;
+    // this set's scale/zero pairs one group ahead, so their global load is
+    // not on the unpack's critical path
+    float4 zn = uset < G ? __ldg(szp + (size_t)uset * 8) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const bool r1 = (rot & 1) != 0, r2 = (rot & 2) != 0;
     for (int g = uset; g < G; g += 2) {
       const int s = g % NS, ab = g % NA;
-      const float4 zz = __ldg(szp + (size_t)g * 8);
+      const float4 zz = zn;
+      if (g + 2 < G) zn = __ldg(szp + (size_t)(g + 2) * 8);
       const float sc = (hi ? zz.z : zz.x) * W.wscale;
       const float nzs = -(hi ? zz.w : zz.y) * sc;
+      const unsigned long long sc2 = f32x2_splat(sc), nzs2 = f32x2_splat(nzs);
       int ok = 1;
       if (lane == 0)
         ok = (!stop() && mbar_wait_t<kT6Wait>(&sfull[s], (g / NS) & 1) &&
@@ -307,20 +332,15 @@ __global__ void __launch_bounds__(kT6Threads, 1)
           u[j] = make_uint4(0u, 0u, 0u, 0u);
           if (rl < nrt) u[j] = wsrc[(rl * KQG + qq) * 32 + g8 * 4 + ((j + rot) & 3)];
         }
-        // back to fragment order: u[t] <- u[(t - rot) & 3]
-        if (rot & 1) {
-          const uint4 t3 = u[3];
-          u[3] = u[2];
-          u[2] = u[1];
-          u[1] = u[0];
-          u[0] = t3;
-        }
-        if (rot & 2) {
-          const uint4 t0 = u[0], t1 = u[1];
-          u[0] = u[2];
-          u[1] = u[3];
-          u[2] = t0;
-          u[3] = t1;
+        // back to fragment order, u[t] <- u[(t - rot) & 3], with selects
+        // (a per-lane branch here stalled the warps on branch resolution)
+        {
+          const uint4 v0 = sel4(r1, u[3], u[0]), v1 = sel4(r1, u[0], u[1]);
+          const uint4 v2 = sel4(r1, u[1], u[2]), v3 = sel4(r1, u[2], u[3]);
+          u[0] = sel4(r2, v2, v0);
+          u[1] = sel4(r2, v3, v1);
+          u[2] = sel4(r2, v0, v2);
+          u[3] = sel4(r2, v1, v3);
         }
         uint32_t col[32];
 #pragma unroll
@@ -329,14 +349,8 @@ __global__ void __launch_bounds__(kT6Threads, 1)
 #pragma unroll
           for (int wi = 0; wi < 4; ++wi) {
             const uint32_t mm = (hi ? (wv[wi] >> 4) : wv[wi]) & 0x0F0F0F0Fu;
-            const float f0 = fmaf(nib_f(mm, 0x7540u), sc, nzs);
-            const float f1 = fmaf(nib_f(mm, 0x7541u), sc, nzs);
-            const float f2 = fmaf(nib_f(mm, 0x7542u), sc, nzs);
-            const float f3 = fmaf(nib_f(mm, 0x7543u), sc, nzs);
-            const __half2 p02 = __floats2half2_rn(f0, f2);
-            const __half2 p13 = __floats2half2_rn(f1, f3);
-            col[wi * 8 + 2 * t] = *reinterpret_cast<const uint32_t*>(&p02);
-            col[wi * 8 + 2 * t + 1] = *reinterpret_cast<const uint32_t*>(&p13);
+            col[wi * 8 + 2 * t] = nib2_h2(mm, 0x7540u, 0x7542u, sc2, nzs2);       // k offsets 0, 2
+            col[wi * 8 + 2 * t + 1] = nib2_h2(mm, 0x7541u, 0x7543u, sc2, nzs2);   // k offsets 1, 3
           }
         }
         tmem_st32(ta + (uint32_t)qq * 32u, col);
