@@ -73,6 +73,7 @@ constexpr int kIssuers = 4;                      // producer lanes (lane l issue
 constexpr int kMaxK = 14336;                     // largest K of a stage
 constexpr int kMaxGroups = kMaxK / kGS;
 constexpr int kNV = (kMaxK / 4 + kConsThreads - 1) / kConsThreads;  // float4 of x per thread
+constexpr int kPB = 4;                           // prologue slots whose loads are issued together
 constexpr int kMaxHeads = 64;
 constexpr int kMaxSplit = 8;
 constexpr int kMaxProb = 3;
@@ -389,30 +390,42 @@ __device__ void prologue(const DecArgs& a, const DecStage& st, int cid, int tok,
   const int f4 = K >> 2;
   for (int i = tid; i < st.groups * 16; i += kConsThreads) sdi[i] = 0;
   float4 v[kNV];
+  // Every global load of a slot set is issued before any of its values is
+  // used (no fence, shuffle or data-dependent branch in between), so a
+  // prologue costs about one L2 round trip per phase rather than one per
+  // load.  Slots j with 512 j >= K / 4 are empty for the whole warp.
+  const int warp = tid >> 5;
   if (st.pro == PRO_COMBINE) {
-    // per head: M = max_j m_j, L = sum_j [l_j > 0] e^(m_j - M) l_j, weights
-    // e^(m_j - M) (attn_combine_kernel's arithmetic, splits in order)
+    // per head: M = max_j m_j, L = sum_j [l_j > 0] e^(m_j - M) l_j in split
+    // order, weights e^(m_j - M) (attn_combine_kernel's arithmetic): lane j
+    // of the head's warp holds split j
     float* cw = reinterpret_cast<float*>(smem + kOffComb);
     float* cml = reinterpret_cast<float*>(smem + kOffCombML);
     const int ns = a.nsplit;
-    for (int h = tid >> 5; h < a.H; h += kCons) {
+    for (int h = warp; h < a.H; h += kCons) {
       const float* ml = a.part_ml + (size_t)h * ns * 2;
+      float mj = -INFINITY, lj = 0.f;
+      if (lane < ns) {
+        mj = __ldcg(ml + 2 * lane);
+        lj = __ldcg(ml + 2 * lane + 1);
+      }
+      float M = mj;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+      const bool live = lane < ns && lj > 0.f;
+      const float e = live ? expf(__fsub_rn(mj, M)) : 0.f;
+      const float el = live ? __fmul_rn(e, lj) : 0.f;
+      float L = 0.f;
+      for (int j = 0; j < ns; ++j) {
+        const float t = __shfl_sync(0xffffffffu, el, j);
+        const int lv = __shfl_sync(0xffffffffu, live ? 1 : 0, j);
+        if (lv) L = __fadd_rn(L, t);
+      }
+      const unsigned mask = __ballot_sync(0xffffffffu, live);
+      if (lane < kMaxSplit) cw[h * kMaxSplit + lane] = e;
       if (lane == 0) {
-        float M = -INFINITY;
-        for (int j = 0; j < ns; ++j) M = fmaxf(M, __ldcg(ml + 2 * j));
-        float L = 0.f;
-        for (int j = 0; j < ns; ++j) {
-          const float l = __ldcg(ml + 2 * j + 1);
-          const float e = expf(__fsub_rn(__ldcg(ml + 2 * j), M));
-          cw[h * kMaxSplit + j] = l > 0.f ? e : 0.f;
-          if (l > 0.f) L = __fadd_rn(L, __fmul_rn(e, l));
-        }
-        for (int j = ns; j < kMaxSplit; ++j) cw[h * kMaxSplit + j] = 0.f;
         cml[2 * h] = L;
-        // splits with l_j = 0 take no part (flag in the sign of a second copy)
-        int mask = 0;
-        for (int j = 0; j < ns; ++j) mask |= (__ldcg(ml + 2 * j + 1) > 0.f) << j;
-        cml[2 * h + 1] = __int_as_float(mask);
+        cml[2 * h + 1] = __int_as_float((int)mask);
       }
     }
     named_barrier(kBarCons, kConsThreads);
@@ -425,14 +438,27 @@ __device__ void prologue(const DecArgs& a, const DecStage& st, int cid, int tok,
         const int h = e0 / a.HD, d = e0 - h * a.HD;
         const int mask = __float_as_int(cml[2 * h + 1]);
         float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
-        for (int s = 0; s < ns; ++s) {
-          if (!((mask >> s) & 1)) continue;
-          const float wgt = cw[h * kMaxSplit + s];
-          const float4 o = ldcg4(a.part_o + ((size_t)h * ns + s) * a.HD + d);
-          o0 = __fadd_rn(o0, __fmul_rn(wgt, o.x));
-          o1 = __fadd_rn(o1, __fmul_rn(wgt, o.y));
-          o2 = __fadd_rn(o2, __fmul_rn(wgt, o.z));
-          o3 = __fadd_rn(o3, __fmul_rn(wgt, o.w));
+#pragma unroll
+        for (int s0 = 0; s0 < kMaxSplit; s0 += 4) {
+          if (s0 >= ns) break;
+          float4 o[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int sp = s0 + q;
+            o[q] = (sp < ns && ((mask >> sp) & 1)) ? ldcg4(a.part_o + ((size_t)h * ns + sp) * a.HD + d)
+                                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int sp = s0 + q;
+            if (sp < ns && ((mask >> sp) & 1)) {
+              const float wgt = cw[h * kMaxSplit + sp];
+              o0 = __fadd_rn(o0, __fmul_rn(wgt, o[q].x));
+              o1 = __fadd_rn(o1, __fmul_rn(wgt, o[q].y));
+              o2 = __fadd_rn(o2, __fmul_rn(wgt, o[q].z));
+              o3 = __fadd_rn(o3, __fmul_rn(wgt, o[q].w));
+            }
+          }
         }
         const float L = cml[2 * h];
         r = make_float4(__fdiv_rn(o0, L), __fdiv_rn(o1, L), __fdiv_rn(o2, L), __fdiv_rn(o3, L));
@@ -440,59 +466,96 @@ __device__ void prologue(const DecArgs& a, const DecStage& st, int cid, int tok,
       v[j] = r;
     }
   } else if (st.pro == PRO_SWIGLU) {
+    // slots in batches of kPB: the batch's loads first, then its values
 #pragma unroll
-    for (int j = 0; j < kNV; ++j) {
-      const int f = tid + j * kConsThreads;
-      float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (f < f4) {
-        const float4 g = ldcg4(st.a + 4 * f), u = ldcg4(st.b + 4 * f);
-        const float gv[4] = {g.x, g.y, g.z, g.w}, uv[4] = {u.x, u.y, u.z, u.w};
+    for (int j0 = 0; j0 < kNV; j0 += kPB) {
+      float4 g[kPB], u[kPB];
+#pragma unroll
+      for (int jj = 0; jj < kPB; ++jj) {
+        const int f = tid + (j0 + jj) * kConsThreads;
+        const bool in = j0 + jj < kNV && f < f4;
+        g[jj] = in ? ldcg4(st.a + 4 * f) : make_float4(0.f, 0.f, 0.f, 0.f);
+        u[jj] = in ? ldcg4(st.b + 4 * f) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int jj = 0; jj < kPB; ++jj) {
+        if (j0 + jj >= kNV) break;
+        const float gv[4] = {g[jj].x, g[jj].y, g[jj].z, g[jj].w}, uv[4] = {u[jj].x, u[jj].y, u[jj].z, u[jj].w};
         float o[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gv[e])));
           o[e] = __fmul_rn(__fmul_rn(gv[e], sig), uv[e]);
         }
-        r = make_float4(o[0], o[1], o[2], o[3]);
+        v[j0 + jj] = make_float4(o[0], o[1], o[2], o[3]);   // zeros give zeros
       }
-      v[j] = r;
     }
   } else {
     // RMSNorm of (embedding row) or (a + b); the sum is the residual stream
     const bool emb = st.pro == PRO_EMB_RMS;
     const float* erow = a.emb + (size_t)tok * K;
     const bool tok_ok = tok >= 0 && tok < a.vocab;
+    if (emb) {
+#pragma unroll
+      for (int j = 0; j < kNV; ++j) {
+        const int f = tid + j * kConsThreads;
+        v[j] = (f < f4 && tok_ok) ? __ldg(reinterpret_cast<const float4*>(erow) + f)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    } else {
+#pragma unroll
+      for (int j0 = 0; j0 < kNV; j0 += kPB) {
+        float4 xa[kPB], xb[kPB];
+#pragma unroll
+        for (int jj = 0; jj < kPB; ++jj) {
+          const int f = tid + (j0 + jj) * kConsThreads;
+          const bool in = j0 + jj < kNV && f < f4;
+          xa[jj] = in ? ldcg4(st.a + 4 * f) : make_float4(0.f, 0.f, 0.f, 0.f);
+          xb[jj] = in ? ldcg4(st.b + 4 * f) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int jj = 0; jj < kPB; ++jj) {
+          if (j0 + jj >= kNV) break;
+          v[j0 + jj] = make_float4(__fadd_rn(xa[jj].x, xb[jj].x), __fadd_rn(xa[jj].y, xb[jj].y),
+                                   __fadd_rn(xa[jj].z, xb[jj].z), __fadd_rn(xa[jj].w, xb[jj].w));
+        }
+      }
+    }
+    if (cid == 0 && st.res_out) {
+#pragma unroll
+      for (int j = 0; j < kNV; ++j) {
+        const int f = tid + j * kConsThreads;
+        if (f < f4) reinterpret_cast<float4*>(st.res_out)[f] = v[j];
+      }
+      __threadfence();
+    }
     float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < kNV; ++j) {
       const int f = tid + j * kConsThreads;
-      float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
       if (f < f4) {
-        if (emb) {
-          if (tok_ok) r = __ldg(reinterpret_cast<const float4*>(erow) + f);
-        } else {
-          const float4 x0 = ldcg4(st.a + 4 * f), x1 = ldcg4(st.b + 4 * f);
-          r = make_float4(__fadd_rn(x0.x, x1.x), __fadd_rn(x0.y, x1.y), __fadd_rn(x0.z, x1.z),
-                          __fadd_rn(x0.w, x1.w));
-        }
-        if (cid == 0 && st.res_out) {
-          reinterpret_cast<float4*>(st.res_out)[f] = r;
-          __threadfence();
-        }
+        const float4 r = v[j];
         ss = __fadd_rn(ss, __fadd_rn(__fadd_rn(__fmul_rn(r.x, r.x), __fmul_rn(r.y, r.y)),
                                      __fadd_rn(__fmul_rn(r.z, r.z), __fmul_rn(r.w, r.w))));
       }
-      v[j] = r;
     }
     ss = cons_sum(ss, red);
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
 #pragma unroll
-    for (int j = 0; j < kNV; ++j) {
-      const int f = tid + j * kConsThreads;
-      if (f < f4) {
-        const float4 w = __ldg(reinterpret_cast<const float4*>(st.w) + f);
-        v[j] = make_float4(__fmul_rn(__fmul_rn(v[j].x, inv), w.x), __fmul_rn(__fmul_rn(v[j].y, inv), w.y),
-                           __fmul_rn(__fmul_rn(v[j].z, inv), w.z), __fmul_rn(__fmul_rn(v[j].w, inv), w.w));
+    for (int j0 = 0; j0 < kNV; j0 += kPB) {
+      float4 w[kPB];
+#pragma unroll
+      for (int jj = 0; jj < kPB; ++jj) {
+        const int f = tid + (j0 + jj) * kConsThreads;
+        w[jj] = (j0 + jj < kNV && f < f4) ? __ldg(reinterpret_cast<const float4*>(st.w) + f)
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int jj = 0; jj < kPB; ++jj) {
+        if (j0 + jj >= kNV) break;
+        const float4 x = v[j0 + jj];
+        v[j0 + jj] = make_float4(__fmul_rn(__fmul_rn(x.x, inv), w[jj].x), __fmul_rn(__fmul_rn(x.y, inv), w[jj].y),
+                                 __fmul_rn(__fmul_rn(x.z, inv), w[jj].z), __fmul_rn(__fmul_rn(x.w, inv), w[jj].w));
       }
     }
   }
@@ -507,6 +570,7 @@ __device__ void prologue(const DecArgs& a, const DecStage& st, int cid, int tok,
 #pragma unroll
   for (int j = 0; j < kNV; ++j) {
     const int f = tid + j * kConsThreads;
+    if ((f & ~31) >= f4) break;   // the whole warp is past K (f4 is a multiple of 32)
     const float xv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
     uint32_t w0 = 0, w1 = 0;
     int s0 = 0, s1 = 0;
@@ -720,7 +784,26 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecArgs 
       if (a.l2_ahead <= 0) ahead.valid = false;
       for (int s = 0; s < nst && ok; ++s) {
         const DecStage& st = a.stages[s];
-        if (__ldg(&st.kind) != ST_GEMV) continue;
+        if (__ldg(&st.kind) != ST_GEMV) {
+          // attention: pull this CTA's units' cached K / V rows (known before
+          // the stage: they do not depend on q) into L2 while the q/k/v GEMV
+          // runs; row pos is appended in the stage itself
+          if (lane == 0 && pos >= 0 && pos < a.max_seq) {
+            const int S = pos, nsp = a.nsplit, HD = a.HD;
+            const int ps = (S + 1 + nsp - 1) / nsp;
+            for (int u = cid; u < a.hloc * nsp; u += G) {
+              const int h = a.h0 + u / nsp, j = u - (h - a.h0) * nsp;
+              const int hkl = h / (a.H / a.HKV) - a.hk0;
+              const int s0 = j * ps, s1 = min(S, s0 + ps);
+              if (s1 <= s0) continue;
+              const size_t off = ((size_t)hkl * a.max_seq + s0) * HD;
+              const uint32_t bytes = (uint32_t)((s1 - s0) * HD * 4);
+              bulk_prefetch_l2(st.kc + off, bytes);
+              bulk_prefetch_l2(st.vc + off, bytes);
+            }
+          }
+          continue;
+        }
         int rt0, nrt;
         row_split(__ldg(&st.n_rt), cid, G, &rt0, &nrt);
         const int nstg = nrt * __ldg(&st.nkb);
