@@ -52,17 +52,19 @@ struct T6Layout {
   static constexpr int RB = 2 * GS;                    // bytes per prepared x row (one group)
   static constexpr int XB = NR * RB;                   // one prepared x tile
   static constexpr int WBYTES = 8 * KQG * 512;         // packed weights of 8 row tiles
-  static constexpr int STAGE = XB + WBYTES;
-  static constexpr int FIT = (227 * 1024 - 1024) / STAGE;
-  static constexpr int STAGES = FIT < 8 ? FIT : 8;
+  // two rings: the weights (small; the unpack warps run ahead on them) and
+  // the x tiles (large; the MMA's B operand)
+  static constexpr int NSW = 4;
+  static constexpr int FIT = (227 * 1024 - 1024 - NSW * WBYTES) / XB;
+  static constexpr int NSX = FIT < 8 ? FIT : 8;
   static constexpr int XOFF = 1024;
-  static constexpr int WOFF = XOFF + STAGES * XB;
-  static constexpr int TOTAL = WOFF + STAGES * WBYTES;
+  static constexpr int WOFF = XOFF + NSX * XB;
+  static constexpr int TOTAL = WOFF + NSW * WBYTES;
   static constexpr int KSTEPS = GS / 16;
   static constexpr uint32_t ACOL = NR;                 // accumulator columns
   static constexpr uint32_t AW = GS / 2;               // columns of one A tile
   static constexpr int ABUF = (int)((kTmemCols - ACOL) / AW) < 4 ? (int)((kTmemCols - ACOL) / AW) : 4;
-  static_assert(STAGES >= 2, "shared memory");
+  static_assert(NSX >= 2, "shared memory");
   static_assert(ABUF >= 2, "TMEM columns");
   static_assert(TOTAL <= 227 * 1024, "shared memory");
 };
@@ -164,12 +166,14 @@ template <int KQG, int NR>
 __global__ void __launch_bounds__(kT6Threads, 1)
     q4g_tc16_kernel(const T6Args a, const __grid_constant__ T6Maps maps) {
   using L = T6Layout<KQG, NR>;
-  constexpr int NS = L::STAGES, NA = L::ABUF;
+  constexpr int NSX = L::NSX, NSW = L::NSW, NA = L::ABUF;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = smem_raw;
-  uint64_t* sfull = reinterpret_cast<uint64_t*>(smem);    // producer -> MMA, unpack
-  uint64_t* sempty = sfull + NS;                           // MMA + 4 unpack warps -> producer
-  uint64_t* afull = sempty + NS;                           // [NA] unpack -> MMA
+  uint64_t* xfull = reinterpret_cast<uint64_t*>(smem);    // producer -> MMA (x tile)
+  uint64_t* xempty = xfull + NSX;                          // MMA -> producer
+  uint64_t* wfull = xempty + NSX;                          // producer -> unpack (weights)
+  uint64_t* wempty = wfull + NSW;                          // 4 unpack warps -> producer
+  uint64_t* afull = wempty + NSW;                          // [NA] unpack -> MMA
   uint64_t* aempty = afull + NA;                           // [NA] MMA -> unpack
   uint64_t* tfull = aempty + NA;                           // MMA -> epilogue (once)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
@@ -189,9 +193,13 @@ __global__ void __launch_bounds__(kT6Threads, 1)
   const int npad = (nrows + 15) & ~15;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < NS; ++s) {
-      mbar_init(&sfull[s], 1);
-      mbar_init(&sempty[s], 1 + 4);
+    for (int s = 0; s < NSX; ++s) {
+      mbar_init(&xfull[s], 1);
+      mbar_init(&xempty[s], 1);
+    }
+    for (int s = 0; s < NSW; ++s) {
+      mbar_init(&wfull[s], 1);
+      mbar_init(&wempty[s], 4);
     }
     for (int b = 0; b < NA; ++b) {
       mbar_init(&afull[b], 4);
@@ -216,35 +224,56 @@ __global__ void __launch_bounds__(kT6Threads, 1)
   auto stop = [&]() { return *reinterpret_cast<volatile int*>(failed) != 0; };
 
   if (warp == 0) {
-    // ---------------- producer
+    // ---------------- producer: the weights of up to NSW groups ahead of the
+    // x tile in flight (weights do not depend on the previous kernel, so the
+    // first ones go out before griddep_wait)
     const uint32_t xbytes = (uint32_t)npad * L::RB;
-    int last = -1;
-    for (int g = 0; g < G; ++g) {
-      const int s = g % NS;
+    int xlast = -1, wnext = 0;
+    bool bad = false;
+    for (int g = 0; g < G && !bad; ++g) {
+      while (wnext < G && wnext < g + NSW) {
+        const int sw = wnext % NSW;
+        int ok = 1;
+        if (lane == 0)
+          ok = (!stop() && (wnext < NSW || mbar_wait_t<kT6Wait>(&wempty[sw], ((wnext / NSW) - 1) & 1))) ? 1 : 0;
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) {
+          bad = true;
+          break;
+        }
+        if (elect_one()) {
+          mbar_arrive_expect_tx(&wfull[sw], L::WBYTES);
+          tma_load_2d(smem + L::WOFF + sw * L::WBYTES, wmap, wnext * KQG * 128, rt0, &wfull[sw]);
+        }
+        __syncwarp();
+        ++wnext;
+      }
+      if (bad) break;
+      const int s = g % NSX;
       int ok = 1;
       if (lane == 0)
-        ok = (!stop() && (g < NS || mbar_wait_t<kT6Wait>(&sempty[s], ((g / NS) - 1) & 1))) ? 1 : 0;
+        ok = (!stop() && (g < NSX || mbar_wait_t<kT6Wait>(&xempty[s], ((g / NSX) - 1) & 1))) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) {
-        if (lane == 0 && !stop()) fail(3);
+        bad = true;
         break;
       }
-      unsigned char* xs = smem + L::XOFF + s * L::XB;
-      unsigned char* ws = smem + L::WOFF + s * L::WBYTES;
       const unsigned char* src = a.xp + ((size_t)mt * G + g) * L::XB;
       if (g == 0) griddep_wait();  // the prepared x comes from the previous kernel
       if (elect_one()) {
-        mbar_arrive_expect_tx(&sfull[s], xbytes + L::WBYTES);
-        bulk_g2s(xs, src, xbytes, &sfull[s]);
-        tma_load_2d(ws, wmap, g * KQG * 128, rt0, &sfull[s]);
+        mbar_arrive_expect_tx(&xfull[s], xbytes);
+        bulk_g2s(smem + L::XOFF + s * L::XB, src, xbytes, &xfull[s]);
       }
       __syncwarp();
-      last = g;
+      xlast = g;
     }
+    if (bad && lane == 0 && !stop()) fail(3);
     // the last copies land before the CTA may exit
-    if (lane == 0 && last >= 0) {
-      for (int g = max(0, last - NS + 1); g <= last; ++g)
-        if (!mbar_wait_t<kT6Wait>(&sfull[g % NS], (g / NS) & 1)) fail(3);
+    if (lane == 0) {
+      for (int g = max(0, xlast - NSX + 1); g <= xlast; ++g)
+        if (!mbar_wait_t<kT6Wait>(&xfull[g % NSX], (g / NSX) & 1)) fail(3);
+      for (int g = max(0, wnext - NSW); g < wnext; ++g)
+        if (!mbar_wait_t<kT6Wait>(&wfull[g % NSW], (g / NSW) & 1)) fail(3);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer: one accumulator over all groups
@@ -252,10 +281,10 @@ __global__ void __launch_bounds__(kT6Threads, 1)
     const uint64_t bdesc0 = smem_desc(smem + L::XOFF, 128, L::RB * 8);
     int issued = 0;
     for (int g = 0; g < G; ++g) {
-      const int s = g % NS, ab = g % NA;
+      const int s = g % NSX, ab = g % NA;
       int ok = 1;
       if (lane == 0)
-        ok = (!stop() && mbar_wait_t<kT6Wait>(&sfull[s], (g / NS) & 1) &&
+        ok = (!stop() && mbar_wait_t<kT6Wait>(&xfull[s], (g / NSX) & 1) &&
               mbar_wait_t<kT6Wait>(&afull[ab], (g / NA) & 1))
                  ? 1
                  : 0;
@@ -275,7 +304,7 @@ __global__ void __launch_bounds__(kT6Threads, 1)
                       (g > 0 || kk > 0) ? 1u : 0u);
       if (elect_one()) {
         umma_commit(&aempty[ab]);
-        umma_commit(&sempty[s]);
+        umma_commit(&xempty[s]);
       }
       __syncwarp();
       issued = g + 1;
@@ -302,7 +331,7 @@ __global__ void __launch_bounds__(kT6Threads, 1)
     float4 zn = uset < G ? __ldg(szp + (size_t)uset * 8) : make_float4(0.f, 0.f, 0.f, 0.f);
     const bool r1 = (rot & 1) != 0, r2 = (rot & 2) != 0;
     for (int g = uset; g < G; g += 2) {
-      const int s = g % NS, ab = g % NA;
+      const int s = g % NSW, ab = g % NA;
       const float4 zz = zn;
       if (g + 2 < G) zn = __ldg(szp + (size_t)(g + 2) * 8);
       const float sc = (hi ? zz.z : zz.x) * W.wscale;
@@ -310,7 +339,7 @@ __global__ void __launch_bounds__(kT6Threads, 1)
       const unsigned long long sc2 = f32x2_splat(sc), nzs2 = f32x2_splat(nzs);
       int ok = 1;
       if (lane == 0)
-        ok = (!stop() && mbar_wait_t<kT6Wait>(&sfull[s], (g / NS) & 1) &&
+        ok = (!stop() && mbar_wait_t<kT6Wait>(&wfull[s], (g / NSW) & 1) &&
               (g < NA || mbar_wait_t<kT6Wait>(&aempty[ab], ((g / NA) - 1) & 1)))
                  ? 1
                  : 0;
@@ -355,13 +384,13 @@ __global__ void __launch_bounds__(kT6Threads, 1)
         }
         tmem_st32(ta + (uint32_t)qq * 32u, col);
       }
+      // the group's weights are in registers / TMEM: their slot is free
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&wempty[s]);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&afull[ab]);
-        mbar_arrive(&sempty[s]);
-      }
+      if (lane == 0) mbar_arrive(&afull[ab]);
     }
   } else {
     // ---------------- epilogue: thread = output channel (TMEM lane), NR/2 x rows
