@@ -685,6 +685,7 @@ def run_decode_7b_sharded(nimf, torch, steps, warmup, rank, world, pos=512, max_
         recent = torch.from_numpy(np.random.default_rng(7).integers(0, V7, size=64)
                                   .astype(np.int32)).to(dev)
         keep += [nf, cos_t, sin_t, table, recent]
+        nimf.check(nimf.lib().nimf_decode_set_timeout_ms(500))
         plan = nimf.DecodePlan(layers=lws, embedding=table.data_ptr(), final_norm=nf.data_ptr(),
                                lm_head=head, rope_cos=cos_t.data_ptr(), rope_sin=sin_t.data_ptr(),
                                d_model=D7, n_heads=H, n_kv_heads=H, head_dim=HD, ffn_dim=F7,
@@ -1338,6 +1339,9 @@ def run_ours(args, rank, world, local_rank):
         # the library's own communicator and a gather buffer shared by every
         # rank: the GEMV's merge warps store each output into every GPU
         lib_comm_init(nimf, rank, world)
+        # waits between GPUs take microseconds; a short bound makes a broken
+        # exchange fail within the warm-up instead of stretching every step
+        nimf.check(nimf.lib().nimf_gather_set_timeout_ms(500))
         gid_c, base = ctypes.c_int64(), ctypes.c_void_p()
         nimf.check(nimf.lib().nimf_gather_create(R * M * n_total * 4, ctypes.byref(gid_c),
                                                  ctypes.byref(base)))
@@ -1369,6 +1373,12 @@ def run_ours(args, rank, world, local_rank):
             step(stream)
             step_single(stream)
     torch.cuda.synchronize()
+    if world > 1:
+        # every rank learns whether any rank's warm-up exchange timed out
+        bad = torch.tensor([float(nimf.lib().nimf_sync() != 0)], device="cuda")
+        dist.all_reduce(bad, op=dist.ReduceOp.MAX)
+        if bad.item() > 0:
+            raise RuntimeError("bench: the fused all-gather's arrival wait expired in the warm-up")
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         step(stream)
