@@ -375,7 +375,7 @@ typedef struct nimf_decode_desc {
 } nimf_decode_desc;
 
 /* Builds the step's stage table and its device scratch (a few hundred KB).
- * The environment variable NIMF_DECODE_L2_AHEAD (0 .. 16, default 2), read
+ * The environment variable NIMF_DECODE_L2_AHEAD (0 .. 16, default 0), read
  * here, sets how many of its items each weight-streaming lane prefetches into
  * L2 ahead of its shared-memory ring (0: none). */
 int nimf_decode_create(const nimf_decode_desc* desc, int64_t* plan);

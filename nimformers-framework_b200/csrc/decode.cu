@@ -101,7 +101,9 @@ constexpr int kOffSdi = kOffXs + kXsBytes;
 constexpr int kSdiBytes = kMaxGroups * 16 * 4;
 constexpr int kOffPart = kOffSdi + kSdiBytes;
 constexpr int kPartBytes = kNS * kNcs * 128 * 4;
-constexpr int kSmemBytes = kOffPart + kPartBytes;
+constexpr int kWbufK = 4096;                     // RMSNorm weights staged in shared memory up to this K
+constexpr int kOffWbuf = kOffPart + kPartBytes;
+constexpr int kSmemBytes = kOffWbuf + kWbufK * 4;
 // attention scratch reuses xs + sdi (the digits are dead during attention)
 constexpr int kAttnBytes = (3 * kMaxHeadDim + kMaxPs) * 4 + kCons * kMaxHeadDim * 4;
 static_assert(kAttnBytes <= kXsBytes + kSdiBytes, "attention scratch");
@@ -109,6 +111,17 @@ static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 static_assert(kOffRing >= kOffMark + 128 * 4, "head layout");
 
 enum { ST_GEMV = 0, ST_ATTN = 1 };
+
+// The fields of a GEMV stage the consumers need, read before the stage's
+// grid barrier so that their global loads are not on the critical path.
+struct ProDesc {
+  int k, groups, pro, nkb, n_rt;
+  const float* a;
+  const float* b;
+  const float* w;
+  float* res_out;
+  bool wstaged;             // w is in shared memory (kOffWbuf)
+};
 enum { PRO_EMB_RMS = 0, PRO_ADD_RMS = 1, PRO_COMBINE = 2, PRO_SWIGLU = 3 };
 
 struct DecStage {
@@ -379,7 +392,7 @@ __device__ __forceinline__ float cons_max(float v, float* red) {
 // Computes x of a GEMV stage (K values, float4 f = tid + 512 j), writes the
 // residual (CTA 0), then the digits into xs, the group digit sums into sdi and
 // max|x| into *xmax.
-__device__ void prologue(const DecArgs& a, const DecStage& st, int cid, int tok, unsigned char* smem) {
+__device__ void prologue(const DecArgs& a, const ProDesc& st, int cid, int tok, unsigned char* smem) {
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   float* red = reinterpret_cast<float*>(smem + kOffRed);
@@ -547,8 +560,10 @@ __device__ void prologue(const DecArgs& a, const DecStage& st, int cid, int tok,
 #pragma unroll
       for (int jj = 0; jj < kPB; ++jj) {
         const int f = tid + (j0 + jj) * kConsThreads;
-        w[jj] = (j0 + jj < kNV && f < f4) ? __ldg(reinterpret_cast<const float4*>(st.w) + f)
-                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+        const bool in = j0 + jj < kNV && f < f4;
+        w[jj] = !in ? make_float4(0.f, 0.f, 0.f, 0.f)
+                    : st.wstaged ? reinterpret_cast<const float4*>(smem + kOffWbuf)[f]
+                                 : __ldg(reinterpret_cast<const float4*>(st.w) + f);
       }
 #pragma unroll
       for (int jj = 0; jj < kPB; ++jj) {
@@ -981,18 +996,36 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecArgs 
         }
         continue;
       }
+      ProDesc pd;
+      pd.k = st.k;
+      pd.groups = st.groups;
+      pd.pro = st.pro;
+      pd.nkb = st.nkb;
+      pd.n_rt = st.n_rt;
+      pd.a = st.a;
+      pd.b = st.b;
+      pd.w = st.w;
+      pd.res_out = st.res_out;
+      // the norm weights do not depend on the previous stage: staged in
+      // shared memory while the grid barrier is pending
+      pd.wstaged = (pd.pro == PRO_ADD_RMS || pd.pro == PRO_EMB_RMS) && pd.k <= kWbufK;
+      if (pd.wstaged) {
+        float4* wb = reinterpret_cast<float4*>(smem + kOffWbuf);
+        for (int f = threadIdx.x; f < (pd.k >> 2); f += kConsThreads)
+          wb[f] = __ldg(reinterpret_cast<const float4*>(pd.w) + f);
+      }
       int rt0, nrt;
-      row_split(st.n_rt, cid, G, &rt0, &nrt);
-      const int nkb = st.nkb;
+      row_split(pd.n_rt, cid, G, &rt0, &nrt);
+      const int nkb = pd.nkb;
       const int nstg = nrt * nkb;
       if (threadIdx.x == 0 && s > 0) stage_wait(a, s - 1, target, gtarget);
       named_barrier(kBarCons, kConsThreads);  // also: every warp is done with the last x
       if (threadIdx.x == 0) tl_mark(a, s, 0);
-      prologue(a, st, cid, tok, smem);
+      prologue(a, pd, cid, tok, smem);
       if (threadIdx.x == 0) tl_mark(a, s, 1);
       const float sm = *xmaxp / 127.0f;
       const float dsc = t < 2 ? sm : sm * (1.0f / 256.0f);
-      const int groups = st.groups;
+      const int groups = pd.groups;
       const int ubeg = q0 * kNcs, uend = (q0 + nstg) * kNcs;
       const int u0 = ubeg + ((warp - ubeg) % kCons + kCons) % kCons;
       for (int u = u0; u < uend; u += kCons) {
@@ -1416,8 +1449,8 @@ int create_plan(const nimf_decode_desc* d, int world, int rank, int64_t* plan_ou
   A.rank = rank;
   A.timeline = nullptr;
   // L2 look-ahead of the producer lanes, in items of up to 36 KB per lane
-  // (NIMF_DECODE_L2_AHEAD, 0 .. 16; default 2: 8 ring stages ahead per SM)
-  A.l2_ahead = 2;
+  // (NIMF_DECODE_L2_AHEAD, 0 .. 16; default 0: measured slower at 2)
+  A.l2_ahead = 0;
   if (const char* ev = getenv("NIMF_DECODE_L2_AHEAD")) A.l2_ahead = std::max(0, std::min(16, atoi(ev)));
   A.hloc = (int)(H / world);
   A.h0 = (int)(rank * (H / world));
