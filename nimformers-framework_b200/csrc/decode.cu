@@ -181,11 +181,12 @@ struct DecArgs {
   int tl_cta;
 };
 
+constexpr int kTlMarks = 6;   // per stage: barrier, prologue done, arrival, x loaded, sum, max
 __device__ __forceinline__ void tl_mark(const DecArgs& a, int s, int what) {
   if (a.timeline != nullptr && (int)blockIdx.x == a.tl_cta) {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    a.timeline[(size_t)s * 3 + what] = t;
+    a.timeline[(size_t)s * kTlMarks + what] = t;
   }
 }
 
@@ -389,10 +390,14 @@ __device__ __forceinline__ float cons_max(float v, float* red) {
 }
 
 // ------------------------------------------------------------ x prologue
-// Computes x of a GEMV stage (K values, float4 f = tid + 512 j), writes the
-// residual (CTA 0), then the digits into xs, the group digit sums into sdi and
-// max|x| into *xmax.
-__device__ void prologue(const DecArgs& a, const ProDesc& st, int cid, int tok, unsigned char* smem) {
+// Computes x of a GEMV stage (K values, float4 f = tid + 512 j, j < NV),
+// writes the residual (CTA 0), then the digits into xs, the group digit sums
+// into sdi and max|x| into *xmax.  NV is the smallest slot count that holds K:
+// x lives in registers across the two consumer-wide reductions, and slots
+// sized for the largest K would not fit the 96-register budget.
+template <int NV>
+__device__ void prologue_nv(const DecArgs& a, const ProDesc& st, int cid, int tok, unsigned char* smem,
+                            int stage) {
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   float* red = reinterpret_cast<float*>(smem + kOffRed);
@@ -402,7 +407,7 @@ __device__ void prologue(const DecArgs& a, const ProDesc& st, int cid, int tok, 
   const int K = st.k;
   const int f4 = K >> 2;
   for (int i = tid; i < st.groups * 16; i += kConsThreads) sdi[i] = 0;
-  float4 v[kNV];
+  float4 v[NV];
   // Every global load of a slot set is issued before any of its values is
   // used (no fence, shuffle or data-dependent branch in between), so a
   // prologue costs about one L2 round trip per phase rather than one per
@@ -443,7 +448,7 @@ __device__ void prologue(const DecArgs& a, const ProDesc& st, int cid, int tok, 
     }
     named_barrier(kBarCons, kConsThreads);
 #pragma unroll
-    for (int j = 0; j < kNV; ++j) {
+    for (int j = 0; j < NV; ++j) {
       const int f = tid + j * kConsThreads;
       float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
       if (f < f4) {
@@ -481,18 +486,18 @@ __device__ void prologue(const DecArgs& a, const ProDesc& st, int cid, int tok, 
   } else if (st.pro == PRO_SWIGLU) {
     // slots in batches of kPB: the batch's loads first, then its values
 #pragma unroll
-    for (int j0 = 0; j0 < kNV; j0 += kPB) {
+    for (int j0 = 0; j0 < NV; j0 += kPB) {
       float4 g[kPB], u[kPB];
 #pragma unroll
       for (int jj = 0; jj < kPB; ++jj) {
         const int f = tid + (j0 + jj) * kConsThreads;
-        const bool in = j0 + jj < kNV && f < f4;
+        const bool in = j0 + jj < NV && f < f4;
         g[jj] = in ? ldcg4(st.a + 4 * f) : make_float4(0.f, 0.f, 0.f, 0.f);
         u[jj] = in ? ldcg4(st.b + 4 * f) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
       for (int jj = 0; jj < kPB; ++jj) {
-        if (j0 + jj >= kNV) break;
+        if (j0 + jj >= NV) break;
         const float gv[4] = {g[jj].x, g[jj].y, g[jj].z, g[jj].w}, uv[4] = {u[jj].x, u[jj].y, u[jj].z, u[jj].w};
         float o[4];
 #pragma unroll
@@ -510,25 +515,25 @@ __device__ void prologue(const DecArgs& a, const ProDesc& st, int cid, int tok, 
     const bool tok_ok = tok >= 0 && tok < a.vocab;
     if (emb) {
 #pragma unroll
-      for (int j = 0; j < kNV; ++j) {
+      for (int j = 0; j < NV; ++j) {
         const int f = tid + j * kConsThreads;
         v[j] = (f < f4 && tok_ok) ? __ldg(reinterpret_cast<const float4*>(erow) + f)
                                   : make_float4(0.f, 0.f, 0.f, 0.f);
       }
     } else {
 #pragma unroll
-      for (int j0 = 0; j0 < kNV; j0 += kPB) {
+      for (int j0 = 0; j0 < NV; j0 += kPB) {
         float4 xa[kPB], xb[kPB];
 #pragma unroll
         for (int jj = 0; jj < kPB; ++jj) {
           const int f = tid + (j0 + jj) * kConsThreads;
-          const bool in = j0 + jj < kNV && f < f4;
+          const bool in = j0 + jj < NV && f < f4;
           xa[jj] = in ? ldcg4(st.a + 4 * f) : make_float4(0.f, 0.f, 0.f, 0.f);
           xb[jj] = in ? ldcg4(st.b + 4 * f) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
         for (int jj = 0; jj < kPB; ++jj) {
-          if (j0 + jj >= kNV) break;
+          if (j0 + jj >= NV) break;
           v[j0 + jj] = make_float4(__fadd_rn(xa[jj].x, xb[jj].x), __fadd_rn(xa[jj].y, xb[jj].y),
                                    __fadd_rn(xa[jj].z, xb[jj].z), __fadd_rn(xa[jj].w, xb[jj].w));
         }
@@ -536,7 +541,7 @@ __device__ void prologue(const DecArgs& a, const ProDesc& st, int cid, int tok, 
     }
     if (cid == 0 && st.res_out) {
 #pragma unroll
-      for (int j = 0; j < kNV; ++j) {
+      for (int j = 0; j < NV; ++j) {
         const int f = tid + j * kConsThreads;
         if (f < f4) reinterpret_cast<float4*>(st.res_out)[f] = v[j];
       }
@@ -544,7 +549,7 @@ __device__ void prologue(const DecArgs& a, const ProDesc& st, int cid, int tok, 
     }
     float ss = 0.f;
 #pragma unroll
-    for (int j = 0; j < kNV; ++j) {
+    for (int j = 0; j < NV; ++j) {
       const int f = tid + j * kConsThreads;
       if (f < f4) {
         const float4 r = v[j];
@@ -552,22 +557,24 @@ __device__ void prologue(const DecArgs& a, const ProDesc& st, int cid, int tok, 
                                      __fadd_rn(__fmul_rn(r.z, r.z), __fmul_rn(r.w, r.w))));
       }
     }
+    if (tid == 0) tl_mark(a, stage, 3);
     ss = cons_sum(ss, red);
+    if (tid == 0) tl_mark(a, stage, 4);
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
 #pragma unroll
-    for (int j0 = 0; j0 < kNV; j0 += kPB) {
+    for (int j0 = 0; j0 < NV; j0 += kPB) {
       float4 w[kPB];
 #pragma unroll
       for (int jj = 0; jj < kPB; ++jj) {
         const int f = tid + (j0 + jj) * kConsThreads;
-        const bool in = j0 + jj < kNV && f < f4;
+        const bool in = j0 + jj < NV && f < f4;
         w[jj] = !in ? make_float4(0.f, 0.f, 0.f, 0.f)
                     : st.wstaged ? reinterpret_cast<const float4*>(smem + kOffWbuf)[f]
                                  : __ldg(reinterpret_cast<const float4*>(st.w) + f);
       }
 #pragma unroll
       for (int jj = 0; jj < kPB; ++jj) {
-        if (j0 + jj >= kNV) break;
+        if (j0 + jj >= NV) break;
         const float4 x = v[j0 + jj];
         v[j0 + jj] = make_float4(__fmul_rn(__fmul_rn(x.x, inv), w[jj].x), __fmul_rn(__fmul_rn(x.y, inv), w[jj].y),
                                  __fmul_rn(__fmul_rn(x.z, inv), w[jj].z), __fmul_rn(__fmul_rn(x.w, inv), w[jj].w));
@@ -577,13 +584,14 @@ __device__ void prologue(const DecArgs& a, const ProDesc& st, int cid, int tok, 
   // max |x|, then the digits (as q4g_gemv_kernel, M = 1)
   float mx = 0.f;
 #pragma unroll
-  for (int j = 0; j < kNV; ++j)
+  for (int j = 0; j < NV; ++j)
     mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
   mx = cons_max(mx, red);
+  if (tid == 0) tl_mark(a, stage, 5);
   if (tid == 0) *xmaxp = mx;
   const float inv = mx > 0.f ? 127.0f / mx : 0.f;
 #pragma unroll
-  for (int j = 0; j < kNV; ++j) {
+  for (int j = 0; j < NV; ++j) {
     const int f = tid + j * kConsThreads;
     if ((f & ~31) >= f4) break;   // the whole warp is past K (f4 is a multiple of 32)
     const float xv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
@@ -618,6 +626,15 @@ __device__ void prologue(const DecArgs& a, const ProDesc& st, int cid, int tok, 
     }
   }
   named_barrier(kBarCons, kConsThreads);
+}
+
+// The prologue instance whose register slots just hold K.
+__device__ __forceinline__ void prologue(const DecArgs& a, const ProDesc& st, int cid, int tok,
+                                         unsigned char* smem, int stage) {
+  const int f4 = st.k >> 2;
+  if (f4 <= 2 * kConsThreads) prologue_nv<2>(a, st, cid, tok, smem, stage);
+  else if (f4 <= 6 * kConsThreads) prologue_nv<6>(a, st, cid, tok, smem, stage);
+  else prologue_nv<kNV>(a, st, cid, tok, smem, stage);
 }
 
 // ------------------------------------------------------------ attention unit
@@ -1021,7 +1038,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecArgs 
       if (threadIdx.x == 0 && s > 0) stage_wait(a, s - 1, target, gtarget);
       named_barrier(kBarCons, kConsThreads);  // also: every warp is done with the last x
       if (threadIdx.x == 0) tl_mark(a, s, 0);
-      prologue(a, pd, cid, tok, smem);
+      prologue(a, pd, cid, tok, smem, s);
       if (threadIdx.x == 0) tl_mark(a, s, 1);
       const float sm = *xmaxp / 127.0f;
       const float dsc = t < 2 ? sm : sm * (1.0f / 256.0f);
@@ -1532,7 +1549,7 @@ int nimf_decode_step_dev(int64_t plan, int32_t* token_dev, int32_t* next_token_d
 int nimf_decode_timeline(int64_t plan, uint64_t* timeline_dev, int64_t n, int cta) {
   DecodePlan* P = find_plan(plan);
   if (!P) return set_error(NIMF_ERR_STATE, "decode_timeline: unknown plan %lld", (long long)plan);
-  if (timeline_dev && (n < 3 * (int64_t)P->stages.size() || cta < 0 || cta >= P->grid))
+  if (timeline_dev && (n < kTlMarks * (int64_t)P->stages.size() || cta < 0 || cta >= P->grid))
     return set_error(NIMF_ERR_SHAPE, "decode_timeline: %lld entries for %zu stages, CTA %d of %d",
                      (long long)n, P->stages.size(), cta, P->grid);
   P->base.timeline = (unsigned long long*)timeline_dev;
