@@ -411,12 +411,16 @@ int nimf_decode_step_dev(int64_t plan, int32_t* token_dev, int32_t* next_token_d
                          int32_t* pos_dev, int advance_pos, const int32_t* recent_dev,
                          int64_t n_recent, float repeat_penalty, float* logits_dev, void* stream);
 /* Profiling aid (no reference counterpart): while timeline_dev (device,
- * n >= 6 * stages uint64 entries) is set, each step records for CTA `cta`
+ * n >= 12 * stages uint64 entries) is set, each step records for CTA `cta`
  * the %globaltimer nanoseconds at which, per stage: [0] its consumers passed
  * the stage's grid barrier, [1] finished the stage's x prologue, [2] its merge
  * warp (attention stages: its consumers) arrived, and inside the prologue
- * [3] x's inputs were in, [4] the norm's sum, [5] max|x| was reduced (0 where
- * a stage has no such step).  NULL stops recording. */
+ * [3] x's inputs were in, [4] the norm's sum, [5] max|x| was reduced, and in
+ * the GEMV body [6] consumer warp 0 had its first item, [7] finished its last
+ * chunk, [8] the merge warp had stored y, and for warp 0's first chunk [9] its
+ * products were summed, [10] its partial slot was free, [11] the partial was
+ * handed to the merge warp (0 where a stage has no such step).  NULL stops
+ * recording. */
 int nimf_decode_timeline(int64_t plan, uint64_t* timeline_dev, int64_t n, int cta);
 /* Grid size (CTAs), number of stages and attention position splits of a plan. */
 int nimf_decode_info(int64_t plan, int64_t* grid, int64_t* stages, int64_t* attn_splits);

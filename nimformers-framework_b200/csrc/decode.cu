@@ -181,7 +181,10 @@ struct DecArgs {
   int tl_cta;
 };
 
-constexpr int kTlMarks = 6;   // per stage: barrier, prologue done, arrival, x loaded, sum, max
+// per stage: barrier, prologue done, arrival, x loaded, sum, max, first item,
+// last chunk of consumer warp 0, merge stores done; warp 0's first chunk:
+// computed, partial slot free, partial handed over
+constexpr int kTlMarks = 12;
 __device__ __forceinline__ void tl_mark(const DecArgs& a, int s, int what) {
   if (a.timeline != nullptr && (int)blockIdx.x == a.tl_cta) {
     unsigned long long t;
@@ -212,6 +215,9 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
+}
+__device__ __forceinline__ float2 ldcg2(const float* p) {
+  return __ldcg(reinterpret_cast<const float2*>(p));
 }
 __device__ __forceinline__ float4 ldcg4(const float* p) {
   return __ldcg(reinterpret_cast<const float4*>(p));
@@ -413,10 +419,76 @@ __device__ void prologue_nv(const DecArgs& a, const ProDesc& st, int cid, int to
   // prologue costs about one L2 round trip per phase rather than one per
   // load.  Slots j with 512 j >= K / 4 are empty for the whole warp.
   const int warp = tid >> 5;
-  if (st.pro == PRO_COMBINE) {
-    // per head: M = max_j m_j, L = sum_j [l_j > 0] e^(m_j - M) l_j in split
-    // order, weights e^(m_j - M) (attn_combine_kernel's arithmetic): lane j
-    // of the head's warp holds split j
+  if (NV <= 2 && st.pro == PRO_COMBINE && a.HD == 128) {
+    // Head dimension 128, up to 32 heads: slot j of warp w is all of head
+    // w + 16 j (lane l
+    // holds d = 4 l .. 4 l + 3), so one warp combines one head per slot with
+    // shuffles, and every load of a slot set (lane j's (m_j, l_j), the
+    // lane's d of the first four splits) is issued before any is used.
+    // Arithmetic as below: M = max_j m_j, L = sum over live j (l_j > 0) of
+    // e^(m_j - M) l_j in split order, o = sum over live j of e^(m_j - M) o_j
+    // in split order, x = o / L.
+    const int ns = a.nsplit;
+    float2 ml[NV];
+    float4 o[NV][4];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int f = tid + j * kConsThreads;
+      const bool in = (f & ~31) < f4;                  // warp-uniform
+      const int h = f >> 5;
+      ml[j] = (in && lane < ns) ? ldcg2(a.part_ml + ((size_t)h * ns + lane) * 2) : make_float2(-INFINITY, 0.f);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        o[j][q] = (in && q < ns) ? ldcg4(a.part_o + ((size_t)h * ns + q) * 128 + 4 * lane)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int f = tid + j * kConsThreads;
+      if ((f & ~31) >= f4) {
+        v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        continue;
+      }
+      const int h = f >> 5;
+      float M = ml[j].x;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+      const bool live = lane < ns && ml[j].y > 0.f;
+      const float e = live ? expf(__fsub_rn(ml[j].x, M)) : 0.f;
+      const float el = live ? __fmul_rn(e, ml[j].y) : 0.f;
+      const unsigned mask = __ballot_sync(0xffffffffu, live);
+      float L = 0.f;
+      for (int sp = 0; sp < ns; ++sp) {
+        const float t = __shfl_sync(0xffffffffu, el, sp);
+        if ((mask >> sp) & 1u) L = __fadd_rn(L, t);
+      }
+      float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+      for (int s0 = 0; s0 < ns; s0 += 4) {
+        float4 ob[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          ob[q] = s0 == 0 ? o[j][q]
+                          : (s0 + q < ns ? ldcg4(a.part_o + ((size_t)h * ns + s0 + q) * 128 + 4 * lane)
+                                         : make_float4(0.f, 0.f, 0.f, 0.f));
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int sp = s0 + q;
+          const float wgt = __shfl_sync(0xffffffffu, e, sp & 31);
+          if (sp < ns && ((mask >> sp) & 1u)) {
+            o0 = __fadd_rn(o0, __fmul_rn(wgt, ob[q].x));
+            o1 = __fadd_rn(o1, __fmul_rn(wgt, ob[q].y));
+            o2 = __fadd_rn(o2, __fmul_rn(wgt, ob[q].z));
+            o3 = __fadd_rn(o3, __fmul_rn(wgt, ob[q].w));
+          }
+        }
+      }
+      v[j] = make_float4(__fdiv_rn(o0, L), __fdiv_rn(o1, L), __fdiv_rn(o2, L), __fdiv_rn(o3, L));
+    }
+  } else if (st.pro == PRO_COMBINE) {
+    // any head dimension: per head, M = max_j m_j, L = sum_j [l_j > 0]
+    // e^(m_j - M) l_j in split order, weights e^(m_j - M)
+    // (attn_combine_kernel's arithmetic): lane j of the head's warp holds
+    // split j
     float* cw = reinterpret_cast<float*>(smem + kOffComb);
     float* cml = reinterpret_cast<float*>(smem + kOffCombML);
     const int ns = a.nsplit;
@@ -686,7 +758,9 @@ __device__ void attn_unit(const DecArgs& a, const DecStage& st, int h, int j, in
   float ql[DV];
 #pragma unroll
   for (int i = 0; i < DV; ++i) ql[i] = qs[lane + 32 * i];
-  constexpr int U = 4;
+  // warp w takes positions [w U, w U + U) of every block of kCons U: at the
+  // split lengths of a 4-way split of a few hundred positions, one block
+  constexpr int U = 8;
   for (int b = warp * U; b < ns; b += kCons * U) {
     float kv[U][DV];
 #pragma unroll
@@ -723,13 +797,15 @@ __device__ void attn_unit(const DecArgs& a, const DecStage& st, int h, int j, in
   for (int i = 0; i < DV; ++i) acc[i] = 0.f;
   for (int b = warp * U; b < ns; b += kCons * U) {
     float vv[U][DV];
+    {
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int p = b + u;
-      const bool isnew = s0 + p == pos;
+      for (int u = 0; u < U; ++u) {
+        const int p = b + u;
+        const bool isnew = s0 + p == pos;
 #pragma unroll
-      for (int i = 0; i < DV; ++i)
-        vv[u][i] = p < ns ? (isnew ? vn[lane + 32 * i] : __ldg(V + (size_t)p * HD + lane + 32 * i)) : 0.f;
+        for (int i = 0; i < DV; ++i)
+          vv[u][i] = p < ns ? (isnew ? vn[lane + 32 * i] : __ldg(V + (size_t)p * HD + lane + 32 * i)) : 0.f;
+      }
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -968,6 +1044,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecArgs 
           }
         }
       }
+      if (lane == 0) tl_mark(a, s, 8);
       // this lane's y (and argmax) visible before the arrival
       if (a.world == 1) __threadfence();
       else __threadfence_system();
@@ -1057,33 +1134,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecArgs 
         if (!dwait<1000>(a, &full[slot], (qq / kNS) & 1)) {
           if (lane == 0 && a.err) atomicExch(a.err, 1);
         } else {
+          if (threadIdx.x == 0 && u == u0) tl_mark(a, s, 6);
           const unsigned char* stg = ring + (size_t)slot * kStageBytes;
           const uint4* wq = reinterpret_cast<const uint4*>(stg + (size_t)c * kChunkQ * 512) + lane;
           const float4* szp = reinterpret_cast<const float4*>(stg + kStageW + (size_t)cg0 * 128) + g;
-          uint4 wr[kChunkQ];
-          float4 sr[kCG];
 #pragma unroll
           for (int gl = 0; gl < kCG; ++gl) {
             if (gl < ncg) {
-#pragma unroll
-              for (int qq2 = 0; qq2 < kKQG; ++qq2) wr[gl * kKQG + qq2] = wq[(gl * kKQG + qq2) * 32];
-              sr[gl] = szp[gl * 8];
-            }
-          }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&empty[slot]);
-          int acc[kCG][4];
-#pragma unroll
-          for (int gl = 0; gl < kCG; ++gl)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) acc[gl][e] = 0;
-#pragma unroll
-          for (int gl = 0; gl < kCG; ++gl) {
-            if (gl < ncg) {
+              int ac[4] = {0, 0, 0, 0};
 #pragma unroll
               for (int qq2 = 0; qq2 < kKQG; ++qq2) {
                 const int ql = gl * kKQG + qq2;
-                const uint4 w = wr[ql];
+                const uint4 w = wq[ql * 32];
 #pragma unroll
                 for (int hh = 0; hh < 2; ++hh) {
                   const uint32_t wa = hh == 0 ? w.x : w.z, wb = hh == 0 ? w.y : w.w;
@@ -1091,20 +1153,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecArgs 
                   const uint32_t a2 = wb & 0x0F0F0F0Fu, a3 = (wb >> 4) & 0x0F0F0F0Fu;
                   const int kt32 = (gb * kKQG + ql) * 2 + hh;
                   const uint2 bfr = xs2[(size_t)kt32 * xstride];
-                  mma_s8_16832(acc[gl], a0, a1, a2, a3, bfr.x, bfr.y);
+                  mma_s8_16832(ac, a0, a1, a2, a3, bfr.x, bfr.y);
                 }
               }
-            }
-          }
-#pragma unroll
-          for (int gl = 0; gl < kCG; ++gl) {
-            if (gl < ncg) {
-              const float4 sp = sr[gl];
+              const float4 sp = szp[gl * 8];
               const float d0 = (float)sdi[(gb + gl) * 16 + sd_off];
-              tot[0] = fmaf(sp.x * dsc, fmaf(-sp.y, d0, (float)acc[gl][0]), tot[0]);
-              tot[2] = fmaf(sp.z * dsc, fmaf(-sp.w, d0, (float)acc[gl][2]), tot[2]);
+              tot[0] = fmaf(sp.x * dsc, fmaf(-sp.y, d0, (float)ac[0]), tot[0]);
+              tot[2] = fmaf(sp.z * dsc, fmaf(-sp.w, d0, (float)ac[2]), tot[2]);
             }
           }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[slot]);
+          if (threadIdx.x == 0 && u == u0) tl_mark(a, s, 9);
         }
         // hand the chunk's partial to the merge warp (slot reused: wait until
         // the merge warp has read the previous round)
@@ -1113,6 +1173,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecArgs 
           if (lane == 0 && a.err) atomicExch(a.err, 1);
           continue;
         }
+        if (threadIdx.x == 0 && u == u0) tl_mark(a, s, 10);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int r = g + ((e & 2) ? 8 : 0);
@@ -1122,6 +1183,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecArgs 
         __threadfence_block();
         __syncwarp();
         if (lane == 0) mbar_arrive(&pfull[slot]);
+        if (threadIdx.x == 0 && u == u0) tl_mark(a, s, 11);
+        if (threadIdx.x == 0 && u + kCons >= uend) tl_mark(a, s, 7);
       }
       q0 += nstg;
     }
