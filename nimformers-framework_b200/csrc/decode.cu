@@ -574,7 +574,7 @@ __device__ void prologue_nv(const DecArgs& a, const ProDesc& st, int cid, int to
         float o[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gv[e])));
+          const float sig = __frcp_rn(__fadd_rn(1.0f, expf(-gv[e])));   // = 1 / (1 + e^-g), rounded once
           o[e] = __fmul_rn(__fmul_rn(gv[e], sig), uv[e]);
         }
         v[j0 + jj] = make_float4(o[0], o[1], o[2], o[3]);   // zeros give zeros

@@ -301,7 +301,7 @@ __global__ void swiglu_kernel(const float* __restrict__ g, const float* __restri
   griddep_launch_dependents();
   griddep_wait();
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g[i])));
+    const float sig = __frcp_rn(__fadd_rn(1.0f, expf(-g[i])));   // = 1 / (1 + e^-g), rounded once
     out[i] = __fmul_rn(__fmul_rn(g[i], sig), u[i]);
   }
 }
