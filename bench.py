@@ -429,6 +429,46 @@ def run_decode_7b(nimf, torch, steps, warmup, rank=0, world=1, exchange="p2p", b
     return out
 
 
+def decode_timeline(nimf, torch, plan, one, tok):
+    """Per-stage averages (microseconds) of one recorded step of a decode plan
+    for CTA 0, from nimf_decode_timeline's %globaltimer marks: for each stage
+    kind of a layer (q/k/v GEMV, attention, o GEMV, gate/up GEMV, down GEMV;
+    lm_head last) the wait at the grid barrier after the previous stage
+    (`gap`), the x prologue (`pro`: inputs, norm, max|x|, digits) and the body
+    up to the CTA's arrival (`body`); `chunk0` is consumer warp 0's first
+    chunk (16 rows x 512 k: fragment loads, 16 MMAs, scales)."""
+    import ctypes
+    L = nimf.lib()
+    nst = plan.info()["stages"]
+    marks = 12
+    tl = torch.zeros(marks * nst, dtype=torch.int64, device="cuda")
+    nimf.check(L.nimf_decode_timeline(plan.plan, ctypes.c_void_p(tl.data_ptr()), marks * nst, 0))
+    one(tok)
+    torch.cuda.synchronize()
+    nimf.check(L.nimf_sync())
+    nimf.check(L.nimf_decode_timeline(plan.plan, None, 0, 0))
+    t = tl.cpu().numpy().reshape(nst, marks).astype(float) / 1e3
+    names = ["qkv", "attn", "o", "gate_up", "down"]
+    agg = {}
+    for i in range(nst):
+        kind = "lm_head" if i == nst - 1 else names[i % 5]
+        r = t[i]
+        gap = r[0] - t[i - 1][2] if i > 0 else 0.0
+        pro = r[1] - r[0] if r[1] > 0 else 0.0
+        body = r[2] - (r[1] if r[1] > 0 else r[0])
+        c0 = r[9] - r[6] if (r[9] > 0 and r[6] > 0) else 0.0
+        d = agg.setdefault(kind, [0, 0.0, 0.0, 0.0, 0.0])
+        d[0] += 1
+        d[1] += gap
+        d[2] += pro
+        d[3] += body
+        d[4] += c0
+    out = {k: {"gap": round(v[1] / v[0], 2), "pro": round(v[2] / v[0], 2), "body": round(v[3] / v[0], 2),
+               "chunk0": round(v[4] / v[0], 2)} for k, v in agg.items()}
+    out["step_us"] = round(float(t[-1][2] - t[t > 0].min()), 1)
+    return out
+
+
 def run_decode_7b_full(nimf, torch, steps, warmup, pos=512, max_seq=640, layers=L7):
     """tok/s of one whole 7B-shape decode step at batch 1 with the glue on the
     device: per layer RMSNorm, fused q/k/v GEMV, RoPE on q and k (one launch),
@@ -575,7 +615,8 @@ def run_decode_7b_full(nimf, torch, steps, warmup, pos=512, max_seq=640, layers=
                              "gb_s": (decode7b_bytes(1) + kv_bytes) / (ms1 * 1e-3) / 1e9,
                              "launches_per_step": 1, "plan": plan.info(),
                              "logits_rel_err_vs_per_op": err,
-                             "same_token_as_per_op": one_tok == ref_tok}
+                             "same_token_as_per_op": one_tok == ref_tok,
+                             "timeline_cta0_us": decode_timeline(nimf, torch, plan, one, tok1)}
         # the same plan with the producers' L2 look-ahead, for comparison
         plan.destroy()
         os.environ["NIMF_DECODE_L2_AHEAD"] = "2"
