@@ -88,8 +88,7 @@ static_assert(kNS == kIssuers && (kNS * kNcs) % kCons == 0, "ring period: produc
 // ---- shared memory
 constexpr int kOffBar = 0;                        // full, empty, merged, pfull [kNS] uint64
 constexpr int kOffRed = 128;                      // float[32] reduction scratch
-constexpr int kOffZpad = 256;                     // 32 zero bytes
-constexpr int kOffMisc = 288;                     // xmax, counters
+constexpr int kOffMisc = 288;                     // xmax, counters (256 .. 287 unused)
 constexpr int kOffComb = 384;                     // combine weights [kMaxHeads][kMaxSplit]
 constexpr int kOffCombML = kOffComb + kMaxHeads * kMaxSplit * 4;   // [kMaxHeads][2]
 constexpr int kOffRecent = kOffCombML + kMaxHeads * 2 * 4;         // int[kMaxRecent]
@@ -874,7 +873,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecArgs 
     }
     mbar_fence_init();
   }
-  if (threadIdx.x < 8) reinterpret_cast<unsigned*>(smem + kOffZpad)[threadIdx.x] = 0u;
   for (int i = threadIdx.x; i < a.n_recent; i += blockDim.x) rec[i] = __ldg(a.recent + i);
   __syncthreads();
 
@@ -1059,11 +1057,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecArgs 
     const int g = lane >> 2, t = lane & 3;
     const float* xmaxp = reinterpret_cast<const float*>(smem + kOffMisc);
     const int* sdi = reinterpret_cast<const int*>(smem + kOffSdi);
-    const bool bvalid = (g & 3) == 0;               // x row 0: columns 0 (d0) and 4 (d1)
+    // x row 0 is B columns 0 (d0) and 4 (d1); the lanes of columns 1-3 and
+    // 5-7 read the same digits (one wavefront per B load), and those MMA
+    // columns are never read back
     const int ccol = g < 4 ? 0 : 1;
-    const uint2* zpad = reinterpret_cast<const uint2*>(smem + kOffZpad);
-    const uint2* xs2 = bvalid ? reinterpret_cast<const uint2*>(smem + kOffXs) + ccol * 4 + t : zpad;
-    const int xstride = bvalid ? 8 : 0;
+    const uint2* xs2 = reinterpret_cast<const uint2*>(smem + kOffXs) + ccol * 4 + t;
+    const int xstride = 8;
     const int sd_off = t < 2 ? 2 * t : 2 * t + 4;
     int q0 = 0;
     for (int s = 0; s < nst; ++s) {

@@ -282,7 +282,7 @@ constexpr int kConsWait = NIMF_Q4G_CWAIT;
 
 // Shared-memory layout of one CTA:
 //   head: full/empty/merged/pfull[kStages] mbarriers,
-//         xmax[8] (|x| maxima as float bits), zero pad (16 B), problem table
+//         xmax[8] (|x| maxima as float bits), 16 B spare, problem table
 //   ring[ns][stage]   k-blocks of row tiles (packed weights, then the
 //                     scale/zero pairs of their groups)
 //   xs    B fragments of the two s8 digits of x for the k-split:
@@ -370,7 +370,6 @@ q4g_gemv_kernel(const GemvArgs a) {
   uint64_t* merged = empty + kStages;  // direct mode: the stage's partial slots are free again
   uint64_t* pfull = merged + kStages;  // direct mode: all chunk partials of the stage written
   unsigned* xmax = reinterpret_cast<unsigned*>(pfull + kStages);
-  const uint4* zpad = reinterpret_cast<const uint4*>(xmax + 8);
   const uint4** tfrag = reinterpret_cast<const uint4**>(smem + kBarBytes);
   const float4** tsz = reinterpret_cast<const float4**>(tfrag + kMaxProblems);
   float** ty = reinterpret_cast<float**>(smem + kBarBytes + 2 * kMaxProblems * 8);
@@ -406,7 +405,6 @@ q4g_gemv_kernel(const GemvArgs a) {
   }
   if (threadIdx.x <= a.nprob) tpref[threadIdx.x] = a.rt_prefix[threadIdx.x];
   if (threadIdx.x < 8) xmax[threadIdx.x] = 0u;
-  if (threadIdx.x < 4) reinterpret_cast<unsigned*>(xmax + 8)[threadIdx.x] = 0u;  // zero pad
   for (int i = threadIdx.x; i < ng * 16; i += blockDim.x) sdi[i] = 0;
   __syncthreads();
 
@@ -638,11 +636,15 @@ q4g_gemv_kernel(const GemvArgs a) {
       dsc[c] = (MODE == 1 && t >= 2) ? sm * (1.0f / 256.0f) : sm;
       dsc2[c] = sm * (1.0f / 256.0f);
     }
-    // invalid columns read a zero pad (unconditional loads, no divergence)
-    const uint2* xs2 = bvalid ? reinterpret_cast<const uint2*>(xs) + ccol * 4 + t
-                              : reinterpret_cast<const uint2*>(zpad);
-    const uint4* xs4 = bvalid ? reinterpret_cast<const uint4*>(xs) + ccol * 4 + t : zpad;
-    const int xstride = bvalid ? cols * 4 : 0;
+    // Lanes of columns past M read column 0's digits (d0 / d1 half) of the
+    // same k32 tile: the warp's B load then touches the tile's digits only
+    // (one shared-memory wavefront at M = 1, not two with a separate zero
+    // pad).  Those MMA columns belong to x rows >= M, whose results are never
+    // stored.
+    const int ccol_rd = bvalid ? ccol : (MODE == 1 ? (g < 4 ? 0 : a.m) : 0);
+    const uint2* xs2 = reinterpret_cast<const uint2*>(xs) + ccol_rd * 4 + t;
+    const uint4* xs4 = reinterpret_cast<const uint4*>(xs) + ccol_rd * 4 + t;
+    const int xstride = cols * 4;
 
     for (int u = warp; u < nunits; u += kCons) {
       const int q = u / ncs, c = u - q * ncs;
