@@ -1147,18 +1147,20 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecArgs 
                 const uint4 w = wq[ql * 32];
 #pragma unroll
                 for (int hh = 0; hh < 2; ++hh) {
+                  // high nibbles masked in place: rows g + 8 at 16 times
+                  // their value (u8 A operand), shifted out below
                   const uint32_t wa = hh == 0 ? w.x : w.z, wb = hh == 0 ? w.y : w.w;
-                  const uint32_t a0 = wa & 0x0F0F0F0Fu, a1 = (wa >> 4) & 0x0F0F0F0Fu;
-                  const uint32_t a2 = wb & 0x0F0F0F0Fu, a3 = (wb >> 4) & 0x0F0F0F0Fu;
+                  const uint32_t a0 = wa & 0x0F0F0F0Fu, a1 = wa & 0xF0F0F0F0u;
+                  const uint32_t a2 = wb & 0x0F0F0F0Fu, a3 = wb & 0xF0F0F0F0u;
                   const int kt32 = (gb * kKQG + ql) * 2 + hh;
                   const uint2 bfr = xs2[(size_t)kt32 * xstride];
-                  mma_s8_16832(ac, a0, a1, a2, a3, bfr.x, bfr.y);
+                  mma_u8s8_16832(ac, a0, a1, a2, a3, bfr.x, bfr.y);
                 }
               }
               const float4 sp = szp[gl * 8];
               const float d0 = (float)sdi[(gb + gl) * 16 + sd_off];
               tot[0] = fmaf(sp.x * dsc, fmaf(-sp.y, d0, (float)ac[0]), tot[0]);
-              tot[2] = fmaf(sp.z * dsc, fmaf(-sp.w, d0, (float)ac[2]), tot[2]);
+              tot[2] = fmaf(sp.z * dsc, fmaf(-sp.w, d0, (float)(ac[2] >> 4)), tot[2]);   // exact: 16 A
             }
           }
           __syncwarp();

@@ -74,6 +74,18 @@ __device__ __forceinline__ void mma_s8_16832(int* d, uint32_t a0, uint32_t a1, u
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// The same MMA with an unsigned A operand (u8 x s8): an int4 weight word's
+// high nibbles masked in place (0x00, 0x10 .. 0xF0) enter as 16 times their
+// value, so the rows they feed come out scaled by exactly 16.
+__device__ __forceinline__ void mma_u8s8_16832(int* d, uint32_t a0, uint32_t a1, uint32_t a2,
+                                               uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 // Splits two fp32 values into bf16x2 hi and lo parts with x ~= hi + lo to
 // about 2^-17 relative (each part rounded to nearest).
 __device__ __forceinline__ void split_bf16x2(float x0, float x1, uint32_t& hi, uint32_t& lo) {

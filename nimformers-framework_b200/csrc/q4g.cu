@@ -700,23 +700,37 @@ q4g_gemv_kernel(const GemvArgs a) {
               const uint4 w = kStaged ? wr[kStaged ? ql : 0] : wq[ql * 32];
 #pragma unroll
               for (int h = 0; h < 2; ++h) {
+                // low nibbles: rows g (a0, a2); high nibbles masked in
+                // place: rows g + 8 (a1, a3) at 16 times their value, taken
+                // out of the sums in the group epilogue (exact)
                 const uint32_t wa = h == 0 ? w.x : w.z, wb = h == 0 ? w.y : w.w;
-                const uint32_t a0 = wa & 0x0F0F0F0Fu, a1 = (wa >> 4) & 0x0F0F0F0Fu;
-                const uint32_t a2 = wb & 0x0F0F0F0Fu, a3 = (wb >> 4) & 0x0F0F0F0Fu;
+                const uint32_t a0 = wa & 0x0F0F0F0Fu, a1 = wa & 0xF0F0F0F0u;
+                const uint32_t a2 = wb & 0x0F0F0F0Fu, a3 = wb & 0xF0F0F0F0u;
                 const int kt32 = (gb * KQG + ql) * 2 + h;  // k32 tile within the k-split
                 if (MODE == 1) {
                   const uint2 b = xs2[(size_t)kt32 * xstride];
-                  mma_s8_16832(acc[gl], a0, a1, a2, a3, b.x, b.y);
+                  mma_u8s8_16832(acc[gl], a0, a1, a2, a3, b.x, b.y);
                 } else {
                   const uint4 b = xs4[(size_t)kt32 * xstride];
-                  mma_s8_16832(acc[gl], a0, a1, a2, a3, b.x, b.y);
-                  mma_s8_16832(acc2[MODE == 2 ? gl : 0], a0, a1, a2, a3, b.z, b.w);
+                  mma_u8s8_16832(acc[gl], a0, a1, a2, a3, b.x, b.y);
+                  mma_u8s8_16832(acc2[MODE == 2 ? gl : 0], a0, a1, a2, a3, b.z, b.w);
                 }
               }
             }
           }
         }
-        // per-group epilogue: sum_k (n - zp) sc x = sc s (A - zp D)
+        // per-group epilogue: sum_k (n - zp) sc x = sc s (A - zp D); rows
+        // g + 8 (accumulator elements 2, 3) carry 16 A: every term is a
+        // multiple of 16, so the shift is exact
+#pragma unroll
+        for (int gl = 0; gl < CG; ++gl) {
+          acc[gl][2] >>= 4;
+          acc[gl][3] >>= 4;
+          if (MODE == 2) {
+            acc2[MODE == 2 ? gl : 0][2] >>= 4;
+            acc2[MODE == 2 ? gl : 0][3] >>= 4;
+          }
+        }
 #pragma unroll
         for (int gl = 0; gl < CG; ++gl) {
           if (gl < ncg) {
