@@ -335,7 +335,9 @@ __host__ __device__ inline SmemLayout q4g_smem_layout(int mode, int kqg, int gps
 // MODE 1: M <= 4, one MMA per 32 k (d0 in columns 0..3, d1 in 4..7).
 // MODE 2: M <= 8, two MMAs per 32 k (d0 and d1 each in columns 0..7).
 // KQG: k-quads (64 k) per quantisation group (group size 64 * KQG).
-template <int MODE, int KQG>
+// M1 (MODE 1 only): exactly one row of x, so the B column stride is a
+// constant and only the two result columns of x row 0 are computed.
+template <int MODE, int KQG, bool M1>
 __global__ void __launch_bounds__((kCons + 2) * 32, kCtasPerSm)
 q4g_gemv_kernel(const GemvArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -644,19 +646,33 @@ q4g_gemv_kernel(const GemvArgs a) {
     const int ccol_rd = bvalid ? ccol : (MODE == 1 ? (g < 4 ? 0 : a.m) : 0);
     const uint2* xs2 = reinterpret_cast<const uint2*>(xs) + ccol_rd * 4 + t;
     const uint4* xs4 = reinterpret_cast<const uint4*>(xs) + ccol_rd * 4 + t;
-    const int xstride = cols * 4;
+    const int xstride = M1 ? 8 : cols * 4;
 
-    for (int u = warp; u < nunits; u += kCons) {
-      const int q = u / ncs, c = u - q * ncs;
+    // unit u = q ncs + c (stage q, chunk c) steps by kCons units without
+    // divisions: s = q mod NS (ring slot), ph = (q / NS) & 1 (its phase),
+    // kb = q mod nkb (k-block)
+    int q = warp / ncs, c = warp - (warp / ncs) * ncs;
+    int s = q % NS, ph = (q / NS) & 1, kb = q % nkb;
+    auto advance = [&]() {
+      c += kCons;
+      while (c >= ncs) {
+        c -= ncs;
+        ++q;
+        if (++s == NS) {
+          s = 0;
+          ph ^= 1;
+        }
+        if (++kb == nkb) kb = 0;
+      }
+    };
+    for (int u = warp; u < nunits; u += kCons, advance()) {
       if (c >= nchunk) continue;  // the last k-split may have fewer chunks
-      const int s = q % NS;
-      const int kb = q % nkb;
       // chunks past the end of a short last k-block (direct mode) still take
       // part in the stage's barriers, with no groups (their partial is zero)
       const int cg0 = c * CG, ncg = max(0, min(CG, kb_groups(kb) - cg0));
       const int gb = kb * a.kbg + cg0;  // first group of the chunk in the k-split
       float tot[4] = {0.f, 0.f, 0.f, 0.f};
-      if (!mbar_wait_t<kConsWait>(&full[s], (q / NS) & 1)) {
+      if (!mbar_wait_t<kConsWait>(&full[s], ph)) {
         if (lane == 0 && a.err) atomicExch(a.err, 1);
       } else {
         // MODE 1 (group size >= 128) loads the chunk (weights and scales) into
@@ -737,7 +753,11 @@ q4g_gemv_kernel(const GemvArgs a) {
             const float4 sp = kStaged ? sr[kStaged ? gl : 0] : szp[gl * 8];
             const int* sd = sdi + (gb + gl) * 16;
             const float d0a = (float)sd[sd_off], d0b = (float)sd[sd_off + 1];
-            if (MODE == 1) {
+            if (MODE == 1 && M1) {
+              // column 2t only (x row 0's d0 or d1 part); 2t + 1 stays zero
+              tot[0] = fmaf(sp.x * dsc[0], fmaf(-sp.y, d0a, (float)acc[gl][0]), tot[0]);
+              tot[2] = fmaf(sp.z * dsc[0], fmaf(-sp.w, d0a, (float)acc[gl][2]), tot[2]);
+            } else if (MODE == 1) {
               tot[0] = fmaf(sp.x * dsc[0], fmaf(-sp.y, d0a, (float)acc[gl][0]), tot[0]);
               tot[1] = fmaf(sp.x * dsc[1], fmaf(-sp.y, d0b, (float)acc[gl][1]), tot[1]);
               tot[2] = fmaf(sp.z * dsc[0], fmaf(-sp.w, d0a, (float)acc[gl][2]), tot[2]);
@@ -780,7 +800,7 @@ q4g_gemv_kernel(const GemvArgs a) {
       // merger warp.  The stage's partial slots are reused by the next round
       // of the same stage: wait until the merger has read the previous one.
       float* red = part + ((size_t)s * ncs) * 128;
-      if (q >= NS && !mbar_wait_t<kConsWait>(&merged[s], ((q / NS) - 1) & 1)) {
+      if (q >= NS && !mbar_wait_t<kConsWait>(&merged[s], ph ^ 1)) {
         if (lane == 0 && a.err) atomicExch(a.err, 1);
         continue;
       }
@@ -1030,11 +1050,14 @@ int launch_fast(const Piece* pcs, int npc, const float* x, int64_t ldx, int mc, 
   int n_rt = 0;
   for (int i = 0; i < npc; ++i) n_rt += pcs[i].n_rt;
   const int slots = num_sms * kCtasPerSm;
-  auto kern = q4g_gemv_kernel<MODE, KQG>;
+  auto kern = q4g_gemv_kernel<MODE, KQG, false>;
+  auto kern1 = q4g_gemv_kernel<MODE, KQG, MODE == 1>;
   static int attr_dev = -1;
   static int max_active[kMaxSplits + 1];
   if (c && attr_dev != c->device) {
     NIMF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kSmemBudget));
+    NIMF_CUDA_TRY(cudaFuncSetAttribute(kern1, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)kSmemBudget));
     // clusters of each size that fit on the GPU at once (GPC boundaries make
     // this less than SMs / size for sizes that do not divide a GPC)
@@ -1154,7 +1177,7 @@ int launch_fast(const Piece* pcs, int npc, const float* x, int64_t ldx, int mc, 
   attrs[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
   cfg.numAttrs = 2;
-  NIMF_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a));
+  NIMF_CUDA_TRY(cudaLaunchKernelEx(&cfg, (MODE == 1 && mc == 1) ? kern1 : kern, a));
   return NIMF_OK;
 }
 
