@@ -302,6 +302,16 @@ __device__ __forceinline__ void row_split(int n_rt, int cid, int G, int* rt0, in
   *nrt = base + (cid < rem ? 1 : 0);
 }
 
+// v[i] for a small register array and a runtime i (selects, no local memory)
+template <typename T, int N>
+__device__ __forceinline__ T pick(const T (&v)[N], int i) {
+  T r = v[0];
+#pragma unroll
+  for (int j = 1; j < N; ++j)
+    if (i == j) r = v[j];
+  return r;
+}
+
 __device__ __forceinline__ int prob_of(const DecStage& st, int grt) {
   int p = 0;
   while (p + 1 < st.nprob && grt >= st.rt_prefix[p + 1]) ++p;
@@ -970,10 +980,26 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecArgs 
       float bestv = -INFINITY;
       int besti = -1, nan0 = 0;
       float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      // the stage's problem table in registers: read once per stage, not
+      // once per item (each read would be a global load on this serial warp)
+      int prt[kMaxProb + 1], prow[kMaxProb], pr0[kMaxProb];
+      float* pyp[kMaxProb];
+      bool ploc[kMaxProb];
+#pragma unroll
+      for (int j = 0; j < kMaxProb; ++j) {
+        prt[j] = st.rt_prefix[j];
+        prow[j] = st.rows[j];
+        pr0[j] = st.row0[j];
+        float* yj = st.y[j];
+        pyp[j] = yj ? yj : a.logits;
+        ploc[j] = a.world == 1 || !yj;   // logits: this rank's rows, locally
+      }
+      prt[kMaxProb] = st.rt_prefix[kMaxProb];
+      const int np = st.nprob;
+      int kb = 0, rti = 0, p = 0;       // k-block, row tile, problem of item i
       for (int i = 0; i < nstg; ++i) {
         const int qq = q0 + i;
         const int slot = qq % kNS;
-        const int kb = i % nkb;
         if (!dwait<1000>(a, &pfull[slot], (qq / kNS) & 1)) {
           if (lane == 0 && a.err) atomicExch(a.err, 1);
           break;
@@ -990,17 +1016,19 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecArgs 
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&merged[slot]);
-        if (kb != nkb - 1) continue;
+        const bool row_done = kb == nkb - 1;
+        if (++kb == nkb) kb = 0;
+        if (!row_done) continue;
         // columns 4..7 hold the second digit's part of x row 0
         const float yv = v.x + __shfl_xor_sync(0xffffffffu, v.x, 1);
-        const int grt = rt0 + i / nkb;
-        const int p = prob_of(st, grt);
-        const int r = (grt - st.rt_prefix[p]) * 16 + (lane >> 1);
-        if ((lane & 1) == 0 && r < st.rows[p]) {
-          float* yp = st.y[p] ? st.y[p] : a.logits;
-          const int gr = st.row0[p] + r;   // output row of the full weight
-          if (a.world == 1 || !st.y[p]) {
-            yp[gr] = yv;                   // (logits: this rank's rows, locally)
+        const int grt = rt0 + rti++;
+        while (p + 1 < np && grt >= pick(prt, p + 1)) ++p;
+        const int r = (grt - pick(prt, p)) * 16 + (lane >> 1);
+        if ((lane & 1) == 0 && r < pick(prow, p)) {
+          float* yp = pick(pyp, p);
+          const int gr = pick(pr0, p) + r;   // output row of the full weight
+          if (pick(ploc, p)) {
+            yp[gr] = yv;
           } else {
             for (int q2 = 0; q2 < a.world; ++q2) at_rank(a, yp, q2)[gr] = yv;
           }
@@ -1121,11 +1149,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecArgs 
       const int groups = pd.groups;
       const int ubeg = q0 * kNcs, uend = (q0 + nstg) * kNcs;
       const int u0 = ubeg + ((warp - ubeg) % kCons + kCons) % kCons;
-      for (int u = u0; u < uend; u += kCons) {
+      // k-block of the warp's item, stepped without a division (kCons units
+      // are kCons / kNcs items)
+      int kb = (u0 / kNcs - q0) % nkb;
+      static_assert(kCons % kNcs == 0, "whole items per consumer round");
+      auto step_kb = [&]() {
+        kb += kCons / kNcs;
+        while (kb >= nkb) kb -= nkb;
+      };
+      for (int u = u0; u < uend; u += kCons, step_kb()) {
         const int qq = u / kNcs, c = u - qq * kNcs;
-        const int i = qq - q0;
         const int slot = qq % kNS;
-        const int kb = i % nkb;
         const int ngk = min(kKbg, groups - kb * kKbg);
         const int cg0 = c * kCG, ncg = max(0, min(kCG, ngk - cg0));
         const int gb = kb * kKbg + cg0;  // first group of the chunk
