@@ -304,6 +304,10 @@ __global__ void __launch_bounds__(kFwThreads, 1) fw_gemv_kernel(const FwArgs a) 
   constexpr int SUB = TK / 16;                       // 16-k subtiles per tile
   constexpr int NB = MODE == 1 ? 1 : (MODE == 2 ? 2 : 4);
   constexpr int NACC = MODE == 3 ? 2 : 1;
+  // byte codes, MODE 1 / 2: two accumulator sets, alternating by 16-k
+  // subtile, so that consecutive MMAs of a warp do not wait on each other;
+  // summed at flush (FP4 is bound by its decode and has no registers left)
+  constexpr int NPAR = (MODE == 3 || FMT == FW_FP4) ? 1 : 2;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int grp = blockIdx.x, split = blockIdx.y;
@@ -428,7 +432,7 @@ __global__ void __launch_bounds__(kFwThreads, 1) fw_gemv_kernel(const FwArgs a) 
     bp[cb] = xr < a.m ? (lo ? xl : xh) + (size_t)xr * a.xstride + 4 * t : nullptr;
   }
 
-  float acc[NACC][4];
+  float acc[NACC * NPAR][4];
   int cur = -1;
   const int slot0 = cpr > 0 ? c0 / cpr : 0;
   auto flush = [&](int rl) {
@@ -436,7 +440,7 @@ __global__ void __launch_bounds__(kFwThreads, 1) fw_gemv_kernel(const FwArgs a) 
 #pragma unroll
     for (int q = 0; q < NACC; ++q)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) v[q][e] = acc[q][e];
+      for (int e = 0; e < 4; ++e) v[q][e] = NPAR == 2 ? acc[2 * q][e] + acc[2 * q + 1][e] : acc[q][e];
     if (MODE == 1) {
       // columns 4..7 hold the lo parts of x rows 0..3
 #pragma unroll
@@ -465,7 +469,7 @@ __global__ void __launch_bounds__(kFwThreads, 1) fw_gemv_kernel(const FwArgs a) 
       if (cur >= 0) flush(cur);
       cur = rl;
 #pragma unroll
-      for (int q = 0; q < NACC; ++q)
+      for (int q = 0; q < NACC * NPAR; ++q)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[q][e] = 0.f;
     }
@@ -486,7 +490,7 @@ __global__ void __launch_bounds__(kFwThreads, 1) fw_gemv_kernel(const FwArgs a) 
           for (int cb = 0; cb < NB; ++cb) {
             uint2 b = make_uint2(0u, 0u);
             if (bp[cb]) b = *reinterpret_cast<const uint2*>(bp[cb] + (size_t)k16 * 16);
-            mma_f16_16816(acc[MODE == 3 ? (cb & 1) : 0], af[0], af[1], af[2], af[3], b.x, b.y);
+            mma_f16_16816(acc[MODE == 3 ? (cb & 1) : (NPAR == 2 ? (sub & 1) : 0)], af[0], af[1], af[2], af[3], b.x, b.y);
           }
         }
       }
