@@ -22,8 +22,10 @@
 //                                the new k, KV append, scores, softmax
 //                                partials (max, sum, unnormalised P.V)
 //              S3 o GEMV         x = the split partials combined
-//              S4 gate/up GEMV   x = RMSNorm(residual + o), sum kept
-//              S5 down GEMV      x = SwiGLU(gate, up)
+//              S4 gate/up GEMV   x = RMSNorm(residual + o), sum kept; gate
+//                                and up row tiles interleave, so each merge
+//                                warp stores SwiGLU(gate, up) of its rows
+//              S5 down GEMV      x = that SwiGLU output
 //   then       lm_head GEMV      x = RMSNorm(residual + down) with the final
 //                                norm; the merge warps keep the repetition-
 //                                penalised argmax of their rows, and CTA 0
@@ -114,18 +116,23 @@ enum { ST_GEMV = 0, ST_ATTN = 1 };
 // The fields of a GEMV stage the consumers need, read before the stage's
 // grid barrier so that their global loads are not on the critical path.
 struct ProDesc {
-  int k, groups, pro, nkb, n_rt;
+  int k, groups, pro, nkb, n_rt, pair;
   const float* a;
   const float* b;
   const float* w;
   float* res_out;
   bool wstaged;             // w is in shared memory (kOffWbuf)
 };
-enum { PRO_EMB_RMS = 0, PRO_ADD_RMS = 1, PRO_COMBINE = 2, PRO_SWIGLU = 3 };
+enum { PRO_EMB_RMS = 0, PRO_ADD_RMS = 1, PRO_COMBINE = 2, PRO_PLAIN = 3 };
 
 struct DecStage {
   int kind, pro;
   int k, groups, nkb, n_rt, nprob, greedy;
+  // pair = 1: two problems of equal rows (gate, up) whose row tiles
+  // interleave (tile 2 t = gate tile t, 2 t + 1 = up tile t) and are split
+  // over the CTAs in whole pairs, so that one merge warp holds both halves of
+  // its rows and stores SwiGLU(gate, up) into y[0]
+  int pair;
   int rt_prefix[kMaxProb + 1];
   int rows[kMaxProb];
   int row0[kMaxProb];       // first output row of this rank's shard (0 unsharded)
@@ -301,6 +308,16 @@ __device__ __forceinline__ void row_split(int n_rt, int cid, int G, int* rt0, in
   *rt0 = cid * base + min(cid, rem);
   *nrt = base + (cid < rem ? 1 : 0);
 }
+// The row tiles of a GEMV stage for CTA cid (whole gate/up pairs when paired).
+__device__ __forceinline__ void stage_rows(int n_rt, int pair, int cid, int G, int* rt0, int* nrt) {
+  if (!pair) {
+    row_split(n_rt, cid, G, rt0, nrt);
+    return;
+  }
+  row_split(n_rt >> 1, cid, G, rt0, nrt);
+  *rt0 *= 2;
+  *nrt *= 2;
+}
 
 // v[i] for a small register array and a runtime i (selects, no local memory)
 template <typename T, int N>
@@ -329,8 +346,9 @@ __device__ __forceinline__ ItemSrc item_src(const DecStage& st, int rt0, int i) 
   const int nkb = __ldg(&st.nkb), groups = __ldg(&st.groups);
   const int rti = i / nkb, kb = i - rti * nkb;
   const int grt = rt0 + rti;
-  const int p = prob_of(st, grt);
-  const int rt = grt - __ldg(&st.rt_prefix[p]);
+  const bool pair = __ldg(&st.pair) != 0;
+  const int p = pair ? (grt & 1) : prob_of(st, grt);
+  const int rt = pair ? (grt >> 1) : grt - __ldg(&st.rt_prefix[p]);
   const int ngk = min(kKbg, groups - kb * kKbg);
   const uint4* fr = reinterpret_cast<const uint4*>(__ldg(reinterpret_cast<const unsigned long long*>(&st.frag[p])));
   const float4* sz = reinterpret_cast<const float4*>(__ldg(reinterpret_cast<const unsigned long long*>(&st.sz[p])));
@@ -356,7 +374,7 @@ __device__ void cursor_seek(const DecArgs& a, LaneCursor& c, int s, int q0, int 
     const DecStage& st = a.stages[s];
     if (__ldg(&st.kind) != ST_GEMV) continue;
     int nrt;
-    row_split(__ldg(&st.n_rt), cid, G, &c.rt0, &nrt);
+    stage_rows(__ldg(&st.n_rt), __ldg(&st.pair), cid, G, &c.rt0, &nrt);
     const int nstg = nrt * __ldg(&st.nkb);
     if (want < q0 + nstg) {
       c.s = s;
@@ -564,30 +582,12 @@ __device__ void prologue_nv(const DecArgs& a, const ProDesc& st, int cid, int to
       }
       v[j] = r;
     }
-  } else if (st.pro == PRO_SWIGLU) {
-    // slots in batches of kPB: the batch's loads first, then its values
+  } else if (st.pro == PRO_PLAIN) {
+    // x as stored by the previous stage (the gate/up stage's SwiGLU output)
 #pragma unroll
-    for (int j0 = 0; j0 < NV; j0 += kPB) {
-      float4 g[kPB], u[kPB];
-#pragma unroll
-      for (int jj = 0; jj < kPB; ++jj) {
-        const int f = tid + (j0 + jj) * kConsThreads;
-        const bool in = j0 + jj < NV && f < f4;
-        g[jj] = in ? ldcg4(st.a + 4 * f) : make_float4(0.f, 0.f, 0.f, 0.f);
-        u[jj] = in ? ldcg4(st.b + 4 * f) : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-#pragma unroll
-      for (int jj = 0; jj < kPB; ++jj) {
-        if (j0 + jj >= NV) break;
-        const float gv[4] = {g[jj].x, g[jj].y, g[jj].z, g[jj].w}, uv[4] = {u[jj].x, u[jj].y, u[jj].z, u[jj].w};
-        float o[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float sig = __frcp_rn(__fadd_rn(1.0f, expf(-gv[e])));   // = 1 / (1 + e^-g), rounded once
-          o[e] = __fmul_rn(__fmul_rn(gv[e], sig), uv[e]);
-        }
-        v[j0 + jj] = make_float4(o[0], o[1], o[2], o[3]);   // zeros give zeros
-      }
+    for (int j = 0; j < NV; ++j) {
+      const int f = tid + j * kConsThreads;
+      v[j] = f < f4 ? ldcg4(st.a + 4 * f) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
   } else {
     // RMSNorm of (embedding row) or (a + b); the sum is the residual stream
@@ -921,7 +921,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecArgs 
           continue;
         }
         int rt0, nrt;
-        row_split(__ldg(&st.n_rt), cid, G, &rt0, &nrt);
+        stage_rows(__ldg(&st.n_rt), __ldg(&st.pair), cid, G, &rt0, &nrt);
         const int nstg = nrt * __ldg(&st.nkb);
         const int first = ((lane - q0) % kIssuers + kIssuers) % kIssuers;
         for (int i = first; i < nstg; i += kIssuers) {
@@ -963,7 +963,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecArgs 
       const DecStage& st = a.stages[s];
       if (st.kind != ST_GEMV) continue;
       int rt0, nrt;
-      row_split(st.n_rt, cid, G, &rt0, &nrt);
+      stage_rows(st.n_rt, st.pair, cid, G, &rt0, &nrt);
       const int nkb = st.nkb;
       const int nstg = nrt * nkb;
       const bool greedy = st.greedy && a.tok_out != nullptr;
@@ -996,7 +996,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecArgs 
       }
       prt[kMaxProb] = st.rt_prefix[kMaxProb];
       const int np = st.nprob;
+      const bool pair = st.pair != 0;
       int kb = 0, rti = 0, p = 0;       // k-block, row tile, problem of item i
+      float gate = 0.f;                 // paired stage: this lane's gate value
       for (int i = 0; i < nstg; ++i) {
         const int qq = q0 + i;
         const int slot = qq % kNS;
@@ -1020,10 +1022,24 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecArgs 
         if (++kb == nkb) kb = 0;
         if (!row_done) continue;
         // columns 4..7 hold the second digit's part of x row 0
-        const float yv = v.x + __shfl_xor_sync(0xffffffffu, v.x, 1);
+        float yv = v.x + __shfl_xor_sync(0xffffffffu, v.x, 1);
         const int grt = rt0 + rti++;
-        while (p + 1 < np && grt >= pick(prt, p + 1)) ++p;
-        const int r = (grt - pick(prt, p)) * 16 + (lane >> 1);
+        int r;
+        if (pair) {
+          // gate tile (even): keep; up tile (odd): store SwiGLU into y[0],
+          // as swiglu_kernel: sigmoid = 1 / (1 + e^-g), (g sigmoid) u
+          r = (grt >> 1) * 16 + (lane >> 1);
+          if ((grt & 1) == 0) {
+            gate = yv;
+            continue;
+          }
+          const float sig = __frcp_rn(__fadd_rn(1.0f, expf(-gate)));
+          yv = __fmul_rn(__fmul_rn(gate, sig), yv);
+          p = 0;
+        } else {
+          while (p + 1 < np && grt >= pick(prt, p + 1)) ++p;
+          r = (grt - pick(prt, p)) * 16 + (lane >> 1);
+        }
         if ((lane & 1) == 0 && r < pick(prow, p)) {
           float* yp = pick(pyp, p);
           const int gr = pick(pr0, p) + r;   // output row of the full weight
@@ -1123,6 +1139,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecArgs 
       pd.pro = st.pro;
       pd.nkb = st.nkb;
       pd.n_rt = st.n_rt;
+      pd.pair = st.pair;
       pd.a = st.a;
       pd.b = st.b;
       pd.w = st.w;
@@ -1136,7 +1153,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const DecArgs 
           wb[f] = __ldg(reinterpret_cast<const float4*>(pd.w) + f);
       }
       int rt0, nrt;
-      row_split(pd.n_rt, cid, G, &rt0, &nrt);
+      stage_rows(pd.n_rt, pd.pair, cid, G, &rt0, &nrt);
       const int nkb = pd.nkb;
       const int nstg = nrt * nkb;
       if (threadIdx.x == 0 && s > 0) stage_wait(a, s - 1, target, gtarget);
@@ -1303,7 +1320,7 @@ int q4_of(nimf_weight_t h, int64_t k, int64_t n, int world, int rank, const char
 }
 
 DecStage gemv_stage(int pro, const Q4GWeight* const* ws, const int* row0, float* const* ys, int n,
-                    int64_t k) {
+                    int64_t k, bool pair = false) {
   DecStage s = {};
   s.kind = ST_GEMV;
   s.pro = pro;
@@ -1321,6 +1338,7 @@ DecStage gemv_stage(int pro, const Q4GWeight* const* ws, const int* row0, float*
     s.rt_prefix[i + 1] = s.rt_prefix[i] + (int)ws[i]->n_rt;
   }
   s.n_rt = s.rt_prefix[n];
+  s.pair = pair ? 1 : 0;   // (callers check: two problems with equal rows)
   return s;
 }
 
@@ -1464,10 +1482,16 @@ int create_plan(const nimf_decode_desc* d, int world, int rank, int64_t* plan_ou
         P->stages.push_back(gemv_stage(PRO_COMBINE, ws, r0s, ys, 1, D));
       }
       {
+        // gate and up rows interleaved per 16-row tile: the merge warps store
+        // SwiGLU(gate, up) into bg, which the down stage reads as its x
         const Q4GWeight* ws[2] = {wg, wu};
         const int r0s[2] = {r0g, r0u};
         float* ys[2] = {bg, bu};
-        DecStage s = gemv_stage(PRO_ADD_RMS, ws, r0s, ys, 2, D);
+        if (wg->rows != wu->rows || r0g != r0u) {
+          rc = set_error(NIMF_ERR_SHAPE, "decode plan: layer %lld gate and up shards differ", (long long)l);
+          break;
+        }
+        DecStage s = gemv_stage(PRO_ADD_RMS, ws, r0s, ys, 2, D, true);
         s.a = bxr;
         s.b = bao;
         s.w = ld.ffn_norm;
@@ -1478,9 +1502,8 @@ int create_plan(const nimf_decode_desc* d, int world, int rank, int64_t* plan_ou
         const Q4GWeight* ws[1] = {wd};
         const int r0s[1] = {r0d};
         float* ys[1] = {bdn};
-        DecStage s = gemv_stage(PRO_SWIGLU, ws, r0s, ys, 1, F);
+        DecStage s = gemv_stage(PRO_PLAIN, ws, r0s, ys, 1, F);
         s.a = bg;
-        s.b = bu;
         P->stages.push_back(s);
       }
     }
