@@ -1525,7 +1525,7 @@ def run_ours(args, rank, world, local_rank):
     achieved = per_launch_bytes / launch_s / 1e9
     roofline = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                 "frac": achieved / pk["hbm_gbs"], "traffic": profile_traffic(),
-                "peak_source": how, "kernel": "q4g_gemv_kernel<1,2> (grouped, %d weights)" % R,
+                "peak_source": how, "kernel": "q4g_gemv_kernel<1,2,%d> (grouped, %d weights)" % (1 if M == 1 else 0, R),
                 "algorithmic_bytes_per_launch": per_launch_bytes,
                 "note": "launch duration = timed region / launches, CUDA events"}
 
