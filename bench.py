@@ -1262,8 +1262,9 @@ def run_ncu_case(name):
       prefill: run_prefill_7b with one layer copy (both int4 GEMMs, each
           projection alone);
       fw: an FP4 E2M1 block-16 weight and a one-byte CustomFloat(4,3) weight
-          with per-row scales, both 28672 x 8192 (random codes), at M = 1 and 1
-          (GEMV), 16 (GEMV), 17 and 128 (tcgen05 GEMM) and 512."""
+          with per-row scales, both 28672 x 8192 (random codes): GEMV launches
+          FP4 M=1, fp8 M=1, FP4 M=8, fp8 M=8, fp8 M=16, then the tcgen05 GEMM at
+          fp8 M=17, FP4 M=128 and fp8 M=512."""
     import numpy as np
     import torch
     import nimf
@@ -1293,7 +1294,7 @@ def run_ncu_case(name):
     codes[(codes & 0x78) == 0] = 0                                # no exponent-0 mantissas
     h8 = nimf.Weight.cf(codes, nimf.newCustomFloat(4, 3), n3, k3,
                         row_scales=np.ones(n3, np.float32))
-    cases = [(h4, 1), (h8, 1), (h8, 16), (h8, 17), (h4, 128), (h8, 512)]
+    cases = [(h4, 1), (h8, 1), (h4, 8), (h8, 8), (h8, 16), (h8, 17), (h4, 128), (h8, 512)]
     xs = {m: torch.randn(m, k3, device="cuda") for _, m in cases}
     ys = {m: torch.empty(m, n3, device="cuda") for _, m in cases}
     for _ in range(4):

@@ -10,11 +10,13 @@
 // decodes as inf, and exponent 0 with a non-zero mantissa, which the reference
 // decodes as 2^-bias (1.m); the encoder never emits either), and the product
 // e2m1 x e4m3 (at most 6 significant bits, magnitude in [2^-10, 2688]).  So
-// the weights are decoded exactly into fp16 mma.sync A fragments; x is split
-// into fp16 hi + lo parts after a per-row power-of-two scale (x ~= (hi + lo)
-// 2^-p to about 2^-22 relative), and both parts are multiplied on the tensor
-// cores with fp32 accumulation.  The per-row / tensor scales are applied once
-// per output in fp32.
+// the weights are decoded exactly into fp16 mma.sync A fragments.  For M <= 4
+// x is split into fp16 hi + lo parts after a per-row power-of-two scale
+// (x ~= (hi + lo) 2^-p to about 2^-22 relative) and both parts share one MMA
+// (hi in columns 0..3, lo in 4..7); for 5 <= M <= 16 x is one fp16 term, the
+// x precision of the tensor-core GEMM (fw_tc.cu: about 2e-4 of max|y|), which
+// halves the MMAs and B loads per weight tile.  Products accumulate in fp32;
+// the per-row / tensor scales are applied once per output in fp32.
 //
 // Layout (built once at registration, the reference bytes are kept too):
 //   frag  [n_rt][ntk][32 lanes] uint4 -- one 512-byte tile per 16 rows x TK k
@@ -292,9 +294,11 @@ __device__ __forceinline__ int fw_xscale_pow(unsigned maxbits) {
   return max(-126, min(126, 141 - E));
 }
 
-// Shared memory: xmax[16] | x hi [M][xstride] | x lo [M][xstride] | partials.
+// Shared memory: xmax[16] | x hi [M][xstride] | x lo [M][xstride] (M <= 4 only) | partials.
+// x terms staged per row: hi and lo for M <= 4, hi alone above.
+__host__ __device__ inline int fw_xterms(int m) { return m <= 4 ? 2 : 1; }
 __host__ __device__ inline size_t fw_smem_bytes(int m, int xstride, int nseg) {
-  return 64 + (size_t)2 * m * xstride * 2 + (size_t)kFwWarps * nseg * 16 * m * 4 + 16;
+  return 64 + (size_t)fw_xterms(m) * m * xstride * 2 + (size_t)kFwWarps * nseg * 16 * m * 4 + 16;
 }
 
 template <int FMT, int MODE>
@@ -302,7 +306,10 @@ __global__ void __launch_bounds__(kFwThreads, 1) fw_gemv_kernel(const FwArgs a) 
   extern __shared__ __align__(16) unsigned char smem[];
   constexpr int TK = fw_tk(FMT);
   constexpr int SUB = TK / 16;                       // 16-k subtiles per tile
-  constexpr int NB = MODE == 1 ? 1 : (MODE == 2 ? 2 : 4);
+  // B column blocks per MMA step: M <= 4 puts hi and lo of x rows 0..3 in
+  // one block; M <= 8 (16) multiplies x rows 0..7 (and 8..15) as one fp16
+  // term, the x precision of the GEMM path (about 2e-4 of max|y|)
+  constexpr int NB = MODE == 3 ? 2 : 1;
   constexpr int NACC = MODE == 3 ? 2 : 1;
   // byte codes, MODE 1 / 2: two accumulator sets, alternating by 16-k
   // subtile, so that consecutive MMAs of a warp do not wait on each other;
@@ -325,11 +332,10 @@ __global__ void __launch_bounds__(kFwThreads, 1) fw_gemv_kernel(const FwArgs a) 
   unsigned* xmax = reinterpret_cast<unsigned*>(smem);
   __half* xh = reinterpret_cast<__half*>(smem + 64);
   __half* xl = xh + (size_t)a.m * a.xstride;
-  float* wpart = reinterpret_cast<float*>(xl + (size_t)a.m * a.xstride);
+  float* wpart = reinterpret_cast<float*>((MODE == 1 ? xl : xh) + (size_t)a.m * a.xstride);
 
   // first chunk of weights: issued before waiting on the previous kernel
-  auto load_chunk = [&](int c, uint4 (&wv)[kChunkTiles], uint2 (&sv)[kChunkTiles]) {
-    const int rl = c / cpr, ch = c - rl * cpr;
+  auto load_chunk = [&](int rl, int ch, uint4 (&wv)[kChunkTiles], uint2 (&sv)[kChunkTiles]) {
     const int kt = kt0 + ch * kChunkTiles;
     const int nt = min(kChunkTiles, kt0 + nkt - kt);
     const size_t tile0 = (size_t)(rt0 + rl) * a.ntk + kt;
@@ -346,8 +352,7 @@ __global__ void __launch_bounds__(kFwThreads, 1) fw_gemv_kernel(const FwArgs a) 
   };
   // the chunk after the next one is pulled into L2 by one bulk prefetch, so
   // the register loads of the next chunk find their lines in L2
-  auto prefetch_chunk = [&](int c) {
-    const int rl = c / cpr, ch = c - rl * cpr;
+  auto prefetch_chunk = [&](int rl, int ch) {
     const int kt = kt0 + ch * kChunkTiles;
     const int nt = min(kChunkTiles, kt0 + nkt - kt);
     const size_t tile0 = (size_t)(rt0 + rl) * a.ntk + kt;
@@ -358,9 +363,22 @@ __global__ void __launch_bounds__(kFwThreads, 1) fw_gemv_kernel(const FwArgs a) 
   };
   uint4 wv[kChunkTiles], nv[kChunkTiles];
   uint2 sv[kChunkTiles], nsv[kChunkTiles];
+  // chunk c = rl cpr + ch: (rl, ch) of chunks c, c + 1 and c + 2 advance
+  // without divisions
+  auto next_rc = [&](int& rl, int& ch) {
+    if (++ch == cpr) {
+      ch = 0;
+      ++rl;
+    }
+  };
+  int rl0 = cpr > 0 ? c0 / cpr : 0, ch0 = c0 - rl0 * cpr;
+  int rl1 = rl0, ch1 = ch0;
+  next_rc(rl1, ch1);
+  int rl2 = rl1, ch2 = ch1;
+  next_rc(rl2, ch2);
   griddep_launch_dependents();
-  if (c0 + 1 < c1) prefetch_chunk(c0 + 1);
-  if (c0 < c1) load_chunk(c0, wv, sv);
+  if (c0 + 1 < c1) prefetch_chunk(rl1, ch1);
+  if (c0 < c1) load_chunk(rl0, ch0, wv, sv);
 
   if (threadIdx.x < 16) xmax[threadIdx.x] = 0u;
   __syncthreads();
@@ -387,36 +405,62 @@ __global__ void __launch_bounds__(kFwThreads, 1) fw_gemv_kernel(const FwArgs a) 
     }
     return v;
   };
-  for (int it = threadIdx.x; it - lane < total; it += kFwThreads) {
-    const float4 v = it < total ? load4(it) : make_float4(0.f, 0.f, 0.f, 0.f);
-    float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+  // Both passes over x issue kXB independent loads per thread before using
+  // any of them, so a pass costs about total / (512 kXB) L2 round trips
+  // rather than one per element (x is M K floats: 8 rows are 16 per thread).
+  constexpr int kXB = 8;
+  for (int it0 = threadIdx.x; it0 - lane < total; it0 += kFwThreads * kXB) {
+    float4 v[kXB];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if (lane == 0 && it < total) atomicMax(&xmax[it / f4p], __float_as_uint(mx));
+    for (int r = 0; r < kXB; ++r) {
+      const int it = it0 + r * kFwThreads;
+      v[r] = it < total ? load4(it) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int r = 0; r < kXB; ++r) {
+      const int it = it0 + r * kFwThreads;
+      if (it - lane >= total) break;   // warp-uniform (f4p is a multiple of 32)
+      float mx = fmaxf(fmaxf(fabsf(v[r].x), fabsf(v[r].y)), fmaxf(fabsf(v[r].z), fabsf(v[r].w)));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      if (lane == 0 && it < total) atomicMax(&xmax[it / f4p], __float_as_uint(mx));
+    }
   }
   __syncthreads();
-  for (int it = threadIdx.x; it < total; it += kFwThreads) {
-    const int mrow = it / f4p, f = it - mrow * f4p;
-    if (f >= f4) continue;
-    const float4 v = load4(it);
-    const float sc = ldexpf(1.0f, fw_xscale_pow(xmax[mrow]));
-    const float xv[4] = {v.x * sc, v.y * sc, v.z * sc, v.w * sc};
-    __half hv[4], lv[4];
+  for (int it0 = threadIdx.x; it0 < total; it0 += kFwThreads * kXB) {
+    float4 v[kXB];
 #pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      hv[b] = __float2half_rn(xv[b]);
-      lv[b] = __float2half_rn(xv[b] - __half2float(hv[b]));
+    for (int r = 0; r < kXB; ++r) {
+      const int it = it0 + r * kFwThreads;
+      const int mrow = it / f4p, f = it - mrow * f4p;
+      v[r] = (it < total && f < f4) ? load4(it) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    // k = 4f .. 4f+3 within the slice: positions in the permuted 16-k block
-    const int kk = (4 * f) & 15, blk = (4 * f) >> 4;
-    const int p0 = 4 * ((kk & 7) >> 1) + 2 * (kk >> 3);  // pair (k, k+1)
-    const int p1 = 4 * (((kk + 2) & 7) >> 1) + 2 * ((kk + 2) >> 3);  // pair (k+2, k+3)
-    __half* hr = xh + (size_t)mrow * a.xstride + blk * 16;
-    __half* lr = xl + (size_t)mrow * a.xstride + blk * 16;
-    *reinterpret_cast<__half2*>(hr + p0) = __halves2half2(hv[0], hv[1]);
-    *reinterpret_cast<__half2*>(hr + p1) = __halves2half2(hv[2], hv[3]);
-    *reinterpret_cast<__half2*>(lr + p0) = __halves2half2(lv[0], lv[1]);
-    *reinterpret_cast<__half2*>(lr + p1) = __halves2half2(lv[2], lv[3]);
+#pragma unroll
+    for (int r = 0; r < kXB; ++r) {
+      const int it = it0 + r * kFwThreads;
+      const int mrow = it / f4p, f = it - mrow * f4p;
+      if (it >= total || f >= f4) continue;
+      const float sc = ldexpf(1.0f, fw_xscale_pow(xmax[mrow]));
+      const float xv[4] = {v[r].x * sc, v[r].y * sc, v[r].z * sc, v[r].w * sc};
+      __half hv[4], lv[4];
+#pragma unroll
+      for (int bb = 0; bb < 4; ++bb) {
+        hv[bb] = __float2half_rn(xv[bb]);
+        lv[bb] = MODE == 1 ? __float2half_rn(xv[bb] - __half2float(hv[bb])) : __float2half_rn(0.f);
+      }
+      // k = 4f .. 4f+3 within the slice: positions in the permuted 16-k block
+      const int kk = (4 * f) & 15, blk = (4 * f) >> 4;
+      const int p0 = 4 * ((kk & 7) >> 1) + 2 * (kk >> 3);  // pair (k, k+1)
+      const int p1 = 4 * (((kk + 2) & 7) >> 1) + 2 * ((kk + 2) >> 3);  // pair (k+2, k+3)
+      __half* hr = xh + (size_t)mrow * a.xstride + blk * 16;
+      __half* lr = xl + (size_t)mrow * a.xstride + blk * 16;
+      *reinterpret_cast<__half2*>(hr + p0) = __halves2half2(hv[0], hv[1]);
+      *reinterpret_cast<__half2*>(hr + p1) = __halves2half2(hv[2], hv[3]);
+      if (MODE == 1) {
+        *reinterpret_cast<__half2*>(lr + p0) = __halves2half2(lv[0], lv[1]);
+        *reinterpret_cast<__half2*>(lr + p1) = __halves2half2(lv[2], lv[3]);
+      }
+    }
   }
   __syncthreads();
 
@@ -427,8 +471,8 @@ __global__ void __launch_bounds__(kFwThreads, 1) fw_gemv_kernel(const FwArgs a) 
     int xr;
     bool lo;
     if (MODE == 1) { xr = g & 3; lo = g >= 4; }
-    else if (MODE == 2) { xr = g; lo = cb == 1; }
-    else { xr = g + 8 * (cb & 1); lo = cb >= 2; }
+    else if (MODE == 2) { xr = g; lo = false; }
+    else { xr = g + 8 * cb; lo = false; }
     bp[cb] = xr < a.m ? (lo ? xl : xh) + (size_t)xr * a.xstride + 4 * t : nullptr;
   }
 
@@ -464,7 +508,7 @@ __global__ void __launch_bounds__(kFwThreads, 1) fw_gemv_kernel(const FwArgs a) 
 
 #pragma unroll 1
   for (int c = c0; c < c1; ++c) {
-    const int rl = c / cpr, ch = c - rl * cpr;
+    const int rl = rl0, ch = ch0;
     if (rl != cur) {
       if (cur >= 0) flush(cur);
       cur = rl;
@@ -473,23 +517,28 @@ __global__ void __launch_bounds__(kFwThreads, 1) fw_gemv_kernel(const FwArgs a) 
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[q][e] = 0.f;
     }
-    if (c + 2 < c1) prefetch_chunk(c + 2);
-    if (c + 1 < c1) load_chunk(c + 1, nv, nsv);
+    if (c + 2 < c1) prefetch_chunk(rl2, ch2);
+    if (c + 1 < c1) load_chunk(rl1, ch1, nv, nsv);
+    rl0 = rl1, ch0 = ch1;
+    rl1 = rl2, ch1 = ch2;
+    next_rc(rl2, ch2);
     const int nt = min(kChunkTiles, nkt - ch * kChunkTiles);
+    // B rows of this chunk's first 16-k subtile (then constant offsets)
+    const __half* bq[NB];
+#pragma unroll
+    for (int cb = 0; cb < NB; ++cb) bq[cb] = bp[cb] ? bp[cb] + (size_t)ch * kChunkTiles * SUB * 16 : nullptr;
 #pragma unroll
     for (int j = 0; j < kChunkTiles; ++j) {
       if (j < nt) {
-        const int tk = ch * kChunkTiles + j;  // tile within the split
 #pragma unroll
         for (int sub = 0; sub < SUB; ++sub) {
           const uint32_t swv = FMT == FW_FP4 ? ((sub < 2 ? sv[j].x : sv[j].y) >> (16 * (sub & 1))) : 0u;
           uint32_t af[4];
           tile_a<FMT>(wv[j], swv, sub, af);
-          const int k16 = tk * SUB + sub;
 #pragma unroll
           for (int cb = 0; cb < NB; ++cb) {
             uint2 b = make_uint2(0u, 0u);
-            if (bp[cb]) b = *reinterpret_cast<const uint2*>(bp[cb] + (size_t)k16 * 16);
+            if (bq[cb]) b = *reinterpret_cast<const uint2*>(bq[cb] + (j * SUB + sub) * 16);
             mma_f16_16816(acc[MODE == 3 ? (cb & 1) : (NPAR == 2 ? (sub & 1) : 0)], af[0], af[1], af[2], af[3], b.x, b.y);
           }
         }
@@ -504,15 +553,22 @@ __global__ void __launch_bounds__(kFwThreads, 1) fw_gemv_kernel(const FwArgs a) 
   if (cur >= 0) flush(cur);
   __syncthreads();
 
-  // ---- sum the warps' partials of each row tile in warp order
+  // ---- sum the warps' partials of each row tile in warp order; the row
+  // tiles [s0, s1] each warp touched are worked out once per CTA
+  __shared__ int wrange[kFwWarps][2];
+  if (threadIdx.x < kFwWarps) {
+    const int w = threadIdx.x;
+    const int w0 = (int)((int64_t)w * C / kFwWarps), w1 = (int)((int64_t)(w + 1) * C / kFwWarps);
+    wrange[w][0] = w1 > w0 ? w0 / cpr : 1;
+    wrange[w][1] = w1 > w0 ? (w1 - 1) / cpr : 0;
+  }
+  __syncthreads();
   const int items = nrt * 16 * a.m;
   for (int idx = threadIdx.x; idx < items; idx += kFwThreads) {
     const int rl = idx / (16 * a.m), r = (idx / a.m) & 15, mcol = idx % a.m;
     float v = 0.f;
     for (int w = 0; w < kFwWarps; ++w) {
-      const int w0 = (int)((int64_t)w * C / kFwWarps), w1 = (int)((int64_t)(w + 1) * C / kFwWarps);
-      if (w1 <= w0) continue;
-      const int s0 = w0 / cpr, s1 = (w1 - 1) / cpr;
+      const int s0 = wrange[w][0], s1 = wrange[w][1];
       if (rl < s0 || rl > s1) continue;
       v += wpart[((size_t)w * a.nseg + (rl - s0)) * 16 * a.m + r * a.m + mcol];
     }
@@ -556,8 +612,8 @@ FwPlan fw_plan_budget(const FWLayout& L, int m, int num_sms, size_t xbudget) {
   FwPlan p;
   const int TK = fw_tk(L.fmt);
   const int ntk = (int)L.ntk, n_rt = (int)L.n_rt;
-  // k-tiles whose hi/lo x rows fit the budget (whole chunks of tiles)
-  const int64_t kmax = (int64_t)(xbudget / ((size_t)4 * m)) - 16;
+  // k-tiles whose staged x rows fit the budget (whole chunks of tiles)
+  const int64_t kmax = (int64_t)(xbudget / ((size_t)2 * fw_xterms(m) * m)) - 16;
   int ks_cap = (int)std::max<int64_t>(kChunkTiles, kmax / TK / kChunkTiles * kChunkTiles);
   int S = (ntk + ks_cap - 1) / ks_cap;
   // few row tiles: split k further so that every SM has work
