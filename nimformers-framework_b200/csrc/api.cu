@@ -250,11 +250,11 @@ static int finish_register(std::unique_ptr<Weight> w, nimf_weight_t* out) {
   return NIMF_OK;
 }
 
-// Byte-coded float weights: decode GEMV for up to 8 rows of x, the tcgen05
-// GEMM above (at K=8192, N=28672 the GEMM takes 145 us for 17 rows where the
-// GEMV takes 200 us for 16 and 93 us for 8).
+// Byte-coded float weights: decode GEMV for up to 16 rows of x, the tcgen05
+// GEMM above (at K=8192, N=28672: the GEMV takes 86 us for 16 rows where the
+// GEMM takes 141 us, and the GEMM 135 us for 17).
 static int fw_matmul(const FWLayout& L, const float* x, int64_t m, float* y, cudaStream_t st) {
-  return m > 8 ? fw_gemm_tc(L, x, m, y, st) : fw_gemv(L, x, m, y, st);
+  return m > 16 ? fw_gemm_tc(L, x, m, y, st) : fw_gemv(L, x, m, y, st);
 }
 
 // Runs the kernel path of a weight on device buffers.

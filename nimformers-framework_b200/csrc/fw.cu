@@ -591,13 +591,41 @@ __global__ void __launch_bounds__(kFwThreads, 1) fw_gemv_kernel(const FwArgs a) 
   __syncthreads();
   if (!last) return;
   __threadfence();
-  for (int idx = threadIdx.x; idx < nrt * 16 * a.m; idx += kFwThreads) {
-    const int rl = idx / (16 * a.m), r = (idx / a.m) & 15, mcol = idx % a.m;
-    const int row = (rt0 + rl) * 16 + r;
-    if (row >= a.rows) continue;
-    float v = 0.f;
-    for (int s = 0; s < a.S; ++s) v += __ldcg(&a.part[((size_t)s * a.m + mcol) * a.rows + row]);
-    a.y[(size_t)mcol * a.ldy + row] = v * (a.rscale ? a.rscale[row] : a.uscale);
+  // kFix outputs per thread per pass, all their split partials loaded before
+  // any is added (the adds stay in split order)
+  constexpr int kFix = 4;
+  const int nfix = nrt * 16 * a.m;
+  for (int i0 = threadIdx.x; i0 < nfix; i0 += kFwThreads * kFix) {
+    int rowv[kFix], colv[kFix];
+#pragma unroll
+    for (int u = 0; u < kFix; ++u) {
+      const int idx = i0 + u * kFwThreads;
+      const int rl = idx / (16 * a.m), r = (idx / a.m) & 15;
+      colv[u] = idx % a.m;
+      rowv[u] = (idx < nfix && (rt0 + rl) * 16 + r < a.rows) ? (rt0 + rl) * 16 + r : -1;
+    }
+    float v[kFix];
+#pragma unroll
+    for (int u = 0; u < kFix; ++u) v[u] = 0.f;
+    for (int s0 = 0; s0 < a.S; s0 += 4) {
+      float pv[kFix][4];
+#pragma unroll
+      for (int u = 0; u < kFix; ++u)
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          pv[u][q] = (rowv[u] >= 0 && s0 + q < a.S)
+                         ? __ldcg(&a.part[((size_t)(s0 + q) * a.m + colv[u]) * a.rows + rowv[u]])
+                         : 0.f;
+#pragma unroll
+      for (int u = 0; u < kFix; ++u)
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (s0 + q < a.S) v[u] += pv[u][q];
+    }
+#pragma unroll
+    for (int u = 0; u < kFix; ++u)
+      if (rowv[u] >= 0)
+        a.y[(size_t)colv[u] * a.ldy + rowv[u]] = v[u] * (a.rscale ? a.rscale[rowv[u]] : a.uscale);
   }
   if (threadIdx.x == 0) a.cnt[grp] = 0u;
 }
