@@ -148,6 +148,32 @@ def test_int8_config_layer(nimf_gpu):
     h.free()
 
 
+@pytest.mark.parametrize("fmt", ["e4m3", "fp4"])
+def test_byte_format_gemv_every_row_count(nimf_gpu, fmt):
+    """The byte-format GEMV at every x row count it serves (1 .. 16): hi + lo
+    x parts up to 4 rows, one fp16 term above, a k-split at K = 8192 for the
+    larger counts; each within 1e-3 of float64, and the same bits on a repeat
+    (fixed summation order)."""
+    rng = np.random.default_rng(21)
+    n, k = 272, 8192
+    w = (rng.standard_normal((n, k)) * 0.015).astype(np.float32)
+    if fmt == "e4m3":
+        enc = O.cf_encode(w, 4, 3)
+        wd = O.cf_decode(enc, 4, 3).reshape(n, k)
+        h = nimf_gpu.Weight.cf(enc, nimf_gpu.newCustomFloat(4, 3), n, k)
+    else:
+        ts = float(np.abs(w).max()) / (6 * 448)
+        p, b = O.quantize_fp4_block16(w, ts)
+        h = nimf_gpu.Weight.fp4(p, b, ts, n, k)
+        wd = O.dequantize_fp4_block16(p, b, ts, n, k)
+    for m in (1, 2, 4, 5, 7, 8, 9, 12, 16):
+        x = rng.standard_normal((m, k)).astype(np.float32)
+        y = h.matmul(x, m)
+        assert rel_err(y, O.gemv_f64(x, wd)) <= TOL, m
+        assert np.array_equal(y, h.matmul(x, m)), m
+    h.free()
+
+
 def test_fp4_block16(nimf_gpu):
     rng = np.random.default_rng(2)
     n, k = 64, 8192
