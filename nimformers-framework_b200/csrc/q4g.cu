@@ -763,16 +763,16 @@ q4g_gemv_kernel(const GemvArgs a) {
               tot[2] = fmaf(sp.z * dsc[0], fmaf(-sp.w, d0a, (float)acc[gl][2]), tot[2]);
               tot[3] = fmaf(sp.z * dsc[1], fmaf(-sp.w, d0b, (float)acc[gl][3]), tot[3]);
             } else {
+              // the two digits' sums joined in integers first: 256 (A0 - zp D0)
+              // + (A1 - zp D1) = (256 A0 + A1) - zp (256 D0 + D1), scaled by
+              // s / 256 (|256 A0 + A1| < 2^26; the digit sums are exact)
               const int g2 = MODE == 2 ? gl : 0;
-              const float d1a = (float)sd[8 + sd_off], d1b = (float)sd[8 + sd_off + 1];
-              tot[0] += sp.x * (dsc[0] * fmaf(-sp.y, d0a, (float)acc[gl][0]) +
-                                dsc2[0] * fmaf(-sp.y, d1a, (float)acc2[g2][0]));
-              tot[1] += sp.x * (dsc[1] * fmaf(-sp.y, d0b, (float)acc[gl][1]) +
-                                dsc2[1] * fmaf(-sp.y, d1b, (float)acc2[g2][1]));
-              tot[2] += sp.z * (dsc[0] * fmaf(-sp.w, d0a, (float)acc[gl][2]) +
-                                dsc2[0] * fmaf(-sp.w, d1a, (float)acc2[g2][2]));
-              tot[3] += sp.z * (dsc[1] * fmaf(-sp.w, d0b, (float)acc[gl][3]) +
-                                dsc2[1] * fmaf(-sp.w, d1b, (float)acc2[g2][3]));
+              const float da = (float)(sd[sd_off] * 256 + sd[8 + sd_off]);
+              const float db = (float)(sd[sd_off + 1] * 256 + sd[8 + sd_off + 1]);
+              tot[0] = fmaf(sp.x * dsc2[0], fmaf(-sp.y, da, (float)(acc[gl][0] * 256 + acc2[g2][0])), tot[0]);
+              tot[1] = fmaf(sp.x * dsc2[1], fmaf(-sp.y, db, (float)(acc[gl][1] * 256 + acc2[g2][1])), tot[1]);
+              tot[2] = fmaf(sp.z * dsc2[0], fmaf(-sp.w, da, (float)(acc[gl][2] * 256 + acc2[g2][2])), tot[2]);
+              tot[3] = fmaf(sp.z * dsc2[1], fmaf(-sp.w, db, (float)(acc[gl][3] * 256 + acc2[g2][3])), tot[3]);
             }
           }
         }
