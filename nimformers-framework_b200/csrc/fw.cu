@@ -386,10 +386,14 @@ __global__ void __launch_bounds__(kFwThreads, 1) fw_gemv_kernel(const FwArgs a) 
 
   // ---- stage x[:, kbeg : kbeg + klen) as hi / lo fp16 rows (permuted per 16 k)
   const int f4 = klen >> 2;
-  const int f4p = (f4 + 31) & ~31;
-  const int total = a.m * f4p;
-  auto load4 = [&](int it) -> float4 {
-    const int mrow = it / f4p, f = it - mrow * f4p;
+  // x item (mrow, j): float4 f = threadIdx.x + 512 j of row mrow; fpt items
+  // per row, M fpt per thread, stepped as (mrow, j) without divisions.  A
+  // warp's 32 lanes share (mrow, j) (512 is a multiple of 32), so the row
+  // maxima reduce per warp; float4 past the slice load as zeros.
+  const int fpt = (f4 + kFwThreads - 1) / kFwThreads;
+  const int nit = a.m * fpt;
+  auto load_x = [&](int mrow, int j) -> float4 {
+    const int f = threadIdx.x + j * kFwThreads;
     const int k = kbeg + 4 * f;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
     if (f < f4) {
@@ -405,61 +409,94 @@ __global__ void __launch_bounds__(kFwThreads, 1) fw_gemv_kernel(const FwArgs a) 
     }
     return v;
   };
-  // Both passes over x issue kXB independent loads per thread before using
-  // any of them, so a pass costs about total / (512 kXB) L2 round trips
-  // rather than one per element (x is M K floats: 8 rows are 16 per thread).
-  constexpr int kXB = 8;
-  for (int it0 = threadIdx.x; it0 - lane < total; it0 += kFwThreads * kXB) {
-    float4 v[kXB];
+  auto row_max = [&](int mrow, const float4& v) {
+    float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 #pragma unroll
-    for (int r = 0; r < kXB; ++r) {
-      const int it = it0 + r * kFwThreads;
-      v[r] = it < total ? load4(it) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) atomicMax(&xmax[mrow], __float_as_uint(mx));
+  };
+  auto stage = [&](int mrow, int j, const float4& v) {
+    const int f = threadIdx.x + j * kFwThreads;
+    if (f >= f4) return;
+    const float sc = ldexpf(1.0f, fw_xscale_pow(xmax[mrow]));
+    const float xv[4] = {v.x * sc, v.y * sc, v.z * sc, v.w * sc};
+    __half hv[4], lv[4];
+#pragma unroll
+    for (int bb = 0; bb < 4; ++bb) {
+      hv[bb] = __float2half_rn(xv[bb]);
+      lv[bb] = MODE == 1 ? __float2half_rn(xv[bb] - __half2float(hv[bb])) : __float2half_rn(0.f);
     }
-#pragma unroll
-    for (int r = 0; r < kXB; ++r) {
-      const int it = it0 + r * kFwThreads;
-      if (it - lane >= total) break;   // warp-uniform (f4p is a multiple of 32)
-      float mx = fmaxf(fmaxf(fabsf(v[r].x), fabsf(v[r].y)), fmaxf(fabsf(v[r].z), fabsf(v[r].w)));
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      if (lane == 0 && it < total) atomicMax(&xmax[it / f4p], __float_as_uint(mx));
+    // k = 4f .. 4f+3 within the slice: positions in the permuted 16-k block
+    const int kk = (4 * f) & 15, blk = (4 * f) >> 4;
+    const int p0 = 4 * ((kk & 7) >> 1) + 2 * (kk >> 3);  // pair (k, k+1)
+    const int p1 = 4 * (((kk + 2) & 7) >> 1) + 2 * ((kk + 2) >> 3);  // pair (k+2, k+3)
+    __half* hr = xh + (size_t)mrow * a.xstride + blk * 16;
+    __half* lr = xl + (size_t)mrow * a.xstride + blk * 16;
+    *reinterpret_cast<__half2*>(hr + p0) = __halves2half2(hv[0], hv[1]);
+    *reinterpret_cast<__half2*>(hr + p1) = __halves2half2(hv[2], hv[3]);
+    if (MODE == 1) {
+      *reinterpret_cast<__half2*>(lr + p0) = __halves2half2(lv[0], lv[1]);
+      *reinterpret_cast<__half2*>(lr + p1) = __halves2half2(lv[2], lv[3]);
     }
-  }
-  __syncthreads();
-  for (int it0 = threadIdx.x; it0 < total; it0 += kFwThreads * kXB) {
-    float4 v[kXB];
-#pragma unroll
-    for (int r = 0; r < kXB; ++r) {
-      const int it = it0 + r * kFwThreads;
-      const int mrow = it / f4p, f = it - mrow * f4p;
-      v[r] = (it < total && f < f4) ? load4(it) : make_float4(0.f, 0.f, 0.f, 0.f);
+  };
+  auto next_item = [&](int& mrow, int& j) {
+    if (++j == fpt) {
+      j = 0;
+      ++mrow;
     }
+  };
+  // Pass 1 finds each row's max|x|, pass 2 converts x into the staged fp16
+  // rows; each pass issues a batch of loads before using any.  When a
+  // thread's share is at most kXR float4, pass 1 keeps it in registers and
+  // pass 2 reads nothing again (one L2 round trip and one read of x per CTA).
+  constexpr int kXR = FMT == FW_FP4 ? 8 : 16;   // FP4 has fewer registers to spare
+  if (nit <= kXR) {
+    float4 v[kXR];
+    int mr = 0, jj = 0;
 #pragma unroll
-    for (int r = 0; r < kXB; ++r) {
-      const int it = it0 + r * kFwThreads;
-      const int mrow = it / f4p, f = it - mrow * f4p;
-      if (it >= total || f >= f4) continue;
-      const float sc = ldexpf(1.0f, fw_xscale_pow(xmax[mrow]));
-      const float xv[4] = {v[r].x * sc, v[r].y * sc, v[r].z * sc, v[r].w * sc};
-      __half hv[4], lv[4];
+    for (int r = 0; r < kXR; ++r) {
+      v[r] = r < nit ? load_x(mr, jj) : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (r < nit) next_item(mr, jj);
+    }
+    mr = 0, jj = 0;
 #pragma unroll
-      for (int bb = 0; bb < 4; ++bb) {
-        hv[bb] = __float2half_rn(xv[bb]);
-        lv[bb] = MODE == 1 ? __float2half_rn(xv[bb] - __half2float(hv[bb])) : __float2half_rn(0.f);
+    for (int r = 0; r < kXR; ++r) {
+      if (r < nit) {
+        row_max(mr, v[r]);
+        next_item(mr, jj);
       }
-      // k = 4f .. 4f+3 within the slice: positions in the permuted 16-k block
-      const int kk = (4 * f) & 15, blk = (4 * f) >> 4;
-      const int p0 = 4 * ((kk & 7) >> 1) + 2 * (kk >> 3);  // pair (k, k+1)
-      const int p1 = 4 * (((kk + 2) & 7) >> 1) + 2 * ((kk + 2) >> 3);  // pair (k+2, k+3)
-      __half* hr = xh + (size_t)mrow * a.xstride + blk * 16;
-      __half* lr = xl + (size_t)mrow * a.xstride + blk * 16;
-      *reinterpret_cast<__half2*>(hr + p0) = __halves2half2(hv[0], hv[1]);
-      *reinterpret_cast<__half2*>(hr + p1) = __halves2half2(hv[2], hv[3]);
-      if (MODE == 1) {
-        *reinterpret_cast<__half2*>(lr + p0) = __halves2half2(lv[0], lv[1]);
-        *reinterpret_cast<__half2*>(lr + p1) = __halves2half2(lv[2], lv[3]);
+    }
+    __syncthreads();
+    mr = 0, jj = 0;
+#pragma unroll
+    for (int r = 0; r < kXR; ++r) {
+      if (r < nit) {
+        stage(mr, jj, v[r]);
+        next_item(mr, jj);
       }
+    }
+  } else {
+    constexpr int kXB = 8;
+    for (int pass = 0; pass < 2; ++pass) {
+      int mr = 0, jj = 0;
+      for (int i0 = 0; i0 < nit; i0 += kXB) {
+        float4 v[kXB];
+        int m0 = mr, j0 = jj;
+#pragma unroll
+        for (int r = 0; r < kXB; ++r) {
+          v[r] = i0 + r < nit ? load_x(mr, jj) : make_float4(0.f, 0.f, 0.f, 0.f);
+          if (i0 + r < nit) next_item(mr, jj);
+        }
+#pragma unroll
+        for (int r = 0; r < kXB; ++r) {
+          if (i0 + r < nit) {
+            if (pass == 0) row_max(m0, v[r]);
+            else stage(m0, j0, v[r]);
+            next_item(m0, j0);
+          }
+        }
+      }
+      __syncthreads();
     }
   }
   __syncthreads();
