@@ -506,14 +506,26 @@ q4g_gemv_kernel(const GemvArgs a) {
     griddep_wait();  // x may be written by the previous kernel in the stream
     const int kb0 = g0 * GS;
     const int f4 = (ng * GS) >> 2;
-    const int f4p = (f4 + 31) & ~31;  // per-row item runs padded to whole warps
     constexpr int kUnroll = 4;
     const int nthr = kCons * 32;
-    auto load4 = [&](int it) -> float4 {
-      const int mrow = it / f4p, f = it - mrow * f4p;
+    // x item (mrow, j): float4 f = threadIdx.x + nthr j of row mrow; fpt per
+    // row, m fpt per thread, stepped as (mrow, j) without divisions.  A warp's
+    // 32 lanes share (mrow, j) and cover 32 consecutive f (128 k): the row
+    // maxima and the 64-k digit sums reduce per warp.  Float4 past the slice
+    // load as zeros and store no digits.
+    const int fpt = (f4 + nthr - 1) / nthr;
+    const int nit = a.m * fpt;
+    auto next_item = [&](int& mrow, int& j) {
+      if (++j == fpt) {
+        j = 0;
+        ++mrow;
+      }
+    };
+    auto load_x = [&](int mrow, int j) -> float4 {
+      const int f = threadIdx.x + j * nthr;
       const int k = kb0 + 4 * f;
       float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (it < a.m * f4p && f < f4) {
+      if (f < f4) {
         const float* xr = a.x + (size_t)mrow * a.ldx + k;
         if (a.vec4 && k + 3 < a.k) {
           v = __ldg(reinterpret_cast<const float4*>(xr));
@@ -526,35 +538,44 @@ q4g_gemv_kernel(const GemvArgs a) {
       }
       return v;
     };
-    const int total = a.m * f4p;
-    // pass 1: max |x| per row (a warp's 32 items always belong to one row).
-    // The first kCache items of every thread are loaded at once and kept in
-    // registers for pass 2; only a larger x is read a second time.
+    // pass 1: max |x| per row.  The first kCache items of every thread are
+    // loaded at once and kept in registers for pass 2; only a larger x is
+    // read a second time.
     constexpr int kCache = MODE == 1 ? 8 : (KQG == 1 ? 0 : 4);
     float4 cache[kCache > 0 ? kCache : 1];
+    {
+      int mr = 0, jj = 0;
 #pragma unroll
-    for (int r = 0; r < kCache; ++r) cache[r] = load4(threadIdx.x + r * nthr);
-    auto row_max = [&](const float4& v, int it) {
+      for (int r = 0; r < kCache; ++r) {
+        cache[r] = r < nit ? load_x(mr, jj) : make_float4(0.f, 0.f, 0.f, 0.f);
+        next_item(mr, jj);
+      }
+    }
+    auto row_max = [&](const float4& v, int mrow) {
       float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      if (lane == 0) atomicMax(&xmax[it / f4p], __float_as_uint(mx));
+      if (lane == 0) atomicMax(&xmax[mrow], __float_as_uint(mx));
     };
+    int mr1 = 0, jj1 = 0;   // the first item past the cached ones
 #pragma unroll
     for (int r = 0; r < kCache; ++r) {
-      const int it = threadIdx.x + r * nthr;
-      if (it - lane >= total) break;  // uniform across the warp (total is a multiple of 32)
-      row_max(cache[r], it);
+      if (r < nit) row_max(cache[r], mr1);
+      next_item(mr1, jj1);
     }
-    for (int it0 = threadIdx.x + kCache * nthr; it0 - lane < total; it0 += nthr * kUnroll) {
+    for (int i0 = kCache, mr = mr1, jj = jj1; i0 < nit; i0 += kUnroll) {
       float4 vv[kUnroll];
-#pragma unroll
-      for (int r = 0; r < kUnroll; ++r) vv[r] = load4(it0 + r * nthr);
+      int mq = mr, jq = jj;
 #pragma unroll
       for (int r = 0; r < kUnroll; ++r) {
-        const int it = it0 + r * nthr;
-        if (it - lane >= total) break;
-        row_max(vv[r], it);
+        vv[r] = i0 + r < nit ? load_x(mr, jj) : make_float4(0.f, 0.f, 0.f, 0.f);
+        next_item(mr, jj);
+      }
+#pragma unroll
+      for (int r = 0; r < kUnroll; ++r) {
+        if (i0 + r >= nit) break;   // the same for every thread
+        row_max(vv[r], mq);
+        next_item(mq, jq);
       }
     }
     named_barrier(1, nthr);
@@ -562,10 +583,15 @@ q4g_gemv_kernel(const GemvArgs a) {
     // 4 k per word straight into the B fragment slots, and exact digit sums
     const int cols = MODE == 1 ? 2 * a.m : a.m;
     uint32_t* xw = reinterpret_cast<uint32_t*>(xs);
-    auto digits = [&](const float4& v, int it) {
-      const int mrow = it / f4p, f = it - mrow * f4p;
-      const float mxv = __uint_as_float(xmax[mrow]);
-      const float inv = mxv > 0.f ? 127.0f / mxv : 0.f;
+    int inv_row = -1;
+    float inv = 0.f;
+    auto digits = [&](const float4& v, int mrow, int jidx) {
+      const int f = threadIdx.x + jidx * nthr;
+      if (mrow != inv_row) {        // 127 / max|x| once per row, not per item
+        const float mxv = __uint_as_float(xmax[mrow]);
+        inv = mxv > 0.f ? 127.0f / mxv : 0.f;
+        inv_row = mrow;
+      }
       const float xv[4] = {v.x, v.y, v.z, v.w};
       uint32_t w0 = 0, w1 = 0;
       int s0 = 0, s1 = 0;
@@ -602,21 +628,27 @@ q4g_gemv_kernel(const GemvArgs a) {
         atomicAdd(&sdi[grp * 16 + 8 + mrow], s1);
       }
     };
+    {
+      int mr = 0, jj = 0;
 #pragma unroll
-    for (int r = 0; r < kCache; ++r) {
-      const int it = threadIdx.x + r * nthr;
-      if (it - lane >= total) break;
-      digits(cache[r], it);
-    }
-    for (int it0 = threadIdx.x + kCache * nthr; it0 - lane < total; it0 += nthr * kUnroll) {
-      float4 vv[kUnroll];
+      for (int r = 0; r < kCache; ++r) {
+        if (r < nit) digits(cache[r], mr, jj);
+        next_item(mr, jj);
+      }
+      for (int i0 = kCache; i0 < nit; i0 += kUnroll) {
+        float4 vv[kUnroll];
+        int mq = mr, jq = jj;
 #pragma unroll
-      for (int r = 0; r < kUnroll; ++r) vv[r] = load4(it0 + r * nthr);
+        for (int r = 0; r < kUnroll; ++r) {
+          vv[r] = i0 + r < nit ? load_x(mr, jj) : make_float4(0.f, 0.f, 0.f, 0.f);
+          next_item(mr, jj);
+        }
 #pragma unroll
-      for (int r = 0; r < kUnroll; ++r) {
-        const int it = it0 + r * nthr;
-        if (it - lane >= total) break;
-        digits(vv[r], it);
+        for (int r = 0; r < kUnroll; ++r) {
+          if (i0 + r >= nit) break;
+          digits(vv[r], mq, jq);
+          next_item(mq, jq);
+        }
       }
     }
     named_barrier(1, nthr);
