@@ -1558,8 +1558,9 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
     e2e = {"value": bytes_step / e2e_s / 1e9, "unit": "GB/s",
-           "h2d_bytes_per_step": R * M * K * 4, "d2h_bytes_per_step": R * M * N_PER_GPU * 4,
-           "api": "nimf_matmul_w_group (host buffers, blocking)",
+           "h2d_bytes_per_step": M * K * 4, "d2h_bytes_per_step": R * M * N_PER_GPU * 4,
+           "api": "nimf_matmul_w_group (host buffers, blocking; x copied once for the group, "
+                  "the outputs in one copy because their host buffers are contiguous)",
            "note": "per-rank shard outputs; no host all-gather" if world > 1 else ""}
 
     cpu = None

@@ -171,7 +171,9 @@ int nimf_matmul_w_dev(nimf_weight_t w, const float* x_dev, int64_t m, float* y_d
 int nimf_matmul_w_group_dev(const nimf_weight_t* handles, int count, const float* x_dev,
                             int64_t m, float* const* y_devs, void* stream);
 
-/* HOST-buffer, blocking form of nimf_matmul_w_group_dev. */
+/* HOST-buffer, blocking form of nimf_matmul_w_group_dev.  x is copied in
+ * once for the group; outputs whose host buffers follow one another
+ * (ys[i+1] == ys[i] + M * N_i) come back in one copy. */
 int nimf_matmul_w_group(const nimf_weight_t* handles, int count, const float* x, int64_t m,
                         float* const* ys);
 

@@ -276,3 +276,40 @@ def test_grouped_gemv_matches_individual(nimf_gpu, m):
         # differently from a single one: agreement to ~1e-5, far inside TOL
         assert rel_err(y, w.matmul(x, m)) <= 1e-4
         w.free()
+
+
+@pytest.mark.parametrize("m", [1, 3])
+def test_grouped_host_outputs_contiguous_or_scattered(nimf_gpu, m):
+    """nimf_matmul_w_group with host outputs that follow one another in one
+    buffer (returned in one copy), in reverse order inside that buffer, and
+    with a zero-row weight between them: every layout gives the same bytes."""
+    k, gs = 1024, 128
+    shapes = [384, 256, 0, 512]
+    ws = []
+    for i, n in enumerate(shapes):
+        p, s, z, _ = quantized(max(n, 64), k, gs, seed=70 + i)
+        # n == 0: an empty row shard of a 64-row weight
+        ws.append(nimf_gpu.Weight.q4g(p, s, z, max(n, 64), k, gs, rows=(0, n)))
+    x = np.random.default_rng(5).standard_normal((m, k)).astype(np.float32)
+    want = nimf_gpu.Weight.matmul_group(ws, x, m)
+    L = nimf_gpu.lib()
+    hs = (ctypes.c_uint64 * len(ws))(*[w.handle for w in ws])
+    total = m * sum(shapes)
+    offs = np.cumsum([0] + [m * n for n in shapes])
+    # contiguous, in call order
+    buf = np.full(total, np.nan, np.float32)
+    yp = (ctypes.c_void_p * len(ws))(*[buf.ctypes.data + 4 * int(o) for o in offs[:-1]])
+    nimf_gpu.check(L.nimf_matmul_w_group(hs, len(ws), x.ctypes.data, m, yp))
+    for i, n in enumerate(shapes):
+        got = buf[offs[i]:offs[i + 1]].reshape(m, n)
+        assert np.array_equal(got, want[i])
+    # reverse order inside one buffer: no two outputs follow one another
+    roffs = np.cumsum([0] + [m * n for n in shapes[::-1]])[:-1][::-1]
+    buf2 = np.full(total, np.nan, np.float32)
+    yp2 = (ctypes.c_void_p * len(ws))(*[buf2.ctypes.data + 4 * int(o) for o in roffs])
+    nimf_gpu.check(L.nimf_matmul_w_group(hs, len(ws), x.ctypes.data, m, yp2))
+    for i, n in enumerate(shapes):
+        got = buf2[roffs[i]:roffs[i] + m * n].reshape(m, n)
+        assert np.array_equal(got, want[i])
+    for w in ws:
+        w.free()
