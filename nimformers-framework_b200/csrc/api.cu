@@ -160,6 +160,113 @@ int stage_out(size_t bytes, void** p) {
   return NIMF_OK;
 }
 
+// Pinned host staging for the matmul entry points' PAGEABLE host buffers (a
+// Nim seq, a numpy array).  cudaMemcpyAsync on pageable memory goes through
+// the driver's own staging and, device to host, waits for the stream: one
+// host wait per copy.  Up to kHostStageMax bytes go through these pinned
+// buffers instead (a host memcpy each way), so a call waits on its stream
+// once.  Pinned buffers, and larger pageable ones, are copied directly.
+namespace {
+constexpr size_t kHostStageMax = 4u << 20;
+struct HostStage {
+  void* p = nullptr;
+  size_t bytes = 0;
+  bool busy = false;   // an async copy from / to it may still be pending
+};
+HostStage g_hin, g_hout;
+
+bool is_pageable(const void* p) {
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();   // not a CUDA-known pointer: treat as pageable
+    return true;
+  }
+  return at.type == cudaMemoryTypeUnregistered;
+}
+
+// Makes s hold `bytes` and be free to overwrite.
+int host_stage(HostStage& s, size_t bytes) {
+  if (s.busy) {
+    NIMF_CUDA_TRY(cudaStreamSynchronize(g_ctx.stream));
+    s.busy = false;
+  }
+  if (s.bytes >= bytes && s.p) return NIMF_OK;
+  if (s.p) cudaFreeHost(s.p);
+  s.p = nullptr;
+  s.bytes = 0;
+  const size_t want = std::max<size_t>(bytes, 64u << 10);
+  NIMF_CUDA_TRY(cudaHostAlloc(&s.p, want, cudaHostAllocDefault));
+  s.bytes = want;
+  return NIMF_OK;
+}
+
+void release_host_stages() {
+  for (HostStage* s : {&g_hin, &g_hout}) {
+    if (s->p) cudaFreeHost(s->p);
+    *s = HostStage();
+  }
+}
+
+// Host x -> device, through the pinned stage when x is small and pageable.
+int copy_in(void* dst_dev, const void* src, size_t bytes, cudaStream_t st) {
+  if (bytes == 0) return NIMF_OK;
+  if (bytes <= kHostStageMax && is_pageable(src)) {
+    NIMF_TRY(host_stage(g_hin, bytes));
+    std::memcpy(g_hin.p, src, bytes);
+    g_hin.busy = true;
+    src = g_hin.p;
+  }
+  NIMF_CUDA_TRY(cudaMemcpyAsync(dst_dev, src, bytes, cudaMemcpyHostToDevice, st));
+  return NIMF_OK;
+}
+
+// Device outputs -> host: outs[i] receives bytes[i] from src_dev + offset of
+// the outputs before it (the device staging is contiguous).  Synchronises the
+// stream.  Pageable outputs whose total fits the pinned stage come back in
+// one copy and are spread on the host; otherwise host outputs that follow one
+// another go back in one copy each run.
+int copy_out_sync(float* const* outs, const size_t* bytes, int count, const void* src_dev,
+                  cudaStream_t st) {
+  size_t total = 0;
+  bool pageable = false;
+  for (int i = 0; i < count; ++i) {
+    total += bytes[i];
+    if (bytes[i] > 0 && !pageable) pageable = is_pageable(outs[i]);
+  }
+  if (total > 0 && pageable && total <= kHostStageMax) {
+    NIMF_TRY(host_stage(g_hout, total));
+    NIMF_CUDA_TRY(cudaMemcpyAsync(g_hout.p, src_dev, total, cudaMemcpyDeviceToHost, st));
+    g_hout.busy = true;
+    NIMF_CUDA_TRY(cudaStreamSynchronize(st));
+    g_hout.busy = false;
+    g_hin.busy = false;
+    size_t off = 0;
+    for (int i = 0; i < count; ++i) {
+      if (bytes[i] > 0) std::memcpy(outs[i], (const char*)g_hout.p + off, bytes[i]);
+      off += bytes[i];
+    }
+    return NIMF_OK;
+  }
+  const char* src = (const char*)src_dev;
+  for (int i = 0; i < count;) {
+    if (bytes[i] == 0) {
+      ++i;
+      continue;
+    }
+    size_t n = bytes[i];
+    int j = i + 1;
+    while (j < count && bytes[j] > 0 && (const char*)outs[j] == (const char*)outs[i] + n)
+      n += bytes[j++];
+    NIMF_CUDA_TRY(cudaMemcpyAsync(outs[i], src, n, cudaMemcpyDeviceToHost, st));
+    src += n;
+    i = j;
+  }
+  NIMF_CUDA_TRY(cudaStreamSynchronize(st));
+  g_hin.busy = false;
+  return NIMF_OK;
+}
+}  // namespace
+
 int64_t Weight::rows() const {
   switch (kind) {
     case NIMF_KIND_INT4_ASYM: return q4.rows;
@@ -349,6 +456,7 @@ int nimf_shutdown(void) {
   release_f32_scratch();
   device_free(g_ctx.stage_in);
   device_free(g_ctx.stage_out);
+  release_host_stages();
   if (g_ctx.host_err) cudaFreeHost((void*)g_ctx.host_err);
   cudaStreamDestroy(g_ctx.stream);
   g_ctx = Context();
@@ -612,11 +720,10 @@ int nimf_matmul_w(nimf_weight_t h, const float* x, int64_t m, float* y) {
   void *dx, *dy;
   NIMF_TRY(stage_in((size_t)(m * k) * 4, &dx));
   NIMF_TRY(stage_out((size_t)(m * rows) * 4, &dy));
-  if (m * k > 0)
-    NIMF_CUDA_TRY(cudaMemcpyAsync(dx, x, (size_t)(m * k) * 4, cudaMemcpyHostToDevice, c->stream));
+  NIMF_TRY(copy_in(dx, x, (size_t)(m * k) * 4, c->stream));
   NIMF_TRY(matmul_dev(w, (const float*)dx, m, (float*)dy, c->stream));
-  NIMF_CUDA_TRY(cudaMemcpyAsync(y, dy, (size_t)(m * rows) * 4, cudaMemcpyDeviceToHost, c->stream));
-  NIMF_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  const size_t yb = (size_t)(m * rows) * 4;
+  NIMF_TRY(copy_out_sync(&y, &yb, 1, dy, c->stream));
   return check_device_error();
 }
 
@@ -680,24 +787,15 @@ int nimf_matmul_w_group(const nimf_weight_t* handles, int count, const float* x,
     yd[i] = (float*)dy + off;
     off += m * rows[i];
   }
-  if (m * k > 0)
-    NIMF_CUDA_TRY(cudaMemcpyAsync(dx, x, (size_t)(m * k) * 4, cudaMemcpyHostToDevice, c->stream));
+  NIMF_TRY(copy_in(dx, x, (size_t)(m * k) * 4, c->stream));
   NIMF_TRY(nimf_matmul_w_group_dev(handles, count, (const float*)dx, m, yd.data(), c->stream));
-  // The staged outputs are contiguous; outputs whose host buffers also follow
-  // one another go back in one copy (each copy costs a few microseconds of
-  // set-up, more than moving one projection's y).
-  for (int i = 0; i < count;) {
-    if (rows[i] == 0) {
-      ++i;
-      continue;
-    }
-    int64_t n = m * rows[i];
-    int j = i + 1;
-    while (j < count && rows[j] > 0 && ys[j] == ys[i] + n) n += m * rows[j++];
-    NIMF_CUDA_TRY(cudaMemcpyAsync(ys[i], yd[i], (size_t)n * 4, cudaMemcpyDeviceToHost, c->stream));
-    i = j;
-  }
-  NIMF_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  // The staged outputs are contiguous: they come back in one copy when they
+  // are pageable and small, else in one copy per run of host buffers that
+  // follow one another (each copy costs a few microseconds of set-up, more
+  // than moving one projection's y).
+  std::vector<size_t> yb((size_t)count);
+  for (int i = 0; i < count; ++i) yb[i] = (size_t)(m * rows[i]) * 4;
+  NIMF_TRY(copy_out_sync(ys, yb.data(), count, dy, c->stream));
   return check_device_error();
 }
 

@@ -313,3 +313,33 @@ def test_grouped_host_outputs_contiguous_or_scattered(nimf_gpu, m):
         assert np.array_equal(got, want[i])
     for w in ws:
         w.free()
+
+
+def test_host_buffers_pageable_pinned_and_over_the_stage(nimf_gpu):
+    """nimf_matmul_w with pageable x / y (through the library's pinned stage),
+    with pinned x / y (copied directly), and with a pageable y larger than the
+    4 MiB stage (copied directly): the same bytes every way."""
+    import torch
+    k, gs, n = 1024, 128, 8192
+    p, s, z, ngr = quantized(n, k, gs, seed=81)
+    w = nimf_gpu.Weight.q4g(p, s, z, n, k, gs)
+    L = nimf_gpu.lib()
+    for m in (1, 130):   # 130 rows of y are 4.26 MB
+        x = np.random.default_rng(m).standard_normal((m, k)).astype(np.float32)
+        y_pageable = w.matmul(x, m)
+        assert rel_err(y_pageable, O.dequant_matmul_q4(x, p, s, z, m, k, n, gs, ngr)) <= TOL
+        xp = torch.from_numpy(x).pin_memory()
+        yp = torch.full((m, n), float("nan")).pin_memory()
+        nimf_gpu.check(L.nimf_matmul_w(w.handle, ctypes.c_void_p(xp.data_ptr()), m,
+                                       ctypes.c_void_p(yp.data_ptr())))
+        assert np.array_equal(yp.numpy(), y_pageable)
+        # pinned x, pageable y and the reverse
+        yq = np.full((m, n), np.nan, np.float32)
+        nimf_gpu.check(L.nimf_matmul_w(w.handle, ctypes.c_void_p(xp.data_ptr()), m,
+                                       ctypes.c_void_p(yq.ctypes.data)))
+        assert np.array_equal(yq, y_pageable)
+        yp.fill_(float("nan"))
+        nimf_gpu.check(L.nimf_matmul_w(w.handle, ctypes.c_void_p(x.ctypes.data), m,
+                                       ctypes.c_void_p(yp.data_ptr())))
+        assert np.array_equal(yp.numpy(), y_pageable)
+    w.free()
