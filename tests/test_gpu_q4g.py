@@ -311,6 +311,17 @@ def test_grouped_host_outputs_contiguous_or_scattered(nimf_gpu, m):
     for i, n in enumerate(shapes):
         got = buf2[roffs[i]:roffs[i] + m * n].reshape(m, n)
         assert np.array_equal(got, want[i])
+    # the same two layouts in pinned memory: copied straight into the buffers,
+    # one copy per run of outputs that follow one another
+    import torch
+    for layout in (offs[:-1], roffs):
+        pbuf = torch.full((total,), float("nan")).pin_memory()
+        ypp = (ctypes.c_void_p * len(ws))(*[pbuf.data_ptr() + 4 * int(o) for o in layout])
+        nimf_gpu.check(L.nimf_matmul_w_group(hs, len(ws), x.ctypes.data, m, ypp))
+        got_all = pbuf.numpy()
+        for i, n in enumerate(shapes):
+            o = int(layout[i])
+            assert np.array_equal(got_all[o:o + m * n].reshape(m, n), want[i])
     for w in ws:
         w.free()
 
