@@ -1261,6 +1261,9 @@ def run_ncu_case(name):
           (graph replays: 2 warm-up, 2 timed);
       prefill: run_prefill_7b with one layer copy (both int4 GEMMs, each
           projection alone);
+      decode_matmul: the 7B-shape int4 decode matmul stack of run_decode_7b at
+          batch 1 (one eager step, then graph replays: 2 warm-up, 2 timed; 129
+          GEMV launches per step);
       fw: an FP4 E2M1 block-16 weight and a one-byte CustomFloat(4,3) weight
           with per-row scales, both 28672 x 8192 (random codes): GEMV launches
           FP4 M=1, fp8 M=1, FP4 M=8, fp8 M=8, fp8 M=16, then the tcgen05 GEMM at
@@ -1271,6 +1274,11 @@ def run_ncu_case(name):
     if name == "decode_step":
         nimf.init(0)
         run_decode_7b_full(nimf, torch, 2, 2, layers=2)
+        print("ncu case %s done" % name)
+        return
+    if name == "decode_matmul":
+        nimf.init(0)
+        run_decode_7b(nimf, torch, 2, 2, batches=(1,))
         print("ncu case %s done" % name)
         return
     if name == "prefill":
@@ -1663,7 +1671,7 @@ def main():
     ap.add_argument("--format-steps", type=int, default=40,
                     help="timed steps of the FP4/fp8/APF/int8 measurements (0: skip)")
     ap.add_argument("--ncu-case", default=None,
-                    help="run one small fixed workload for an ncu capture and exit (fw, decode_step, prefill)")
+                    help="run one fixed workload for an ncu capture and exit (fw, decode_step, decode_matmul, prefill)")
     args = ap.parse_args()
     if args.ncu_case:
         run_ncu_case(args.ncu_case)
